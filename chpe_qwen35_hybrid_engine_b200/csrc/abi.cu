@@ -1,0 +1,965 @@
+// abi.cu -- the C ABI (include/chpe_b200.h): contexts, device tensors, the
+// host-pointer operators that mirror the reference's Zig GEMV operators, and
+// the device-pointer GEMV entry points.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "../../include/chpe_b200.h"
+#include "internal.h"
+
+using namespace chpe;
+
+struct chpe_tensor {
+    DevMatrix m;
+    uint64_t fingerprint = 0;  // content hash of the host bytes it was made from
+};
+
+struct chpe_ctx {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    std::string err;
+    int *d_err = nullptr;
+    GemvScratch scr;
+    // staging for the host-pointer operators
+    void *d_in = nullptr;
+    size_t d_in_bytes = 0;
+    float *d_out = nullptr;
+    size_t d_out_bytes = 0;
+    float *d_scales = nullptr;
+    std::unordered_map<const void *, chpe_tensor *> registry;
+    std::vector<chpe_tensor *> owned;
+};
+
+namespace {
+
+int fail(chpe_ctx *ctx, int code, const char *fmt, ...) {
+    if (ctx) {
+        char buf[512];
+        va_list ap;
+        va_start(ap, fmt);
+        vsnprintf(buf, sizeof buf, fmt, ap);
+        va_end(ap);
+        ctx->err = buf;
+    }
+    return code;
+}
+
+#define CK(call)                                                                                     \
+    do {                                                                                             \
+        cudaError_t e_ = (call);                                                                     \
+        if (e_ != cudaSuccess)                                                                       \
+            return fail(ctx, e_ == cudaErrorMemoryAllocation ? CHPE_ENOMEM : CHPE_ECUDA, "%s: %s (%s:%d)", \
+                        #call, cudaGetErrorString(e_), __FILE__, __LINE__);                          \
+    } while (0)
+
+bool is_device_ptr(const void *p) {
+    if (!p) return false;
+    cudaPointerAttributes a;
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged;
+}
+
+int grow(chpe_ctx *ctx, void **p, size_t *cap, size_t need) {
+    if (need <= *cap) return CHPE_OK;
+    if (*p) cudaFree(*p);
+    *p = nullptr;
+    *cap = 0;
+    size_t sz = need < 4096 ? 4096 : need + need / 4;
+    CK(cudaMalloc(p, sz));
+    *cap = sz;
+    return CHPE_OK;
+}
+
+// Copy `bytes` from host or device memory into a fresh device buffer (or
+// return the device pointer itself when it already is one).
+int to_device(chpe_ctx *ctx, const void *src, size_t bytes, const void **dev, void **owned) {
+    *owned = nullptr;
+    if (!src || bytes == 0) {
+        *dev = nullptr;
+        return CHPE_OK;
+    }
+    if (is_device_ptr(src)) {
+        *dev = src;
+        return CHPE_OK;
+    }
+    CK(cudaMalloc(owned, bytes));
+    CK(cudaMemcpy(*owned, src, bytes, cudaMemcpyHostToDevice));
+    *dev = *owned;
+    return CHPE_OK;
+}
+
+int log2_exact(int v) {
+    int s = 0;
+    while ((1 << s) < v) ++s;
+    return (1 << s) == v ? s : -1;
+}
+
+void free_matrix(DevMatrix &m) {
+    cudaFree(m.codes);
+    cudaFree(m.meta);
+    cudaFree(m.bias);
+    cudaFree(m.out_cols);
+    cudaFree(m.out_w);
+    m = DevMatrix();
+}
+
+struct UploadSpec {
+    int bits, layout, meta_kind, group;
+    uint32_t xorv;
+    float zc, scale;
+    float f32_zc;  // stored-code offset removed from ROW_AFFINE offsets
+};
+
+// Build a DevMatrix from device-resident inputs.
+int build_matrix(chpe_ctx *ctx, const UploadSpec &u, const uint8_t *d_codes, size_t row_stride, int src_bits,
+                 const __half *d_s, const __half *d_z, const float *d_fs, const float *d_fo, const float *d_bias,
+                 size_t rows, size_t cols, DevMatrix *out) {
+    DevMatrix m;
+    m.bits = u.bits;
+    m.layout = u.layout;
+    m.meta_kind = u.meta_kind;
+    m.N = (int)rows;
+    m.K = (int)cols;
+    m.n_strips = ceil_div((long)rows, kStripRows);
+    const int kc = u.layout == kLayoutS8 ? 32 : chunk_cols(u.bits);
+    m.n_chunks = ceil_div((long)cols, kc);
+    m.group = u.group;
+    m.n_groups = (u.layout == kLayoutS8) ? 0 : (int)(cols / u.group);
+    m.group_shift = m.n_groups > 1 ? log2_exact(u.group) : 0;
+    m.scale = u.scale;
+    m.zc = u.zc;
+    m.code_bytes = (size_t)m.n_strips * m.n_chunks * kChunkBytes;
+    cudaError_t e = cudaMalloc(&m.codes, m.code_bytes);
+    if (e != cudaSuccess) return fail(ctx, CHPE_ENOMEM, "cudaMalloc codes (%zu B): %s", m.code_bytes, cudaGetErrorString(e));
+    e = launch_repack2(d_codes, row_stride, m.N, m.K, src_bits, u.bits, u.layout, u.xorv, m.codes, m.n_strips,
+                       m.n_chunks, ctx->stream);
+    if (e != cudaSuccess) {
+        free_matrix(m);
+        return fail(ctx, CHPE_ECUDA, "repack: %s", cudaGetErrorString(e));
+    }
+    if (u.meta_kind != kMetaNone) {
+        m.meta_bytes_total = (size_t)m.n_strips * m.n_groups * 16 * meta_bytes(u.meta_kind);
+        e = cudaMalloc(&m.meta, m.meta_bytes_total);
+        if (e == cudaSuccess)
+            e = launch_meta_repack(u.meta_kind, d_s, d_z, d_fs, d_fo, u.f32_zc, m.N, m.n_groups, m.meta, m.n_strips,
+                                   ctx->stream);
+        if (e != cudaSuccess) {
+            free_matrix(m);
+            return fail(ctx, CHPE_ECUDA, "metadata: %s", cudaGetErrorString(e));
+        }
+    }
+    if (d_bias) {
+        e = cudaMalloc(&m.bias, rows * sizeof(float));
+        if (e == cudaSuccess) e = cudaMemcpyAsync(m.bias, d_bias, rows * sizeof(float), cudaMemcpyDeviceToDevice, ctx->stream);
+        if (e != cudaSuccess) {
+            free_matrix(m);
+            return fail(ctx, CHPE_ECUDA, "bias: %s", cudaGetErrorString(e));
+        }
+    }
+    e = cudaStreamSynchronize(ctx->stream);
+    if (e != cudaSuccess) {
+        free_matrix(m);
+        return fail(ctx, CHPE_ECUDA, "upload sync: %s", cudaGetErrorString(e));
+    }
+    *out = m;
+    return CHPE_OK;
+}
+
+int spec_from_fmt(chpe_ctx *ctx, const chpe_fmt *f, size_t cols, UploadSpec *u) {
+    UploadSpec s = {};
+    s.bits = f->bits;
+    if (s.bits != 2 && s.bits != 4 && s.bits != 8) return fail(ctx, CHPE_EINVAL, "bits must be 2, 4 or 8 (got %d)", s.bits);
+    s.group = f->group > 0 ? f->group : (int)cols;
+    s.layout = kLayoutF16;
+    s.xorv = 0;
+    s.zc = 0.0f;
+    s.scale = 1.0f;
+    s.f32_zc = 0.0f;
+    switch (f->scheme) {
+    case CHPE_SCHEME_I8_TENSOR:
+        if (s.bits != 8) return fail(ctx, CHPE_EINVAL, "I8_TENSOR needs bits = 8");
+        s.layout = kLayoutS8;
+        s.meta_kind = kMetaNone;
+        s.group = (int)cols;
+        break;
+    case CHPE_SCHEME_I8_GROUP_F16:
+        if (s.bits != 8) return fail(ctx, CHPE_EINVAL, "I8_GROUP_F16 needs bits = 8");
+        s.meta_kind = kMetaS16;
+        s.xorv = 0x80;
+        s.zc = 128.0f;
+        break;
+    case CHPE_SCHEME_U_GROUP_F16_ZERO:
+        s.meta_kind = kMetaSZ16;
+        break;
+    case CHPE_SCHEME_U_GROUP_F16_CONST_ZERO:
+        s.meta_kind = kMetaS16;
+        s.zc = f->zero;
+        break;
+    case CHPE_SCHEME_W2_CODEBOOK_GROUP_F16:
+        if (s.bits != 2) return fail(ctx, CHPE_EINVAL, "W2_CODEBOOK needs bits = 2");
+        s.meta_kind = kMetaS16;
+        s.xorv = 2;
+        s.zc = 2.0f;
+        break;
+    case CHPE_SCHEME_ROW_AFFINE_F32:
+        s.meta_kind = kMetaF32;
+        s.group = (int)cols;
+        s.xorv = s.bits == 8 ? 0x80 : s.bits == 2 ? 2 : 0;
+        s.f32_zc = s.bits == 8 ? 128.0f : s.bits == 4 ? 8.0f : 2.0f;
+        break;
+    default:
+        return fail(ctx, CHPE_EINVAL, "unknown scheme %d", f->scheme);
+    }
+    if (s.layout == kLayoutF16) {
+        if (cols % (size_t)s.group != 0) return fail(ctx, CHPE_EINVAL, "cols %zu not a multiple of group %d", cols, s.group);
+        const int n_groups = (int)(cols / s.group);
+        if (n_groups > 1) {
+            const int kc = chunk_cols(s.bits);
+            const int min_group = s.bits == 2 ? 64 : kc;
+            if (log2_exact(s.group) < 0 || s.group < min_group)
+                return fail(ctx, CHPE_ENOTSUP, "group %d unsupported for %d-bit codes (power of two >= %d)", s.group,
+                            s.bits, min_group);
+        }
+    }
+    *u = s;
+    return CHPE_OK;
+}
+
+int ensure_scratch(chpe_ctx *ctx, const GemvPlan &P, bool, int) {
+    int rc;
+    if ((rc = grow(ctx, &ctx->scr.ws, &ctx->scr.ws_bytes, P.ws_bytes + 64))) return rc;
+    if ((size_t)P.counters > ctx->scr.counters_n) {
+        if (ctx->scr.counters) cudaFree(ctx->scr.counters);
+        ctx->scr.counters = nullptr;
+        size_t n = (size_t)P.counters + 1024;
+        CK(cudaMalloc(&ctx->scr.counters, n * sizeof(unsigned)));
+        CK(cudaMemset(ctx->scr.counters, 0, n * sizeof(unsigned)));
+        ctx->scr.counters_n = n;
+    }
+    return CHPE_OK;
+}
+
+// Activation fragments of one block of <= 8 rows, ready for the GEMV kernel.
+struct Xfrag {
+    int layout = kLayoutF16, M = 0, K = 0, Kp = 0, e_cols = 0, x_dtype = 0;
+    bool xsplit = false;
+    void *xf = nullptr, *xlo = nullptr;
+    float *xs = nullptr;
+    const float *sx = nullptr;
+    const float *xrow = nullptr;  // fp32 rows for outlier columns
+};
+
+int check_x(chpe_ctx *ctx, const DevMatrix &w, int x_dtype, const float *x_scales) {
+    if (w.layout == kLayoutS8) {
+        if (x_dtype != CHPE_X_I8 && x_dtype != CHPE_X_F32)
+            return fail(ctx, CHPE_ENOTSUP, "int8 weights take int8 or fp32 activations");
+        if (x_dtype == CHPE_X_I8 && !x_scales) return fail(ctx, CHPE_EINVAL, "int8 activations need x_scales");
+    } else {
+        if (x_dtype == CHPE_X_I8) return fail(ctx, CHPE_ENOTSUP, "int8 activations need an I8_TENSOR weight");
+        if (x_dtype != CHPE_X_F32 && x_dtype != CHPE_X_BF16 && x_dtype != CHPE_X_F16)
+            return fail(ctx, CHPE_EINVAL, "unknown activation dtype %d", x_dtype);
+    }
+    return CHPE_OK;
+}
+
+int w_kp(const DevMatrix &w) { return w.n_chunks * (w.layout == kLayoutS8 ? 32 : chunk_cols(w.bits)); }
+
+// Fill fragments (buffers already sized) from M <= 8 rows of x.
+int prep_x(chpe_ctx *ctx, Xfrag &f, const void *x, const float *x_scales, float *sx_buf, cudaStream_t st) {
+    cudaError_t e;
+    if (f.layout == kLayoutS8) {
+        if (f.x_dtype == CHPE_X_I8) {
+            e = launch_xprep_s8(static_cast<const int8_t *>(x), f.M, f.K, f.Kp, f.xf, st);
+            if (e == cudaSuccess && sx_buf) e = cudaMemcpyAsync(sx_buf, x_scales, f.M * sizeof(float), cudaMemcpyDeviceToDevice, st);
+            f.sx = sx_buf ? sx_buf : x_scales;
+        } else {
+            e = launch_act_quant_s8(static_cast<const float *>(x), f.M, f.K, f.Kp, nullptr, sx_buf, f.xf, st);
+            f.sx = sx_buf;
+        }
+    } else {
+        e = launch_xprep_f16(x, f.x_dtype, f.M, f.K, f.Kp, f.e_cols, f.xsplit, f.xf, f.xlo, f.xs, st);
+    }
+    if (e != cudaSuccess) return fail(ctx, CHPE_ECUDA, "activation prep: %s", cudaGetErrorString(e));
+    return CHPE_OK;
+}
+
+int gemv_core(chpe_ctx *ctx, const DevMatrix &w0, const DevMatrix *w1, int mode, const Xfrag &f, float *y, int ldy,
+              int accumulate, const float *scale_override0, const float *scale_override1, cudaStream_t st) {
+    GemvPlan P;
+    plan_gemv(w0, f.M, mode, f.xsplit, &P);
+    if (w0.layout != f.layout || w0.K != f.K || w_kp(w0) > f.Kp || (w0.layout == kLayoutF16 && P.e_cols != f.e_cols))
+        return fail(ctx, CHPE_EINVAL, "activation fragments do not match this tensor (K %d/%d, Kp %d/%d, block %d/%d)",
+                    w0.K, f.K, w_kp(w0), f.Kp, P.e_cols, f.e_cols);
+    int rc = ensure_scratch(ctx, P, false, f.M);
+    if (rc) return rc;
+    GemvParams p;
+    memset(&p, 0, sizeof p);
+    const DevMatrix *ws[2] = {&w0, w1 ? w1 : &w0};
+    const float *ovr[2] = {scale_override0, scale_override1};
+    for (int i = 0; i < 2; ++i) {
+        p.src[i].codes = ws[i]->codes;
+        p.src[i].meta = ws[i]->meta;
+        p.src[i].bias = ws[i]->bias;
+        p.src[i].out_cols = ws[i]->out_cols;
+        p.src[i].out_w = ws[i]->out_w;
+        p.src[i].scale = ovr[i] ? *ovr[i] : ws[i]->scale;
+        p.src[i].zc = ws[i]->zc;
+    }
+    if (w0.out_cols && !f.xrow) return fail(ctx, CHPE_EINVAL, "outlier columns need fp32 activations");
+    p.N = w0.N;
+    p.K = w0.K;
+    p.M = f.M;
+    p.n_strips = w0.n_strips;
+    p.n_chunks = w0.n_chunks;
+    p.n_groups = w0.n_groups;
+    p.group_shift = w0.group_shift;
+    p.meta_kind = w0.meta_kind;
+    p.n_sg = P.n_sg;
+    p.n_ks = P.n_ks;
+    p.cpk = P.cpk;
+    p.gps = P.gps;
+    p.xf = f.xf;
+    p.xlo = f.xlo;
+    p.xs = f.xs;
+    p.sx = f.sx;
+    p.xrow = f.xrow;
+    p.y = y;
+    p.ldy = ldy;
+    p.accumulate = accumulate;
+    p.ws = ctx->scr.ws;
+    p.counters = ctx->scr.counters;
+    p.err = ctx->d_err;
+    cudaError_t e = launch_gemv(w0, w1, P, p, st);
+    if (e != cudaSuccess) return fail(ctx, CHPE_ECUDA, "gemv launch: %s", cudaGetErrorString(e));
+    return CHPE_OK;
+}
+
+Xfrag xfrag_shape(const DevMatrix &w, int M, int x_dtype, size_t *xf_bytes, size_t *xs_bytes) {
+    Xfrag f;
+    f.layout = w.layout;
+    f.M = M;
+    f.K = w.K;
+    f.Kp = w_kp(w);
+    f.x_dtype = x_dtype;
+    f.xsplit = w.layout == kLayoutF16 && x_dtype == CHPE_X_F32;
+    GemvPlan P;
+    plan_gemv(w, M, 0, f.xsplit, &P);
+    f.e_cols = P.e_cols;
+    *xf_bytes = P.xf_bytes;
+    *xs_bytes = P.xs_bytes;
+    return f;
+}
+
+// Core GEMV driver shared by the entry points that take plain activations
+// (x is a device pointer [M][K]); blocks of 8 rows use the context scratch.
+int run_gemv(chpe_ctx *ctx, const DevMatrix &w0, const DevMatrix *w1, int mode, const void *x, int x_dtype,
+             const float *x_scales, int M, float *y, int ldy, int accumulate, const float *scale_override0,
+             const float *scale_override1, const float *xrow, cudaStream_t st) {
+    if (M < 1) return fail(ctx, CHPE_EINVAL, "M must be >= 1");
+    if (!x || !y) return fail(ctx, CHPE_EINVAL, "null x or y");
+    int rc = check_x(ctx, w0, x_dtype, x_scales);
+    if (rc) return rc;
+    const size_t elt = x_dtype == CHPE_X_F32 ? 4 : x_dtype == CHPE_X_I8 ? 1 : 2;
+    for (int m0 = 0; m0 < M; m0 += kMaxTokens) {
+        const int Mb = (M - m0) < kMaxTokens ? (M - m0) : kMaxTokens;
+        size_t xfb, xsb;
+        Xfrag f = xfrag_shape(w0, Mb, x_dtype, &xfb, &xsb);
+        if ((rc = grow(ctx, &ctx->scr.xf, &ctx->scr.xf_bytes, xfb))) return rc;
+        if (f.xsplit && (rc = grow(ctx, &ctx->scr.xlo, &ctx->scr.xlo_bytes, xfb))) return rc;
+        if ((rc = grow(ctx, reinterpret_cast<void **>(&ctx->scr.xs), &ctx->scr.xs_bytes, xsb + 32))) return rc;
+        if ((rc = grow(ctx, reinterpret_cast<void **>(&ctx->scr.sx), &ctx->scr.sx_bytes, 64 * sizeof(float)))) return rc;
+        f.xf = ctx->scr.xf;
+        f.xlo = ctx->scr.xlo;
+        f.xs = ctx->scr.xs;
+        f.xrow = xrow ? xrow + (size_t)m0 * w0.K : nullptr;
+        const void *xb = static_cast<const uint8_t *>(x) + (size_t)m0 * w0.K * elt;
+        if ((rc = prep_x(ctx, f, xb, x_scales ? x_scales + m0 : nullptr,
+                         (w0.layout == kLayoutS8 && x_dtype == CHPE_X_F32) ? ctx->scr.sx : nullptr, st)))
+            return rc;
+        if ((rc = gemv_core(ctx, w0, w1, mode, f, y + (size_t)m0 * ldy, ldy, accumulate, scale_override0,
+                            scale_override1, st)))
+            return rc;
+    }
+    return CHPE_OK;
+}
+
+int stage_in(chpe_ctx *ctx, const void *src, size_t bytes) {
+    int rc = grow(ctx, &ctx->d_in, &ctx->d_in_bytes, bytes);
+    if (rc) return rc;
+    CK(cudaMemcpyAsync(ctx->d_in, src, bytes, cudaMemcpyHostToDevice, ctx->stream));
+    return CHPE_OK;
+}
+
+int stage_out(chpe_ctx *ctx, size_t bytes) {
+    return grow(ctx, reinterpret_cast<void **>(&ctx->d_out), &ctx->d_out_bytes, bytes);
+}
+
+int finish(chpe_ctx *ctx) {
+    CK(cudaStreamSynchronize(ctx->stream));
+    int h_err = 0;
+    CK(cudaMemcpy(&h_err, ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (h_err) {
+        cudaMemset(ctx->d_err, 0, sizeof(int));
+        return fail(ctx, CHPE_ETIMEOUT, "kernel bounded wait expired (code %d)", h_err);
+    }
+    return CHPE_OK;
+}
+
+chpe_tensor *lookup(chpe_ctx *ctx, const void *key) {
+    auto it = ctx->registry.find(key);
+    return it == ctx->registry.end() ? nullptr : it->second;
+}
+
+// FNV-1a over `n` bytes; `sampled` hashes the first and last 4 KiB plus 64
+// strided 64-byte windows, enough to notice a host buffer that was freed and
+// reused for different weights at the same address.
+uint64_t fingerprint(const void *p, size_t n, bool sampled) {
+    const uint8_t *b = static_cast<const uint8_t *>(p);
+    uint64_t h = 1469598103934665603ull ^ n;
+    auto mix = [&](size_t off, size_t len) {
+        for (size_t i = 0; i < len && off + i < n; ++i) h = (h ^ b[off + i]) * 1099511628211ull;
+    };
+    if (!sampled || n <= 16384) {
+        mix(0, n);
+        return h;
+    }
+    mix(0, 4096);
+    mix(n - 4096, 4096);
+    for (int k = 0; k < 64; ++k) mix((n / 64) * k + 4096 % (n / 64), 64);
+    return h;
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// context
+// ---------------------------------------------------------------------------
+
+extern "C" const char *chpe_version(void) { return "chpe_b200 1.0 sm_100a"; }
+
+extern "C" int chpe_init(int device, chpe_ctx **out) {
+    if (!out) return CHPE_EINVAL;
+    *out = nullptr;
+    chpe_ctx *ctx = new chpe_ctx();
+    ctx->device = device;
+    cudaError_t e = cudaSetDevice(device);
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaMalloc(&ctx->d_err, sizeof(int));
+    if (e == cudaSuccess) e = cudaMemset(ctx->d_err, 0, sizeof(int));
+    if (e == cudaSuccess) e = cudaMalloc(reinterpret_cast<void **>(&ctx->d_scales), 64 * sizeof(float));
+    if (e != cudaSuccess) {
+        delete ctx;
+        return CHPE_ECUDA;
+    }
+    *out = ctx;
+    return CHPE_OK;
+}
+
+extern "C" int chpe_destroy(chpe_ctx *ctx) {
+    if (!ctx) return CHPE_EINVAL;
+    cudaSetDevice(ctx->device);
+    cudaStreamSynchronize(ctx->stream);
+    for (chpe_tensor *t : ctx->owned) {
+        free_matrix(t->m);
+        delete t;
+    }
+    cudaFree(ctx->scr.xf);
+    cudaFree(ctx->scr.xlo);
+    cudaFree(ctx->scr.xs);
+    cudaFree(ctx->scr.sx);
+    cudaFree(ctx->scr.ws);
+    cudaFree(ctx->scr.counters);
+    cudaFree(ctx->d_in);
+    cudaFree(ctx->d_out);
+    cudaFree(ctx->d_scales);
+    cudaFree(ctx->d_err);
+    cudaStreamDestroy(ctx->stream);
+    delete ctx;
+    return CHPE_OK;
+}
+
+extern "C" const char *chpe_last_error_string(const chpe_ctx *ctx) { return ctx ? ctx->err.c_str() : "null context"; }
+
+extern "C" int chpe_sync(chpe_ctx *ctx) {
+    if (!ctx) return CHPE_EINVAL;
+    CK(cudaDeviceSynchronize());
+    return finish(ctx);
+}
+
+// ---------------------------------------------------------------------------
+// tensors
+// ---------------------------------------------------------------------------
+
+static int upload_common(chpe_ctx *ctx, const chpe_fmt *fmt, const void *codes, size_t row_stride,
+                         const void *scales, const void *zeros, const float *bias, size_t rows, size_t cols,
+                         int src_bits, chpe_tensor **out) {
+    UploadSpec u;
+    int rc = spec_from_fmt(ctx, fmt, cols, &u);
+    if (rc) return rc;
+    if (rows == 0 || cols == 0 || rows > (1u << 30) || cols > (1u << 30)) return fail(ctx, CHPE_EINVAL, "bad shape");
+    if (row_stride * 8 < cols * (size_t)src_bits) return fail(ctx, CHPE_EINVAL, "row_stride too small");
+    const size_t G = u.layout == kLayoutS8 ? 0 : cols / u.group;
+    const void *d_codes, *d_s = nullptr, *d_z = nullptr, *d_bias;
+    void *o_codes, *o_s = nullptr, *o_z = nullptr, *o_bias;
+    if ((rc = to_device(ctx, codes, rows * row_stride, &d_codes, &o_codes))) return rc;
+    const bool f32meta = u.meta_kind == kMetaF32;
+    if (u.layout == kLayoutS8) {
+        if (!scales) return fail(ctx, CHPE_EINVAL, "I8_TENSOR needs a scale");
+        if (is_device_ptr(scales))
+            cudaMemcpy(&u.scale, scales, 4, cudaMemcpyDeviceToHost);
+        else
+            u.scale = *static_cast<const float *>(scales);
+    } else {
+        if (!scales) return fail(ctx, CHPE_EINVAL, "scales required");
+        if ((rc = to_device(ctx, scales, f32meta ? rows * 4 : rows * G * 2, &d_s, &o_s))) return rc;
+        if (u.meta_kind == kMetaSZ16 && !zeros) return fail(ctx, CHPE_EINVAL, "zeros required");
+        if (zeros && (rc = to_device(ctx, zeros, f32meta ? rows * 4 : rows * G * 2, &d_z, &o_z))) return rc;
+    }
+    if ((rc = to_device(ctx, bias, bias ? rows * 4 : 0, &d_bias, &o_bias))) return rc;
+    chpe_tensor *t = new chpe_tensor();
+    rc = build_matrix(ctx, u, static_cast<const uint8_t *>(d_codes), row_stride, src_bits,
+                      f32meta ? nullptr : static_cast<const __half *>(d_s),
+                      f32meta ? nullptr : static_cast<const __half *>(d_z),
+                      f32meta ? static_cast<const float *>(d_s) : nullptr,
+                      f32meta ? static_cast<const float *>(d_z) : nullptr, static_cast<const float *>(d_bias), rows,
+                      cols, &t->m);
+    cudaFree(o_codes);
+    cudaFree(o_s);
+    cudaFree(o_z);
+    cudaFree(o_bias);
+    if (rc) {
+        delete t;
+        return rc;
+    }
+    ctx->owned.push_back(t);
+    *out = t;
+    return CHPE_OK;
+}
+
+extern "C" int chpe_upload_matrix(chpe_ctx *ctx, const chpe_fmt *fmt, const void *codes, size_t row_stride,
+                                  const void *scales, const void *zeros, const float *bias, size_t rows, size_t cols,
+                                  chpe_tensor **out) {
+    if (!ctx || !fmt || !codes || !out) return fail(ctx, CHPE_EINVAL, "null argument");
+    cudaSetDevice(ctx->device);
+    return upload_common(ctx, fmt, codes, row_stride, scales, zeros, bias, rows, cols, fmt->bits, out);
+}
+
+extern "C" int chpe_quantize_group_dev(chpe_ctx *ctx, const float *w, size_t rows, size_t cols, int bits, int group,
+                                       int symmetric, uint8_t *codes, uint16_t *scales, uint16_t *zeros,
+                                       void *stream) {
+    if (!ctx || !w || !codes || !scales) return fail(ctx, CHPE_EINVAL, "null argument");
+    if (group <= 0 || cols % (size_t)group) return fail(ctx, CHPE_EINVAL, "cols must be a multiple of group");
+    if (!symmetric && (!zeros || (bits != 2 && bits != 4 && bits != 8)))
+        return fail(ctx, CHPE_EINVAL, "asymmetric quantization needs zeros and bits in {2,4,8}");
+    cudaError_t e = launch_quant_group(w, (int)rows, (int)cols, group, bits, symmetric, codes,
+                                       reinterpret_cast<__half *>(scales), reinterpret_cast<__half *>(zeros),
+                                       static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return fail(ctx, CHPE_ECUDA, "quantize: %s", cudaGetErrorString(e));
+    return CHPE_OK;
+}
+
+// Cell layout constants (src/geometry.zig:243-256, src/weight_archive.zig:92-105,
+// src/chpe_engine.zig:146-151).
+static constexpr size_t kCellBytes = 17408, kHdr = 64, kCodes = 16384, kPayload = kHdr + kCodes;
+
+static uint8_t cell_bits(const uint8_t *c) { return c[kPayload + 20]; }
+static uint64_t cell_flags(const uint8_t *c) {
+    uint64_t f;
+    memcpy(&f, c + kPayload + 24, 8);
+    return f;
+}
+struct TileDims {
+    float scale, bias;
+    uint32_t rows, cols;
+};
+static TileDims cell_dims(const uint8_t *c) {
+    TileDims d;
+    memcpy(&d, c + kPayload + 32, 16);
+    return d;
+}
+
+extern "C" int chpe_upload_cells(chpe_ctx *ctx, const void *first_cell, size_t n_cells, size_t tile_stride,
+                                 chpe_tensor **out) {
+    if (!ctx || !first_cell || !out || n_cells == 0) return fail(ctx, CHPE_EINVAL, "null argument");
+    if (tile_stride < kCellBytes) return fail(ctx, CHPE_EINVAL, "tile_stride < 17408");
+    cudaSetDevice(ctx->device);
+    std::vector<uint8_t> devcopy;
+    const uint8_t *base = static_cast<const uint8_t *>(first_cell);
+    if (is_device_ptr(first_cell)) {
+        devcopy.resize((n_cells - 1) * tile_stride + kCellBytes);
+        CK(cudaMemcpy(devcopy.data(), first_cell, devcopy.size(), cudaMemcpyDeviceToHost));
+        base = devcopy.data();
+    }
+    const uint8_t *c0 = base;
+    int qb = cell_bits(c0);
+    const TileDims d0 = cell_dims(c0);
+    const bool g128 = (cell_flags(c0) & 1ull) != 0;
+    if (qb == 16 || qb == 32) return fail(ctx, CHPE_ENOTSUP, "fp16/fp32 cells are not quantized (quant_bits %d)", qb);
+    if (qb != 4 && qb != 8) qb = 2;  // src/chpe_engine.zig:483-486: unknown widths run as 2-bit
+    const size_t cols = d0.cols;
+    if (cols == 0 || cols % 4) return fail(ctx, CHPE_EINVAL, "cell cols %zu", cols);
+    size_t rows = 0;
+    for (size_t i = 0; i < n_cells; ++i) {
+        const uint8_t *c = base + i * tile_stride;
+        int b = cell_bits(c);
+        if (b != 4 && b != 8 && b != 16 && b != 32) b = 2;
+        const TileDims d = cell_dims(c);
+        if (b != qb || d.cols != cols || ((cell_flags(c) & 1ull) != 0) != g128)
+            return fail(ctx, CHPE_ENOTSUP, "cells must share quant_bits, cols and flags");
+        if ((size_t)d.rows * cols * qb / 8 > kCodes) return fail(ctx, CHPE_EINVAL, "cell %zu overflows its codes", i);
+        rows += d.rows;
+    }
+    const size_t rs = cols * qb / 8;
+    const bool grouped = qb == 2 && g128;
+    if (grouped && cols % 128) return fail(ctx, CHPE_ENOTSUP, "group-128 cells need cols %% 128 == 0");
+    const size_t G = grouped ? cols / 128 : 1;
+    std::vector<uint8_t> codes(rows * rs);
+    std::vector<uint16_t> gs(grouped ? rows * G : 0);
+    std::vector<float> sc(rows), off(rows), bias(rows);
+    std::vector<int> ocols;
+    std::vector<uint16_t> ow;
+    bool any_out = false;
+    size_t r0 = 0;
+    for (size_t i = 0; i < n_cells; ++i) {
+        const uint8_t *c = base + i * tile_stride;
+        const TileDims d = cell_dims(c);
+        memcpy(codes.data() + r0 * rs, c + kHdr, d.rows * rs);
+        for (uint32_t r = 0; r < d.rows; ++r) {
+            sc[r0 + r] = d.scale;
+            // per-weight offset for 4/2-bit cells, per-row bias for 8-bit cells
+            off[r0 + r] = qb == 8 ? 0.0f : d.bias;
+            bias[r0 + r] = qb == 8 ? d.bias : 0.0f;
+        }
+        if (grouped) {
+            for (uint32_t r = 0; r < d.rows; ++r)
+                memcpy(&gs[(r0 + r) * G], c + kPayload + 48 + 2 * (r * G), 2 * G);
+            if (d.rows == 16) {  // outlier columns (src/chpe_engine.zig:240-252)
+                if (!any_out) {
+                    ocols.assign(rows * 8, -1);
+                    ow.assign(rows * 8, 0);
+                    any_out = true;
+                }
+                uint16_t colsv[8];
+                memcpy(colsv, c + kPayload + 816, 16);
+                for (uint32_t r = 0; r < 16; ++r)
+                    for (int k = 0; k < 8; ++k) {
+                        ocols[(r0 + r) * 8 + k] = colsv[k] < cols ? colsv[k] : -1;
+                        memcpy(&ow[(r0 + r) * 8 + k], c + kPayload + 560 + 2 * (r * 8 + k), 2);
+                    }
+            }
+        }
+        r0 += d.rows;
+    }
+    chpe_fmt f = {};
+    f.bits = qb;
+    int rc;
+    chpe_tensor *t = nullptr;
+    if (grouped) {
+        f.scheme = CHPE_SCHEME_W2_CODEBOOK_GROUP_F16;
+        f.group = 128;
+        rc = upload_common(ctx, &f, codes.data(), rs, gs.data(), nullptr, nullptr, rows, cols, qb, &t);
+    } else {
+        f.scheme = CHPE_SCHEME_ROW_AFFINE_F32;
+        bool any_bias = false;
+        for (float b : bias) any_bias |= b != 0.0f;
+        rc = upload_common(ctx, &f, codes.data(), rs, sc.data(), off.data(), any_bias ? bias.data() : nullptr, rows,
+                           cols, qb, &t);
+    }
+    if (rc) return rc;
+    if (any_out) {
+        CK(cudaMalloc(&t->m.out_cols, rows * 8 * sizeof(int)));
+        CK(cudaMalloc(&t->m.out_w, rows * 8 * sizeof(uint16_t)));
+        CK(cudaMemcpy(t->m.out_cols, ocols.data(), rows * 8 * sizeof(int), cudaMemcpyHostToDevice));
+        CK(cudaMemcpy(t->m.out_w, ow.data(), rows * 8 * sizeof(uint16_t), cudaMemcpyHostToDevice));
+    }
+    *out = t;
+    return CHPE_OK;
+}
+
+extern "C" int chpe_tensor_free(chpe_ctx *ctx, chpe_tensor *t) {
+    if (!ctx || !t) return fail(ctx, CHPE_EINVAL, "null argument");
+    for (size_t i = 0; i < ctx->owned.size(); ++i)
+        if (ctx->owned[i] == t) {
+            for (auto it = ctx->registry.begin(); it != ctx->registry.end();)
+                it = (it->second == t) ? ctx->registry.erase(it) : std::next(it);
+            cudaStreamSynchronize(ctx->stream);
+            free_matrix(t->m);
+            delete t;
+            ctx->owned.erase(ctx->owned.begin() + i);
+            return CHPE_OK;
+        }
+    return fail(ctx, CHPE_ENOENT, "tensor not owned by this context");
+}
+
+extern "C" int chpe_tensor_info(const chpe_tensor *t, size_t *rows, size_t *cols, int *bits, size_t *device_bytes) {
+    if (!t) return CHPE_EINVAL;
+    if (rows) *rows = t->m.N;
+    if (cols) *cols = t->m.K;
+    if (bits) *bits = t->m.bits;
+    if (device_bytes) *device_bytes = t->m.code_bytes + t->m.meta_bytes_total;
+    return CHPE_OK;
+}
+
+static void drop_registered(chpe_ctx *ctx, const void *key) {
+    chpe_tensor *t = lookup(ctx, key);
+    if (!t) return;
+    ctx->registry.erase(key);
+    chpe_tensor_free(ctx, t);
+}
+
+extern "C" int chpe_register_i8(chpe_ctx *ctx, const int8_t *host_weights, size_t rows, size_t cols) {
+    if (!ctx || !host_weights) return fail(ctx, CHPE_EINVAL, "null argument");
+    const uint64_t fp = is_device_ptr(host_weights) ? 0 : fingerprint(host_weights, rows * cols, true);
+    if (chpe_tensor *old = lookup(ctx, host_weights)) {
+        if ((size_t)old->m.N == rows && (size_t)old->m.K == cols && old->fingerprint == fp) return CHPE_OK;
+        drop_registered(ctx, host_weights);
+    }
+    cudaSetDevice(ctx->device);
+    chpe_fmt f = {8, CHPE_SCHEME_I8_TENSOR, 0, 0.0f};
+    const float one = 1.0f;
+    chpe_tensor *t;
+    int rc = upload_common(ctx, &f, host_weights, cols, &one, nullptr, nullptr, rows, cols, 8, &t);
+    if (rc) return rc;
+    t->fingerprint = fp;
+    ctx->registry[host_weights] = t;
+    return CHPE_OK;
+}
+
+// ---------------------------------------------------------------------------
+// device-pointer GEMV
+// ---------------------------------------------------------------------------
+
+extern "C" int chpe_gemv_dev(chpe_ctx *ctx, const chpe_tensor *w, const void *x, int x_dtype, const float *x_scales,
+                             int M, float *y, int accumulate, void *stream) {
+    if (!ctx || !w) return fail(ctx, CHPE_EINVAL, "null argument");
+    return run_gemv(ctx, w->m, nullptr, 0, x, x_dtype, x_scales, M, y, w->m.N, accumulate, nullptr, nullptr,
+                    x_dtype == CHPE_X_F32 ? static_cast<const float *>(x) : nullptr, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int chpe_gemv_gateup_swiglu_dev(chpe_ctx *ctx, const chpe_tensor *gate, const chpe_tensor *up,
+                                           const void *x, int x_dtype, const float *x_scales, int M, float *mlp_out,
+                                           void *stream) {
+    if (!ctx || !gate || !up) return fail(ctx, CHPE_EINVAL, "null argument");
+    const DevMatrix &g = gate->m, &u = up->m;
+    if (g.N != u.N || g.K != u.K || g.bits != u.bits || g.layout != u.layout || g.meta_kind != u.meta_kind ||
+        g.group != u.group || g.zc != u.zc)
+        return fail(ctx, CHPE_EINVAL, "gate and up must share shape and format");
+    if (g.out_cols || u.out_cols) return fail(ctx, CHPE_ENOTSUP, "outlier columns not supported in gate/up");
+    return run_gemv(ctx, g, &u, 1, x, x_dtype, x_scales, M, mlp_out, g.N, 0, nullptr, nullptr, nullptr,
+                    static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int chpe_quantize_act_i8_dev(chpe_ctx *ctx, const float *x, int M, size_t n, int8_t *q, float *scales,
+                                        void *stream) {
+    if (!ctx || !x || (!q && !scales) || M < 1) return fail(ctx, CHPE_EINVAL, "bad argument");
+    cudaError_t e = launch_act_quant_s8(x, M, (int)n, (int)((n + 31) / 32 * 32), q, scales, nullptr,
+                                        static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return fail(ctx, CHPE_ECUDA, "act quant: %s", cudaGetErrorString(e));
+    return CHPE_OK;
+}
+
+// ---------------------------------------------------------------------------
+// host-pointer operators mirroring src/engine.zig / src/kernels/neon.zig
+// ---------------------------------------------------------------------------
+
+// Registered tensor for a host weight pointer, (re)uploaded when the pointer is
+// new or its shape or sampled content changed.
+static chpe_tensor *weights_for(chpe_ctx *ctx, const int8_t *w, size_t rows, size_t cols, int *rc) {
+    *rc = chpe_register_i8(ctx, w, rows, cols);
+    return *rc ? nullptr : lookup(ctx, w);
+}
+
+static int batch_common(chpe_ctx *ctx, const int8_t *weights, float scale_w, const int8_t *const *xs,
+                        const float *scales_x, int nb, size_t rows, size_t cols, float *const *outs) {
+    if (!ctx || !weights || !xs || !outs || !scales_x) return fail(ctx, CHPE_EINVAL, "null argument");
+    cudaSetDevice(ctx->device);
+    int rc = CHPE_OK;
+    chpe_tensor *t = weights_for(ctx, weights, rows, cols, &rc);
+    if (!t) return rc;
+    if ((rc = grow(ctx, &ctx->d_in, &ctx->d_in_bytes, (size_t)nb * cols))) return rc;
+    for (int b = 0; b < nb; ++b)
+        CK(cudaMemcpyAsync(static_cast<int8_t *>(ctx->d_in) + (size_t)b * cols, xs[b], cols, cudaMemcpyHostToDevice,
+                           ctx->stream));
+    CK(cudaMemcpyAsync(ctx->d_scales, scales_x, nb * sizeof(float), cudaMemcpyHostToDevice, ctx->stream));
+    if ((rc = stage_out(ctx, (size_t)nb * rows * sizeof(float)))) return rc;
+    rc = run_gemv(ctx, t->m, nullptr, 0, ctx->d_in, CHPE_X_I8, ctx->d_scales, nb, ctx->d_out, (int)rows, 0, &scale_w,
+                  nullptr, nullptr, ctx->stream);
+    if (rc) return rc;
+    for (int b = 0; b < nb; ++b)
+        CK(cudaMemcpyAsync(outs[b], ctx->d_out + (size_t)b * rows, rows * sizeof(float), cudaMemcpyDeviceToHost,
+                           ctx->stream));
+    return finish(ctx);
+}
+
+extern "C" int chpe_gemv_parallel(chpe_ctx *ctx, const int8_t *weights, float scale_w, const int8_t *x_q8,
+                                  float scale_x, size_t rows, size_t cols, float *out) {
+    const int8_t *xs[1] = {x_q8};
+    float *outs[1] = {out};
+    return batch_common(ctx, weights, scale_w, xs, &scale_x, 1, rows, cols, outs);
+}
+
+extern "C" int chpe_gemv_batch4_parallel(chpe_ctx *ctx, const int8_t *weights, float scale_w, const int8_t *x0,
+                                         const int8_t *x1, const int8_t *x2, const int8_t *x3,
+                                         const float scales_x[4], size_t rows, size_t cols, float *out0, float *out1,
+                                         float *out2, float *out3) {
+    const int8_t *xs[4] = {x0, x1, x2, x3};
+    float *outs[4] = {out0, out1, out2, out3};
+    return batch_common(ctx, weights, scale_w, xs, scales_x, 4, rows, cols, outs);
+}
+
+extern "C" int chpe_gemv_batch8_parallel(chpe_ctx *ctx, const int8_t *weights, float scale_w, const int8_t *const x[8],
+                                         const float scales_x[8], size_t rows, size_t cols, float *const out[8]) {
+    return batch_common(ctx, weights, scale_w, x, scales_x, 8, rows, cols, out);
+}
+
+extern "C" int chpe_gemv_gate_up_swiglu_parallel(chpe_ctx *ctx, const int8_t *gate_weights, float scale_gate,
+                                                 const int8_t *up_weights, float scale_up, const int8_t *x_q8,
+                                                 float scale_x, size_t rows, size_t cols, float *mlp_out) {
+    if (!ctx || !gate_weights || !up_weights || !x_q8 || !mlp_out) return fail(ctx, CHPE_EINVAL, "null argument");
+    cudaSetDevice(ctx->device);
+    int rc = CHPE_OK;
+    chpe_tensor *g = weights_for(ctx, gate_weights, rows, cols, &rc);
+    if (!g) return rc;
+    chpe_tensor *u = weights_for(ctx, up_weights, rows, cols, &rc);
+    if (!u) return rc;
+    if ((rc = stage_in(ctx, x_q8, cols))) return rc;
+    CK(cudaMemcpyAsync(ctx->d_scales, &scale_x, sizeof(float), cudaMemcpyHostToDevice, ctx->stream));
+    if ((rc = stage_out(ctx, rows * sizeof(float)))) return rc;
+    rc = run_gemv(ctx, g->m, &u->m, 1, ctx->d_in, CHPE_X_I8, ctx->d_scales, 1, ctx->d_out, (int)rows, 0, &scale_gate,
+                  &scale_up, nullptr, ctx->stream);
+    if (rc) return rc;
+    CK(cudaMemcpyAsync(mlp_out, ctx->d_out, rows * sizeof(float), cudaMemcpyDeviceToHost, ctx->stream));
+    return finish(ctx);
+}
+
+extern "C" int chpe_quantize_activation_int8(chpe_ctx *ctx, const float *x, size_t n, int8_t *out_q8,
+                                             float *scale_out) {
+    if (!ctx || !x || !out_q8 || !scale_out || n == 0) return fail(ctx, CHPE_EINVAL, "bad argument");
+    cudaSetDevice(ctx->device);
+    int rc = stage_in(ctx, x, n * sizeof(float));
+    if (rc) return rc;
+    if ((rc = stage_out(ctx, n + 64))) return rc;
+    int8_t *dq = reinterpret_cast<int8_t *>(ctx->d_out);
+    cudaError_t e = launch_act_quant_s8(static_cast<const float *>(ctx->d_in), 1, (int)n, (int)((n + 31) / 32 * 32),
+                                        dq, ctx->d_scales, nullptr, ctx->stream);
+    if (e != cudaSuccess) return fail(ctx, CHPE_ECUDA, "act quant: %s", cudaGetErrorString(e));
+    CK(cudaMemcpyAsync(out_q8, dq, n, cudaMemcpyDeviceToHost, ctx->stream));
+    CK(cudaMemcpyAsync(scale_out, ctx->d_scales, sizeof(float), cudaMemcpyDeviceToHost, ctx->stream));
+    return finish(ctx);
+}
+
+extern "C" int chpe_gemv_tile_polymorphic(chpe_ctx *ctx, const void *cell, const float *x, size_t x_len, float *y,
+                                          size_t row_base, int accumulate) {
+    if (!ctx || !cell || !x || !y) return fail(ctx, CHPE_EINVAL, "null argument");
+    cudaSetDevice(ctx->device);
+    const uint64_t fp = fingerprint(cell, kCellBytes, false);
+    chpe_tensor *t = lookup(ctx, cell);
+    int rc;
+    if (t && t->fingerprint != fp) {
+        drop_registered(ctx, cell);
+        t = nullptr;
+    }
+    if (!t) {
+        if ((rc = chpe_upload_cells(ctx, cell, 1, kCellBytes, &t))) return rc;
+        t->fingerprint = fp;
+        ctx->registry[cell] = t;
+    }
+    const DevMatrix &m = t->m;
+    if (x_len < (size_t)m.K) return fail(ctx, CHPE_EINVAL, "x_len %zu < cols %d", x_len, m.K);
+    if ((rc = stage_in(ctx, x, (size_t)m.K * sizeof(float)))) return rc;
+    if ((rc = stage_out(ctx, (size_t)m.N * sizeof(float)))) return rc;
+    if (accumulate)
+        CK(cudaMemcpyAsync(ctx->d_out, y + row_base, (size_t)m.N * sizeof(float), cudaMemcpyHostToDevice, ctx->stream));
+    rc = run_gemv(ctx, m, nullptr, 0, ctx->d_in, CHPE_X_F32, nullptr, 1, ctx->d_out, m.N, accumulate, nullptr, nullptr,
+                  static_cast<const float *>(ctx->d_in), ctx->stream);
+    if (rc) return rc;
+    CK(cudaMemcpyAsync(y + row_base, ctx->d_out, (size_t)m.N * sizeof(float), cudaMemcpyDeviceToHost, ctx->stream));
+    return finish(ctx);
+}
+
+// ---------------------------------------------------------------------------
+// shared activation fragments
+// ---------------------------------------------------------------------------
+
+struct chpe_xfrag {
+    Xfrag f;
+    size_t xf_bytes = 0, xs_bytes = 0;
+    float *sx = nullptr;
+    float *xrow = nullptr;
+};
+
+extern "C" int chpe_xfrag_create(chpe_ctx *ctx, const chpe_tensor *like, int M, int x_dtype, chpe_xfrag **out) {
+    if (!ctx || !like || !out) return fail(ctx, CHPE_EINVAL, "null argument");
+    if (M < 1 || M > kMaxTokens) return fail(ctx, CHPE_EINVAL, "fragments hold 1..8 rows (got %d)", M);
+    int rc = check_x(ctx, like->m, x_dtype, x_dtype == CHPE_X_I8 ? reinterpret_cast<const float *>(1) : nullptr);
+    if (rc) return rc;
+    cudaSetDevice(ctx->device);
+    chpe_xfrag *h = new chpe_xfrag();
+    h->f = xfrag_shape(like->m, M, x_dtype, &h->xf_bytes, &h->xs_bytes);
+    cudaError_t e = cudaMalloc(&h->f.xf, h->xf_bytes);
+    if (e == cudaSuccess && h->f.xsplit) e = cudaMalloc(&h->f.xlo, h->xf_bytes);
+    if (e == cudaSuccess) e = cudaMalloc(reinterpret_cast<void **>(&h->f.xs), h->xs_bytes + 32);
+    if (e == cudaSuccess) e = cudaMalloc(reinterpret_cast<void **>(&h->sx), 64 * sizeof(float));
+    if (e == cudaSuccess && x_dtype == CHPE_X_F32)
+        e = cudaMalloc(reinterpret_cast<void **>(&h->xrow), (size_t)M * like->m.K * sizeof(float));
+    if (e != cudaSuccess) {
+        cudaFree(h->f.xf);
+        cudaFree(h->f.xlo);
+        cudaFree(h->f.xs);
+        cudaFree(h->sx);
+        cudaFree(h->xrow);
+        delete h;
+        return fail(ctx, CHPE_ENOMEM, "xfrag alloc: %s", cudaGetErrorString(e));
+    }
+    *out = h;
+    return CHPE_OK;
+}
+
+extern "C" int chpe_xfrag_fill_dev(chpe_ctx *ctx, chpe_xfrag *xf, const void *x, const float *x_scales,
+                                   void *stream) {
+    if (!ctx || !xf || !x) return fail(ctx, CHPE_EINVAL, "null argument");
+    if (xf->f.x_dtype == CHPE_X_I8 && !x_scales) return fail(ctx, CHPE_EINVAL, "int8 activations need x_scales");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (xf->xrow) {
+        cudaError_t e = cudaMemcpyAsync(xf->xrow, x, (size_t)xf->f.M * xf->f.K * sizeof(float), cudaMemcpyDeviceToDevice, st);
+        if (e != cudaSuccess) return fail(ctx, CHPE_ECUDA, "xfrag copy: %s", cudaGetErrorString(e));
+        xf->f.xrow = xf->xrow;
+    }
+    return prep_x(ctx, xf->f, x, x_scales, xf->sx, st);
+}
+
+extern "C" int chpe_gemv_xfrag_dev(chpe_ctx *ctx, const chpe_tensor *w, const chpe_xfrag *xf, float *y,
+                                   int accumulate, void *stream) {
+    if (!ctx || !w || !xf || !y) return fail(ctx, CHPE_EINVAL, "null argument");
+    return gemv_core(ctx, w->m, nullptr, 0, xf->f, y, w->m.N, accumulate, nullptr, nullptr,
+                     static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int chpe_gemv_gateup_swiglu_xfrag_dev(chpe_ctx *ctx, const chpe_tensor *gate, const chpe_tensor *up,
+                                                 const chpe_xfrag *xf, float *mlp_out, void *stream) {
+    if (!ctx || !gate || !up || !xf || !mlp_out) return fail(ctx, CHPE_EINVAL, "null argument");
+    const DevMatrix &g = gate->m, &u = up->m;
+    if (g.N != u.N || g.K != u.K || g.bits != u.bits || g.layout != u.layout || g.meta_kind != u.meta_kind ||
+        g.group != u.group || g.zc != u.zc)
+        return fail(ctx, CHPE_EINVAL, "gate and up must share shape and format");
+    return gemv_core(ctx, g, &u, 1, xf->f, mlp_out, g.N, 0, nullptr, nullptr, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int chpe_xfrag_free(chpe_ctx *ctx, chpe_xfrag *xf) {
+    if (!ctx || !xf) return fail(ctx, CHPE_EINVAL, "null argument");
+    cudaStreamSynchronize(ctx->stream);
+    cudaFree(xf->f.xf);
+    cudaFree(xf->f.xlo);
+    cudaFree(xf->f.xs);
+    cudaFree(xf->sx);
+    cudaFree(xf->xrow);
+    delete xf;
+    return CHPE_OK;
+}

@@ -1,0 +1,312 @@
+// prep.cu -- activation-fragment preparation, dynamic int8 activation
+// quantization, weight repacking into the strip layout, and the GPU
+// quantizers used to build device tensors from fp32 weights.
+#include "common.cuh"
+#include "internal.h"
+
+namespace chpe {
+
+// ---------------------------------------------------------------------------
+// activations
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ float load_x(const void *x, int dt, size_t i) {
+    if (dt == 0) return static_cast<const float *>(x)[i];
+    if (dt == 1) return __bfloat162float(static_cast<const __nv_bfloat16 *>(x)[i]);
+    return __half2float(static_cast<const __half *>(x)[i]);
+}
+
+__device__ __forceinline__ uint32_t pack_h2(__half a, __half b) {
+    __half2 h = __halves2half2(a, b);
+    return *reinterpret_cast<uint32_t *>(&h);
+}
+
+// One block per E-column block, one warp per activation row (8 warps).
+// Lane l < E/4 converts fragment entry (k-step e*E/16 + l/4, t = l%4).
+__global__ void xprep_f16_kernel(const void *__restrict__ x, int dt, int M, int K, int E, uint2 *__restrict__ xf,
+                                 uint2 *__restrict__ xlo, float *__restrict__ xs) {
+    const int eb = blockIdx.x, tok = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float part = 0.0f;
+    if (lane < E / 4 && tok < M) {
+        const int s = eb * (E / 16) + lane / 4, t = lane & 3;
+        const int kb = 16 * s + 2 * t;
+        const int kk[4] = {kb, kb + 1, kb + 8, kb + 9};
+        __half h[4], l[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const float v = kk[q] < K ? load_x(x, dt, (size_t)tok * K + kk[q]) : 0.0f;
+            h[q] = __float2half_rn(v);
+            l[q] = xlo ? __float2half_rn(v - __half2float(h[q])) : __float2half_rn(0.0f);
+            part += __half2float(h[q]) + __half2float(l[q]);
+        }
+        const size_t idx = ((size_t)s * M + tok) * 4 + t;
+        xf[idx] = make_uint2(pack_h2(h[0], h[1]), pack_h2(h[2], h[3]));
+        if (xlo) xlo[idx] = make_uint2(pack_h2(l[0], l[1]), pack_h2(l[2], l[3]));
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) part += __shfl_xor_sync(0xffffffffu, part, off);
+    if (lane == 0) xs[(size_t)eb * 8 + tok] = part;
+}
+
+cudaError_t launch_xprep_f16(const void *x, int x_dtype, int M, int K, int Kp, int e_cols, bool xsplit, void *xf,
+                             void *xlo, float *xs, cudaStream_t st) {
+    const int nblk = Kp / e_cols;
+    xprep_f16_kernel<<<nblk, 256, 0, st>>>(x, x_dtype, M, K, e_cols, static_cast<uint2 *>(xf),
+                                           xsplit ? static_cast<uint2 *>(xlo) : nullptr, xs);
+    return cudaGetLastError();
+}
+
+__device__ __forceinline__ uint32_t pack4_i8(const int8_t *p, int k, int K) {
+    uint32_t w = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const uint32_t b = (k + i < K) ? (uint32_t)(uint8_t)p[k + i] : 0u;
+        w |= b << (8 * i);
+    }
+    return w;
+}
+
+// int8 activations [M][K] -> fragments [kstep32][M][4] uint2.
+__global__ void xprep_s8_kernel(const int8_t *__restrict__ xq, int M, int K, int nsteps, uint2 *__restrict__ xf) {
+    const size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const size_t total = (size_t)nsteps * M * 4;
+    if (idx >= total) return;
+    const int t = (int)(idx & 3);
+    const int tok = (int)((idx >> 2) % M);
+    const int s = (int)(idx / (4 * (size_t)M));
+    const int8_t *row = xq + (size_t)tok * K;
+    const int kb = 32 * s + 4 * t;
+    xf[idx] = make_uint2(pack4_i8(row, kb, K), pack4_i8(row, kb + 16, K));
+}
+
+cudaError_t launch_xprep_s8(const int8_t *xq, int M, int K, int Kp, void *xf, cudaStream_t st) {
+    const int nsteps = Kp / 32;
+    const size_t total = (size_t)nsteps * M * 4;
+    xprep_s8_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(xq, M, K, nsteps, static_cast<uint2 *>(xf));
+    return cudaGetLastError();
+}
+
+// Per-row dynamic int8 quantization, bit-exact with the reference
+// (src/kernels/neon.zig:644-670): s = max|x|/127 (1 when max <= 1e-9),
+// q = clamp(round_half_away(x * (1/s)), -128, 127).  One block per row.
+__global__ void act_quant_s8_kernel(const float *__restrict__ x, int M, int K, int nsteps, int8_t *__restrict__ q,
+                                    float *__restrict__ scales, uint2 *__restrict__ xf) {
+    __shared__ float red[32];
+    __shared__ float s_inv;
+    const int tok = blockIdx.x;
+    const float *row = x + (size_t)tok * K;
+    float m = 0.0f;
+    for (int k = threadIdx.x; k < K; k += blockDim.x) m = fmaxf(m, fabsf(row[k]));
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float mm = 0.0f;
+        for (int w = 0; w < (int)(blockDim.x >> 5); ++w) mm = fmaxf(mm, red[w]);
+        const float scale = (mm > 1e-9f) ? __fdiv_rn(mm, 127.0f) : 1.0f;
+        s_inv = __fdiv_rn(1.0f, scale);
+        if (scales) scales[tok] = scale;
+    }
+    __syncthreads();
+    const float inv = s_inv;
+    auto quant = [&](int k) -> uint32_t {
+        if (k >= K) return 0u;
+        const float r = roundf(__fmul_rn(row[k], inv));
+        const float c = fmaxf(-128.0f, fminf(127.0f, r));
+        return (uint32_t)(uint8_t)(int8_t)c;
+    };
+    if (q)
+        for (int k = threadIdx.x; k < K; k += blockDim.x) q[(size_t)tok * K + k] = (int8_t)(uint8_t)quant(k);
+    if (xf) {
+        for (int e = threadIdx.x; e < nsteps * 4; e += blockDim.x) {
+            const int s = e >> 2, t = e & 3;
+            const int kb = 32 * s + 4 * t;
+            uint32_t w0 = 0, w1 = 0;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                w0 |= quant(kb + i) << (8 * i);
+                w1 |= quant(kb + 16 + i) << (8 * i);
+            }
+            xf[((size_t)s * M + tok) * 4 + t] = make_uint2(w0, w1);
+        }
+    }
+}
+
+cudaError_t launch_act_quant_s8(const float *x, int M, int K, int Kp, int8_t *q, float *scales, void *xf,
+                                cudaStream_t st) {
+    act_quant_s8_kernel<<<M, 256, 0, st>>>(x, M, K, Kp / 32, q, scales, static_cast<uint2 *>(xf));
+    return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// weights
+// ---------------------------------------------------------------------------
+
+// Code of element (row, k) from packed row-major codes of `sbits` bits each
+// (LSB first within a byte); 0 outside the matrix (padding).
+__device__ __forceinline__ uint32_t src_code(const uint8_t *src, size_t stride, int N, int K, int sbits, int row,
+                                             int k, uint32_t xorv) {
+    if (row >= N || k >= K) return 0u;
+    const size_t bit = (size_t)k * sbits;
+    const uint32_t byte = src[(size_t)row * stride + (bit >> 3)];
+    const uint32_t mask = (1u << sbits) - 1u;
+    return ((byte >> (bit & 7)) & mask) ^ xorv;
+}
+
+// One thread per 32-bit word of the strip layout.
+__global__ void repack_kernel(const uint8_t *__restrict__ src, size_t stride, int N, int K, int sbits, int bits,
+                              int layout, uint32_t xorv, uint32_t *__restrict__ dst, int n_strips, int n_chunks) {
+    const size_t wi = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const size_t total = (size_t)n_strips * n_chunks * 128;
+    if (wi >= total) return;
+    const int lw = (int)(wi & 127);
+    const size_t sc = wi >> 7;
+    const int chunk = (int)(sc % n_chunks);
+    const int strip = (int)(sc / n_chunks);
+    const int lane = lw >> 2, r = lw & 3;
+    const int g = lane >> 2, t = lane & 3;
+    const int row = strip * kStripRows + g + 8 * (r & 1);
+    uint32_t w = 0;
+    if (layout == kLayoutS8) {
+        const int kb = chunk * 32 + 4 * t + 16 * (r >> 1);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) w |= src_code(src, stride, N, K, sbits, row, kb + i, 0u) << (8 * i);
+    } else {
+        const int kc = 256 / bits;
+        const int col = 2 * t + 8 * (r >> 1);
+        const int kb = chunk * kc + col;
+        if (bits == 4) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                w |= src_code(src, stride, N, K, sbits, row, kb + 16 * j, xorv) << (4 * j);
+                w |= src_code(src, stride, N, K, sbits, row, kb + 16 * j + 1, xorv) << (4 * (j + 4));
+            }
+        } else if (bits == 2) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                w |= src_code(src, stride, N, K, sbits, row, kb + 16 * j, xorv) << (2 * j);
+                w |= src_code(src, stride, N, K, sbits, row, kb + 16 * j + 1, xorv) << (2 * (j + 8));
+            }
+        } else {
+            w |= src_code(src, stride, N, K, sbits, row, kb, xorv);
+            w |= src_code(src, stride, N, K, sbits, row, kb + 1, xorv) << 8;
+            w |= src_code(src, stride, N, K, sbits, row, kb + 16, xorv) << 16;
+            w |= src_code(src, stride, N, K, sbits, row, kb + 17, xorv) << 24;
+        }
+    }
+    dst[wi] = w;
+}
+
+cudaError_t launch_repack2(const uint8_t *src, size_t row_stride, int N, int K, int src_bits, int bits, int layout,
+                           uint32_t xorv, uint8_t *dst, int n_strips, int n_chunks, cudaStream_t st) {
+    const size_t total = (size_t)n_strips * n_chunks * 128;
+    repack_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(src, row_stride, N, K, src_bits, bits, layout,
+                                                                   xorv, reinterpret_cast<uint32_t *>(dst),
+                                                                   n_strips, n_chunks);
+    return cudaGetLastError();
+}
+
+// Metadata into [strip][G][16]; rows beyond N get scale 0.
+__global__ void meta_repack_kernel(int kind, const __half *__restrict__ s, const __half *__restrict__ z,
+                                   const float *__restrict__ fs, const float *__restrict__ fo, float zc, int N,
+                                   int G, void *__restrict__ dst, int n_strips) {
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const size_t total = (size_t)n_strips * G * 16;
+    if (i >= total) return;
+    const int r16 = (int)(i & 15);
+    const size_t sg = i >> 4;
+    const int grp = (int)(sg % G);
+    const int strip = (int)(sg / G);
+    const int row = strip * kStripRows + r16;
+    const bool in = row < N;
+    if (kind == kMetaS16) {
+        static_cast<__half *>(dst)[i] = in ? s[(size_t)row * G + grp] : __float2half_rn(0.0f);
+    } else if (kind == kMetaSZ16) {
+        __half2 v = in ? __halves2half2(s[(size_t)row * G + grp], z[(size_t)row * G + grp])
+                       : __halves2half2(__float2half_rn(0.0f), __float2half_rn(0.0f));
+        static_cast<__half2 *>(dst)[i] = v;
+    } else {
+        float2 v = make_float2(0.0f, 0.0f);
+        if (in) {
+            const float sc = fs[row];
+            v = make_float2(sc, (fo ? fo[row] : 0.0f) - zc * sc);
+        }
+        static_cast<float2 *>(dst)[i] = v;
+    }
+}
+
+cudaError_t launch_meta_repack(int kind, const __half *s, const __half *z, const float *fs, const float *fo,
+                               float zc_for_f32, int N, int G, void *dst, int n_strips, cudaStream_t st) {
+    const size_t total = (size_t)n_strips * G * 16;
+    meta_repack_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(kind, s, z, fs, fo, zc_for_f32, N, G, dst,
+                                                                       n_strips);
+    return cudaGetLastError();
+}
+
+// GPU grouped quantizers (the formulas of chpe_quantize_group_dev in the header):
+// one warp per (row, group); codes are written one byte per weight.
+__global__ void quant_group_kernel(const float *__restrict__ w, int N, int K, int group, int bits, int symmetric,
+                                   uint8_t *__restrict__ codes, __half *__restrict__ scales,
+                                   __half *__restrict__ zeros) {
+    const size_t gw = ((size_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    const int G = K / group;
+    if (gw >= (size_t)N * G) return;
+    const int row = (int)(gw / G), grp = (int)(gw % G);
+    const float *v = w + (size_t)row * K + (size_t)grp * group;
+    float mn = INFINITY, mx = -INFINITY, am = 0.0f;
+    for (int i = lane; i < group; i += 32) {
+        mn = fminf(mn, v[i]);
+        mx = fmaxf(mx, v[i]);
+        am = fmaxf(am, fabsf(v[i]));
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+        mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, off));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+        am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, off));
+    }
+    if (symmetric) {
+        __half s = __float2half_rn(am > 1e-8f ? __fdiv_rn(am, 127.0f) : 1.0f);
+        float s32 = __half2float(s);
+        if (!(s32 > 0.0f)) {
+            s32 = 1.0f;
+            s = __float2half_rn(1.0f);
+        }
+        for (int i = lane; i < group; i += 32) {
+            const float q = fminf(fmaxf(rintf(__fdiv_rn(v[i], s32)), -127.0f), 127.0f);
+            codes[(size_t)row * K + (size_t)grp * group + i] = (uint8_t)(int8_t)q;
+        }
+        if (lane == 0) scales[(size_t)row * G + grp] = s;
+    } else {
+        const float qmax = (float)((1 << bits) - 1);
+        const float range = mx - mn;
+        __half s = __float2half_rn(range > 1e-8f ? __fdiv_rn(range, qmax) : 1.0f);
+        float s32 = __half2float(s);
+        if (!(s32 > 0.0f)) {
+            s32 = 1.0f;
+            s = __float2half_rn(1.0f);
+        }
+        const float zf = fminf(fmaxf(rintf(__fdiv_rn(-mn, s32)), 0.0f), qmax);
+        for (int i = lane; i < group; i += 32) {
+            const float c = fminf(fmaxf(rintf(__fdiv_rn(v[i], s32)) + zf, 0.0f), qmax);
+            codes[(size_t)row * K + (size_t)grp * group + i] = (uint8_t)c;
+        }
+        if (lane == 0) {
+            scales[(size_t)row * G + grp] = s;
+            zeros[(size_t)row * G + grp] = __float2half_rn(zf);
+        }
+    }
+}
+
+cudaError_t launch_quant_group(const float *w, int N, int K, int group, int bits, int symmetric, uint8_t *codes,
+                               __half *scales, __half *zeros, cudaStream_t st) {
+    const size_t warps = (size_t)N * (K / group);
+    const size_t threads = warps * 32;
+    quant_group_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, st>>>(w, N, K, group, bits, symmetric, codes,
+                                                                        scales, zeros);
+    return cudaGetLastError();
+}
+
+}  // namespace chpe

@@ -1,0 +1,207 @@
+/*
+ * chpe_b200.h -- C ABI of the B200 (sm_100a) quantized dequant-matmul library.
+ *
+ * Drop-in replacement for the CHPE engine's CPU GEMV operator layer.  Every
+ * entry point returns an int status (0 = OK, negative CHPE_E* on error) and
+ * never aborts the process; chpe_last_error_string() describes the last error
+ * of a context.  Signatures use plain pointers and sizes only.
+ *
+ * Pointer rules.  Functions with a `_parallel` / `_tile_` name mirror the
+ * reference's Zig operators and take HOST pointers, exactly as the reference
+ * does: activations are copied to the device, the kernel runs, the result is
+ * copied back before the call returns.  Weight pointers passed to them are
+ * looked up in the context's registry (chpe_register_*): a registered host
+ * weight pointer is served from its resident device copy; an unregistered one
+ * is uploaded on first use and cached under that pointer.  The cache checks
+ * the shape and a content fingerprint (every byte of a cell; the first and
+ * last 4 KiB plus 64 strided windows of a weight matrix), so a host buffer
+ * freed and reused for other weights at the same address is re-uploaded;
+ * weights modified in place inside the sampled-out bytes must be
+ * re-registered with chpe_register_i8.  Functions with a
+ * `_dev` suffix take DEVICE pointers and a cudaStream_t (passed as void*) and
+ * are asynchronous.
+ *
+ * Thread safety: calls on one context are serialised by the caller (one
+ * context per thread or stream), as the reference's single caller thread is
+ * (src/engine.zig:174).
+ */
+#ifndef CHPE_B200_H
+#define CHPE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------- */
+enum {
+    CHPE_OK = 0,
+    CHPE_EINVAL = -1,   /* bad argument (size, format, null pointer)          */
+    CHPE_EALIGN = -2,   /* pointer or size misaligned for the device layout   */
+    CHPE_ENOMEM = -3,   /* device or host allocation failed                   */
+    CHPE_ECUDA = -4,    /* CUDA runtime error                                 */
+    CHPE_ETIMEOUT = -5, /* a kernel's bounded wait expired (error flag set)   */
+    CHPE_ENOTSUP = -6,  /* combination not supported                          */
+    CHPE_ENOENT = -7    /* handle / registered pointer not found              */
+};
+
+/* ---- formats ------------------------------------------------------------ */
+/* How the stored codes map to weight values.  `bits` is 2, 4 or 8; codes are
+ * packed row-major, K contiguous, least-significant bits first inside each
+ * byte (element 2i in the low nibble of byte i for 4-bit; element 4i in bits
+ * 1:0 for 2-bit).  That is the reference packer's byte order
+ * (scripts/pack_qwen72b_chpe.py:138-148, :110-135) and also little-endian
+ * uint32 packing. */
+enum {
+    /* int8 codes, one fp32 scale per tensor; activations int8 (W8A8).
+     * src/tensor_map.zig:7-51 scales, src/engine.zig:227-251 gemvParallel. */
+    CHPE_SCHEME_I8_TENSOR = 1,
+    /* signed int8 codes, fp16 scale per group:  w = q * s[n, k/group] */
+    CHPE_SCHEME_I8_GROUP_F16 = 2,
+    /* unsigned codes, fp16 scale + fp16 zero per group: w = (c - z) * s */
+    CHPE_SCHEME_U_GROUP_F16_ZERO = 3,
+    /* unsigned codes, fp16 scale per group, constant zero-point `zero`:
+     * w = (c - zero) * s.  zero = 8 is the reference's offset-8 int4 with
+     * group-128 scales (src/kernels/cuda/bench_t4_qwen35.cu:24-87). */
+    CHPE_SCHEME_U_GROUP_F16_CONST_ZERO = 4,
+    /* the reference 2-bit codebook {0:0, 1:+1, 2:-2, 3:-1} with fp16 group
+     * scales: w = LUT[c] * s  (src/chpe_engine.zig:216-286) */
+    CHPE_SCHEME_W2_CODEBOOK_GROUP_F16 = 5,
+    /* per-row fp32 affine: w = value(c) * scale[n] + offset[n] summed per
+     * weight, plus bias[n] added once per row; value(c) is the signed int8,
+     * offset-8 nibble or 2-bit codebook value.  Covers the per-tile
+     * scale/bias cells (src/chpe_engine.zig:319-406). */
+    CHPE_SCHEME_ROW_AFFINE_F32 = 6
+};
+
+/* activation dtypes */
+enum { CHPE_X_F32 = 0, CHPE_X_BF16 = 1, CHPE_X_F16 = 2, CHPE_X_I8 = 3 };
+
+typedef struct chpe_fmt {
+    int32_t bits;   /* 2, 4, 8                                                */
+    int32_t scheme; /* CHPE_SCHEME_*                                          */
+    int32_t group;  /* group size along K; 0 means one group per row (= K)     */
+    float zero;     /* constant zero-point for CHPE_SCHEME_U_GROUP_F16_CONST_ZERO */
+} chpe_fmt;
+
+typedef struct chpe_ctx chpe_ctx;
+typedef struct chpe_tensor chpe_tensor;
+
+/* ---- context ------------------------------------------------------------ */
+int chpe_init(int device, chpe_ctx **out);
+int chpe_destroy(chpe_ctx *ctx);
+const char *chpe_last_error_string(const chpe_ctx *ctx);
+/* Library build/version string (no context needed). */
+const char *chpe_version(void);
+/* Device sync + read-back of the kernels' error flag (bounded waits that
+ * expired); returns CHPE_ETIMEOUT if any kernel recorded one. */
+int chpe_sync(chpe_ctx *ctx);
+
+/* ---- weight upload (the operator surface's tiles become device tensors) --- */
+/* Upload a [rows, cols] matrix given as packed codes plus its scales.
+ *   codes:  rows * row_stride bytes (row_stride >= cols*bits/8), host or device
+ *   scales: per scheme -- fp16 [rows, cols/group]; fp32 [1] (I8_TENSOR);
+ *           fp32 [rows] (ROW_AFFINE_F32)
+ *   zeros:  fp16 [rows, cols/group] (U_GROUP_F16_ZERO) or fp32 offsets [rows]
+ *           (ROW_AFFINE_F32), else NULL
+ *   bias:   fp32 [rows] added once per output row, or NULL
+ * Pointers may be host or device memory (detected).  The device copy is
+ * repacked into the strip layout and owned by the context.
+ * Replaces: archive.getTileU16Direct(lmap.*_tile) + the per-tensor scales of
+ * LayerTensorMap (src/engine.zig:609-612, src/tensor_map.zig:7-51). */
+int chpe_upload_matrix(chpe_ctx *ctx, const chpe_fmt *fmt, const void *codes, size_t row_stride, const void *scales,
+                       const void *zeros, const float *bias, size_t rows, size_t cols, chpe_tensor **out);
+
+/* Upload a run of CHPE cells (17408-byte Cell = 64 B header + 16384 B codes +
+ * 960 B payload, src/geometry.zig:243-256) found every `tile_stride` bytes
+ * starting at `first_cell` (20480 for standard archives, 17408 for dense).
+ * Each cell contributes TileDims.rows rows of TileDims.cols columns; all cells
+ * must share quant_bits, cols and the group-128 flag.  Semantics per cell
+ * follow gemvTileW2/W4/W8 (src/chpe_engine.zig:219-406), including the
+ * group-128 scales and 8 fp16 outlier columns of 2-bit cells. */
+int chpe_upload_cells(chpe_ctx *ctx, const void *first_cell, size_t n_cells, size_t tile_stride, chpe_tensor **out);
+
+/* Grouped quantizer on the device (this library's packer; the reference has
+ * none for these formats): fp32 w [rows, cols] -> one code byte per weight
+ * [rows, cols] plus fp16 scales (and zeros) [rows, cols/group].
+ *   symmetric != 0: s = fp16(max|w|/127), q = clamp(rint(w/s), -127, 127)
+ *   symmetric == 0: s = fp16((max-min)/(2^bits-1)), z = fp16(clamp(rint(-min/s))),
+ *                   c = clamp(rint(w/s) + z, 0, 2^bits-1)
+ * All pointers are device pointers; asynchronous on `stream`. */
+int chpe_quantize_group_dev(chpe_ctx *ctx, const float *w, size_t rows, size_t cols, int bits, int group,
+                            int symmetric, uint8_t *codes, uint16_t *scales, uint16_t *zeros, void *stream);
+
+int chpe_tensor_free(chpe_ctx *ctx, chpe_tensor *t);
+/* rows / cols / bits of a tensor and its device bytes (codes + metadata). */
+int chpe_tensor_info(const chpe_tensor *t, size_t *rows, size_t *cols, int *bits, size_t *device_bytes);
+
+/* Register a host weight region as the source of later `_parallel` calls.
+ * Replaces the mmap'd archive handed to the engine (src/weight_archive.zig:173-211):
+ * the shim registers each int8 weight tensor once at init. */
+int chpe_register_i8(chpe_ctx *ctx, const int8_t *host_weights, size_t rows, size_t cols);
+
+/* ---- GEMV on resident tensors (device pointers, async on `stream`) ------- */
+/* y[M, rows] = x[M, cols] . W^T for M = 1..64 activation rows.
+ *   x: x_dtype CHPE_X_F32/BF16/F16, or CHPE_X_I8 with per-row scales
+ *      x_scales[M] (W8A8: y = float(sum q_w q_x) * (scale_w * x_scales[m]))
+ *   accumulate != 0 adds into y (gemvTile* `accumulate`, src/chpe_engine.zig:310-314) */
+int chpe_gemv_dev(chpe_ctx *ctx, const chpe_tensor *w, const void *x, int x_dtype, const float *x_scales, int M,
+                  float *y, int accumulate, void *stream);
+/* mlp_out[M, rows] = silu(x.Wg^T) * (x.Wu^T), one pass over both weights.
+ * Replaces gemvGateUpSwiGLUParallel (src/engine.zig:285-313). */
+int chpe_gemv_gateup_swiglu_dev(chpe_ctx *ctx, const chpe_tensor *gate, const chpe_tensor *up, const void *x,
+                                int x_dtype, const float *x_scales, int M, float *mlp_out, void *stream);
+/* Activation fragments shared by several GEMVs that read the same input (the
+ * Q/K/V projections, gate/up, the Gated-DeltaNet in-projections read one
+ * normalised hidden state: src/engine.zig:615-617, :641-642).  The reference
+ * quantizes x once and passes the int8 vector to each gemvParallel; here x is
+ * converted once into the MMA operand layout (fp16 pairs plus block sums, or
+ * int8 with per-row scales) and each GEMV streams only its weights.
+ *   create: M = 1..8 rows of `like`'s cols; any tensor with the same cols,
+ *           code layout and epilogue block (same bits / group) can consume it
+ *   fill:   x [M, cols] device pointer of x_dtype (int8 needs x_scales[M];
+ *           fp32 into an int8 weight runs the reference's dynamic quantizer) */
+typedef struct chpe_xfrag chpe_xfrag;
+int chpe_xfrag_create(chpe_ctx *ctx, const chpe_tensor *like, int M, int x_dtype, chpe_xfrag **out);
+int chpe_xfrag_fill_dev(chpe_ctx *ctx, chpe_xfrag *xf, const void *x, const float *x_scales, void *stream);
+int chpe_gemv_xfrag_dev(chpe_ctx *ctx, const chpe_tensor *w, const chpe_xfrag *xf, float *y, int accumulate,
+                        void *stream);
+int chpe_gemv_gateup_swiglu_xfrag_dev(chpe_ctx *ctx, const chpe_tensor *gate, const chpe_tensor *up,
+                                      const chpe_xfrag *xf, float *mlp_out, void *stream);
+int chpe_xfrag_free(chpe_ctx *ctx, chpe_xfrag *xf);
+
+/* Dynamic per-row int8 activation quantization (device): for each of M rows of
+ * length n: s = max|x|/127 (1 if max <= 1e-9), q = clamp(round_half_away(x/s))
+ * -- src/kernels/neon.zig:644-670 quantizeActivationInt8, bit-exact. */
+int chpe_quantize_act_i8_dev(chpe_ctx *ctx, const float *x, int M, size_t n, int8_t *q, float *scales,
+                             void *stream);
+
+/* ---- reference-shaped host-pointer operators (synchronous) --------------- */
+/* src/engine.zig:227-251 gemvParallel(weights, scale_w, x_q8, scale_x, rows, cols, out) */
+int chpe_gemv_parallel(chpe_ctx *ctx, const int8_t *weights, float scale_w, const int8_t *x_q8, float scale_x,
+                       size_t rows, size_t cols, float *out);
+/* src/engine.zig:285-313 gemvGateUpSwiGLUParallel(gate, sg, up, su, x_q8, sx, rows, cols, mlp_out) */
+int chpe_gemv_gate_up_swiglu_parallel(chpe_ctx *ctx, const int8_t *gate_weights, float scale_gate,
+                                      const int8_t *up_weights, float scale_up, const int8_t *x_q8, float scale_x,
+                                      size_t rows, size_t cols, float *mlp_out);
+/* src/engine.zig:357-391 gemvBatch4Parallel(w, s_w, x0..x3, scales_x[4], rows, cols, out0..out3) */
+int chpe_gemv_batch4_parallel(chpe_ctx *ctx, const int8_t *weights, float scale_w, const int8_t *x0,
+                              const int8_t *x1, const int8_t *x2, const int8_t *x3, const float scales_x[4],
+                              size_t rows, size_t cols, float *out0, float *out1, float *out2, float *out3);
+/* src/engine.zig:434-460 gemvBatch8Parallel(w, s_w, x[8], scales_x[8], rows, cols, out[8]) */
+int chpe_gemv_batch8_parallel(chpe_ctx *ctx, const int8_t *weights, float scale_w, const int8_t *const x[8],
+                              const float scales_x[8], size_t rows, size_t cols, float *const out[8]);
+/* src/kernels/neon.zig:644-670 quantizeActivationInt8(x, out_q8) -> scale (host) */
+int chpe_quantize_activation_int8(chpe_ctx *ctx, const float *x, size_t n, int8_t *out_q8, float *scale_out);
+/* src/chpe_engine.zig:469-488 gemvTilePolymorphic(cell, x, y, row_base, accumulate):
+ * x has x_len fp32 values, y is written at y[row_base + r].  Cells with
+ * quant_bits 16/32 return CHPE_ENOTSUP. */
+int chpe_gemv_tile_polymorphic(chpe_ctx *ctx, const void *cell, const float *x, size_t x_len, float *y,
+                               size_t row_base, int accumulate);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* CHPE_B200_H */
