@@ -42,7 +42,7 @@ def measured_peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+    """nvidia-smi clocks / throttle reasons sampled every 20 ms across the measurement window."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -56,7 +56,7 @@ class ClockSampler:
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "20"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
@@ -137,17 +137,18 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.synchronize()
     dist_barrier(world)
 
+    clk = ClockSampler(local_rank).__enter__()
+    time.sleep(0.1)
     # device-timed region (whole step)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local_rank) as clk:
-        torch.cuda.synchronize()
-        dist_barrier(world)
-        e0.record(st)
-        for i in range(args.steps):
-            step(i)
-        e1.record(st)
-        torch.cuda.synchronize()
-        dist_barrier(world)
+    torch.cuda.synchronize()
+    dist_barrier(world)
+    e0.record(st)
+    for i in range(args.steps):
+        step(i)
+    e1.record(st)
+    torch.cuda.synchronize()
+    dist_barrier(world)
     ms_total = e0.elapsed_time(e1)
     ms_total = dist_max(ms_total, world)
     ms_step = ms_total / args.steps
@@ -174,6 +175,7 @@ def run_ours(args, rank, world, local_rank):
     e3.record(st)
     torch.cuda.synchronize()
     e2e_ms = dist_max(e2.elapsed_time(e3), world) / args.steps
+    clk.__exit__()
 
     peaks = measured_peaks()
     kern_avg = statistics.mean(kern_ms)

@@ -103,7 +103,6 @@ int log2_exact(int v) {
 
 void free_matrix(DevMatrix &m) {
     cudaFree(m.codes);
-    cudaFree(m.meta);
     cudaFree(m.bias);
     cudaFree(m.out_cols);
     cudaFree(m.out_w);
@@ -128,32 +127,31 @@ int build_matrix(chpe_ctx *ctx, const UploadSpec &u, const uint8_t *d_codes, siz
     m.N = (int)rows;
     m.K = (int)cols;
     m.n_strips = ceil_div((long)rows, kStripRows);
-    const int kc = u.layout == kLayoutS8 ? 32 : chunk_cols(u.bits);
-    m.n_chunks = ceil_div((long)cols, kc);
+    m.span = block_cols(u.bits);
+    m.n_blocks = ceil_div((long)cols, m.span);
     m.group = u.group;
     m.n_groups = (u.layout == kLayoutS8) ? 0 : (int)(cols / u.group);
-    m.group_shift = m.n_groups > 1 ? log2_exact(u.group) : 0;
+    if (u.meta_kind == kMetaNone) {
+        m.gpb = 0;
+        m.gshift = -1;
+    } else if (m.n_groups == 1 || u.group > m.span) {
+        m.gpb = 1;
+        m.gshift = -1;
+    } else {
+        m.gpb = m.span / u.group;
+        m.gshift = log2_exact(u.group);
+    }
+    m.block_bytes = kBlockCodeBytes + 16 * m.gpb * meta_bytes(u.meta_kind);
     m.scale = u.scale;
     m.zc = u.zc;
-    m.code_bytes = (size_t)m.n_strips * m.n_chunks * kChunkBytes;
-    cudaError_t e = cudaMalloc(&m.codes, m.code_bytes);
-    if (e != cudaSuccess) return fail(ctx, CHPE_ENOMEM, "cudaMalloc codes (%zu B): %s", m.code_bytes, cudaGetErrorString(e));
-    e = launch_repack2(d_codes, row_stride, m.N, m.K, src_bits, u.bits, u.layout, u.xorv, m.codes, m.n_strips,
-                       m.n_chunks, ctx->stream);
+    m.bytes = (size_t)m.n_strips * m.n_blocks * m.block_bytes;
+    cudaError_t e = cudaMalloc(&m.codes, m.bytes);
+    if (e != cudaSuccess) return fail(ctx, CHPE_ENOMEM, "cudaMalloc weights (%zu B): %s", m.bytes, cudaGetErrorString(e));
+    e = launch_repack_codes(d_codes, row_stride, src_bits, u.xorv, m, ctx->stream);
+    if (e == cudaSuccess && u.meta_kind != kMetaNone) e = launch_meta_repack(d_s, d_z, d_fs, d_fo, u.f32_zc, m, ctx->stream);
     if (e != cudaSuccess) {
         free_matrix(m);
         return fail(ctx, CHPE_ECUDA, "repack: %s", cudaGetErrorString(e));
-    }
-    if (u.meta_kind != kMetaNone) {
-        m.meta_bytes_total = (size_t)m.n_strips * m.n_groups * 16 * meta_bytes(u.meta_kind);
-        e = cudaMalloc(&m.meta, m.meta_bytes_total);
-        if (e == cudaSuccess)
-            e = launch_meta_repack(u.meta_kind, d_s, d_z, d_fs, d_fo, u.f32_zc, m.N, m.n_groups, m.meta, m.n_strips,
-                                   ctx->stream);
-        if (e != cudaSuccess) {
-            free_matrix(m);
-            return fail(ctx, CHPE_ECUDA, "metadata: %s", cudaGetErrorString(e));
-        }
     }
     if (d_bias) {
         e = cudaMalloc(&m.bias, rows * sizeof(float));
@@ -232,15 +230,17 @@ int spec_from_fmt(chpe_ctx *ctx, const chpe_fmt *f, size_t cols, UploadSpec *u) 
     return CHPE_OK;
 }
 
-int ensure_scratch(chpe_ctx *ctx, const GemvPlan &P, bool, int) {
+int ensure_scratch(chpe_ctx *ctx, const GemvPlan &P, cudaStream_t st) {
     int rc;
     if ((rc = grow(ctx, &ctx->scr.ws, &ctx->scr.ws_bytes, P.ws_bytes + 64))) return rc;
-    if ((size_t)P.counters > ctx->scr.counters_n) {
+    const size_t need = (size_t)P.split_counters;
+    if (need > ctx->scr.counters_n) {
         if (ctx->scr.counters) cudaFree(ctx->scr.counters);
         ctx->scr.counters = nullptr;
-        size_t n = (size_t)P.counters + 1024;
+        size_t n = need + 1024;
         CK(cudaMalloc(&ctx->scr.counters, n * sizeof(unsigned)));
-        CK(cudaMemset(ctx->scr.counters, 0, n * sizeof(unsigned)));
+        // zeroed on the launch stream so the first kernel sees clean tickets
+        CK(cudaMemsetAsync(ctx->scr.counters, 0, n * sizeof(unsigned), st));
         ctx->scr.counters_n = n;
     }
     return CHPE_OK;
@@ -248,7 +248,7 @@ int ensure_scratch(chpe_ctx *ctx, const GemvPlan &P, bool, int) {
 
 // Activation fragments of one block of <= 8 rows, ready for the GEMV kernel.
 struct Xfrag {
-    int layout = kLayoutF16, M = 0, K = 0, Kp = 0, e_cols = 0, x_dtype = 0;
+    int layout = kLayoutF16, bits = 8, M = 0, K = 0, Kp = 0, e_cols = 0, x_dtype = 0;
     bool xsplit = false;
     void *xf = nullptr, *xlo = nullptr;
     float *xs = nullptr;
@@ -269,7 +269,7 @@ int check_x(chpe_ctx *ctx, const DevMatrix &w, int x_dtype, const float *x_scale
     return CHPE_OK;
 }
 
-int w_kp(const DevMatrix &w) { return w.n_chunks * (w.layout == kLayoutS8 ? 32 : chunk_cols(w.bits)); }
+int w_kp(const DevMatrix &w) { return w.n_blocks * w.span; }
 
 // Fill fragments (buffers already sized) from M <= 8 rows of x.
 int prep_x(chpe_ctx *ctx, Xfrag &f, const void *x, const float *x_scales, float *sx_buf, cudaStream_t st) {
@@ -284,7 +284,7 @@ int prep_x(chpe_ctx *ctx, Xfrag &f, const void *x, const float *x_scales, float 
             f.sx = sx_buf;
         }
     } else {
-        e = launch_xprep_f16(x, f.x_dtype, f.M, f.K, f.Kp, f.e_cols, f.xsplit, f.xf, f.xlo, f.xs, st);
+        e = launch_xprep_f16(x, f.x_dtype, f.M, f.K, f.Kp, f.e_cols, f.xsplit, f.bits, f.xf, f.xs, st);
     }
     if (e != cudaSuccess) return fail(ctx, CHPE_ECUDA, "activation prep: %s", cudaGetErrorString(e));
     return CHPE_OK;
@@ -294,10 +294,12 @@ int gemv_core(chpe_ctx *ctx, const DevMatrix &w0, const DevMatrix *w1, int mode,
               int accumulate, const float *scale_override0, const float *scale_override1, cudaStream_t st) {
     GemvPlan P;
     plan_gemv(w0, f.M, mode, f.xsplit, &P);
-    if (w0.layout != f.layout || w0.K != f.K || w_kp(w0) > f.Kp || (w0.layout == kLayoutF16 && P.e_cols != f.e_cols))
-        return fail(ctx, CHPE_EINVAL, "activation fragments do not match this tensor (K %d/%d, Kp %d/%d, block %d/%d)",
-                    w0.K, f.K, w_kp(w0), f.Kp, P.e_cols, f.e_cols);
-    int rc = ensure_scratch(ctx, P, false, f.M);
+    if (w0.layout != f.layout || w0.K != f.K || w_kp(w0) > f.Kp ||
+        (w0.layout == kLayoutF16 && (P.e_cols != f.e_cols || w0.bits != f.bits)))
+        return fail(ctx, CHPE_EINVAL,
+                    "activation fragments do not match this tensor (K %d/%d, Kp %d/%d, block %d/%d, bits %d/%d)", w0.K,
+                    f.K, w_kp(w0), f.Kp, P.e_cols, f.e_cols, w0.bits, f.bits);
+    int rc = ensure_scratch(ctx, P, st);
     if (rc) return rc;
     GemvParams p;
     memset(&p, 0, sizeof p);
@@ -305,7 +307,6 @@ int gemv_core(chpe_ctx *ctx, const DevMatrix &w0, const DevMatrix *w1, int mode,
     const float *ovr[2] = {scale_override0, scale_override1};
     for (int i = 0; i < 2; ++i) {
         p.src[i].codes = ws[i]->codes;
-        p.src[i].meta = ws[i]->meta;
         p.src[i].bias = ws[i]->bias;
         p.src[i].out_cols = ws[i]->out_cols;
         p.src[i].out_w = ws[i]->out_w;
@@ -317,16 +318,14 @@ int gemv_core(chpe_ctx *ctx, const DevMatrix &w0, const DevMatrix *w1, int mode,
     p.K = w0.K;
     p.M = f.M;
     p.n_strips = w0.n_strips;
-    p.n_chunks = w0.n_chunks;
-    p.n_groups = w0.n_groups;
-    p.group_shift = w0.group_shift;
+    p.n_blocks = w0.n_blocks;
+    p.block_bytes = w0.block_bytes;
+    p.gshift = w0.gshift;
     p.meta_kind = w0.meta_kind;
     p.n_sg = P.n_sg;
     p.n_ks = P.n_ks;
-    p.cpk = P.cpk;
-    p.gps = P.gps;
+    p.bpk = P.bpk;
     p.xf = f.xf;
-    p.xlo = f.xlo;
     p.xs = f.xs;
     p.sx = f.sx;
     p.xrow = f.xrow;
@@ -334,7 +333,8 @@ int gemv_core(chpe_ctx *ctx, const DevMatrix &w0, const DevMatrix *w1, int mode,
     p.ldy = ldy;
     p.accumulate = accumulate;
     p.ws = ctx->scr.ws;
-    p.counters = ctx->scr.counters;
+    p.split_cnt = ctx->scr.counters;
+    p.maxp = P.maxp;
     p.err = ctx->d_err;
     cudaError_t e = launch_gemv(w0, w1, P, p, st);
     if (e != cudaSuccess) return fail(ctx, CHPE_ECUDA, "gemv launch: %s", cudaGetErrorString(e));
@@ -344,6 +344,7 @@ int gemv_core(chpe_ctx *ctx, const DevMatrix &w0, const DevMatrix *w1, int mode,
 Xfrag xfrag_shape(const DevMatrix &w, int M, int x_dtype, size_t *xf_bytes, size_t *xs_bytes) {
     Xfrag f;
     f.layout = w.layout;
+    f.bits = w.bits;
     f.M = M;
     f.K = w.K;
     f.Kp = w_kp(w);
@@ -372,7 +373,6 @@ int run_gemv(chpe_ctx *ctx, const DevMatrix &w0, const DevMatrix *w1, int mode, 
         size_t xfb, xsb;
         Xfrag f = xfrag_shape(w0, Mb, x_dtype, &xfb, &xsb);
         if ((rc = grow(ctx, &ctx->scr.xf, &ctx->scr.xf_bytes, xfb))) return rc;
-        if (f.xsplit && (rc = grow(ctx, &ctx->scr.xlo, &ctx->scr.xlo_bytes, xfb))) return rc;
         if ((rc = grow(ctx, reinterpret_cast<void **>(&ctx->scr.xs), &ctx->scr.xs_bytes, xsb + 32))) return rc;
         if ((rc = grow(ctx, reinterpret_cast<void **>(&ctx->scr.sx), &ctx->scr.sx_bytes, 64 * sizeof(float)))) return rc;
         f.xf = ctx->scr.xf;
@@ -703,7 +703,7 @@ extern "C" int chpe_tensor_info(const chpe_tensor *t, size_t *rows, size_t *cols
     if (rows) *rows = t->m.N;
     if (cols) *cols = t->m.K;
     if (bits) *bits = t->m.bits;
-    if (device_bytes) *device_bytes = t->m.code_bytes + t->m.meta_bytes_total;
+    if (device_bytes) *device_bytes = t->m.bytes;
     return CHPE_OK;
 }
 
@@ -904,7 +904,6 @@ extern "C" int chpe_xfrag_create(chpe_ctx *ctx, const chpe_tensor *like, int M, 
     chpe_xfrag *h = new chpe_xfrag();
     h->f = xfrag_shape(like->m, M, x_dtype, &h->xf_bytes, &h->xs_bytes);
     cudaError_t e = cudaMalloc(&h->f.xf, h->xf_bytes);
-    if (e == cudaSuccess && h->f.xsplit) e = cudaMalloc(&h->f.xlo, h->xf_bytes);
     if (e == cudaSuccess) e = cudaMalloc(reinterpret_cast<void **>(&h->f.xs), h->xs_bytes + 32);
     if (e == cudaSuccess) e = cudaMalloc(reinterpret_cast<void **>(&h->sx), 64 * sizeof(float));
     if (e == cudaSuccess && x_dtype == CHPE_X_F32)

@@ -1,0 +1,577 @@
+// gemv_impl.cuh -- decode/verify GEMV kernel template for M = 1..8 activation
+// rows over quantized weights in the strip layout (layout.h).  Instantiated per
+// code width in gemv_b8.cu / gemv_b4.cu / gemv_b2.cu / gemv_s8.cu; planned and
+// dispatched in gemv.cu.
+//
+// Persistent, warp-specialised kernel.  A CTA (8 consumer warps + 1 producer
+// warp) is bound to one K-slice for its lifetime: its activation fragments are
+// bulk-copied into shared memory once.  The (strip group, block) items of the
+// slice are split stream-K style into one equal contiguous range per CTA.  The
+// producer thread streams its range -- per strip and stage one block, 4 KiB of
+// codes plus the block's group metadata, in one 1-D bulk copy (TMA engine,
+// mbarrier completion, L2 evict-first) -- through a 4-stage shared-memory
+// ring.  A strip group is four 16-row strips, or for the fused gate/up SwiGLU
+// the same two strips of the gate and of the up matrix.
+//
+// Each MMA warp takes one chunk of every block, turns codes into fp16 MMA
+// operands in registers with one LOP3 / PRMT per pair (the code as an exact
+// fp16 subnormal, code * 2^-24 -- or code * 2^-24 * 2^4m for codes read at a
+// higher bit position, with 2^-4m pre-applied to that k-step's activations),
+// issues m16n8k16 MMAs against the staged activation fragments, and folds the
+// per-group scale / zero-point into fp32 register accumulators:
+//     acc += s * D + (-z * s * 2^-24) * sum(x over the block),  y = 2^24 * acc.
+// The int8 x int8 path (W8A8) feeds raw codes to m16n8k32 integer MMAs and
+// keeps exact int32 sums.  When a CTA's range leaves a strip group, its warps
+// reduce through shared memory in a fixed order; a strip group covered by
+// several CTAs (range boundaries, K-slices) collects one partial sum per CTA
+// in a workspace slot numbered by slice and range, and the last CTA to arrive
+// (atomic count) sums the slots in slot order, so results are deterministic.
+#pragma once
+#include <algorithm>
+#include <type_traits>
+
+#include "common.cuh"
+#include "internal.h"
+
+namespace chpe {
+
+constexpr int kNW = 8;      // MMA warps per CTA (one chunk of each block)
+constexpr int kStages = 8;  // ring depth (blocks per strip)
+constexpr int kSG = 4;      // strips per strip group
+constexpr int kProducerWarp = kNW, kEpilogueWarp = kNW + 1;
+constexpr int kThreads = (kNW + 2) * 32;
+constexpr int kXMaxBytes = 20 * 1024;  // activation fragments staged per CTA
+constexpr int kSmemBudget = 220 * 1024;
+static_assert(kNW == kChunksPerBlock, "one block per stage, one chunk per warp");
+
+struct SmemLayout {
+    size_t bar, tags, ring, xf, xs, red, info, total;
+};
+
+// Hand-off of one finished segment from the MMA warps to the epilogue warp.
+struct SegInfo {
+    int sg;     // strip group, -1 = no more segments
+    int whole;  // the segment covers the strip group's whole K
+};
+
+__host__ __device__ inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// Bytes of activation fragments per block of K (fp16 units of 16 bytes).
+__host__ __device__ inline size_t xfrag_bytes_per_block(int layout, int bits, int M, bool xsplit) {
+    const int steps = layout == kLayoutS8 ? 1 : (256 / bits) / 16;
+    return (size_t)kChunksPerBlock * steps * M * 32 * (xsplit ? 2 : 1);
+}
+
+__host__ __device__ inline SmemLayout smem_layout(int layout, int bits, int bpk, int M, bool xsplit, int e_cols,
+                                                  int block_bytes) {
+    SmemLayout L;
+    L.bar = 0;    // full[kStages], empty[kStages], xbar, rfull[2], rempty[2]
+    L.tags = 256; // unit / block / flag tag per ring slot
+    size_t o = 512;
+    static_assert((2 * kStages + 5) * 8 <= 256 && 3 * kStages * 4 <= 256, "barrier / tag area");
+    L.ring = o;
+    o += align_up((size_t)kStages * kSG * block_bytes, 128);
+    L.xf = o;
+    o = align_up(o + (size_t)bpk * xfrag_bytes_per_block(layout, bits, M, xsplit), 128);
+    L.xs = o;
+    if (layout == kLayoutF16) o = align_up(o + (size_t)bpk * kChunksPerBlock * ((256 / bits) / e_cols) * 32, 128);
+    L.red = o;  // two buffers of per-warp accumulators [warp][strip][16 rows][M]
+    o += 2 * (size_t)kNW * kSG * 16 * M * 4;
+    L.info = o;
+    o += 2 * sizeof(SegInfo);
+    L.total = align_up(o, 128);
+    return L;
+}
+
+// Stream-K partition of the (strip group, block) items of one K-slice over the
+// Gk CTAs that work on it: CTA j owns items [start(j), start(j+1)).
+__host__ __device__ inline long part_start(long T, int Gk, int j) { return (long)j * T / Gk; }
+__host__ __device__ inline int part_owner(long T, int Gk, long x) { return (int)(((x + 1) * Gk - 1) / T); }
+
+// Number of CTAs of a slice with nbk blocks whose range touches strip group sg.
+__host__ __device__ inline int part_count(int sg, int nbk, long n_sg, int Gk) {
+    const long T = n_sg * nbk;
+    return part_owner(T, Gk, (long)sg * nbk + nbk - 1) - part_owner(T, Gk, (long)sg * nbk) + 1;
+}
+
+// Codes become fp16 operands with the exponent field left at zero: the bit
+// pattern `code` is the fp16 subnormal code * 2^-24, exact for every code
+// (code < 1024).  One LOP3 (4/2-bit) or PRMT (8-bit) yields two operands and
+// no subtraction is needed.  To avoid a shift per k-step, codes are masked in
+// place in the low 8 bits of each half (w) or of each half of w >> 8: a code
+// at bit 4 (4-bit) or bit 2m (2-bit) reads as code * 2^-24 * 16 (or * 4^m);
+// the activations of that k-step were divided by the same power of two when
+// the fragments were built (act_scale_shift), so every product is
+// code * x * 2^-24.  The accumulator carries sum(code * x) only, so a small
+// result next to a large zero-point term keeps fp32 precision.
+template <int BITS>
+__device__ __forceinline__ uint32_t unpack_f16(uint32_t w, uint32_t w8, int j) {
+    if constexpr (BITS == 4) {
+        const uint32_t src = j < 2 ? w : w8;
+        return src & ((j & 1) ? 0x00F000F0u : 0x000F000Fu);
+    } else if constexpr (BITS == 2) {
+        const uint32_t src = j < 4 ? w : w8;
+        return src & (0x00030003u << (2 * (j & 3)));
+    } else {
+        (void)w8;
+        return __byte_perm(w, 0u, j == 0 ? 0x4140 : 0x4342);
+    }
+}
+
+constexpr float kTwo24 = 16777216.0f;
+
+constexpr float kTwoM24 = 1.0f / 16777216.0f;
+
+// (scale, offset * 2^-24 per unit of x) of rows g and g+8 of one group; the
+// block stores the two rows side by side, so one shared load fetches both.
+// zc24 is the constant zero-point times -2^-24.  F32 metadata already holds
+// the offset times 2^-24.
+template <int META>
+__device__ __forceinline__ void load_meta2(const uint8_t *gbase, int g, float zc24, float &s0, float &o0, float &s1,
+                                           float &o1) {
+    if constexpr (META == kMetaS16) {
+        const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(gbase + g * 4));
+        s0 = f.x;
+        o0 = f.x * zc24;
+        s1 = f.y;
+        o1 = f.y * zc24;
+    } else if constexpr (META == kMetaSZ16) {
+        const uint2 v = *reinterpret_cast<const uint2 *>(gbase + g * 8);
+        const float2 a = __half22float2(*reinterpret_cast<const __half2 *>(&v.x));
+        const float2 b = __half22float2(*reinterpret_cast<const __half2 *>(&v.y));
+        s0 = a.x;
+        o0 = -(a.x * a.y) * kTwoM24;
+        s1 = b.x;
+        o1 = -(b.x * b.y) * kTwoM24;
+    } else {
+        const float4 f = *reinterpret_cast<const float4 *>(gbase + g * 16);
+        s0 = f.x;
+        o0 = f.y;
+        s1 = f.z;
+        o1 = f.w;
+    }
+}
+
+// Strip i (0..kSG-1) of strip group sg, and the weight source it comes from:
+// plain GEMV -> strips 4sg..4sg+3 of source 0; gate/up -> strips 2sg, 2sg+1 of
+// source 0 (gate, i = 0, 1) and of source 1 (up, i = 2, 3).
+template <int MODE>
+__host__ __device__ __forceinline__ int strip_of(int sg, int i) {
+    return MODE == 1 ? 2 * sg + (i & 1) : kSG * sg + i;
+}
+template <int MODE>
+__host__ __device__ __forceinline__ int source_of(int i) {
+    return MODE == 1 ? (i >> 1) : 0;
+}
+
+template <int BITS, int LAYOUT, int E, bool XSPLIT, int MODE, int META>
+__global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
+    using Acc = typename std::conditional<LAYOUT == kLayoutS8, int, float>::type;
+    constexpr int KC = 256 / BITS;
+    constexpr int S = (LAYOUT == kLayoutS8) ? 1 : KC / 16;
+    constexpr int NE = (LAYOUT == kLayoutS8) ? 1 : KC / E;
+    constexpr int SPE = (LAYOUT == kLayoutS8) ? 1 : E / 16;
+    constexpr int MB = META == kMetaS16 ? 2 : META == kMetaSZ16 ? 4 : 8;
+    constexpr int kFirst = 1, kLast = 2;
+
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int ks = blockIdx.x % p.n_ks;
+    const int jk = blockIdx.x / p.n_ks;
+    const int Gk = gridDim.x / p.n_ks;
+    const int b0 = ks * p.bpk;
+    const int b1 = min(b0 + p.bpk, p.n_blocks);
+    const int nb = b1 - b0;
+    const long T = (long)p.n_sg * nb;
+    const long i0 = part_start(T, Gk, jk), i1 = part_start(T, Gk, jk + 1);
+    const int M = p.M;
+    const int BB = p.block_bytes;
+    const SmemLayout L = smem_layout(LAYOUT, BITS, p.bpk, M, XSPLIT, E, BB);
+
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + L.bar);
+    uint64_t *empty = full + kStages;
+    uint64_t *xbar = empty + kStages;
+    uint64_t *rfull = xbar + 1;   // [2] MMA warps -> epilogue warp: accumulators written
+    uint64_t *rempty = rfull + 2; // [2] epilogue warp -> MMA warps: buffer free again
+    int *tag_unit = reinterpret_cast<int *>(smem + L.tags);
+    int *tag_blk = tag_unit + kStages;
+    int *tag_flags = tag_blk + kStages;
+    SegInfo *info = reinterpret_cast<SegInfo *>(smem + L.info);
+
+    if (threadIdx.x == 0) {
+#pragma unroll
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kNW);
+        }
+        mbar_init(xbar, 1);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&rfull[b], kNW * 32);
+            mbar_init(&rempty[b], 1);
+        }
+        fence_barrier_init();
+    }
+    __syncthreads();
+
+    if (warp == kProducerWarp) {
+        // ---------------- producer ----------------
+        if (lane == 0) {
+            const uint64_t pol = l2_policy_evict_first();
+            int it = 0;
+            bool x_issued = false;
+            auto issue_x = [&]() {
+                grid_dependency_wait();
+                const uint32_t xb = (uint32_t)(nb * xfrag_bytes_per_block(LAYOUT, BITS, M, XSPLIT));
+                uint32_t tx = xb;
+                const uint32_t xsb = (uint32_t)nb * kChunksPerBlock * NE * 32;
+                if (LAYOUT == kLayoutF16) tx += xsb;
+                mbar_arrive_expect_tx(xbar, tx);
+                bulk_g2s(smem + L.xf,
+                         static_cast<const uint8_t *>(p.xf) + (size_t)b0 * xfrag_bytes_per_block(LAYOUT, BITS, M, XSPLIT),
+                         xb, xbar);
+                if (LAYOUT == kLayoutF16)
+                    bulk_g2s(smem + L.xs, reinterpret_cast<const uint8_t *>(p.xs) + (size_t)b0 * kChunksPerBlock * NE * 32,
+                             xsb, xbar);
+                x_issued = true;
+            };
+            for (long i = i0; i < i1; ++i, ++it) {
+                const int sg = (int)(i / nb), bi = (int)(i - (long)sg * nb);
+                const int slot = it % kStages, use = it / kStages;
+                if (use > 0 && !mbar_wait_bounded(&empty[slot], (use - 1) & 1)) {
+                    atomicExch(p.err, kErrWaitEmpty);
+                    break;
+                }
+                tag_unit[slot] = sg;
+                tag_blk[slot] = bi;
+                tag_flags[slot] = ((i == i0 || bi == 0) ? kFirst : 0) | ((i == i1 - 1 || bi == nb - 1) ? kLast : 0);
+                uint32_t tx = 0;
+#pragma unroll
+                for (int q = 0; q < kSG; ++q)
+                    if (strip_of<MODE>(sg, q) < p.n_strips) tx += (uint32_t)BB;
+                mbar_arrive_expect_tx(&full[slot], tx);
+#pragma unroll
+                for (int q = 0; q < kSG; ++q) {
+                    const int strip = strip_of<MODE>(sg, q);
+                    if (strip >= p.n_strips) continue;
+                    const uint8_t *src =
+                        p.src[source_of<MODE>(q)].codes + ((size_t)strip * p.n_blocks + b0 + bi) * BB;
+                    bulk_g2s_hint(smem + L.ring + ((size_t)slot * kSG + q) * BB, src, (uint32_t)BB, &full[slot], pol);
+                }
+                // weights first, then (once) the upstream-dependent activations
+                if (!x_issued && it + 1 >= kStages) issue_x();
+            }
+            if (!x_issued) issue_x();
+            // end-of-work marker in the next slot
+            {
+                const int slot = it % kStages, use = it / kStages;
+                if (use > 0 && !mbar_wait_bounded(&empty[slot], (use - 1) & 1)) atomicExch(p.err, kErrWaitEmpty);
+                tag_unit[slot] = -1;
+                mbar_arrive(&full[slot]);
+                ++it;
+            }
+            // every issued copy has landed before the CTA may exit
+            for (int s = 0; s < kStages && s < it; ++s) {
+                const int last = s + ((it - 1 - s) / kStages) * kStages;
+                if (!mbar_wait_bounded(&full[s], (last / kStages) & 1)) atomicExch(p.err, kErrWaitFull);
+            }
+            if (!mbar_wait_bounded(xbar, 0)) atomicExch(p.err, kErrWaitPrologue);
+        }
+    } else if (warp == kEpilogueWarp) {
+        // ---------------- epilogue warp ----------------
+        // Sums the MMA warps' accumulators of each finished segment (fixed warp
+        // order), writes the outputs of a whole strip group, or parks a partial
+        // sum in its workspace slot; the last partial to arrive sums all slots
+        // in slot order.  Runs behind the MMA warps, off the streaming path.
+        Acc *ws = static_cast<Acc *>(p.ws);
+        const int nq = kSG * 16 * M;  // (strip, row, token) entries of a segment
+        for (int k = 0;; ++k) {
+            const int b = k & 1, u = k >> 1;
+            if (!__all_sync(0xffffffffu, mbar_wait_bounded(&rfull[b], u & 1))) {
+                if (lane == 0) atomicExch(p.err, kErrWaitFull);
+                break;
+            }
+            const SegInfo si = info[b];
+            if (si.sg < 0) break;
+            const int sg = si.sg;
+            const Acc *red = reinterpret_cast<const Acc *>(smem + L.red) + (size_t)b * kNW * kSG * 16 * M;
+            // value of entry q = (i*16 + r)*M + tok: output (or partial) of strip i, row r, token tok
+            auto finalize = [&](int q, Acc v, Acc v_up) {
+                const int tok = q % M, ir = q / M, r = ir & 15, i = ir >> 4;
+                const int row = strip_of<MODE>(sg, i) * kStripRows + r;
+                if (strip_of<MODE>(sg, i) >= p.n_strips || row >= p.N) return;
+                if (MODE == 0) {
+                    const GemvSrc &sr = p.src[0];
+                    float out = LAYOUT == kLayoutS8 ? (float)v * (sr.scale * p.sx[tok]) : (float)v * kTwo24;
+                    if (sr.bias) out += sr.bias[row];
+                    if (sr.out_cols) {
+                        float os = 0.0f;
+#pragma unroll
+                        for (int c = 0; c < 8; ++c) {
+                            const int col = sr.out_cols[(size_t)row * 8 + c];
+                            if (col >= 0)
+                                os += __half2float(sr.out_w[(size_t)row * 8 + c]) * p.xrow[(size_t)tok * p.K + col];
+                        }
+                        out += os;
+                    }
+                    float *yp = p.y + (size_t)tok * p.ldy + row;
+                    *yp = p.accumulate ? *yp + out : out;
+                } else {
+                    float gv, uv;
+                    if (LAYOUT == kLayoutS8) {
+                        gv = (float)v * (p.src[0].scale * p.sx[tok]);
+                        uv = (float)v_up * (p.src[1].scale * p.sx[tok]);
+                    } else {
+                        gv = (float)v * kTwo24;
+                        uv = (float)v_up * kTwo24;
+                    }
+                    if (p.src[0].bias) gv += p.src[0].bias[row];
+                    if (p.src[1].bias) uv += p.src[1].bias[row];
+                    p.y[(size_t)tok * p.ldy + row] = silu_f(gv) * uv;
+                }
+            };
+            // gate/up: entry q of a gate strip pairs with q + 2*16*M of the up strip
+            const int nq_out = MODE == 1 ? nq / 2 : nq;
+            const int up_off = 2 * 16 * M;
+            int slot_p = 0, total_p = 1;
+            if (!si.whole) {
+                // partial slot: partials of earlier K-slices first, then this slice's CTAs in order
+                total_p = 0;
+                for (int kk = 0; kk < p.n_ks; ++kk) {
+                    const int nbk = min(p.bpk, p.n_blocks - kk * p.bpk);
+                    const int cnt = part_count(sg, nbk, p.n_sg, Gk);
+                    if (kk < ks) slot_p += cnt;
+                    total_p += cnt;
+                }
+                slot_p += jk - part_owner(T, Gk, (long)sg * nb);
+            }
+            Acc *wslot = ws + ((size_t)sg * p.maxp + slot_p) * (kSG * 16 * 8);
+            for (int q = lane; q < nq; q += 32) {
+                Acc sum = 0;
+#pragma unroll
+                for (int w = 0; w < kNW; ++w) sum += red[(size_t)w * nq + q];
+                if (si.whole) {
+                    if (MODE == 0) {
+                        finalize(q, sum, 0);
+                    } else if (q < nq_out) {
+                        Acc su = 0;
+#pragma unroll
+                        for (int w = 0; w < kNW; ++w) su += red[(size_t)w * nq + q + up_off];
+                        finalize(q, sum, su);
+                    }
+                } else {
+                    wslot[q] = sum;
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&rempty[b]);  // accumulator buffer consumed
+            if (!si.whole) {
+                __threadfence();  // this CTA's partial sums visible before its arrival is counted
+                __syncwarp();
+                int last = 0;
+                if (lane == 0) {
+                    const unsigned old = atomicAdd(&p.split_cnt[sg], 1u);
+                    last = old == (unsigned)(total_p - 1);
+                    if (last) __threadfence();  // ... and the other CTAs' partial sums visible here
+                }
+                last = __shfl_sync(0xffffffffu, last, 0);
+                if (last) {
+                    const Acc *wsg = ws + (size_t)sg * p.maxp * (kSG * 16 * 8);
+                    for (int q = lane; q < nq_out; q += 32) {
+                        Acc sum = 0, su = 0;
+                        for (int c = 0; c < total_p; ++c) {
+                            sum += __ldcg(&wsg[(size_t)c * (kSG * 16 * 8) + q]);
+                            if (MODE == 1) su += __ldcg(&wsg[(size_t)c * (kSG * 16 * 8) + q + up_off]);
+                        }
+                        finalize(q, sum, su);
+                    }
+                    __syncwarp();
+                    if (lane == 0) atomicExch(&p.split_cnt[sg], 0u);
+                }
+            }
+        }
+    } else {
+        // ---------------- MMA warps ----------------
+        const int g = lane >> 2, t = lane & 3;
+        const bool has_x = g < M;
+        const float *xss = reinterpret_cast<const float *>(smem + L.xs);
+        float zc24[kSG];
+#pragma unroll
+        for (int i = 0; i < kSG; ++i) zc24[i] = -p.src[source_of<MODE>(i)].zc * kTwoM24;
+        const int gshift = p.gshift;
+
+        bool aborted = false;
+        // A timed-out wait ends this warp's work; decisions are taken per warp
+        // (__all_sync) and every wait is bounded, so no warp can be left stuck.
+        if (!__all_sync(0xffffffffu, mbar_wait_bounded(xbar, 0))) {
+            if (lane == 0) atomicExch(p.err, kErrWaitPrologue);
+            aborted = true;
+        }
+        grid_dependency_wait();
+
+        Acc acc[kSG][4];
+#pragma unroll
+        for (int i = 0; i < kSG; ++i)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) acc[i][e] = 0;
+        int seg_first = 0, nseg = 0;
+        // Hands the accumulators (or the end-of-work mark, sg < 0) to the epilogue warp.
+        auto hand_off = [&](int sg, int whole) -> bool {
+            const int b = nseg & 1, u = nseg >> 1;
+            if (u > 0 && !__all_sync(0xffffffffu, mbar_wait_bounded(&rempty[b], (u - 1) & 1))) {
+                if (lane == 0) atomicExch(p.err, kErrWaitEmpty);
+                return false;
+            }
+            Acc *red = reinterpret_cast<Acc *>(smem + L.red) + ((size_t)b * kNW + warp) * kSG * 16 * M;
+            // lane (g, t) holds rows g (e = 0, 1) and g + 8 (e = 2, 3), tokens 2t + (e & 1)
+#pragma unroll
+            for (int i = 0; i < kSG; ++i)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int tok = 2 * t + (e & 1), r = g + 8 * (e >> 1);
+                    if (tok < M) red[(i * 16 + r) * M + tok] = acc[i][e];
+                    acc[i][e] = 0;
+                }
+            if (warp == 0 && lane == 0) info[b] = SegInfo{sg, whole};
+            mbar_arrive(&rfull[b]);
+            ++nseg;
+            return true;
+        };
+
+        for (int it = 0; !aborted; ++it) {
+            const int slot = it % kStages, use = it / kStages;
+            if (!__all_sync(0xffffffffu, mbar_wait_bounded(&full[slot], use & 1))) {
+                if (lane == 0) atomicExch(p.err, kErrWaitFull);
+                aborted = true;
+                break;
+            }
+            const int sg = tag_unit[slot];
+            if (sg < 0) break;
+            const int bi = tag_blk[slot];
+            const int flags = tag_flags[slot];
+            if (flags & kFirst) seg_first = bi;
+            const uint8_t *stg = smem + L.ring + (size_t)slot * kSG * BB;
+            const int cs = bi * kChunksPerBlock + warp;  // chunk in slice
+            uint4 wv[kSG];
+#pragma unroll
+            for (int i = 0; i < kSG; ++i)
+                wv[i] = *reinterpret_cast<const uint4 *>(stg + (size_t)i * BB + warp * kChunkBytes + lane * 16);
+            if constexpr (LAYOUT == kLayoutS8) {
+                uint2 b = make_uint2(0u, 0u);
+                if (has_x) b = reinterpret_cast<const uint2 *>(smem + L.xf)[((size_t)cs * M + g) * 4 + t];
+#pragma unroll
+                for (int i = 0; i < kSG; ++i)
+                    mma_s8_m16n8k32(reinterpret_cast<int *>(acc[i]), wv[i].x, wv[i].y, wv[i].z, wv[i].w, b.x, b.y);
+            } else {
+                uint4 w8[kSG];
+#pragma unroll
+                for (int i = 0; i < kSG; ++i)
+                    w8[i] = (BITS == 8) ? wv[i]
+                                        : make_uint4(wv[i].x >> 8, wv[i].y >> 8, wv[i].z >> 8, wv[i].w >> 8);
+                const uint4 *xu = reinterpret_cast<const uint4 *>(smem + L.xf);
+#pragma unroll
+                for (int eb = 0; eb < NE; ++eb) {
+                    float d[kSG][4];
+#pragma unroll
+                    for (int i = 0; i < kSG; ++i)
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) d[i][e] = 0.0f;
+#pragma unroll
+                    for (int jj = 0; jj < SPE; jj += (XSPLIT ? 1 : 2)) {
+                        const int j = eb * SPE + jj;
+                        const int kst = cs * S + j;
+                        uint4 bv = make_uint4(0u, 0u, 0u, 0u);
+                        if (has_x) bv = xu[((size_t)(XSPLIT ? kst : (kst >> 1)) * M + g) * 4 + t];
+#pragma unroll
+                        for (int i = 0; i < kSG; ++i) {
+                            mma_f16_m16n8k16(d[i], unpack_f16<BITS>(wv[i].x, w8[i].x, j),
+                                             unpack_f16<BITS>(wv[i].y, w8[i].y, j),
+                                             unpack_f16<BITS>(wv[i].z, w8[i].z, j),
+                                             unpack_f16<BITS>(wv[i].w, w8[i].w, j), bv.x, bv.y);
+                            const int j2 = XSPLIT ? j : j + 1;
+                            mma_f16_m16n8k16(d[i], unpack_f16<BITS>(wv[i].x, w8[i].x, j2),
+                                             unpack_f16<BITS>(wv[i].y, w8[i].y, j2),
+                                             unpack_f16<BITS>(wv[i].z, w8[i].z, j2),
+                                             unpack_f16<BITS>(wv[i].w, w8[i].w, j2), bv.z, bv.w);
+                        }
+                    }
+                    const int kib = warp * KC + eb * E;  // column within the block
+                    const int gib = gshift >= 0 ? (kib >> gshift) : 0;
+                    const float2 X = *reinterpret_cast<const float2 *>(xss + ((size_t)cs * NE + eb) * 8 + 2 * t);
+#pragma unroll
+                    for (int i = 0; i < kSG; ++i) {
+                        float s0, o0, s1, o1;
+                        load_meta2<META>(stg + (size_t)i * BB + kBlockCodeBytes + (size_t)gib * 16 * MB, g, zc24[i],
+                                         s0, o0, s1, o1);
+                        acc[i][0] = fmaf(o0, X.x, fmaf(s0, d[i][0], acc[i][0]));
+                        acc[i][1] = fmaf(o0, X.y, fmaf(s0, d[i][1], acc[i][1]));
+                        acc[i][2] = fmaf(o1, X.x, fmaf(s1, d[i][2], acc[i][2]));
+                        acc[i][3] = fmaf(o1, X.y, fmaf(s1, d[i][3], acc[i][3]));
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+            if (flags & kLast) {
+                const int whole = p.n_ks == 1 && seg_first == 0 && bi == nb - 1;
+                if (!hand_off(sg, whole)) {
+                    aborted = true;
+                    break;
+                }
+            }
+        }
+        if (!aborted) hand_off(-1, 0);  // end of work for the epilogue warp
+    }
+    __syncthreads();
+}
+
+template <int BITS, int LAYOUT, int E, bool XSPLIT, int MODE, int META>
+cudaError_t launch_gemv_t(const GemvPlan &plan, const GemvParams &p, cudaStream_t st) {
+    auto kern = gemv_kernel<BITS, LAYOUT, E, XSPLIT, MODE, META>;
+    static bool attr_set = false;
+    if (!attr_set) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBudget);
+        if (e != cudaSuccess) return e;
+        attr_set = true;
+    }
+    // one wave of resident CTAs: the planned grid capped by the real occupancy
+    int occ = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kThreads, plan.smem) != cudaSuccess || occ < 1)
+        occ = 1;
+    long gk = std::min<long>((long)plan.sms * occ / plan.n_ks, plan.items_min);
+    gk = std::max<long>(1, std::min<long>(gk, plan.grid / plan.n_ks));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(gk * plan.n_ks));
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = plan.smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, p);
+}
+
+// All variants of one code width / epilogue block, chosen at run time.
+template <int BITS, int LAYOUT, int E>
+cudaError_t launch_gemv_bits(const GemvPlan &plan, const GemvParams &p, int meta, cudaStream_t st) {
+    if constexpr (LAYOUT == kLayoutS8) {
+        if (plan.mode == 0) return launch_gemv_t<BITS, LAYOUT, E, false, 0, kMetaNone>(plan, p, st);
+        return launch_gemv_t<BITS, LAYOUT, E, false, 1, kMetaNone>(plan, p, st);
+    } else {
+#define CHPE_META_CASES(XS, MD)                                                                 \
+    switch (meta) {                                                                             \
+    case kMetaS16: return launch_gemv_t<BITS, LAYOUT, E, XS, MD, kMetaS16>(plan, p, st);        \
+    case kMetaSZ16: return launch_gemv_t<BITS, LAYOUT, E, XS, MD, kMetaSZ16>(plan, p, st);      \
+    default: return launch_gemv_t<BITS, LAYOUT, E, XS, MD, kMetaF32>(plan, p, st);              \
+    }
+        if (plan.mode == 0) {
+            if (plan.xsplit) { CHPE_META_CASES(true, 0) } else { CHPE_META_CASES(false, 0) }
+        } else {
+            if (plan.xsplit) { CHPE_META_CASES(true, 1) } else { CHPE_META_CASES(false, 1) }
+        }
+#undef CHPE_META_CASES
+    }
+}
+
+}  // namespace chpe

@@ -16,23 +16,25 @@ struct DevMatrix {
     int layout = kLayoutF16;
     int meta_kind = kMetaNone;
     int N = 0, K = 0;
-    int n_strips = 0, n_chunks = 0;
-    int group = 0;     // columns per group (K when one group per row)
-    int n_groups = 0;  // groups per row
-    int group_shift = 0;
-    float scale = 1.0f;  // per-tensor scale (S8 layout)
-    float zc = 0.0f;     // constant zero-point (kMetaS16)
-    uint8_t *codes = nullptr;
-    void *meta = nullptr;
+    int n_strips = 0;
+    int n_blocks = 0;     // blocks per strip (K padded to whole blocks)
+    int span = 0;         // columns per block
+    int block_bytes = 0;  // codes + metadata of one block of one strip
+    int gpb = 0;          // metadata groups per block
+    int gshift = -1;      // log2(group) when group <= span, else -1
+    int group = 0;        // columns per group (K when one group per row)
+    int n_groups = 0;     // groups per row
+    float scale = 1.0f;   // per-tensor scale (S8 layout)
+    float zc = 0.0f;      // constant zero-point (kMetaS16)
+    uint8_t *codes = nullptr;  // n_strips * n_blocks * block_bytes
     float *bias = nullptr;
-    int *out_cols = nullptr;        // [N][8] outlier columns, -1 = none
-    __half *out_w = nullptr;        // [N][8] outlier weights
-    size_t code_bytes = 0, meta_bytes_total = 0;
+    int *out_cols = nullptr;  // [N][8] outlier columns, -1 = none
+    __half *out_w = nullptr;  // [N][8] outlier weights
+    size_t bytes = 0;
 };
 
 struct GemvSrc {
     const uint8_t *codes;
-    const void *meta;
     const float *bias;
     const int *out_cols;
     const __half *out_w;
@@ -43,20 +45,21 @@ struct GemvSrc {
 struct GemvParams {
     GemvSrc src[2];
     int N, K, M;
-    int n_strips, n_chunks, n_groups, group_shift;
+    int n_strips, n_blocks, block_bytes, gshift;
     int meta_kind;
-    int n_sg, n_ks, cpk;
-    int gps;  // metadata groups reserved per strip in shared memory
+    int n_sg;  // strip groups (units along N)
+    int n_ks;  // K-slices; CTA b works on slice b % n_ks
+    int bpk;   // blocks per K-slice
+    int maxp;  // workspace slots per strip group (upper bound on partials)
     const void *xf;
-    const void *xlo;
     const float *xs;
     const float *sx;
     const float *xrow;  // fp32 activations [M][K] (outlier columns), or null
     float *y;
     int ldy;
     int accumulate;
-    void *ws;
-    unsigned *counters;
+    void *ws;             // partial sums [n_sg][maxp][2][128]
+    unsigned *split_cnt;  // [n_sg] arrivals of partial sums (self-resetting)
     int *err;
 };
 
@@ -65,27 +68,30 @@ struct GemvScratch {
     void *xf = nullptr, *xlo = nullptr;
     float *xs = nullptr, *sx = nullptr;
     void *ws = nullptr;
-    unsigned *counters = nullptr;
+    unsigned *counters = nullptr;  // split counters, one per strip group
     size_t xf_bytes = 0, xlo_bytes = 0, xs_bytes = 0, sx_bytes = 0, ws_bytes = 0, counters_n = 0;
 };
+
+constexpr int kMaxKs = 256;
 
 // Launch plan of one GEMV (computed on the host).
 struct GemvPlan {
     int mode = 0;  // 0 plain, 1 gate/up SwiGLU
-    int sg = 2;
-    int n_sg = 0, n_ks = 0, cpk = 0, gps = 0;
+    int n_sg = 0, n_ks = 0, bpk = 0, grid = 0, maxp = 0;
+    long items_min = 0;  // items of the shortest K-slice (bound on CTAs per slice)
+    int sms = 148;
     int e_cols = 0;  // epilogue block (columns)
     bool xsplit = false;
     size_t smem = 0;
-    size_t xf_bytes = 0, xlo_bytes = 0, xs_bytes = 0, ws_bytes = 0;
-    int counters = 0;
+    size_t xf_bytes = 0, xs_bytes = 0, ws_bytes = 0;
+    int split_counters = 0;
 };
 
 int plan_gemv(const DevMatrix &w, int M, int mode, bool xsplit, GemvPlan *plan);
 
 // x-fragment preparation (fp activations -> fp16 fragments + block sums).
-cudaError_t launch_xprep_f16(const void *x, int x_dtype, int M, int K, int Kp, int e_cols, bool xsplit, void *xf,
-                             void *xlo, float *xs, cudaStream_t st);
+cudaError_t launch_xprep_f16(const void *x, int x_dtype, int M, int K, int Kp, int e_cols, bool xsplit, int bits,
+                             void *xf, float *xs, cudaStream_t st);
 // int8 activations -> int8 fragments.
 cudaError_t launch_xprep_s8(const int8_t *xq, int M, int K, int Kp, void *xf, cudaStream_t st);
 // fp32 activations -> per-row dynamic int8 quantization (+ fragments).
@@ -96,15 +102,16 @@ cudaError_t launch_gemv(const DevMatrix &w0, const DevMatrix *w1, const GemvPlan
                         cudaStream_t st);
 
 // Repack row-major codes of `src_bits` bits each (LSB first inside a byte;
-// src_bits = 8 for one byte per code) into the strip layout of `bits`-wide
-// codes, XOR-ing each code with `xorv` (F16 layout only).
-cudaError_t launch_repack2(const uint8_t *src, size_t row_stride, int N, int K, int src_bits, int bits, int layout,
-                           uint32_t xorv, uint8_t *dst, int n_strips, int n_chunks, cudaStream_t st);
+// src_bits = 8 for one byte per code) into the code area of the strip layout
+// of `m`, XOR-ing each code with `xorv` (F16 layout only).
+cudaError_t launch_repack_codes(const uint8_t *src, size_t row_stride, int src_bits, uint32_t xorv,
+                                const DevMatrix &m, cudaStream_t st);
 // Grouped quantization of fp32 weights [N][K] (one code byte per weight).
 cudaError_t launch_quant_group(const float *w, int N, int K, int group, int bits, int symmetric, uint8_t *codes,
                                __half *scales, __half *zeros, cudaStream_t st);
-// fp16 scale/zero [N][G] -> strip metadata.
-cudaError_t launch_meta_repack(int kind, const __half *s, const __half *z, const float *fs, const float *fo,
-                               float zc_for_f32, int N, int G, void *dst, int n_strips, cudaStream_t st);
+// Scales [N][n_groups] (fp16, with fp16 zeros) or per-row fp32 scale/offset
+// -> the metadata area of every block of `m`.
+cudaError_t launch_meta_repack(const __half *s, const __half *z, const float *fs, const float *fo,
+                               float zc_for_f32, const DevMatrix &m, cudaStream_t st);
 
 }  // namespace chpe

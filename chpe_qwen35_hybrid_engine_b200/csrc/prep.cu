@@ -23,36 +23,53 @@ __device__ __forceinline__ uint32_t pack_h2(__half a, __half b) {
 
 // One block per E-column block, one warp per activation row (8 warps).
 // Lane l < E/4 converts fragment entry (k-step e*E/16 + l/4, t = l%4).
-__global__ void xprep_f16_kernel(const void *__restrict__ x, int dt, int M, int K, int E, uint2 *__restrict__ xf,
-                                 uint2 *__restrict__ xlo, float *__restrict__ xs) {
+// Fragments are stored as 16-byte units so a consumer fetches two k-steps
+// (or, for fp32 input, the hi and lo parts of one k-step) with one load:
+//   split (fp32 x):  unit (s, m, t) = {hi(16s+2t..), hi(16s+2t+8..), lo(..), lo(..)}
+//   fp16/bf16 x:     unit (s/2, m, t) = {step 2u: ..., step 2u+1: ...}
+// `bits` selects the per-k-step power-of-two pre-scale that matches where the
+// GEMV kernel reads the codes (unpack_f16): 4-bit odd k-steps of a chunk /16,
+// 2-bit k-step j of a chunk / 4^(j%4), 8-bit none.  Block sums stay unscaled.
+__global__ void xprep_f16_kernel(const void *__restrict__ x, int dt, int M, int K, int E, int split, int bits,
+                                 uint2 *__restrict__ xf, float *__restrict__ xs) {
     const int eb = blockIdx.x, tok = threadIdx.x >> 5, lane = threadIdx.x & 31;
     float part = 0.0f;
     if (lane < E / 4 && tok < M) {
         const int s = eb * (E / 16) + lane / 4, t = lane & 3;
+        const int steps = (256 / bits) / 16;  // k-steps per chunk
+        const int j = s % steps;
+        const int sh = bits == 4 ? 4 * (j & 1) : bits == 2 ? 2 * (j & 3) : 0;
+        const float down = __int_as_float((127 - sh) << 23), up = __int_as_float((127 + sh) << 23);
         const int kb = 16 * s + 2 * t;
         const int kk[4] = {kb, kb + 1, kb + 8, kb + 9};
         __half h[4], l[4];
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-            const float v = kk[q] < K ? load_x(x, dt, (size_t)tok * K + kk[q]) : 0.0f;
+            const float v = (kk[q] < K ? load_x(x, dt, (size_t)tok * K + kk[q]) : 0.0f) * down;
             h[q] = __float2half_rn(v);
-            l[q] = xlo ? __float2half_rn(v - __half2float(h[q])) : __float2half_rn(0.0f);
-            part += __half2float(h[q]) + __half2float(l[q]);
+            l[q] = split ? __float2half_rn(v - __half2float(h[q])) : __float2half_rn(0.0f);
+            part += (__half2float(h[q]) + __half2float(l[q])) * up;
         }
-        const size_t idx = ((size_t)s * M + tok) * 4 + t;
-        xf[idx] = make_uint2(pack_h2(h[0], h[1]), pack_h2(h[2], h[3]));
-        if (xlo) xlo[idx] = make_uint2(pack_h2(l[0], l[1]), pack_h2(l[2], l[3]));
+        const uint2 hv = make_uint2(pack_h2(h[0], h[1]), pack_h2(h[2], h[3]));
+        if (split) {
+            const size_t u = ((size_t)s * M + tok) * 4 + t;
+            xf[2 * u] = hv;
+            xf[2 * u + 1] = make_uint2(pack_h2(l[0], l[1]), pack_h2(l[2], l[3]));
+        } else {
+            const size_t u = ((size_t)(s >> 1) * M + tok) * 4 + t;
+            xf[2 * u + (s & 1)] = hv;
+        }
     }
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) part += __shfl_xor_sync(0xffffffffu, part, off);
     if (lane == 0) xs[(size_t)eb * 8 + tok] = part;
 }
 
-cudaError_t launch_xprep_f16(const void *x, int x_dtype, int M, int K, int Kp, int e_cols, bool xsplit, void *xf,
-                             void *xlo, float *xs, cudaStream_t st) {
+cudaError_t launch_xprep_f16(const void *x, int x_dtype, int M, int K, int Kp, int e_cols, bool xsplit, int bits,
+                             void *xf, float *xs, cudaStream_t st) {
     const int nblk = Kp / e_cols;
-    xprep_f16_kernel<<<nblk, 256, 0, st>>>(x, x_dtype, M, K, e_cols, static_cast<uint2 *>(xf),
-                                           xsplit ? static_cast<uint2 *>(xlo) : nullptr, xs);
+    xprep_f16_kernel<<<nblk, 256, 0, st>>>(x, x_dtype, M, K, e_cols, xsplit ? 1 : 0, bits, static_cast<uint2 *>(xf),
+                                           xs);
     return cudaGetLastError();
 }
 
@@ -154,10 +171,12 @@ __device__ __forceinline__ uint32_t src_code(const uint8_t *src, size_t stride, 
     return ((byte >> (bit & 7)) & mask) ^ xorv;
 }
 
-// One thread per 32-bit word of the strip layout.
-__global__ void repack_kernel(const uint8_t *__restrict__ src, size_t stride, int N, int K, int sbits, int bits,
-                              int layout, uint32_t xorv, uint32_t *__restrict__ dst, int n_strips, int n_chunks) {
+// One thread per 32-bit word of the code area of the strip layout.
+__global__ void repack_codes_kernel(const uint8_t *__restrict__ src, size_t stride, int N, int K, int sbits, int bits,
+                                    int layout, uint32_t xorv, uint8_t *__restrict__ dst, int n_strips,
+                                    int n_blocks, int block_bytes) {
     const size_t wi = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int n_chunks = n_blocks * kChunksPerBlock;
     const size_t total = (size_t)n_strips * n_chunks * 128;
     if (wi >= total) return;
     const int lw = (int)(wi & 127);
@@ -195,52 +214,64 @@ __global__ void repack_kernel(const uint8_t *__restrict__ src, size_t stride, in
             w |= src_code(src, stride, N, K, sbits, row, kb + 17, xorv) << 24;
         }
     }
-    dst[wi] = w;
+    const int blk = chunk / kChunksPerBlock, cib = chunk % kChunksPerBlock;
+    const size_t off = ((size_t)strip * n_blocks + blk) * block_bytes + (size_t)cib * kChunkBytes + (size_t)lw * 4;
+    *reinterpret_cast<uint32_t *>(dst + off) = w;
 }
 
-cudaError_t launch_repack2(const uint8_t *src, size_t row_stride, int N, int K, int src_bits, int bits, int layout,
-                           uint32_t xorv, uint8_t *dst, int n_strips, int n_chunks, cudaStream_t st) {
-    const size_t total = (size_t)n_strips * n_chunks * 128;
-    repack_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(src, row_stride, N, K, src_bits, bits, layout,
-                                                                   xorv, reinterpret_cast<uint32_t *>(dst),
-                                                                   n_strips, n_chunks);
+cudaError_t launch_repack_codes(const uint8_t *src, size_t row_stride, int src_bits, uint32_t xorv,
+                                const DevMatrix &m, cudaStream_t st) {
+    const size_t total = (size_t)m.n_strips * m.n_blocks * kChunksPerBlock * 128;
+    repack_codes_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(src, row_stride, m.N, m.K, src_bits, m.bits,
+                                                                        m.layout, xorv, m.codes, m.n_strips,
+                                                                        m.n_blocks, m.block_bytes);
     return cudaGetLastError();
 }
 
-// Metadata into [strip][G][16]; rows beyond N get scale 0.
+// One thread per metadata entry (strip, block, group-in-block, row).  The
+// group of entry gib of block b is b*span/group + gib; groups past the matrix
+// (K padding) and rows past N get zero entries.
 __global__ void meta_repack_kernel(int kind, const __half *__restrict__ s, const __half *__restrict__ z,
                                    const float *__restrict__ fs, const float *__restrict__ fo, float zc, int N,
-                                   int G, void *__restrict__ dst, int n_strips) {
+                                   int n_groups, int group, int span, int gpb, int n_strips, int n_blocks,
+                                   int block_bytes, uint8_t *__restrict__ dst) {
     const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
-    const size_t total = (size_t)n_strips * G * 16;
+    const size_t total = (size_t)n_strips * n_blocks * gpb * 16;
     if (i >= total) return;
     const int r16 = (int)(i & 15);
-    const size_t sg = i >> 4;
-    const int grp = (int)(sg % G);
-    const int strip = (int)(sg / G);
+    size_t rest = i >> 4;
+    const int gib = (int)(rest % gpb);
+    rest /= gpb;
+    const int blk = (int)(rest % n_blocks);
+    const int strip = (int)(rest / n_blocks);
     const int row = strip * kStripRows + r16;
-    const bool in = row < N;
+    const long grp = (long)blk * span / group + gib;
+    const bool in = row < N && grp < n_groups;
+    uint8_t *base = dst + ((size_t)strip * n_blocks + blk) * block_bytes + kBlockCodeBytes;
+    const int e = gib * 16 + (r16 & 7) * 2 + (r16 >> 3);  // rows g and g+8 side by side
     if (kind == kMetaS16) {
-        static_cast<__half *>(dst)[i] = in ? s[(size_t)row * G + grp] : __float2half_rn(0.0f);
+        reinterpret_cast<__half *>(base)[e] = in ? s[(size_t)row * n_groups + grp] : __float2half_rn(0.0f);
     } else if (kind == kMetaSZ16) {
-        __half2 v = in ? __halves2half2(s[(size_t)row * G + grp], z[(size_t)row * G + grp])
-                       : __halves2half2(__float2half_rn(0.0f), __float2half_rn(0.0f));
-        static_cast<__half2 *>(dst)[i] = v;
+        reinterpret_cast<__half2 *>(base)[e] =
+            in ? __halves2half2(s[(size_t)row * n_groups + grp], z[(size_t)row * n_groups + grp])
+               : __halves2half2(__float2half_rn(0.0f), __float2half_rn(0.0f));
     } else {
         float2 v = make_float2(0.0f, 0.0f);
         if (in) {
             const float sc = fs[row];
-            v = make_float2(sc, (fo ? fo[row] : 0.0f) - zc * sc);
+            // offset per unit of x, times 2^-24 (the GEMV scales its sums by 2^24 at the end)
+            v = make_float2(sc, ((fo ? fo[row] : 0.0f) - zc * sc) * (1.0f / 16777216.0f));
         }
-        static_cast<float2 *>(dst)[i] = v;
+        reinterpret_cast<float2 *>(base)[e] = v;
     }
 }
 
-cudaError_t launch_meta_repack(int kind, const __half *s, const __half *z, const float *fs, const float *fo,
-                               float zc_for_f32, int N, int G, void *dst, int n_strips, cudaStream_t st) {
-    const size_t total = (size_t)n_strips * G * 16;
-    meta_repack_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(kind, s, z, fs, fo, zc_for_f32, N, G, dst,
-                                                                       n_strips);
+cudaError_t launch_meta_repack(const __half *s, const __half *z, const float *fs, const float *fo,
+                               float zc_for_f32, const DevMatrix &m, cudaStream_t st) {
+    const size_t total = (size_t)m.n_strips * m.n_blocks * m.gpb * 16;
+    meta_repack_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(
+        m.meta_kind, s, z, fs, fo, zc_for_f32, m.N, m.n_groups, m.group, m.span, m.gpb, m.n_strips, m.n_blocks,
+        m.block_bytes, m.codes);
     return cudaGetLastError();
 }
 
