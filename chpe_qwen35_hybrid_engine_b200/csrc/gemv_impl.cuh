@@ -36,7 +36,7 @@
 namespace chpe {
 
 constexpr int kNW = 8;      // MMA warps per CTA (one chunk of each block)
-constexpr int kStages = 8;  // ring depth (blocks per strip)
+constexpr int kStages = 4;  // ring depth (blocks per strip)
 constexpr int kSG = 4;      // strips per strip group
 constexpr int kProducerWarp = kNW, kEpilogueWarp = kNW + 1;
 constexpr int kThreads = (kNW + 2) * 32;
@@ -534,9 +534,24 @@ cudaError_t launch_gemv_t(const GemvPlan &plan, const GemvParams &p, cudaStream_
         attr_set = true;
     }
     // one wave of resident CTAs: the planned grid capped by the real occupancy
+    // (queried once per shared-memory size; the kernel's registers are fixed)
+    static size_t occ_smem[8] = {0};
+    static int occ_val[8] = {0};
     int occ = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kThreads, plan.smem) != cudaSuccess || occ < 1)
-        occ = 1;
+    for (int i = 0; i < 8 && occ_smem[i]; ++i)
+        if (occ_smem[i] == plan.smem) occ = occ_val[i];
+    if (!occ) {
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kThreads, plan.smem) != cudaSuccess || occ < 1) {
+            cudaGetLastError();
+            occ = 1;
+        }
+        for (int i = 0; i < 8; ++i)
+            if (!occ_smem[i]) {
+                occ_smem[i] = plan.smem;
+                occ_val[i] = occ;
+                break;
+            }
+    }
     long gk = std::min<long>((long)plan.sms * occ / plan.n_ks, plan.items_min);
     gk = std::max<long>(1, std::min<long>(gk, plan.grid / plan.n_ks));
     cudaLaunchConfig_t cfg = {};
