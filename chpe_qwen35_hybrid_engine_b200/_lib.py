@@ -52,6 +52,7 @@ SIGNATURES = {
     "chpe_gemv_dev": (I, [P, P, P, I, P, I, P, I, P]),
     "chpe_gemv_gateup_swiglu_dev": (I, [P, P, P, P, I, P, I, P, P]),
     "chpe_quantize_act_i8_dev": (I, [P, P, I, SZ, P, P, P]),
+    "chpe_gemv_noalloc_dev": (I, [P, P, P, I, P, I, P, P]),
     "chpe_xfrag_create": (I, [P, P, I, I, PP]),
     "chpe_xfrag_fill_dev": (I, [P, P, P, P, P]),
     "chpe_gemv_xfrag_dev": (I, [P, P, P, P, I, P]),

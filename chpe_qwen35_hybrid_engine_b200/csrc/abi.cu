@@ -4,6 +4,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <string>
 #include <unordered_map>
 #include <vector>
@@ -960,5 +961,121 @@ extern "C" int chpe_xfrag_free(chpe_ctx *ctx, chpe_xfrag *xf) {
     cudaFree(xf->sx);
     cudaFree(xf->xrow);
     delete xf;
+    return CHPE_OK;
+}
+
+// ---------------------------------------------------------------------------
+// allocation-free GEMV
+// ---------------------------------------------------------------------------
+// Some callers cannot allocate device memory at the moment they run a GEMV:
+// code recording a CUDA graph (cudaMalloc is not a stream operation and may
+// not be issued during capture), and host engines whose device memory is
+// carved out of one region reserved up front.  chpe_gemv_dev may grow the
+// context's scratch with cudaMalloc on first use of a larger shape; this entry
+// point never does.  Its scratch -- activation fragments, block sums, split-K
+// partial sums and their arrival counters -- lives in one file-scope device
+// array of kNoAllocScratchBytes, which every GPU that loads this library holds
+// until the process exits.  All calls share the array (it keeps the last
+// call's contents), so calls that overlap on the GPU race on it.
+
+constexpr size_t kNoAllocScratchBytes = 16u << 20;  // 16 MiB
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+
+namespace {
+
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void *g_noalloc_ptr[kNoAllocMaxDevices] = {nullptr};
+
+// Device address of the static scratch on the current device (looked up once
+// per device with that device current: in host code the array's name is only
+// a host-side stand-in, not a device address).
+int noalloc_scratch(chpe_ctx *ctx, uint8_t **out) {
+    if (ctx->device < 0 || ctx->device >= kNoAllocMaxDevices) return fail(ctx, CHPE_EINVAL, "device index");
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_ptr[ctx->device]) {
+        void *ptr = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+        if (e != cudaSuccess || !ptr)
+            return fail(ctx, CHPE_ECUDA, "cudaGetSymbolAddress(static scratch): %s", cudaGetErrorString(e));
+        g_noalloc_ptr[ctx->device] = ptr;
+    }
+    *out = static_cast<uint8_t *>(g_noalloc_ptr[ctx->device]);
+    return CHPE_OK;
+}
+
+}  // namespace
+
+extern "C" int chpe_gemv_noalloc_dev(chpe_ctx *ctx, const chpe_tensor *w, const void *x, int x_dtype,
+                                     const float *x_scales, int M, float *y, void *stream) {
+    if (!ctx || !w || !x || !y) return fail(ctx, CHPE_EINVAL, "null argument");
+    if (M < 1 || M > kMaxTokens) return fail(ctx, CHPE_EINVAL, "allocation-free GEMV takes 1..8 rows (got %d)", M);
+    const DevMatrix &m = w->m;
+    int rc = check_x(ctx, m, x_dtype, x_scales);
+    if (rc) return rc;
+    cudaError_t e = cudaSetDevice(ctx->device);
+    if (e != cudaSuccess) return fail(ctx, CHPE_ECUDA, "cudaSetDevice: %s", cudaGetErrorString(e));
+    uint8_t *base = nullptr;
+    if ((rc = noalloc_scratch(ctx, &base))) return rc;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+
+    size_t xfb = 0, xsb = 0;
+    Xfrag f = xfrag_shape(m, M, x_dtype, &xfb, &xsb);
+    GemvPlan P;
+    plan_gemv(m, M, 0, f.xsplit, &P);
+    // [split counters | activation fragments | block sums | activation scales | partial sums]
+    auto al = [](size_t v) { return (v + 255) / 256 * 256; };
+    const size_t cnt_bytes = al((size_t)P.split_counters * sizeof(unsigned));
+    const size_t off_xf = cnt_bytes, off_xs = off_xf + al(xfb), off_sx = off_xs + al(xsb + 32),
+                 off_ws = off_sx + al(kMaxTokens * sizeof(float)), need = off_ws + al(P.ws_bytes);
+    if (need > kNoAllocScratchBytes)
+        return fail(ctx, CHPE_EINVAL,
+                    "shape [%d x %d], M = %d needs %zu bytes of scratch; the allocation-free GEMV has %zu", m.N, m.K, M,
+                    need, kNoAllocScratchBytes);
+    // arrival counters start at zero (they also reset themselves after a clean call)
+    e = cudaMemsetAsync(base, 0, cnt_bytes, st);
+    if (e != cudaSuccess) return fail(ctx, CHPE_ECUDA, "clear counters: %s", cudaGetErrorString(e));
+    f.xf = base + off_xf;
+    f.xs = reinterpret_cast<float *>(base + off_xs);
+    f.xrow = x_dtype == CHPE_X_F32 ? static_cast<const float *>(x) : nullptr;
+    float *sx_buf = reinterpret_cast<float *>(base + off_sx);
+    if ((rc = prep_x(ctx, f, x, x_scales, (m.layout == kLayoutS8 && x_dtype == CHPE_X_F32) ? sx_buf : nullptr, st)))
+        return rc;
+    if (m.out_cols && !f.xrow) return fail(ctx, CHPE_EINVAL, "outlier columns need fp32 activations");
+
+    GemvParams p;
+    memset(&p, 0, sizeof p);
+    for (int i = 0; i < 2; ++i) {
+        p.src[i].codes = m.codes;
+        p.src[i].bias = m.bias;
+        p.src[i].out_cols = m.out_cols;
+        p.src[i].out_w = m.out_w;
+        p.src[i].scale = m.scale;
+        p.src[i].zc = m.zc;
+    }
+    p.N = m.N;
+    p.K = m.K;
+    p.M = M;
+    p.n_strips = m.n_strips;
+    p.n_blocks = m.n_blocks;
+    p.block_bytes = m.block_bytes;
+    p.gshift = m.gshift;
+    p.meta_kind = m.meta_kind;
+    p.n_sg = P.n_sg;
+    p.n_ks = P.n_ks;
+    p.bpk = P.bpk;
+    p.maxp = P.maxp;
+    p.xf = f.xf;
+    p.xs = f.xs;
+    p.sx = f.sx;
+    p.xrow = f.xrow;
+    p.y = y;
+    p.ldy = m.N;
+    p.accumulate = 0;
+    p.ws = base + off_ws;
+    p.split_cnt = reinterpret_cast<unsigned *>(base);
+    p.err = ctx->d_err;
+    e = launch_gemv(m, nullptr, P, p, st);
+    if (e != cudaSuccess) return fail(ctx, CHPE_ECUDA, "gemv launch: %s", cudaGetErrorString(e));
     return CHPE_OK;
 }

@@ -178,6 +178,22 @@ int chpe_xfrag_free(chpe_ctx *ctx, chpe_xfrag *xf);
 int chpe_quantize_act_i8_dev(chpe_ctx *ctx, const float *x, int M, size_t n, int8_t *q, float *scales,
                              void *stream);
 
+/* Allocation-free variant of chpe_gemv_dev (plain GEMV, M = 1..8).  No
+ * counterpart in the reference.  For callers that cannot allocate device
+ * memory when they run a GEMV: code recording a CUDA graph, where cudaMalloc
+ * may not be issued, and host engines that carve all device memory out of one
+ * region reserved up front.  chpe_gemv_dev may grow the context's scratch with
+ * cudaMalloc; this function never calls cudaMalloc, cudaFree or any allocating
+ * routine.  Its scratch is one static device array of 16 MiB that every GPU
+ * loading the library holds until exit; a shape whose scratch needs more
+ * returns CHPE_EINVAL with the required size.  All calls share that array and
+ * it keeps the last call's contents (its arrival counters are cleared with a
+ * memset at the start of every call), so calls that overlap on the GPU race.
+ * The first call on each device looks up the array's device address; make
+ * that first call before any stream capture. */
+int chpe_gemv_noalloc_dev(chpe_ctx *ctx, const chpe_tensor *w, const void *x, int x_dtype, const float *x_scales,
+                          int M, float *y, void *stream);
+
 /* ---- reference-shaped host-pointer operators (synchronous) --------------- */
 /* src/engine.zig:227-251 gemvParallel(weights, scale_w, x_q8, scale_x, rows, cols, out) */
 int chpe_gemv_parallel(chpe_ctx *ctx, const int8_t *weights, float scale_w, const int8_t *x_q8, float scale_x,
