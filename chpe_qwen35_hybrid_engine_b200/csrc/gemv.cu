@@ -40,7 +40,8 @@ int plan_gemv(const DevMatrix &w, int M, int mode, bool xsplit, GemvPlan *plan) 
     P.n_sg = mode == 1 ? ceil_div(w.n_strips, kSG / 2) : ceil_div(w.n_strips, kSG);
     const size_t x_per_block =
         xfrag_bytes_per_block(w.layout, w.bits, M, xsplit) + (size_t)kChunksPerBlock * ne * 32;
-    const int bpk_max = (int)std::max<size_t>(1, kXMaxBytes / x_per_block);
+    const size_t xmax = M <= 2 ? kXMaxBytes : kXMaxBytesWide;
+    const int bpk_max = (int)std::max<size_t>(1, xmax / x_per_block);
     // Fewest K-slices whose activation fragments fit the staging budget, with
     // equal slices; the stream-K partition balances the work, not the slicing.
     int n_ks = std::min(ceil_div(w.n_blocks, std::min(bpk_max, w.n_blocks)), kMaxKs);
@@ -56,6 +57,8 @@ int plan_gemv(const DevMatrix &w, int M, int mode, bool xsplit, GemvPlan *plan) 
     P.sms = num_sms();
     // upper bound here; the launch recomputes the grid from the kernel's occupancy
     long gk = std::min<long>((long)P.sms * per_sm / n_ks, items);
+    // at least ~4 items per CTA: small matrices get fewer, longer ranges
+    gk = std::min<long>(gk, std::max<long>(1, (long)P.n_sg * bpk / 4));
     gk = std::max<long>(1, gk);
     P.n_ks = n_ks;
     P.bpk = bpk;

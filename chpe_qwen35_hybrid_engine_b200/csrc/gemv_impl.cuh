@@ -40,7 +40,10 @@ constexpr int kStages = 4;  // ring depth (blocks per strip)
 constexpr int kSG = 4;      // strips per strip group
 constexpr int kProducerWarp = kNW, kEpilogueWarp = kNW + 1;
 constexpr int kThreads = (kNW + 2) * 32;
-constexpr int kXMaxBytes = 20 * 1024;  // activation fragments staged per CTA
+// activation fragments staged per CTA: small enough for two CTAs per SM at
+// M <= 2; with more rows the reduction buffers already limit a CTA to one SM
+constexpr int kXMaxBytes = 20 * 1024;
+constexpr int kXMaxBytesWide = 64 * 1024;
 constexpr int kSmemBudget = 220 * 1024;
 static_assert(kNW == kChunksPerBlock, "one block per stage, one chunk per warp");
 
@@ -376,13 +379,25 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
                 last = __shfl_sync(0xffffffffu, last, 0);
                 if (last) {
                     const Acc *wsg = ws + (size_t)sg * p.maxp * (kSG * 16 * 8);
+                    // Four independent partial sums over the slots keep several
+                    // L2 loads in flight; the association is fixed, so the result
+                    // is deterministic.
+                    constexpr size_t kSlot = kSG * 16 * 8;
                     for (int q = lane; q < nq_out; q += 32) {
-                        Acc sum = 0, su = 0;
-                        for (int c = 0; c < total_p; ++c) {
-                            sum += __ldcg(&wsg[(size_t)c * (kSG * 16 * 8) + q]);
-                            if (MODE == 1) su += __ldcg(&wsg[(size_t)c * (kSG * 16 * 8) + q + up_off]);
+                        Acc a[4] = {0, 0, 0, 0}, u4[4] = {0, 0, 0, 0};
+                        int c = 0;
+                        for (; c + 4 <= total_p; c += 4) {
+#pragma unroll
+                            for (int h = 0; h < 4; ++h) {
+                                a[h] += __ldcg(&wsg[(size_t)(c + h) * kSlot + q]);
+                                if (MODE == 1) u4[h] += __ldcg(&wsg[(size_t)(c + h) * kSlot + q + up_off]);
+                            }
                         }
-                        finalize(q, sum, su);
+                        for (; c < total_p; ++c) {
+                            a[c & 3] += __ldcg(&wsg[(size_t)c * kSlot + q]);
+                            if (MODE == 1) u4[c & 3] += __ldcg(&wsg[(size_t)c * kSlot + q + up_off]);
+                        }
+                        finalize(q, (a[0] + a[1]) + (a[2] + a[3]), (u4[0] + u4[1]) + (u4[2] + u4[3]));
                     }
                     __syncwarp();
                     if (lane == 0) atomicExch(&p.split_cnt[sg], 0u);

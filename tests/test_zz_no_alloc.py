@@ -69,7 +69,7 @@ def test_noalloc_matches_gemv_dev_twice(ctx, fmt):
 def test_noalloc_rejects_shapes_beyond_its_scratch(ctx):
     import torch
     from chpe_qwen35_hybrid_engine_b200 import SCHEME_U_GROUP_F16_ZERO, X_BF16
-    N, K, M = 32768, 16384, 8  # split-K partial sums alone exceed the 16 MiB array
+    N, K, M = 16, 1 << 21, 8  # the activation fragments alone (32 MiB) exceed the 16 MiB array
     t = ctx.upload_matrix(4, SCHEME_U_GROUP_F16_ZERO, np.zeros((N, K // 2), np.uint8),
                           np.ones((N, K // 64), np.float16), np.zeros((N, K // 64), np.float16), rows=N, cols=K,
                           group=64)
