@@ -53,6 +53,12 @@ SIGNATURES = {
     "chpe_gemv_gateup_swiglu_dev": (I, [P, P, P, P, I, P, I, P, P]),
     "chpe_quantize_act_i8_dev": (I, [P, P, I, SZ, P, P, P]),
     "chpe_gemv_noalloc_dev": (I, [P, P, P, I, P, I, P, P]),
+    "chpe_embed_i8_dev": (I, [P, P, F, I, I, P, I, P, P]),
+    "chpe_rmsnorm_dev": (I, [P, P, P, I, I, F, P, P]),
+    "chpe_mix_attn_stub_dev": (I, [P, P, I, I, I, I, I, P, P]),
+    "chpe_mix_ssm_stub_dev": (I, [P, P, I, P, I, I, I, I, P, P]),
+    "chpe_silu_mul_dev": (I, [P, P, P, SZ, P, P]),
+    "chpe_argmax_dev": (I, [P, P, I, I, P, P, P]),
     "chpe_xfrag_create": (I, [P, P, I, I, PP]),
     "chpe_xfrag_fill_dev": (I, [P, P, P, P, P]),
     "chpe_gemv_xfrag_dev": (I, [P, P, P, P, I, P]),

@@ -1079,3 +1079,6 @@ extern "C" int chpe_gemv_noalloc_dev(chpe_ctx *ctx, const chpe_tensor *w, const 
     if (e != cudaSuccess) return fail(ctx, CHPE_ECUDA, "gemv launch: %s", cudaGetErrorString(e));
     return CHPE_OK;
 }
+
+// Error word of a context (used by the step helpers in model.cu).
+int *chpe_ctx_error_word(chpe_ctx *ctx) { return ctx->d_err; }

@@ -1,0 +1,322 @@
+"""Decode / speculative-verify step of the CHPE hybrid model on the B200 library.
+
+Mirrors the reference's orchestration (src/engine.zig Qwen35Engine):
+  step        (batch 1, :583-734)   fused gate/up SwiGLU, SSM stand-in qkv*silu(z)
+  stepBatch4  (:753-900)            unfused gate, up + siluMul, SSM stand-in silu(qkv)*z
+  stepBatch8  (:902-1095)           same as batch 4 with 8 rows
+with the reference's stand-ins for the token mixers (full attention = V
+broadcast, :619-623; Gated DeltaNet = qkv gated by z, :651-654), RMSNorm before
+each block, residual adds, final RMSNorm, LM head and argmax (:1098-1110).
+Every projection runs on the library's quantized GEMV; the residual add is the
+GEMV's accumulate into the hidden state.  A step of fixed row count is captured
+once into a CUDA graph and replayed; greedy decoding feeds the argmax of one
+step into the next without leaving the device.
+
+Weight schemes:
+  "w8a8"   int8, one fp32 scale per tensor, activations quantized per row to
+           int8 inside the GEMV (the reference engine's own arithmetic)
+  "q8g32"  int8 codes with an fp16 scale per 32 columns, fp32 activations
+  "q4g64"  unsigned 4-bit codes with fp16 scale + zero per 64 columns
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass, field
+
+import numpy as np
+
+from . import _lib as L
+from .ops import Context, Tensor, _dev_ptr, _stream_ptr
+
+
+@dataclass(frozen=True)
+class Geometry:
+    hidden: int = 4096
+    ffn: int = 12288
+    vocab: int = 151936
+    n_layers: int = 32
+    attn_every: int = 4     # layer l is full attention when (l + 1) % attn_every == 0 (src/engine.zig:30-32)
+    q_dim: int = 8192       # query + output gate
+    kv_dim: int = 1024
+    ssm_qkv: int = 6144     # Gated-DeltaNet q, k, v projection rows
+    ssm_z: int = 2048       # Gated-DeltaNet gate projection rows
+    eps: float = 1e-6
+    head_dim: int = 0       # 0: reference stand-in out[i] = v[i % kv_dim]; else head-aligned GQA stand-in
+    q_heads: int = 16
+    kv_heads: int = 4
+
+    def is_attn(self, l: int) -> bool:
+        return (l + 1) % self.attn_every == 0
+
+    def weight_count(self) -> int:
+        H, F = self.hidden, self.ffn
+        n = 0
+        for l in range(self.n_layers):
+            if self.is_attn(l):
+                n += (self.q_dim + 2 * self.kv_dim) * H + H * H
+            else:
+                n += (self.ssm_qkv + self.ssm_z) * H + H * self.ssm_z
+            n += 3 * F * H
+        return n + self.vocab * H  # LM head (the embedding is a table lookup)
+
+
+# Qwen3.5-9B hybrid: 24 Gated DeltaNet + 8 GQA layers, hidden 4096, FFN 12288,
+# 16 q heads / 4 kv heads of 256, DeltaNet 16 heads of 128, vocab 151936.
+QWEN35_9B = Geometry()
+# Qwen2.5-72B: 80 GQA layers, hidden 8192, FFN 29568, 64 q / 8 kv heads of 128, vocab 152064.
+QWEN25_72B = Geometry(hidden=8192, ffn=29568, vocab=152064, n_layers=80, attn_every=1, q_dim=8192, kv_dim=1024,
+                      ssm_qkv=0, ssm_z=0, head_dim=128, q_heads=64, kv_heads=8)
+
+
+@dataclass
+class LayerWeights:
+    in_gamma: object
+    post_gamma: object
+    proj: dict = field(default_factory=dict)  # name -> Tensor
+
+
+SCHEMES = {"w8a8": (8, L.SCHEME_I8_TENSOR, 0), "q8g32": (8, L.SCHEME_I8_GROUP_F16, 32),
+           "q4g64": (4, L.SCHEME_U_GROUP_F16_ZERO, 64)}
+
+
+def quantize_device(ctx: Context, w, scheme: str):
+    """Quantize fp32 device weights [rows, cols] with this library's quantizers.
+    Returns (codes as packed row-major bytes, scales, zeros or None) on the device:
+      w8a8  : s = max|w| / 127 over the tensor, q = clamp(rint(w / s), -127, 127)
+      q8g32 : chpe_quantize_group_dev symmetric, group 32
+      q4g64 : chpe_quantize_group_dev asymmetric 4-bit, group 64 (two codes per byte)"""
+    import torch
+    if scheme == "w8a8":
+        m = w.abs().amax().float()
+        s = torch.where(m > 1e-8, m / 127.0, torch.ones_like(m)).reshape(1)
+        q = torch.clamp(torch.round(w / s), -127, 127).to(torch.int8)
+        return q, s.float(), None
+    bits, _, group = SCHEMES[scheme]
+    codes, scales, zeros = ctx.quantize_group_dev(w, bits, group, symmetric=(scheme == "q8g32"))
+    if bits == 4:
+        codes = (codes[:, 0::2] | (codes[:, 1::2] << 4)).contiguous()
+    return codes, scales, zeros
+
+
+def upload_quantized(ctx: Context, codes, scales, zeros, scheme: str, rows: int, cols: int) -> Tensor:
+    bits, sch, group = SCHEMES[scheme]
+    return ctx.upload_matrix(bits, sch, codes, scales, zeros, rows=rows, cols=cols, group=group)
+
+
+def build_random(ctx: Context, geom: Geometry, scheme: str, seed: int = 0, max_rows: int = 8, keep_host=False,
+                 shard=None):
+    """Random-init model (weights N(0, 0.02), quantized with `scheme`; norm
+    gammas 1 + N(0, 0.02); int8 embedding table with one scale), built on the
+    device.  `shard` = (rank, world) builds the tensor-parallel shard of that
+    rank (column-split q/k/v/gate/up and LM head, row-split o/down).  With
+    keep_host the quantized codes/scales are also returned as numpy arrays
+    (for the oracle) in a dict keyed like the reference tensor map."""
+    import torch
+    gen = torch.Generator(device=f"cuda:{ctx.device}")
+    gen.manual_seed(seed)
+    dev = torch.device("cuda", ctx.device)
+    eng = HybridEngine(ctx, geom, scheme, max_rows=max_rows)
+    host = {} if keep_host else None
+    rank, world = shard or (0, 1)
+    H, F = geom.hidden, geom.ffn
+
+    def mat(name, rows, cols, split=None):
+        # the full matrix is drawn in 1 GiB row blocks so every shard sees the same weights
+        w = torch.empty(rows, cols, device=dev)
+        step = max(1, (1 << 28) // cols)
+        for r0 in range(0, rows, step):
+            r1 = min(rows, r0 + step)
+            w[r0:r1].normal_(0.0, 0.02, generator=gen)
+        if split == "col":
+            w = w[rank * rows // world:(rank + 1) * rows // world]
+        elif split == "ffn":  # rows of gate/up follow the down projection's K split
+            w = w[_row_split(rows, world, rank, scheme)]
+        elif split == "row":
+            w = w[:, _row_split(cols, world, rank, scheme)]
+        w = w.contiguous()
+        codes, scales, zeros = quantize_device(ctx, w, scheme)
+        t = upload_quantized(ctx, codes, scales, zeros, scheme, w.shape[0], w.shape[1])
+        if host is not None:
+            host[name] = (codes.cpu().numpy(), scales.cpu().numpy(), None if zeros is None else zeros.cpu().numpy())
+        del w, codes, scales, zeros
+        return t
+
+    def gamma(name):
+        v = (1.0 + 0.02 * torch.randn(H, device=dev, generator=gen)).float().contiguous()
+        if host is not None:
+            host[name] = v.cpu().numpy()
+        return v
+
+    emb = torch.empty(geom.vocab, H, device=dev).normal_(0.0, 0.02, generator=gen)
+    es = float(emb.abs().amax() / 127.0)
+    eng.embed = torch.clamp(torch.round(emb / es), -127, 127).to(torch.int8).contiguous()
+    eng.embed_scale = es
+    del emb
+    if host is not None:
+        host["embed"] = (eng.embed.cpu().numpy(), np.float32(es))
+    tp = "col" if world > 1 else None
+    for l in range(geom.n_layers):
+        lw = LayerWeights(gamma(f"L{l}.in_gamma"), gamma(f"L{l}.post_gamma"))
+        if geom.is_attn(l):
+            lw.proj["q"] = mat(f"L{l}.q", geom.q_dim, H, tp)
+            lw.proj["k"] = mat(f"L{l}.k", geom.kv_dim, H, tp)
+            lw.proj["v"] = mat(f"L{l}.v", geom.kv_dim, H, tp)
+            lw.proj["o"] = mat(f"L{l}.o", H, H, "row" if world > 1 else None)
+        else:
+            lw.proj["qkv"] = mat(f"L{l}.qkv", geom.ssm_qkv, H, tp)
+            lw.proj["z"] = mat(f"L{l}.z", geom.ssm_z, H, tp)
+            lw.proj["out"] = mat(f"L{l}.out", H, geom.ssm_z, "row" if world > 1 else None)
+        lw.proj["gate"] = mat(f"L{l}.gate", F, H, "ffn" if world > 1 else None)
+        lw.proj["up"] = mat(f"L{l}.up", F, H, "ffn" if world > 1 else None)
+        lw.proj["down"] = mat(f"L{l}.down", H, F, "row" if world > 1 else None)
+        eng.layers.append(lw)
+    eng.final_gamma = gamma("final_gamma")
+    eng.head = mat("head", geom.vocab, H, tp)
+    torch.cuda.synchronize(dev)
+    return eng, host
+
+
+def _row_split(cols: int, world: int, rank: int, scheme: str):
+    """Columns of a row-split (K-split) projection owned by `rank`: contiguous,
+    on group boundaries (64 for 4-bit, 32 for 8-bit) so no group is cut."""
+    g = SCHEMES[scheme][2] or 32
+    ng = cols // g
+    a = rank * ng // world
+    b = (rank + 1) * ng // world
+    return slice(a * g, b * g)
+
+
+class HybridEngine:
+    """One model instance on one GPU (or one tensor-parallel shard; see tp.py)."""
+
+    def __init__(self, ctx: Context, geom: Geometry, scheme: str, max_rows: int = 8):
+        import torch
+        self.ctx, self.geom, self.scheme, self.max_rows = ctx, geom, scheme, max_rows
+        self.dev = torch.device("cuda", ctx.device)
+        self.layers: list[LayerWeights] = []
+        self.final_gamma = None
+        self.embed = None          # int8 [vocab, hidden]
+        self.embed_scale = 1.0
+        self.head: Tensor | None = None
+        self.graphs = {}
+        self.allreduce = None      # set by tensor parallelism: fn(tensor) summing across ranks
+        g, Mx = geom, max_rows
+        f32 = dict(dtype=torch.float32, device=self.dev)
+        widest = max(g.hidden, g.q_dim, g.ssm_qkv or 1, g.ffn)
+        self.buf = {
+            "hidden": torch.zeros(Mx, g.hidden, **f32), "norm": torch.zeros(Mx, g.hidden, **f32),
+            "a": torch.zeros(Mx, widest, **f32), "b": torch.zeros(Mx, max(g.kv_dim, g.ssm_z, g.ffn), **f32),
+            "c": torch.zeros(Mx, max(g.kv_dim, g.ffn), **f32), "mix": torch.zeros(Mx, g.hidden, **f32),
+            "logits": torch.zeros(Mx, g.vocab, **f32), "tokens": torch.zeros(Mx, dtype=torch.int32, device=self.dev),
+            "argmax": torch.zeros(Mx, dtype=torch.int32, device=self.dev), "maxv": torch.zeros(Mx, **f32),
+            "mix_out": torch.zeros(Mx, g.hidden, **f32),
+        }
+
+    # -- weights ---------------------------------------------------------------
+    def n_weight_bytes(self) -> int:
+        b = sum(t.device_bytes for lw in self.layers for t in lw.proj.values())
+        return b + (self.head.device_bytes if self.head else 0)
+
+    def _check(self, rc):
+        self.ctx._check(rc)
+
+    # -- one step ----------------------------------------------------------------
+    def step(self, M: int, stream=None):
+        """Run one step over rows 0..M-1 of buf["tokens"]; leaves logits, argmax, maxv."""
+        import torch
+        g, ctx, lib = self.geom, self.ctx, self.ctx.lib
+        b = self.buf
+        st = stream or torch.cuda.current_stream(self.dev)
+        sp = _stream_ptr(st)
+        H, F = g.hidden, g.ffn
+        xdt = L.X_F32
+
+        def gemv(t: Tensor, x, y, acc=False):
+            self._check(lib.chpe_gemv_dev(ctx.ptr, t.handle, _dev_ptr(x), xdt, None, M, _dev_ptr(y), int(acc), sp))
+
+        def gemv_res(t: Tensor, x, hidden):
+            """hidden += x . W^T (the residual add of the block); with tensor
+            parallelism the shard's partial sum goes through the all-reduce first."""
+            if self.allreduce is None:
+                gemv(t, x, hidden, acc=True)
+            else:
+                part = b["mix_out"][:M]
+                gemv(t, x, part)
+                self.allreduce(part)
+                hidden[:M].add_(part)
+
+        self._check(lib.chpe_embed_i8_dev(ctx.ptr, _dev_ptr(self.embed), C.c_float(self.embed_scale), H, g.vocab,
+                                          _dev_ptr(b["tokens"]), M, _dev_ptr(b["hidden"]), sp))
+        hid, norm = b["hidden"], b["norm"]
+        for l, lw in enumerate(self.layers):
+            self._check(lib.chpe_rmsnorm_dev(ctx.ptr, _dev_ptr(hid), _dev_ptr(lw.in_gamma), M, H, C.c_float(g.eps),
+                                             _dev_ptr(norm), sp))
+            p = lw.proj
+            if "q" in p:  # full attention (GQA) block; stand-in mixer = V broadcast
+                q_out, k_out, v_out = b["a"], b["b"], b["c"]
+                kv = p["v"].rows
+                gemv(p["q"], norm, q_out)
+                gemv(p["k"], norm, k_out)
+                gemv(p["v"], norm, v_out)
+                self._check(lib.chpe_mix_attn_stub_dev(ctx.ptr, _dev_ptr(v_out), kv, M, p["o"].cols, g.head_dim,
+                                                       g.q_heads // g.kv_heads, _dev_ptr(b["mix"]), sp))
+                gemv_res(p["o"], b["mix"], hid)
+            else:  # Gated DeltaNet block; stand-in mixer = qkv gated by z
+                qkv_out, z_out = b["a"], b["b"]
+                gemv(p["qkv"], norm, qkv_out)
+                gemv(p["z"], norm, z_out)
+                self._check(lib.chpe_mix_ssm_stub_dev(ctx.ptr, _dev_ptr(qkv_out), p["qkv"].rows, _dev_ptr(z_out),
+                                                      p["z"].rows, M, p["out"].cols, int(M > 1), _dev_ptr(b["mix"]),
+                                                      sp))
+                gemv_res(p["out"], b["mix"], hid)
+            self._check(lib.chpe_rmsnorm_dev(ctx.ptr, _dev_ptr(hid), _dev_ptr(lw.post_gamma), M, H,
+                                             C.c_float(g.eps), _dev_ptr(norm), sp))
+            if M == 1:  # src/engine.zig:682 fused gate/up SwiGLU
+                self._check(lib.chpe_gemv_gateup_swiglu_dev(ctx.ptr, p["gate"].handle, p["up"].handle,
+                                                            _dev_ptr(norm), xdt, None, M, _dev_ptr(b["a"]), sp))
+            else:  # src/engine.zig:839-844 unfused gate, up, siluMul
+                gemv(p["gate"], norm, b["b"])
+                gemv(p["up"], norm, b["c"])
+                self._check(lib.chpe_silu_mul_dev(ctx.ptr, _dev_ptr(b["b"]), _dev_ptr(b["c"]), M * p["gate"].rows,
+                                                  _dev_ptr(b["a"]), sp))
+                # rows are [M][ffn_shard] contiguous in b/c: silu_mul ran on the first M*rows elements
+            gemv_res(p["down"], b["a"], hid)
+        self._check(lib.chpe_rmsnorm_dev(ctx.ptr, _dev_ptr(hid), _dev_ptr(self.final_gamma), M, H, C.c_float(g.eps),
+                                         _dev_ptr(norm), sp))
+        gemv(self.head, norm, b["logits"])
+        self._check(lib.chpe_argmax_dev(ctx.ptr, _dev_ptr(b["logits"]), M, self.head.rows, _dev_ptr(b["argmax"]),
+                                        _dev_ptr(b["maxv"]), sp))
+
+    def capture(self, M: int):
+        """Capture step(M) as a CUDA graph (after one eager warm-up run)."""
+        import torch
+        st = torch.cuda.Stream(self.dev)
+        st.wait_stream(torch.cuda.current_stream(self.dev))
+        with torch.cuda.stream(st):
+            self.step(M, st)
+        torch.cuda.synchronize(self.dev)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=st):
+            self.step(M, st)
+        self.graphs[M] = g
+        return g
+
+    def decode_greedy(self, first_tokens, steps: int, M: int = 1, use_graph: bool = True):
+        """Greedy decode: each step's argmax rows become the next step's tokens.
+        Returns the argmax tokens of every step as an int array [steps, M]."""
+        import torch
+        b = self.buf
+        b["tokens"][:M].copy_(torch.as_tensor(np.asarray(first_tokens, np.int32)[:M], device=self.dev))
+        out = torch.empty(steps, M, dtype=torch.int32, device=self.dev)
+        if use_graph and M not in self.graphs:
+            self.capture(M)
+            b["tokens"][:M].copy_(torch.as_tensor(np.asarray(first_tokens, np.int32)[:M], device=self.dev))
+        for s in range(steps):
+            if use_graph:
+                self.graphs[M].replay()
+            else:
+                self.step(M)
+            out[s].copy_(b["argmax"][:M])
+            b["tokens"][:M].copy_(b["argmax"][:M])
+        torch.cuda.synchronize(self.dev)
+        return out.cpu().numpy()

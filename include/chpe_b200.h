@@ -178,6 +178,31 @@ int chpe_xfrag_free(chpe_ctx *ctx, chpe_xfrag *xf);
 int chpe_quantize_act_i8_dev(chpe_ctx *ctx, const float *x, int M, size_t n, int8_t *q, float *scales,
                              void *stream);
 
+/* ---- the rest of a decode / verify step (device pointers, async) --------
+ * The reference's Qwen35Engine.step orchestration (src/engine.zig:567-734,
+ * stepBatch4 :753-900, stepBatch8 :902-1095) around the GEMVs.  Rows are
+ * [M][dim] contiguous.  The residual adds of the engine are done by the GEMV
+ * itself (chpe_gemv_dev with accumulate = 1 into the hidden state). */
+/* src/engine.zig:567-580 embedToken: out[m][i] = table[tokens[m]][i] * scale */
+int chpe_embed_i8_dev(chpe_ctx *ctx, const int8_t *table, float scale, int hidden, int vocab, const int *tokens,
+                      int M, float *out, void *stream);
+/* src/kernels/neon.zig:673-702 rmsnorm: y = x * (1/sqrt(mean(x^2)+eps)) * gamma */
+int chpe_rmsnorm_dev(chpe_ctx *ctx, const float *x, const float *gamma, int M, int n, float eps, float *y,
+                     void *stream);
+/* src/engine.zig:619-623 full-attention stand-in: out[i] = v[i % kv_dim] when
+ * head_dim == 0; else head-aligned (query head h of head_dim columns takes kv
+ * head h / group), which shards with the heads under tensor parallelism */
+int chpe_mix_attn_stub_dev(chpe_ctx *ctx, const float *v, int kv_dim, int M, int out_dim, int head_dim, int group,
+                           float *out, void *stream);
+/* src/engine.zig:651-654 Gated-DeltaNet stand-in: out[i] = qkv[i % qkv_dim] * silu(z[i]);
+ * with silu_on_qkv (stepBatch4/8, src/engine.zig:813, :988): out[i] = silu(qkv[i]) * z[i] */
+int chpe_mix_ssm_stub_dev(chpe_ctx *ctx, const float *qkv, int qkv_dim, const float *z, int z_dim, int M,
+                          int out_dim, int silu_on_qkv, float *out, void *stream);
+/* src/kernels/neon.zig:705-712 siluMul */
+int chpe_silu_mul_dev(chpe_ctx *ctx, const float *g, const float *u, size_t n, float *out, void *stream);
+/* src/engine.zig:1098-1110 computeArgmax (first index of the maximum), per row */
+int chpe_argmax_dev(chpe_ctx *ctx, const float *logits, int M, int n, int *idx, float *maxv, void *stream);
+
 /* Allocation-free variant of chpe_gemv_dev (plain GEMV, M = 1..8).  No
  * counterpart in the reference.  For callers that cannot allocate device
  * memory when they run a GEMV: code recording a CUDA graph, where cudaMalloc
