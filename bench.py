@@ -3,16 +3,31 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload NAME]
 
-Prints ONE JSON line (rank 0).  Workloads (synthetic, seeded; no dataset):
-  q8_gemv   y[1,12288] = x[1,4096] . dequant(W)^T, W int8 with an fp16 scale per
-            32 along K (scales 0.02/127*exp(N(0,0.25))), x fp32 N(0,1), y fp32.
-            metric: algorithmic HBM GB/s of the GEMV.
-A "step" is one GEMV call (activation-fragment prep + GEMV kernel); the K timed
-steps run as one CUDA graph.  Inputs are resident in HBM for `value`; `e2e`
-runs the same step eagerly through the public
-API with pinned host buffers (host->device x, device->host y inside the timed
-region).  Weights rotate over enough copies (> 2x the 126 MB L2) that every
-step streams its weights from HBM.
+Prints ONE JSON line (rank 0).  Workloads (synthetic and seeded; there is no
+dataset and no checkpoint):
+
+  decode_72b (default)  Qwen2.5-72B-shaped decode (80 GQA layers, hidden 8192,
+                        FFN 29568, vocab 152064), 4-bit weights with an fp16
+                        scale and zero per 64 columns, tensor parallel over the
+                        N GPUs (NCCL all-reduce after o and down), batch 1;
+                        the batch-8 step is reported beside it.  metric: tokens/s
+                        for the whole job.  At N = 1 the line also carries the
+                        Qwen3.5-9B-shaped decode (8-bit, fp16 scale per 32) at
+                        batch 1 and the batch-4 / batch-8 verify steps.
+  decode_9b             the Qwen3.5-9B-shaped decode alone (N > 1: replicas).
+  q8_gemv               y[1,12288] = x[1,4096] . dequant(W)^T, int8 with an fp16
+                        scale per 32 columns; metric: algorithmic HBM GB/s.
+
+A decode step is one token per row: embedding, every layer, final norm, LM
+head and argmax.  Timed steps replay one CUDA graph per step and feed each
+step's argmax into the next on the device; the weights (7 GB for the 9B shape,
+40 GB / N for the 72B shape) are far larger than the 126 MB L2, so every step
+streams them from HBM.  `e2e` runs the same steps with the token copied in from
+pinned host memory and the argmax copied back to the host every step.  The
+roofline is that of the GEMV kernel: every GEMV of one step is captured on its
+own (activation fragments prepared beforehand) and its algorithmic bytes
+(packed codes + scales/zeros + activations read + outputs written) are divided
+by the replayed GEMV time.
 """
 from __future__ import annotations
 
@@ -31,6 +46,8 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 L2_BYTES = 126 * 1024 * 1024
+DECODE_METRIC = "decode tokens/s (quantized GEMV path; GEMV HBM GB/s vs peak in roofline)"
+GEMV_METRIC = "quantized GEMV HBM GB/s (Q8 int8 g32 fp16-scale, 12288x4096, batch 1)"
 
 
 def measured_peaks():
@@ -54,22 +71,22 @@ class ClockSampler:
         self.proc = None
         self.lines: list[str] = []
 
-    def __enter__(self):
+    def start(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
                                           "--format=csv,noheader,nounits", "-lms", "20"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
-            self.t.start()
+            threading.Thread(target=self._read, daemon=True).start()
         except (OSError, FileNotFoundError):
             self.proc = None
+        time.sleep(0.1)
         return self
 
     def _read(self):
         for line in self.proc.stdout:
             self.lines.append(line.strip())
 
-    def __exit__(self, *a):
+    def stop(self):
         if self.proc:
             self.proc.terminate()
             try:
@@ -98,209 +115,6 @@ class ClockSampler:
 
 
 # ----------------------------------------------------------------------------
-# workloads
-# ----------------------------------------------------------------------------
-
-def q8_gemv_inputs(rng, N=12288, K=4096):
-    codes = rng.integers(-127, 128, (N, K), dtype=np.int8)
-    scales = (0.02 / 127 * np.exp(rng.normal(0, 0.25, (N, K // 32)))).astype(np.float16)
-    x = rng.standard_normal((1, K)).astype(np.float32)
-    return codes, scales, x
-
-
-def q8_gemv_bytes(N=12288, K=4096, M=1):
-    return N * K + N * (K // 32) * 2 + M * K * 4 + M * N * 4
-
-
-def run_ours(args, rank, world, local_rank):
-    import torch
-    from chpe_qwen35_hybrid_engine_b200 import SCHEME_I8_GROUP_F16, Context
-
-    dev = torch.device("cuda", local_rank)
-    torch.cuda.set_device(dev)
-    ctx = Context(local_rank)
-    rng = np.random.default_rng(0)
-    N, K, M = 12288, 4096, 1
-    codes, scales, x = q8_gemv_inputs(rng, N, K)
-    algo = q8_gemv_bytes(N, K, M)
-    n_copies = args.copies or max(2, int(np.ceil(3 * L2_BYTES / (N * K))))
-    tens = [ctx.upload_matrix(8, SCHEME_I8_GROUP_F16, codes, scales, rows=N, cols=K, group=32)
-            for _ in range(n_copies)]
-    xd = torch.from_numpy(x).to(dev)
-    yd = torch.empty((M, N), dtype=torch.float32, device=dev)
-    st = torch.cuda.current_stream(dev)
-
-    def step(i):
-        ctx.gemv(tens[i % n_copies], xd, out=yd, stream=st)
-
-    for i in range(args.warmup):
-        step(i)
-    torch.cuda.synchronize()
-    dist_barrier(world)
-
-    clk = ClockSampler(local_rank).__enter__()
-    time.sleep(0.1)
-    # device-timed region: the K steps run as one CUDA graph (a decode step is
-    # replayed as a graph); bracketed by barrier + synchronize
-    graph = torch.cuda.CUDAGraph()
-    gst = torch.cuda.Stream(dev)
-    gst.wait_stream(st)
-    with torch.cuda.graph(graph, stream=gst):
-        for i in range(args.steps):
-            ctx.gemv(tens[i % n_copies], xd, out=yd, stream=gst)
-    graph.replay()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    dist_barrier(world)
-    torch.cuda.synchronize()
-    rst = torch.cuda.current_stream(dev)  # CUDAGraph.replay() launches on the current stream
-    e0.record(rst)
-    graph.replay()
-    e1.record(rst)
-    torch.cuda.synchronize()
-    dist_barrier(world)
-    ms_total = e0.elapsed_time(e1)
-    ms_total = dist_max(ms_total, world)
-    ms_step = ms_total / args.steps
-    del graph
-
-    # dominant-kernel duration: events bracketing only the GEMV kernel launch
-    kern_ms = kernel_times_q8(ctx, tens, xd, yd, st, args.steps, n_copies)
-
-    # end to end through the public API with pinned host buffers
-    xh = torch.from_numpy(x).pin_memory()
-    yh = torch.empty((M, N), dtype=torch.float32).pin_memory()
-    xd2 = torch.empty_like(xd)
-    for i in range(args.warmup):
-        xd2.copy_(xh, non_blocking=True)
-        ctx.gemv(tens[i % n_copies], xd2, out=yd, stream=st)
-        yh.copy_(yd, non_blocking=True)
-    torch.cuda.synchronize()
-    dist_barrier(world)
-    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e2.record(st)
-    for i in range(args.steps):
-        xd2.copy_(xh, non_blocking=True)
-        ctx.gemv(tens[i % n_copies], xd2, out=yd, stream=st)
-        yh.copy_(yd, non_blocking=True)
-    e3.record(st)
-    torch.cuda.synchronize()
-    e2e_ms = dist_max(e2.elapsed_time(e3), world) / args.steps
-    clk.__exit__()
-
-    peaks = measured_peaks()
-    kern_avg = statistics.mean(kern_ms)
-    achieved = algo / (kern_avg * 1e-3) / 1e9
-    value = world * algo / (ms_step * 1e-3) / 1e9
-    line = {
-        "metric": "quantized GEMV HBM GB/s (Q8 int8 g32 fp16-scale, config 0)",
-        "value": round(value, 2),
-        "unit": "GB/s",
-        "n_gpus": world,
-        "steps": args.steps,
-        "warmup": args.warmup,
-        "ms_per_step": round(ms_step, 6),
-        "higher_is_better": True,
-        "scaling": "weak",
-        "vs_baseline": None,
-        "dtype": "int8 codes x fp32 activations (fp16 tensor-core operands, fp32 accumulate)",
-        "data": "synthetic (seeded: int8 U[-127,127], fp16 scales 0.02/127*exp(N(0,0.25)), x N(0,1))",
-        "config": {"workload": "q8_gemv", "N": N, "K": K, "M": M, "group": 32,
-                   "l2": f"weights rotate over {n_copies} copies ({n_copies * N * K / 2**20:.0f} MiB > 2x L2)",
-                   "parallelism": "replicas" if world > 1 else "single"},
-        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                     "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": None,
-                     "peak_source": peaks["source"], "kernel": "gemv_kernel", "kernel_us": round(kern_avg * 1e3, 3),
-                     "algorithmic_bytes": algo},
-        "e2e": {"value": round(world * algo / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
-                "h2d_bytes_per_step": int(M * K * 4), "d2h_bytes_per_step": int(M * N * 4)},
-        "gpu_launches": 2 * args.steps,
-        "clocks": clk.summary(),
-    }
-    if rank == 0 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline_q8(codes, scales, x, algo)
-    ctx.close()
-    return line
-
-
-def kernel_times_q8(ctx, tens, xd, yd, st, steps, n_copies):
-    """Duration of the GEMV kernel alone: the activation fragments are prepared
-    once (chpe_xfrag_*), then `steps` GEMV launches run as one CUDA graph on a
-    stream of their own, timed with CUDA events on that stream."""
-    import torch
-    from chpe_qwen35_hybrid_engine_b200 import X_F32
-    gst = torch.cuda.Stream()
-    gst.wait_stream(st)
-    xf = ctx.xfrag(tens[0], xd.shape[0], X_F32)
-    ctx.xfrag_fill(xf, xd, stream=gst)
-    for i in range(3):
-        ctx.gemv_xfrag(tens[i % n_copies], xf, yd, stream=gst)
-    torch.cuda.synchronize()
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph, stream=gst):
-        for i in range(steps):
-            ctx.gemv_xfrag(tens[i % n_copies], xf, yd, stream=gst)
-    graph.replay()
-    torch.cuda.synchronize()
-    times = []
-    rst = torch.cuda.current_stream()  # CUDAGraph.replay() launches on the current stream
-    for _ in range(3):
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record(rst)
-        graph.replay()
-        b.record(rst)
-        torch.cuda.synchronize()
-        times.append(a.elapsed_time(b) / steps)
-    del graph
-    xf.free()
-    return times
-
-
-def cpu_baseline_q8(codes, scales, x, algo, budget_s=10.0):
-    from oracle import oracle as O
-    threads = os.cpu_count() or 1
-    t0 = time.perf_counter()
-    n = 0
-    while True:
-        O.gemv_grouped(codes, scales, None, 32, x, num_workers=threads)
-        n += 1
-        if time.perf_counter() - t0 > budget_s:
-            break
-    dt = (time.perf_counter() - t0) / n
-    return {"value": round(algo / dt / 1e9, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-            "sample": f"{n} full config-0 GEMVs (12288x4096) by the C oracle, fp64 accumulation, {threads} threads"}
-
-
-def run_reference(args, rank, world):
-    """CPU reference arm: the oracle port of the reference path on the host cores."""
-    if rank != 0:
-        return None
-    rng = np.random.default_rng(0)
-    codes, scales, x = q8_gemv_inputs(rng)
-    algo = q8_gemv_bytes()
-    from oracle import oracle as O
-    threads = os.cpu_count() or 1
-    for _ in range(args.warmup):
-        O.gemv_grouped(codes, scales, None, 32, x, num_workers=threads)
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        O.gemv_grouped(codes, scales, None, 32, x, num_workers=threads)
-    dt = (time.perf_counter() - t0) / args.steps
-    v = round(algo / dt / 1e9, 3)
-    return {
-        "impl": "reference",
-        "metric": "quantized GEMV HBM GB/s (Q8 int8 g32 fp16-scale, config 0)",
-        "value": v, "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(dt * 1e3, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "int8 codes x fp32 activations (fp64 accumulate)", "data": "synthetic (seeded)",
-        "config": {"workload": "q8_gemv", "N": 12288, "K": 4096, "M": 1, "group": 32},
-        "cpu_baseline": {"value": v, "unit": "GB/s", "cores": threads, "kind": "port",
-                         "sample": "full config-0 GEMV per step (C restatement; the Zig reference needs a Zig 0.17-dev toolchain absent here)"},
-        "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-    }
-
-
-# ----------------------------------------------------------------------------
 # distributed plumbing
 # ----------------------------------------------------------------------------
 
@@ -320,15 +134,451 @@ def dist_max(v, world):
     return float(t.item())
 
 
+def timed_replays(replay, steps, world, dev):
+    """`steps` calls of replay(), bracketed by barrier + synchronize on both
+    sides; device time (ms) from CUDA events on the current stream (where
+    CUDAGraph.replay() launches), max over ranks."""
+    import torch
+    rst = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(dev)
+    dist_barrier(world)
+    torch.cuda.synchronize(dev)
+    e0.record(rst)
+    for _ in range(steps):
+        replay()
+    e1.record(rst)
+    torch.cuda.synchronize(dev)
+    dist_barrier(world)
+    return dist_max(e0.elapsed_time(e1), world)
+
+
+# ----------------------------------------------------------------------------
+# decode workloads
+# ----------------------------------------------------------------------------
+
+def gemv_step_profile(ctx, eng, M, reps, dev):
+    """Every GEMV of one step (as the engine issues them at this row count),
+    with activation fragments prepared beforehand, captured as one graph and
+    replayed `reps` times.  Returns (GEMV ms per step, algorithmic bytes per
+    step, GEMV launches per step)."""
+    import torch
+    from chpe_qwen35_hybrid_engine_b200 import X_F32
+    singles, fused = [], []
+    for lw in eng.layers:
+        p = lw.proj
+        singles += [p[n] for n in ("q", "k", "v", "o", "qkv", "z", "out") if n in p]
+        if M == 1:
+            fused.append((p["gate"], p["up"]))
+        else:
+            singles += [p["gate"], p["up"]]
+        singles.append(p["down"])
+    singles.append(eng.head)
+    xfs = {}
+
+    def xf_for(t):
+        key = (t.cols, t.bits)
+        if key not in xfs:
+            xf = ctx.xfrag(t, M, X_F32)
+            ctx.xfrag_fill(xf, torch.randn(M, t.cols, device=dev))
+            xfs[key] = xf
+        return xfs[key]
+
+    rows = max([t.rows for t in singles] + [g.rows for g, _ in fused])
+    y = torch.empty(M, rows, device=dev)
+    st = torch.cuda.Stream(dev)
+    st.wait_stream(torch.cuda.current_stream(dev))
+
+    def issue():
+        for t in singles:
+            ctx.gemv_xfrag(t, xf_for(t), y, stream=st)
+        for g, u in fused:
+            ctx.gemv_gateup_swiglu_xfrag(g, u, xf_for(g), y, stream=st)
+
+    with torch.cuda.stream(st):
+        issue()
+    torch.cuda.synchronize(dev)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=st):
+        issue()
+    for _ in range(3):
+        graph.replay()
+    ms = timed_replays(graph.replay, reps, 1, dev) / reps
+    del graph
+    for xf in xfs.values():
+        xf.free()
+    nbytes = sum(t.device_bytes + M * t.cols * 4 + M * t.rows * 4 for t in singles)
+    nbytes += sum(g.device_bytes + u.device_bytes + M * g.cols * 4 + M * g.rows * 4 for g, u in fused)
+    return ms, nbytes, len(singles) + len(fused)
+
+
+def decode_line(eng, stepper, M, args, world, dev, label, profile=True):
+    """Graph-replayed greedy decode at M rows; returns a dict of figures."""
+    import torch
+    from chpe_qwen35_hybrid_engine_b200 import kernel_launches
+    b = eng.buf
+    rng = np.random.default_rng(0)
+    context = rng.integers(0, eng.geom.vocab, 1024).astype(np.int32)  # seeded uniform token ids
+    first = np.array([(int(context[-1]) + 7 * i) % eng.geom.vocab for i in range(M)], np.int32)
+    b["tokens"][:M].copy_(torch.from_numpy(first).to(dev))
+    n0 = kernel_launches()
+    stepper.step(M)
+    torch.cuda.synchronize(dev)
+    launches_per_step = kernel_launches() - n0
+    b["tokens"][:M].copy_(torch.from_numpy(first).to(dev))
+    graph = stepper.capture(M)
+    st = torch.cuda.Stream(dev)
+    st.wait_stream(torch.cuda.current_stream(dev))
+    feed = torch.cuda.CUDAGraph()  # next step's tokens = this step's argmax, on the device
+    with torch.cuda.graph(feed, stream=st):
+        b["tokens"][:M].copy_(b["argmax"][:M])
+
+    def replay():
+        graph.replay()
+        feed.replay()
+
+    for _ in range(args.warmup):
+        replay()
+    ms_step = timed_replays(replay, args.steps, world, dev) / args.steps
+    # end to end: the step's token comes from pinned host memory and its argmax goes back
+    tok_h = torch.from_numpy(first.copy()).pin_memory()
+    out_h = torch.zeros(M, dtype=torch.int32).pin_memory()
+    rst = torch.cuda.current_stream(dev)
+
+    def e2e_step():
+        b["tokens"][:M].copy_(tok_h, non_blocking=True)
+        graph.replay()
+        out_h.copy_(b["argmax"][:M], non_blocking=True)
+        rst.synchronize()
+        tok_h.copy_(out_h)
+
+    for _ in range(args.warmup):
+        e2e_step()
+    e2e_ms = timed_replays(e2e_step, args.steps, world, dev) / args.steps
+    del feed
+    stepper.graphs.clear()
+    del graph
+    out = {"label": label, "rows": M, "tok_s": round(M / (ms_step * 1e-3), 2),
+           "ms_per_step": round(ms_step, 4), "e2e_tok_s": round(M / (e2e_ms * 1e-3), 2),
+           "e2e_ms_per_step": round(e2e_ms, 4), "kernel_launches_per_step": int(launches_per_step),
+           "weight_bytes": int(eng.n_weight_bytes())}
+    if profile:
+        gms, gbytes, glaunch = gemv_step_profile(eng.ctx, eng, M, max(5, min(args.steps, 20)), dev)
+        gms = dist_max(gms, world)
+        out.update({"gemv_ms_per_step": round(gms, 4), "gemv_bytes_per_step": int(gbytes),
+                    "gemv_launches_per_step": glaunch, "gemv_gbs": round(gbytes / (gms * 1e-3) / 1e9, 1)})
+    return out
+
+
+def run_decode(args, rank, world, local_rank, which):
+    import torch
+    from chpe_qwen35_hybrid_engine_b200 import Context
+    from chpe_qwen35_hybrid_engine_b200.engine import QWEN25_72B, QWEN35_9B, build_random
+    from chpe_qwen35_hybrid_engine_b200.tp import TensorParallelEngine
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    peaks = measured_peaks()
+    clk = ClockSampler(local_rank)
+    extra = {}
+    ctx = Context(local_rank)
+    if which == "decode_72b":
+        tp = TensorParallelEngine(ctx, QWEN25_72B, "q4g64", rank, world, seed=0, max_rows=8, random_codes=True)
+        clk.start()
+        main = decode_line(tp.eng, tp, 1, args, world, dev, f"72b_tp{world}_b1")
+        clk.stop()
+        extra["decode_72b_b8"] = decode_line(tp.eng, tp, 8, args, world, dev, f"72b_tp{world}_b8")
+        tp.graphs.clear()
+        del tp
+        config = {"workload": "decode_72b",
+                  "model": "Qwen2.5-72B-shaped: 80 GQA layers, hidden 8192, FFN 29568 SwiGLU, 64/8 heads of 128, "
+                           "vocab 152064",
+                  "weights": "4-bit codes, fp16 scale + zero per 64 columns (seeded random codes and scales)",
+                  "tensor_parallel": world, "global_batch": 1, "context": "1024 seeded uniform token ids",
+                  "parallelism": f"tp{world}", "l2": "40 GB / N of weights per step >> 126 MB L2"}
+        scaling, units = "strong", 1
+    else:
+        eng, _ = build_random(ctx, QWEN35_9B, "q8g32", seed=rank, max_rows=8)
+        clk.start()
+        main = decode_line(eng, eng, 1, args, world, dev, "9b_b1")
+        clk.stop()
+        del eng
+        config = {"workload": "decode_9b",
+                  "model": "Qwen3.5-9B-shaped hybrid: 24 Gated DeltaNet + 8 GQA layers, hidden 4096, FFN 12288, "
+                           "vocab 151936",
+                  "weights": "8-bit codes, fp16 scale per 32 columns (random-init N(0,0.02), quantized on device)",
+                  "global_batch": world, "parallelism": f"replicas{world}",
+                  "l2": "7 GB of weights per step >> 126 MB L2"}
+        scaling, units = "weak", world
+    ctx.close()
+    torch.cuda.empty_cache()
+    if which == "decode_72b" and world == 1:
+        ctx9 = Context(local_rank)
+        eng9, _ = build_random(ctx9, QWEN35_9B, "q8g32", seed=0, max_rows=8)
+        for M in (1, 4, 8):
+            extra[f"decode_9b_b{M}"] = decode_line(eng9, eng9, M, args, 1, dev, f"9b_b{M}")
+        del eng9
+        ctx9.close()
+    achieved = main["gemv_gbs"]
+    n_launch = main["kernel_launches_per_step"] * args.steps
+    line = {
+        "metric": DECODE_METRIC, "value": round(main["tok_s"] * units, 2), "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": main["ms_per_step"], "higher_is_better": True,
+        "scaling": scaling, "vs_baseline": None,
+        "dtype": "int4/int8 codes x fp32 activations (fp16 tensor-core operands, fp32 accumulate)",
+        "data": "synthetic (seeded random-init weights, seeded uniform token ids)",
+        "config": config,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": None,
+                     "peak_source": peaks["source"],
+                     "kernel": "gemv_kernel: all GEMVs of one step on one GPU, bytes / GEMV time",
+                     "algorithmic_bytes_per_step": main["gemv_bytes_per_step"],
+                     "gemv_ms_per_step": main["gemv_ms_per_step"]},
+        "e2e": {"value": round(main["e2e_tok_s"] * units, 2), "unit": "tokens/s", "h2d_bytes_per_step": 4,
+                "d2h_bytes_per_step": 4},
+        "gpu_launches": int(n_launch),
+        "clocks": clk.summary(),
+        "detail": main,
+    }
+    line.update(extra)
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        step_s, threads, sample = cpu_decode_sample(which, budget_s=10.0)
+        line["cpu_baseline"] = {"value": round(1.0 / step_s, 4), "unit": "tokens/s", "cores": threads,
+                                "kind": "port", "sample": sample}
+    return line
+
+
+# ----------------------------------------------------------------------------
+# single GEMV workload
+# ----------------------------------------------------------------------------
+
+def q8_gemv_inputs(rng, N=12288, K=4096):
+    codes = rng.integers(-127, 128, (N, K), dtype=np.int8)
+    scales = (0.02 / 127 * np.exp(rng.normal(0, 0.25, (N, K // 32)))).astype(np.float16)
+    x = rng.standard_normal((1, K)).astype(np.float32)
+    return codes, scales, x
+
+
+def q8_gemv_bytes(N=12288, K=4096, M=1):
+    return N * K + N * (K // 32) * 2 + M * K * 4 + M * N * 4
+
+
+def run_q8_gemv(args, rank, world, local_rank):
+    import torch
+    from chpe_qwen35_hybrid_engine_b200 import SCHEME_I8_GROUP_F16, X_F32, Context
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    ctx = Context(local_rank)
+    rng = np.random.default_rng(0)
+    N, K, M = 12288, 4096, 1
+    codes, scales, x = q8_gemv_inputs(rng, N, K)
+    algo = q8_gemv_bytes(N, K, M)
+    n_copies = args.copies or max(2, int(np.ceil(3 * L2_BYTES / (N * K))))
+    tens = [ctx.upload_matrix(8, SCHEME_I8_GROUP_F16, codes, scales, rows=N, cols=K, group=32)
+            for _ in range(n_copies)]
+    xd = torch.from_numpy(x).to(dev)
+    yd = torch.empty((M, N), dtype=torch.float32, device=dev)
+    st = torch.cuda.Stream(dev)
+    st.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(st):
+        for i in range(args.warmup):
+            ctx.gemv(tens[i % n_copies], xd, out=yd, stream=st)
+    torch.cuda.synchronize(dev)
+    clk = ClockSampler(local_rank).start()
+    # a step = activation prep + GEMV through the public call; the K steps run as one graph
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=st):
+        for i in range(args.steps):
+            ctx.gemv(tens[i % n_copies], xd, out=yd, stream=st)
+    graph.replay()
+    ms_step = timed_replays(graph.replay, 1, world, dev) / args.steps
+    del graph
+    # the GEMV kernel alone (fragments prepared once)
+    xf = ctx.xfrag(tens[0], M, X_F32)
+    ctx.xfrag_fill(xf, xd, stream=st)
+    kgraph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(kgraph, stream=st):
+        for i in range(args.steps):
+            ctx.gemv_xfrag(tens[i % n_copies], xf, yd, stream=st)
+    kgraph.replay()
+    kern_ms = timed_replays(kgraph.replay, 3, 1, dev) / (3 * args.steps)
+    del kgraph
+    xf.free()
+    # end to end through the public call, host buffers in pinned memory
+    xh = torch.from_numpy(x).pin_memory()
+    yh = torch.empty((M, N), dtype=torch.float32).pin_memory()
+    xd2 = torch.empty_like(xd)
+    rst = torch.cuda.current_stream(dev)
+    it = [0]
+
+    def e2e_step():
+        xd2.copy_(xh, non_blocking=True)
+        ctx.gemv(tens[it[0] % n_copies], xd2, out=yd, stream=rst)
+        yh.copy_(yd, non_blocking=True)
+        it[0] += 1
+
+    for _ in range(args.warmup):
+        e2e_step()
+    e2e_ms = timed_replays(e2e_step, args.steps, world, dev) / args.steps
+    clk.stop()
+    peaks = measured_peaks()
+    achieved = algo / (kern_ms * 1e-3) / 1e9
+    line = {
+        "metric": GEMV_METRIC, "value": round(world * algo / (ms_step * 1e-3) / 1e9, 2), "unit": "GB/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 6),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "int8 codes x fp32 activations (fp16 tensor-core operands, fp32 accumulate)",
+        "data": "synthetic (seeded: int8 U[-127,127], fp16 scales 0.02/127*exp(N(0,0.25)), x N(0,1))",
+        "config": {"workload": "q8_gemv", "N": N, "K": K, "M": M, "group": 32,
+                   "l2": f"weights rotate over {n_copies} copies ({n_copies * N * K / 2**20:.0f} MiB > 2x L2)",
+                   "parallelism": f"replicas{world}"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": None,
+                     "peak_source": peaks["source"], "kernel": "gemv_kernel", "kernel_us": round(kern_ms * 1e3, 3),
+                     "algorithmic_bytes": algo},
+        "e2e": {"value": round(world * algo / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+                "h2d_bytes_per_step": int(M * K * 4), "d2h_bytes_per_step": int(M * N * 4)},
+        "gpu_launches": 2 * args.steps,
+        "clocks": clk.summary(),
+    }
+    if rank == 0 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline_q8(codes, scales, x, algo)
+    ctx.close()
+    return line
+
+
+# ----------------------------------------------------------------------------
+# CPU baselines: the oracle's C restatement of the reference path, host cores
+# ----------------------------------------------------------------------------
+
+def cpu_baseline_q8(codes, scales, x, algo, budget_s=10.0):
+    from oracle import oracle as O
+    threads = os.cpu_count() or 1
+    t0 = time.perf_counter()
+    n = 0
+    while True:
+        O.gemv_grouped(codes, scales, None, 32, x, num_workers=threads)
+        n += 1
+        if time.perf_counter() - t0 > budget_s:
+            break
+    dt = (time.perf_counter() - t0) / n
+    return {"value": round(algo / dt / 1e9, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"{n} full 12288x4096 GEMVs by the C oracle (fp64 accumulation), {threads} threads"}
+
+
+class CpuDecodeSampler:
+    """Bounded sample of one decode step on the host cores: the GEMVs of one
+    decoder layer of each kind plus 4096 LM-head rows, run by the oracle's
+    grouped GEMV at full (unsharded) size, scaled to the layer count and
+    vocabulary.  The GEMVs are > 95 % of a CPU decode step's time."""
+
+    HEAD_ROWS = 4096
+
+    def __init__(self, which):
+        from chpe_qwen35_hybrid_engine_b200.engine import QWEN25_72B, QWEN35_9B
+        g = QWEN25_72B if which == "decode_72b" else QWEN35_9B
+        self.g, self.q4 = g, which == "decode_72b"
+        self.group = 64 if self.q4 else 32
+        self.threads = os.cpu_count() or 1
+        H, F = g.hidden, g.ffn
+        kinds = {"attn": [(g.q_dim, H), (g.kv_dim, H), (g.kv_dim, H), (H, H)]}
+        if g.attn_every > 1:
+            kinds["ssm"] = [(g.ssm_qkv, H), (g.ssm_z, H), (H, g.ssm_z)]
+        n_attn = sum(1 for l in range(g.n_layers) if g.is_attn(l))
+        self.count = {"attn": n_attn, "ssm": g.n_layers - n_attn, "mlp": g.n_layers, "head": g.vocab / self.HEAD_ROWS}
+        kinds["mlp"] = [(F, H), (F, H), (H, F)]
+        kinds["head"] = [(self.HEAD_ROWS, H)]
+        rng = np.random.default_rng(0)
+        self.mats = {}
+        for kind, shapes in kinds.items():
+            lst = []
+            for n, k in shapes:
+                if self.q4:
+                    c = rng.integers(0, 16, (n, k), dtype=np.uint8)
+                    s = (0.0067 * np.exp(rng.normal(0, 0.25, (n, k // 64)))).astype(np.float16)
+                    z = rng.integers(6, 10, (n, k // 64)).astype(np.float16)
+                else:
+                    c = rng.integers(-127, 128, (n, k), dtype=np.int8)
+                    s = (0.02 / 127 * np.exp(rng.normal(0, 0.25, (n, k // 32)))).astype(np.float16)
+                    z = None
+                lst.append((c, s, z, rng.standard_normal((1, k)).astype(np.float32)))
+            self.mats[kind] = lst
+
+    def step_seconds(self):
+        """One sample: estimated seconds of one full decode step."""
+        from oracle import oracle as O
+        total = 0.0
+        for kind, lst in self.mats.items():
+            t0 = time.perf_counter()
+            for c, s, z, x in lst:
+                O.gemv_grouped(c, s, z, self.group, x, num_workers=self.threads)
+            total += (time.perf_counter() - t0) * self.count[kind]
+        return total
+
+    def describe(self, n):
+        return (f"{n} samples of one decode step: GEMVs of one layer of each kind + {self.HEAD_ROWS} LM-head rows at "
+                f"full size, scaled to {self.g.n_layers} layers and vocab {self.g.vocab} (C oracle, fp64 "
+                f"accumulation, {self.threads} threads)")
+
+
+def cpu_decode_sample(which, budget_s=10.0):
+    s = CpuDecodeSampler(which)
+    s.step_seconds()  # warm-up
+    t0 = time.perf_counter()
+    est = []
+    while not est or time.perf_counter() - t0 < budget_s:
+        est.append(s.step_seconds())
+    return statistics.median(est), s.threads, s.describe(len(est))
+
+
+def run_reference(args, rank, world, workload):
+    """Reference arm: the reference path's CPU arithmetic (the oracle's C
+    restatement, all host threads) on rank 0; other ranks do nothing.  The Zig
+    reference itself needs a Zig 0.17-dev toolchain absent from this image."""
+    if rank != 0:
+        return None
+    threads = os.cpu_count() or 1
+    if workload == "q8_gemv":
+        from oracle import oracle as O
+        codes, scales, x = q8_gemv_inputs(np.random.default_rng(0))
+        algo = q8_gemv_bytes()
+        for _ in range(args.warmup):
+            O.gemv_grouped(codes, scales, None, 32, x, num_workers=threads)
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            O.gemv_grouped(codes, scales, None, 32, x, num_workers=threads)
+        dt = (time.perf_counter() - t0) / args.steps
+        value, unit, metric, ms = round(algo / dt / 1e9, 3), "GB/s", GEMV_METRIC, dt * 1e3
+        sample = "one full 12288x4096 GEMV per step (C oracle, fp64 accumulation)"
+        cfg = {"workload": "q8_gemv", "N": 12288, "K": 4096, "M": 1, "group": 32}
+        scaling = "weak"
+    else:
+        s = CpuDecodeSampler(workload)
+        for _ in range(args.warmup):
+            s.step_seconds()
+        est = [s.step_seconds() for _ in range(args.steps)]
+        step = statistics.mean(est)
+        value, unit, metric, ms = round(1.0 / step, 4), "tokens/s", DECODE_METRIC, step * 1e3
+        sample = s.describe(args.steps)
+        cfg = {"workload": workload, "global_batch": 1,
+               "tensor_parallel": world if workload == "decode_72b" else 1}
+        scaling = "strong" if workload == "decode_72b" else "weak"
+    return {"impl": "reference", "metric": metric, "value": value, "unit": unit, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+            "scaling": scaling, "vs_baseline": None, "dtype": "int codes x fp32 activations (fp64 accumulate)",
+            "data": "synthetic (seeded)", "config": cfg,
+            "cpu_baseline": {"value": value, "unit": unit, "cores": threads, "kind": "port", "sample": sample},
+            "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
-    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="q8_gemv")
+    ap.add_argument("--workload", default="decode_72b", choices=["decode_72b", "decode_9b", "q8_gemv"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--copies", type=int, default=0, help="weight copies to rotate (default: > 3x L2)")
+    ap.add_argument("--copies", type=int, default=0, help="q8_gemv: weight copies to rotate (default: > 3x L2)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -337,7 +587,7 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
 
     if args.impl == "reference":
-        line = run_reference(args, rank, world)
+        line = run_reference(args, rank, world, args.workload)
         if line is not None:
             print(json.dumps(line), flush=True)
         return 0
@@ -348,12 +598,17 @@ def main():
         import torch
         import torch.distributed as dist
         torch.cuda.set_device(local_rank)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
-    line = run_ours(args, rank, world, local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
+                                device_id=torch.device("cuda", local_rank))
+    if args.workload == "q8_gemv":
+        line = run_q8_gemv(args, rank, world, local_rank)
+    else:
+        line = run_decode(args, rank, world, local_rank, args.workload)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist
+        dist.barrier()
         dist.destroy_process_group()
     return 0
 

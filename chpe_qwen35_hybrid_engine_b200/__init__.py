@@ -7,6 +7,6 @@ from ._lib import ChpeError, load  # noqa: F401
 from ._lib import (SCHEME_I8_GROUP_F16, SCHEME_I8_TENSOR, SCHEME_ROW_AFFINE_F32,  # noqa: F401
                    SCHEME_U_GROUP_F16_CONST_ZERO, SCHEME_U_GROUP_F16_ZERO, SCHEME_W2_CODEBOOK_GROUP_F16, X_BF16,
                    X_F16, X_F32, X_I8)
-from .ops import Context, Tensor  # noqa: F401
+from .ops import Context, Tensor, kernel_launches  # noqa: F401
 
 __all__ = ["Context", "Tensor", "ChpeError", "load"]

@@ -42,6 +42,7 @@ SIGNATURES = {
     "chpe_destroy": (I, [P]),
     "chpe_last_error_string": (C.c_char_p, [P]),
     "chpe_version": (C.c_char_p, []),
+    "chpe_kernel_launches": (C.c_ulonglong, []),
     "chpe_sync": (I, [P]),
     "chpe_upload_matrix": (I, [P, C.POINTER(chpe_fmt), P, SZ, P, P, P, SZ, SZ, PP]),
     "chpe_upload_cells": (I, [P, P, SZ, SZ, PP]),

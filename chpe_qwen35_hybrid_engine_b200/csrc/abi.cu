@@ -1,6 +1,7 @@
 // abi.cu -- the C ABI (include/chpe_b200.h): contexts, device tensors, the
 // host-pointer operators that mirror the reference's Zig GEMV operators, and
 // the device-pointer GEMV entry points.
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -444,6 +445,14 @@ uint64_t fingerprint(const void *p, size_t n, bool sampled) {
 // ---------------------------------------------------------------------------
 
 extern "C" const char *chpe_version(void) { return "chpe_b200 1.0 sm_100a"; }
+
+namespace {
+std::atomic<unsigned long long> g_launches{0};
+}
+namespace chpe {
+void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+}  // namespace chpe
+extern "C" unsigned long long chpe_kernel_launches(void) { return g_launches.load(std::memory_order_relaxed); }
 
 extern "C" int chpe_init(int device, chpe_ctx **out) {
     if (!out) return CHPE_EINVAL;

@@ -15,6 +15,10 @@ constexpr unsigned long long kWaitTimeoutNs = 1000000000ull;  // 1 s
 
 enum KernelError : int { kErrNone = 0, kErrWaitFull = 1, kErrWaitEmpty = 2, kErrWaitPrologue = 3 };
 
+// Host side: every kernel launch of the library is counted (process-wide,
+// relaxed atomic; defined in abi.cu, read through chpe_kernel_launches).
+void note_launch();
+
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

@@ -579,6 +579,7 @@ cudaError_t launch_gemv_t(const GemvPlan &plan, const GemvParams &p, cudaStream_
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
+    note_launch();
     return cudaLaunchKernelEx(&cfg, kern, p);
 }
 

@@ -154,6 +154,7 @@ extern "C" int chpe_embed_i8_dev(chpe_ctx *ctx, const int8_t *table, float scale
                                  const int *tokens, int M, float *out, void *stream) {
     if (!ctx || !table || !tokens || !out || M < 1 || hidden < 1) return CHPE_EINVAL;
     dim3 grid(grid_for(hidden, 256) < 16 ? grid_for(hidden, 256) : 16, M);
+    note_launch();
     embed_i8_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(table, scale, hidden, vocab, tokens, out,
                                                                           chpe_ctx_error_word(ctx));
     return launched(cudaGetLastError());
@@ -162,6 +163,7 @@ extern "C" int chpe_embed_i8_dev(chpe_ctx *ctx, const int8_t *table, float scale
 extern "C" int chpe_rmsnorm_dev(chpe_ctx *ctx, const float *x, const float *gamma, int M, int n, float eps, float *y,
                                 void *stream) {
     if (!ctx || !x || !gamma || !y || M < 1 || n < 1) return CHPE_EINVAL;
+    note_launch();
     rmsnorm_kernel<<<M, 512, 0, static_cast<cudaStream_t>(stream)>>>(x, gamma, n, eps, y);
     return launched(cudaGetLastError());
 }
@@ -171,6 +173,7 @@ extern "C" int chpe_mix_attn_stub_dev(chpe_ctx *ctx, const float *v, int kv_dim,
     if (!ctx || !v || !out || M < 1 || kv_dim < 1) return CHPE_EINVAL;
     if (head_dim && (group < 1 || ((out_dim / head_dim + group - 1) / group) * head_dim > kv_dim)) return CHPE_EINVAL;
     dim3 grid(grid_for(out_dim, 256) < 16 ? grid_for(out_dim, 256) : 16, M);
+    note_launch();
     mix_attn_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(v, kv_dim, out_dim, head_dim, group, out);
     return launched(cudaGetLastError());
 }
@@ -179,6 +182,7 @@ extern "C" int chpe_mix_ssm_stub_dev(chpe_ctx *ctx, const float *qkv, int qkv_di
                                      int out_dim, int silu_on_qkv, float *out, void *stream) {
     if (!ctx || !qkv || !z || !out || M < 1 || qkv_dim < 1 || out_dim > z_dim) return CHPE_EINVAL;
     dim3 grid(grid_for(out_dim, 256) < 16 ? grid_for(out_dim, 256) : 16, M);
+    note_launch();
     mix_ssm_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(qkv, qkv_dim, z, z_dim, out_dim, silu_on_qkv,
                                                                          out);
     return launched(cudaGetLastError());
@@ -186,6 +190,7 @@ extern "C" int chpe_mix_ssm_stub_dev(chpe_ctx *ctx, const float *qkv, int qkv_di
 
 extern "C" int chpe_silu_mul_dev(chpe_ctx *ctx, const float *g, const float *u, size_t n, float *out, void *stream) {
     if (!ctx || !g || !u || !out) return CHPE_EINVAL;
+    note_launch();
     silu_mul_kernel<<<grid_for(n, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(g, u, n, out);
     return launched(cudaGetLastError());
 }
@@ -193,6 +198,7 @@ extern "C" int chpe_silu_mul_dev(chpe_ctx *ctx, const float *g, const float *u, 
 extern "C" int chpe_argmax_dev(chpe_ctx *ctx, const float *logits, int M, int n, int *idx, float *maxv,
                                void *stream) {
     if (!ctx || !logits || !idx || M < 1 || n < 1) return CHPE_EINVAL;
+    note_launch();
     argmax_kernel<<<M, 1024, 0, static_cast<cudaStream_t>(stream)>>>(logits, n, idx, maxv);
     return launched(cudaGetLastError());
 }

@@ -68,6 +68,7 @@ __global__ void xprep_f16_kernel(const void *__restrict__ x, int dt, int M, int 
 cudaError_t launch_xprep_f16(const void *x, int x_dtype, int M, int K, int Kp, int e_cols, bool xsplit, int bits,
                              void *xf, float *xs, cudaStream_t st) {
     const int nblk = Kp / e_cols;
+    note_launch();
     xprep_f16_kernel<<<nblk, 256, 0, st>>>(x, x_dtype, M, K, e_cols, xsplit ? 1 : 0, bits, static_cast<uint2 *>(xf),
                                            xs);
     return cudaGetLastError();
@@ -99,6 +100,7 @@ __global__ void xprep_s8_kernel(const int8_t *__restrict__ xq, int M, int K, int
 cudaError_t launch_xprep_s8(const int8_t *xq, int M, int K, int Kp, void *xf, cudaStream_t st) {
     const int nsteps = Kp / 32;
     const size_t total = (size_t)nsteps * M * 4;
+    note_launch();
     xprep_s8_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(xq, M, K, nsteps, static_cast<uint2 *>(xf));
     return cudaGetLastError();
 }
@@ -152,6 +154,7 @@ __global__ void act_quant_s8_kernel(const float *__restrict__ x, int M, int K, i
 
 cudaError_t launch_act_quant_s8(const float *x, int M, int K, int Kp, int8_t *q, float *scales, void *xf,
                                 cudaStream_t st) {
+    note_launch();
     act_quant_s8_kernel<<<M, 256, 0, st>>>(x, M, K, Kp / 32, q, scales, static_cast<uint2 *>(xf));
     return cudaGetLastError();
 }
@@ -222,6 +225,7 @@ __global__ void repack_codes_kernel(const uint8_t *__restrict__ src, size_t stri
 cudaError_t launch_repack_codes(const uint8_t *src, size_t row_stride, int src_bits, uint32_t xorv,
                                 const DevMatrix &m, cudaStream_t st) {
     const size_t total = (size_t)m.n_strips * m.n_blocks * kChunksPerBlock * 128;
+    note_launch();
     repack_codes_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(src, row_stride, m.N, m.K, src_bits, m.bits,
                                                                         m.layout, xorv, m.codes, m.n_strips,
                                                                         m.n_blocks, m.block_bytes);
@@ -269,6 +273,7 @@ __global__ void meta_repack_kernel(int kind, const __half *__restrict__ s, const
 cudaError_t launch_meta_repack(const __half *s, const __half *z, const float *fs, const float *fo,
                                float zc_for_f32, const DevMatrix &m, cudaStream_t st) {
     const size_t total = (size_t)m.n_strips * m.n_blocks * m.gpb * 16;
+    note_launch();
     meta_repack_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(
         m.meta_kind, s, z, fs, fo, zc_for_f32, m.N, m.n_groups, m.group, m.span, m.gpb, m.n_strips, m.n_blocks,
         m.block_bytes, m.codes);
@@ -335,6 +340,7 @@ cudaError_t launch_quant_group(const float *w, int N, int K, int group, int bits
                                __half *scales, __half *zeros, cudaStream_t st) {
     const size_t warps = (size_t)N * (K / group);
     const size_t threads = warps * 32;
+    note_launch();
     quant_group_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, st>>>(w, N, K, group, bits, symmetric, codes,
                                                                         scales, zeros);
     return cudaGetLastError();

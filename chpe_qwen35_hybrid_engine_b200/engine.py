@@ -176,6 +176,73 @@ def build_random(ctx: Context, geom: Geometry, scheme: str, seed: int = 0, max_r
     return eng, host
 
 
+def build_random_codes(ctx: Context, geom: Geometry, scheme: str, seed: int = 0, max_rows: int = 8, shard=None):
+    """Random-init model drawn directly in the quantized format (uniform codes,
+    group scales drawn like those of quantized N(0, 0.02) weights), built shard
+    by shard on the device.  Used for the large benchmark models, where drawing
+    and quantizing ~70 G fp32 weights per rank would dominate start-up; the
+    per-step work is the same as for build_random."""
+    import torch
+    dev = torch.device("cuda", ctx.device)
+    rank, world = shard or (0, 1)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(seed * 1000 + rank)
+    eng = HybridEngine(ctx, geom, scheme, max_rows=max_rows)
+    bits, _, group = SCHEMES[scheme]
+    H, F = geom.hidden, geom.ffn
+
+    def mat(rows, cols):
+        if scheme == "w8a8":
+            codes = torch.randint(-127, 128, (rows, cols), dtype=torch.int8, device=dev, generator=gen)
+            return upload_quantized(ctx, codes, torch.tensor([0.02 / 127 * 3], device=dev), None, scheme, rows, cols)
+        codes = torch.randint(0, 256, (rows, cols * bits // 8), dtype=torch.uint8, device=dev, generator=gen)
+        ng = cols // group
+        base = 0.02 * 5.0 / ((1 << bits) - 1)  # range of ~5 sigma over the code range
+        scales = (base * torch.exp(0.25 * torch.randn(rows, ng, device=dev, generator=gen))).half()
+        zeros = None
+        if scheme == "q4g64":
+            zeros = torch.randint(6, 10, (rows, ng), device=dev, generator=gen).half()
+        return upload_quantized(ctx, codes, scales, zeros, scheme, rows, cols)
+
+    def split_rows(total, kind):
+        if world == 1:
+            return total
+        if kind == "ffn":
+            a, b = _row_split(total, world, rank, scheme).start, _row_split(total, world, rank, scheme).stop
+            return b - a
+        return (rank + 1) * total // world - rank * total // world
+
+    def split_cols(total):
+        if world == 1:
+            return total
+        sl = _row_split(total, world, rank, scheme)
+        return sl.stop - sl.start
+
+    gam = lambda: (1.0 + 0.02 * torch.randn(H, device=dev, generator=gen)).float().contiguous()
+    eng.embed = torch.randint(-127, 128, (geom.vocab, H), dtype=torch.int8, device=dev, generator=gen)
+    eng.embed_scale = 0.02 * 3 / 127
+    for l in range(geom.n_layers):
+        lw = LayerWeights(gam(), gam())
+        if geom.is_attn(l):
+            lw.proj["q"] = mat(split_rows(geom.q_dim, "col"), H)
+            lw.proj["k"] = mat(split_rows(geom.kv_dim, "col"), H)
+            lw.proj["v"] = mat(split_rows(geom.kv_dim, "col"), H)
+            lw.proj["o"] = mat(H, split_cols(H))
+        else:
+            lw.proj["qkv"] = mat(split_rows(geom.ssm_qkv, "col"), H)
+            lw.proj["z"] = mat(split_rows(geom.ssm_z, "col"), H)
+            lw.proj["out"] = mat(H, split_cols(geom.ssm_z))
+        fr = split_rows(F, "ffn")
+        lw.proj["gate"] = mat(fr, H)
+        lw.proj["up"] = mat(fr, H)
+        lw.proj["down"] = mat(H, split_cols(F))
+        eng.layers.append(lw)
+    eng.final_gamma = gam()
+    eng.head = mat(split_rows(geom.vocab, "col"), H)
+    torch.cuda.synchronize(dev)
+    return eng
+
+
 def _row_split(cols: int, world: int, rank: int, scheme: str):
     """Columns of a row-split (K-split) projection owned by `rank`: contiguous,
     on group boundaries (64 for 4-bit, 32 for 8-bit) so no group is cut."""

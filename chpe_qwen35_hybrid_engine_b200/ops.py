@@ -25,6 +25,11 @@ from . import _lib as L
 from ._lib import ChpeError
 
 
+def kernel_launches() -> int:
+    """Kernels launched by the library in this process so far (a launch
+    recorded into a CUDA graph counts once, at capture)."""
+    return int(L.load().chpe_kernel_launches())
+
 def _np_ptr(a: np.ndarray):
     assert a.flags["C_CONTIGUOUS"], "array must be C-contiguous"
     return C.c_void_p(a.ctypes.data)

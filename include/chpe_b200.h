@@ -95,6 +95,9 @@ int chpe_destroy(chpe_ctx *ctx);
 const char *chpe_last_error_string(const chpe_ctx *ctx);
 /* Library build/version string (no context needed). */
 const char *chpe_version(void);
+/* Kernels this library has launched in this process so far (all contexts).
+ * A launch recorded into a CUDA graph counts once, at capture. */
+unsigned long long chpe_kernel_launches(void);
 /* Device sync + read-back of the kernels' error flag (bounded waits that
  * expired); returns CHPE_ETIMEOUT if any kernel recorded one. */
 int chpe_sync(chpe_ctx *ctx);
