@@ -15,8 +15,10 @@ dataset and no checkpoint):
                         Qwen3.5-9B-shaped decode (8-bit, fp16 scale per 32) at
                         batch 1 and the batch-4 / batch-8 verify steps.
   decode_9b             the Qwen3.5-9B-shaped decode alone (N > 1: replicas).
-  q8_gemv               y[1,12288] = x[1,4096] . dequant(W)^T, int8 with an fp16
-                        scale per 32 columns; metric: algorithmic HBM GB/s.
+  gemv                  one quantized GEMV y[M,N] = x[M,K] . dequant(W)^T
+                        (--bits 8|4|2 --rows N --cols K --batch M --x f32|bf16);
+                        metric: algorithmic HBM GB/s.  `q8_gemv` is the
+                        12288x4096 int8 GEMV (fp16 scale per 32) at batch 1.
 
 A decode step is one token per row: embedding, every layer, final norm, LM
 head and argmax.  Timed steps replay one CUDA graph per step and feed each
@@ -47,7 +49,6 @@ sys.path.insert(0, ROOT)
 
 L2_BYTES = 126 * 1024 * 1024
 DECODE_METRIC = "decode tokens/s (quantized GEMV path; GEMV HBM GB/s vs peak in roofline)"
-GEMV_METRIC = "quantized GEMV HBM GB/s (Q8 int8 g32 fp16-scale, 12288x4096, batch 1)"
 
 
 def measured_peaks():
@@ -351,31 +352,82 @@ def run_decode(args, rank, world, local_rank, which):
 # single GEMV workload
 # ----------------------------------------------------------------------------
 
-def q8_gemv_inputs(rng, N=12288, K=4096):
-    codes = rng.integers(-127, 128, (N, K), dtype=np.int8)
-    scales = (0.02 / 127 * np.exp(rng.normal(0, 0.25, (N, K // 32)))).astype(np.float16)
-    x = rng.standard_normal((1, K)).astype(np.float32)
-    return codes, scales, x
+class GemvCase:
+    """One quantized GEMV y[M, N] = x[M, K] . dequant(W)^T, seeded.
+      8-bit : int8 codes U[-127, 127], fp16 scale per 32 columns,
+              scales 0.02/127 * exp(N(0, 0.25))
+      4/2-bit: unsigned codes packed little-endian (uniform), fp16 scale and
+              zero per 64 columns, scales like those of quantized N(0, 0.02)
+              weights, zeros in the middle of the code range
+    x is N(0, 1) in fp32 or bf16."""
+
+    def __init__(self, bits=8, N=12288, K=4096, M=1, xdtype="f32", seed=0):
+        from chpe_qwen35_hybrid_engine_b200 import SCHEME_I8_GROUP_F16, SCHEME_U_GROUP_F16_ZERO
+        self.bits, self.N, self.K, self.M, self.xdtype = bits, N, K, M, xdtype
+        rng = np.random.default_rng(seed)
+        if bits == 8:
+            self.group, self.scheme = 32, SCHEME_I8_GROUP_F16
+            self.codes = rng.integers(-127, 128, (N, K), dtype=np.int8)
+            self.scales = (0.02 / 127 * np.exp(rng.normal(0, 0.25, (N, K // 32)))).astype(np.float16)
+            self.zeros = None
+        else:
+            self.group, self.scheme = 64, SCHEME_U_GROUP_F16_ZERO
+            self.codes = rng.integers(0, 256, (N, K * bits // 8), dtype=np.uint8)  # packed, uniform codes
+            base = 0.02 * 5.0 / ((1 << bits) - 1)
+            self.scales = (base * np.exp(rng.normal(0, 0.25, (N, K // 64)))).astype(np.float16)
+            mid = (1 << bits) // 2
+            self.zeros = rng.integers(mid - 2 if bits == 4 else 1, mid + 2 if bits == 4 else 3,
+                                      (N, K // 64)).astype(np.float16)
+        self.x = rng.standard_normal((M, K)).astype(np.float32)
+        self.meta_bytes = self.scales.nbytes + (self.zeros.nbytes if self.zeros is not None else 0)
+
+    @property
+    def weight_bytes(self):
+        return self.codes.nbytes + self.meta_bytes
+
+    def algo_bytes(self):
+        xb = 4 if self.xdtype == "f32" else 2
+        return self.weight_bytes + self.M * self.K * xb + self.M * self.N * 4
+
+    def unpacked(self):
+        """Codes one per byte (for the oracle)."""
+        if self.bits == 8:
+            return self.codes
+        per = 8 // self.bits
+        out = np.empty((self.N, self.K), np.uint8)
+        for j in range(per):
+            out[:, j::per] = (self.codes >> (self.bits * j)) & ((1 << self.bits) - 1)
+        return out
+
+    def describe(self):
+        return {"workload": "gemv", "bits": self.bits, "N": self.N, "K": self.K, "M": self.M, "group": self.group,
+                "x": self.xdtype}
 
 
-def q8_gemv_bytes(N=12288, K=4096, M=1):
-    return N * K + N * (K // 32) * 2 + M * K * 4 + M * N * 4
+def gemv_metric(c):
+    return (f"quantized GEMV HBM GB/s ({c.bits}-bit, group {c.group}, {c.N}x{c.K}, batch {c.M}, "
+            f"{c.xdtype} activations)")
 
 
-def run_q8_gemv(args, rank, world, local_rank):
+def run_gemv(args, rank, world, local_rank):
     import torch
-    from chpe_qwen35_hybrid_engine_b200 import SCHEME_I8_GROUP_F16, X_F32, Context
+    from chpe_qwen35_hybrid_engine_b200 import X_BF16, X_F32, Context
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
     ctx = Context(local_rank)
-    rng = np.random.default_rng(0)
-    N, K, M = 12288, 4096, 1
-    codes, scales, x = q8_gemv_inputs(rng, N, K)
-    algo = q8_gemv_bytes(N, K, M)
-    n_copies = args.copies or max(2, int(np.ceil(3 * L2_BYTES / (N * K))))
-    tens = [ctx.upload_matrix(8, SCHEME_I8_GROUP_F16, codes, scales, rows=N, cols=K, group=32)
-            for _ in range(n_copies)]
-    xd = torch.from_numpy(x).to(dev)
+    c = GemvCase(args.bits, args.rows, args.cols, args.batch, args.x)
+    N, K, M = c.N, c.K, c.M
+    algo = c.algo_bytes()
+    n_copies = args.copies or max(2, int(np.ceil(3 * L2_BYTES / c.weight_bytes)))
+    cd = torch.from_numpy(c.codes).to(dev)
+    sd = torch.from_numpy(c.scales).to(dev)
+    zd = torch.from_numpy(c.zeros).to(dev) if c.zeros is not None else None
+    tens = [ctx.upload_matrix(c.bits, c.scheme, cd, sd, zd, rows=N, cols=K, group=c.group) for _ in range(n_copies)]
+    del cd, sd, zd
+    xdt = X_F32 if c.xdtype == "f32" else X_BF16
+    xd = torch.from_numpy(c.x).to(dev)
+    if c.xdtype == "bf16":
+        xd = xd.to(torch.bfloat16)
     yd = torch.empty((M, N), dtype=torch.float32, device=dev)
     st = torch.cuda.Stream(dev)
     st.wait_stream(torch.cuda.current_stream(dev))
@@ -393,7 +445,7 @@ def run_q8_gemv(args, rank, world, local_rank):
     ms_step = timed_replays(graph.replay, 1, world, dev) / args.steps
     del graph
     # the GEMV kernel alone (fragments prepared once)
-    xf = ctx.xfrag(tens[0], M, X_F32)
+    xf = ctx.xfrag(tens[0], M, xdt)
     ctx.xfrag_fill(xf, xd, stream=st)
     kgraph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(kgraph, stream=st):
@@ -404,7 +456,7 @@ def run_q8_gemv(args, rank, world, local_rank):
     del kgraph
     xf.free()
     # end to end through the public call, host buffers in pinned memory
-    xh = torch.from_numpy(x).pin_memory()
+    xh = xd.cpu().pin_memory()
     yh = torch.empty((M, N), dtype=torch.float32).pin_memory()
     xd2 = torch.empty_like(xd)
     rst = torch.cuda.current_stream(dev)
@@ -422,26 +474,27 @@ def run_q8_gemv(args, rank, world, local_rank):
     clk.stop()
     peaks = measured_peaks()
     achieved = algo / (kern_ms * 1e-3) / 1e9
+    cfg = c.describe()
+    cfg.update({"l2": f"weights rotate over {n_copies} copies "
+                      f"({n_copies * c.weight_bytes / 2**20:.0f} MiB > 2x L2)", "parallelism": f"replicas{world}"})
     line = {
-        "metric": GEMV_METRIC, "value": round(world * algo / (ms_step * 1e-3) / 1e9, 2), "unit": "GB/s",
+        "metric": gemv_metric(c), "value": round(world * algo / (ms_step * 1e-3) / 1e9, 2), "unit": "GB/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 6),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "int8 codes x fp32 activations (fp16 tensor-core operands, fp32 accumulate)",
-        "data": "synthetic (seeded: int8 U[-127,127], fp16 scales 0.02/127*exp(N(0,0.25)), x N(0,1))",
-        "config": {"workload": "q8_gemv", "N": N, "K": K, "M": M, "group": 32,
-                   "l2": f"weights rotate over {n_copies} copies ({n_copies * N * K / 2**20:.0f} MiB > 2x L2)",
-                   "parallelism": f"replicas{world}"},
+        "dtype": f"int{c.bits} codes x {c.xdtype} activations (fp16 tensor-core operands, fp32 accumulate)",
+        "data": "synthetic (seeded uniform codes, lognormal fp16 group scales, x N(0,1))",
+        "config": cfg,
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": None,
                      "peak_source": peaks["source"], "kernel": "gemv_kernel", "kernel_us": round(kern_ms * 1e3, 3),
                      "algorithmic_bytes": algo},
         "e2e": {"value": round(world * algo / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
-                "h2d_bytes_per_step": int(M * K * 4), "d2h_bytes_per_step": int(M * N * 4)},
+                "h2d_bytes_per_step": int(xd.numel() * xd.element_size()), "d2h_bytes_per_step": int(M * N * 4)},
         "gpu_launches": 2 * args.steps,
         "clocks": clk.summary(),
     }
     if rank == 0 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline_q8(codes, scales, x, algo)
+        line["cpu_baseline"] = cpu_baseline_gemv(c)
     ctx.close()
     return line
 
@@ -450,19 +503,24 @@ def run_q8_gemv(args, rank, world, local_rank):
 # CPU baselines: the oracle's C restatement of the reference path, host cores
 # ----------------------------------------------------------------------------
 
-def cpu_baseline_q8(codes, scales, x, algo, budget_s=10.0):
+def cpu_gemv_seconds(c, threads, reps=None, budget_s=10.0):
     from oracle import oracle as O
-    threads = os.cpu_count() or 1
+    codes = c.unpacked()
+    O.gemv_grouped(codes, c.scales, c.zeros, c.group, c.x, num_workers=threads)  # warm-up
     t0 = time.perf_counter()
     n = 0
-    while True:
-        O.gemv_grouped(codes, scales, None, 32, x, num_workers=threads)
+    while (reps is None and time.perf_counter() - t0 < budget_s) or (reps is not None and n < reps):
+        O.gemv_grouped(codes, c.scales, c.zeros, c.group, c.x, num_workers=threads)
         n += 1
-        if time.perf_counter() - t0 > budget_s:
-            break
-    dt = (time.perf_counter() - t0) / n
-    return {"value": round(algo / dt / 1e9, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-            "sample": f"{n} full 12288x4096 GEMVs by the C oracle (fp64 accumulation), {threads} threads"}
+    return (time.perf_counter() - t0) / max(n, 1), n
+
+
+def cpu_baseline_gemv(c, budget_s=10.0):
+    threads = os.cpu_count() or 1
+    dt, n = cpu_gemv_seconds(c, threads, budget_s=budget_s)
+    return {"value": round(c.algo_bytes() / dt / 1e9, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"{n} full {c.N}x{c.K} GEMVs at batch {c.M} by the C oracle (fp64 accumulation), "
+                      f"{threads} threads"}
 
 
 class CpuDecodeSampler:
@@ -537,19 +595,14 @@ def run_reference(args, rank, world, workload):
     if rank != 0:
         return None
     threads = os.cpu_count() or 1
-    if workload == "q8_gemv":
-        from oracle import oracle as O
-        codes, scales, x = q8_gemv_inputs(np.random.default_rng(0))
-        algo = q8_gemv_bytes()
+    if workload == "gemv":
+        c = GemvCase(args.bits, args.rows, args.cols, args.batch, args.x)
         for _ in range(args.warmup):
-            O.gemv_grouped(codes, scales, None, 32, x, num_workers=threads)
-        t0 = time.perf_counter()
-        for _ in range(args.steps):
-            O.gemv_grouped(codes, scales, None, 32, x, num_workers=threads)
-        dt = (time.perf_counter() - t0) / args.steps
-        value, unit, metric, ms = round(algo / dt / 1e9, 3), "GB/s", GEMV_METRIC, dt * 1e3
-        sample = "one full 12288x4096 GEMV per step (C oracle, fp64 accumulation)"
-        cfg = {"workload": "q8_gemv", "N": 12288, "K": 4096, "M": 1, "group": 32}
+            cpu_gemv_seconds(c, threads, reps=1)
+        dt, _ = cpu_gemv_seconds(c, threads, reps=args.steps)
+        value, unit, metric, ms = round(c.algo_bytes() / dt / 1e9, 3), "GB/s", gemv_metric(c), dt * 1e3
+        sample = f"one full {c.N}x{c.K} GEMV at batch {c.M} per step (C oracle, fp64 accumulation)"
+        cfg = c.describe()
         scaling = "weak"
     else:
         s = CpuDecodeSampler(workload)
@@ -576,11 +629,18 @@ def main():
     ap.add_argument("--steps", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="decode_72b", choices=["decode_72b", "decode_9b", "q8_gemv"])
+    ap.add_argument("--workload", default="decode_72b", choices=["decode_72b", "decode_9b", "gemv", "q8_gemv"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--copies", type=int, default=0, help="q8_gemv: weight copies to rotate (default: > 3x L2)")
+    ap.add_argument("--bits", type=int, default=8, choices=[8, 4, 2], help="gemv: code width")
+    ap.add_argument("--rows", type=int, default=12288, help="gemv: N (output columns)")
+    ap.add_argument("--cols", type=int, default=4096, help="gemv: K (reduction length)")
+    ap.add_argument("--batch", type=int, default=1, help="gemv: M (activation rows, 1..8)")
+    ap.add_argument("--x", default="f32", choices=["f32", "bf16"], help="gemv: activation dtype")
+    ap.add_argument("--copies", type=int, default=0, help="gemv: weight copies to rotate (default: > 3x L2)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.workload == "q8_gemv":  # the single Q8 GEMV: 12288x4096, group 32, batch 1, fp32 x
+        args.workload, args.bits, args.rows, args.cols, args.batch, args.x = "gemv", 8, 12288, 4096, 1, "f32"
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -600,8 +660,8 @@ def main():
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
                                 device_id=torch.device("cuda", local_rank))
-    if args.workload == "q8_gemv":
-        line = run_q8_gemv(args, rank, world, local_rank)
+    if args.workload == "gemv":
+        line = run_gemv(args, rank, world, local_rank)
     else:
         line = run_decode(args, rank, world, local_rank, args.workload)
     if rank == 0:

@@ -34,6 +34,10 @@ int plan_gemv(const DevMatrix &w, int M, int mode, bool xsplit, GemvPlan *plan) 
     GemvPlan P;
     P.mode = mode;
     P.xsplit = xsplit;
+    P.xmode = !xsplit ? 0 : (M <= 4 ? 2 : 1);
+    // with more than two rows the partial sums are too large for one warp to
+    // sum at the end of a CTA's range: a second, fully parallel kernel does
+    P.rmode = M > 2 ? 1 : 0;
     P.e_cols = epilogue_cols(w);
     const int kc = chunk_cols(w.bits);
     const int ne = w.layout == kLayoutS8 ? 0 : kc / P.e_cols;

@@ -41,11 +41,15 @@ constexpr int kSG = 4;      // strips per strip group
 constexpr int kProducerWarp = kNW, kEpilogueWarp = kNW + 1;
 constexpr int kThreads = (kNW + 2) * 32;
 // activation fragments staged per CTA: small enough for two CTAs per SM at
-// M <= 2; with more rows the reduction buffers already limit a CTA to one SM
+// M <= 2; with more rows the reduction buffers already limit a CTA to one SM,
+// which then stages as much of K as fits (fewer K-slices, fewer partials)
 constexpr int kXMaxBytes = 20 * 1024;
-constexpr int kXMaxBytesWide = 64 * 1024;
+constexpr int kXMaxBytesWide = 100 * 1024;
 constexpr int kSmemBudget = 220 * 1024;
 static_assert(kNW == kChunksPerBlock, "one block per stage, one chunk per warp");
+
+// 16 bytes of zeros: the activation operand of MMA columns past the last row
+constexpr size_t kZeroSlot = 496;
 
 struct SmemLayout {
     size_t bar, tags, ring, xf, xs, red, info, total;
@@ -69,9 +73,9 @@ __host__ __device__ inline SmemLayout smem_layout(int layout, int bits, int bpk,
                                                   int block_bytes) {
     SmemLayout L;
     L.bar = 0;    // full[kStages], empty[kStages], xbar, rfull[2], rempty[2]
-    L.tags = 256; // unit / block / flag tag per ring slot
+    L.tags = 256; // unit / block / flag tag per ring slot; 16 zero bytes at kZeroSlot
     size_t o = 512;
-    static_assert((2 * kStages + 5) * 8 <= 256 && 3 * kStages * 4 <= 256, "barrier / tag area");
+    static_assert((2 * kStages + 5) * 8 <= 256 && 256 + 3 * kStages * 4 <= kZeroSlot, "barrier / tag area");
     L.ring = o;
     o += align_up((size_t)kStages * kSG * block_bytes, 128);
     L.xf = o;
@@ -167,9 +171,77 @@ __host__ __device__ __forceinline__ int source_of(int i) {
     return MODE == 1 ? (i >> 1) : 0;
 }
 
-template <int BITS, int LAYOUT, int E, bool XSPLIT, int MODE, int META>
+// Output (or, for gate/up, the SwiGLU of the gate and up outputs) of entry
+// q = (i * 16 + r) * M + tok of strip group sg from its summed accumulator(s):
+// scales the integer (W8A8) or 2^-24-scaled (fp16 path) sum, adds the bias and
+// the outlier columns, and writes or accumulates into y.
+template <int LAYOUT, int MODE, typename Acc>
+__device__ __forceinline__ void finalize_entry(const GemvParams &p, int sg, int q, Acc v, Acc v_up) {
+    const int M = p.M;
+    const int tok = q % M, ir = q / M, r = ir & 15, i = ir >> 4;
+    const int strip = strip_of<MODE>(sg, i);
+    const int row = strip * kStripRows + r;
+    if (strip >= p.n_strips || row >= p.N) return;
+    if (MODE == 0) {
+        const GemvSrc &sr = p.src[0];
+        float out = LAYOUT == kLayoutS8 ? (float)v * (sr.scale * p.sx[tok]) : (float)v * kTwo24;
+        if (sr.bias) out += sr.bias[row];
+        if (sr.out_cols) {
+            float os = 0.0f;
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+                const int col = sr.out_cols[(size_t)row * 8 + c];
+                if (col >= 0) os += __half2float(sr.out_w[(size_t)row * 8 + c]) * p.xrow[(size_t)tok * p.K + col];
+            }
+            out += os;
+        }
+        float *yp = p.y + (size_t)tok * p.ldy + row;
+        *yp = p.accumulate ? *yp + out : out;
+    } else {
+        float gv, uv;
+        if (LAYOUT == kLayoutS8) {
+            gv = (float)v * (p.src[0].scale * p.sx[tok]);
+            uv = (float)v_up * (p.src[1].scale * p.sx[tok]);
+        } else {
+            gv = (float)v * kTwo24;
+            uv = (float)v_up * kTwo24;
+        }
+        if (p.src[0].bias) gv += p.src[0].bias[row];
+        if (p.src[1].bias) uv += p.src[1].bias[row];
+        p.y[(size_t)tok * p.ldy + row] = silu_f(gv) * uv;
+    }
+}
+
+// Workspace slots of strip group sg: one per (K-slice, CTA of that slice whose
+// range touches sg), numbered slice by slice in CTA order.
+__host__ __device__ inline int slot_count(const GemvParams &p, int sg) {
+    int total = 0;
+    for (int kk = 0; kk < p.n_ks; ++kk) total += part_count(sg, min(p.bpk, p.n_blocks - kk * p.bpk), p.n_sg, p.gk);
+    return total;
+}
+
+template <typename Acc> struct Vec4;
+template <> struct Vec4<float> {
+    using T = float4;
+    __device__ static T zero() { return make_float4(0.f, 0.f, 0.f, 0.f); }
+    __device__ static void add(T &a, const T &b) { a.x += b.x; a.y += b.y; a.z += b.z; a.w += b.w; }
+};
+template <> struct Vec4<int> {
+    using T = int4;
+    __device__ static T zero() { return make_int4(0, 0, 0, 0); }
+    __device__ static void add(T &a, const T &b) { a.x += b.x; a.y += b.y; a.z += b.z; a.w += b.w; }
+};
+template <typename V> __device__ __forceinline__ auto comp(const V &v, int c) {
+    return c == 0 ? v.x : c == 1 ? v.y : c == 2 ? v.z : v.w;
+}
+
+// XM: how the activation operand is fed (GemvPlan::xmode).
+template <int BITS, int LAYOUT, int E, int XM, int MODE, int META>
 __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
     using Acc = typename std::conditional<LAYOUT == kLayoutS8, int, float>::type;
+    using V4 = Vec4<Acc>;
+    using Acc4 = typename V4::T;
+    constexpr bool XSPLIT = XM != 0;
     constexpr int KC = 256 / BITS;
     constexpr int S = (LAYOUT == kLayoutS8) ? 1 : KC / 16;
     constexpr int NE = (LAYOUT == kLayoutS8) ? 1 : KC / E;
@@ -212,6 +284,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
             mbar_init(&rfull[b], kNW * 32);
             mbar_init(&rempty[b], 1);
         }
+        *reinterpret_cast<uint4 *>(smem + kZeroSlot) = make_uint4(0u, 0u, 0u, 0u);
         fence_barrier_init();
     }
     __syncthreads();
@@ -237,8 +310,8 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
                              xsb, xbar);
                 x_issued = true;
             };
+            int sg = (int)(i0 / nb), bi = (int)(i0 - (long)sg * nb);
             for (long i = i0; i < i1; ++i, ++it) {
-                const int sg = (int)(i / nb), bi = (int)(i - (long)sg * nb);
                 const int slot = it % kStages, use = it / kStages;
                 if (use > 0 && !mbar_wait_bounded(&empty[slot], (use - 1) & 1)) {
                     atomicExch(p.err, kErrWaitEmpty);
@@ -262,6 +335,10 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
                 }
                 // weights first, then (once) the upstream-dependent activations
                 if (!x_issued && it + 1 >= kStages) issue_x();
+                if (++bi == nb) {
+                    bi = 0;
+                    ++sg;
+                }
             }
             if (!x_issued) issue_x();
             // end-of-work marker in the next slot
@@ -282,11 +359,14 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
     } else if (warp == kEpilogueWarp) {
         // ---------------- epilogue warp ----------------
         // Sums the MMA warps' accumulators of each finished segment (fixed warp
-        // order), writes the outputs of a whole strip group, or parks a partial
-        // sum in its workspace slot; the last partial to arrive sums all slots
-        // in slot order.  Runs behind the MMA warps, off the streaming path.
+        // order, four entries per load), writes the outputs of a whole strip
+        // group, or parks a partial sum in its workspace slot.  With rmode 0
+        // the last partial to arrive (atomic count) sums all slots in slot
+        // order; with rmode 1 gemv_reduce_kernel does, after this kernel.
+        // Runs behind the MMA warps, off the streaming path.
         Acc *ws = static_cast<Acc *>(p.ws);
         const int nq = kSG * 16 * M;  // (strip, row, token) entries of a segment
+        const int nq4 = nq / 4;       // nq is a multiple of 64
         for (int k = 0;; ++k) {
             const int b = k & 1, u = k >> 1;
             if (!__all_sync(0xffffffffu, mbar_wait_bounded(&rfull[b], u & 1))) {
@@ -296,45 +376,10 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
             const SegInfo si = info[b];
             if (si.sg < 0) break;
             const int sg = si.sg;
-            const Acc *red = reinterpret_cast<const Acc *>(smem + L.red) + (size_t)b * kNW * kSG * 16 * M;
-            // value of entry q = (i*16 + r)*M + tok: output (or partial) of strip i, row r, token tok
-            auto finalize = [&](int q, Acc v, Acc v_up) {
-                const int tok = q % M, ir = q / M, r = ir & 15, i = ir >> 4;
-                const int row = strip_of<MODE>(sg, i) * kStripRows + r;
-                if (strip_of<MODE>(sg, i) >= p.n_strips || row >= p.N) return;
-                if (MODE == 0) {
-                    const GemvSrc &sr = p.src[0];
-                    float out = LAYOUT == kLayoutS8 ? (float)v * (sr.scale * p.sx[tok]) : (float)v * kTwo24;
-                    if (sr.bias) out += sr.bias[row];
-                    if (sr.out_cols) {
-                        float os = 0.0f;
-#pragma unroll
-                        for (int c = 0; c < 8; ++c) {
-                            const int col = sr.out_cols[(size_t)row * 8 + c];
-                            if (col >= 0)
-                                os += __half2float(sr.out_w[(size_t)row * 8 + c]) * p.xrow[(size_t)tok * p.K + col];
-                        }
-                        out += os;
-                    }
-                    float *yp = p.y + (size_t)tok * p.ldy + row;
-                    *yp = p.accumulate ? *yp + out : out;
-                } else {
-                    float gv, uv;
-                    if (LAYOUT == kLayoutS8) {
-                        gv = (float)v * (p.src[0].scale * p.sx[tok]);
-                        uv = (float)v_up * (p.src[1].scale * p.sx[tok]);
-                    } else {
-                        gv = (float)v * kTwo24;
-                        uv = (float)v_up * kTwo24;
-                    }
-                    if (p.src[0].bias) gv += p.src[0].bias[row];
-                    if (p.src[1].bias) uv += p.src[1].bias[row];
-                    p.y[(size_t)tok * p.ldy + row] = silu_f(gv) * uv;
-                }
-            };
+            const Acc4 *red4 = reinterpret_cast<const Acc4 *>(smem + L.red) + (size_t)b * kNW * nq4;
             // gate/up: entry q of a gate strip pairs with q + 2*16*M of the up strip
-            const int nq_out = MODE == 1 ? nq / 2 : nq;
-            const int up_off = 2 * 16 * M;
+            const int nq4_out = MODE == 1 ? nq4 / 2 : nq4;
+            const int up4 = 2 * 16 * M / 4;
             int slot_p = 0, total_p = 1;
             if (!si.whole) {
                 // partial slot: partials of earlier K-slices first, then this slice's CTAs in order
@@ -347,27 +392,30 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
                 }
                 slot_p += jk - part_owner(T, Gk, (long)sg * nb);
             }
-            Acc *wslot = ws + ((size_t)sg * p.maxp + slot_p) * (kSG * 16 * 8);
-            for (int q = lane; q < nq; q += 32) {
-                Acc sum = 0;
+            Acc4 *wslot4 = reinterpret_cast<Acc4 *>(ws + ((size_t)sg * p.maxp + slot_p) * (kSG * 16 * 8));
+            for (int q4 = lane; q4 < nq4; q4 += 32) {
+                Acc4 sum = V4::zero();
 #pragma unroll
-                for (int w = 0; w < kNW; ++w) sum += red[(size_t)w * nq + q];
+                for (int w = 0; w < kNW; ++w) V4::add(sum, red4[(size_t)w * nq4 + q4]);
                 if (si.whole) {
                     if (MODE == 0) {
-                        finalize(q, sum, 0);
-                    } else if (q < nq_out) {
-                        Acc su = 0;
 #pragma unroll
-                        for (int w = 0; w < kNW; ++w) su += red[(size_t)w * nq + q + up_off];
-                        finalize(q, sum, su);
+                        for (int c = 0; c < 4; ++c) finalize_entry<LAYOUT, MODE, Acc>(p, sg, 4 * q4 + c, comp(sum, c), 0);
+                    } else if (q4 < nq4_out) {
+                        Acc4 su = V4::zero();
+#pragma unroll
+                        for (int w = 0; w < kNW; ++w) V4::add(su, red4[(size_t)w * nq4 + q4 + up4]);
+#pragma unroll
+                        for (int c = 0; c < 4; ++c)
+                            finalize_entry<LAYOUT, MODE, Acc>(p, sg, 4 * q4 + c, comp(sum, c), comp(su, c));
                     }
                 } else {
-                    wslot[q] = sum;
+                    wslot4[q4] = sum;
                 }
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&rempty[b]);  // accumulator buffer consumed
-            if (!si.whole) {
+            if (!si.whole && p.rmode == 0) {
                 __threadfence();  // this CTA's partial sums visible before its arrival is counted
                 __syncwarp();
                 int last = 0;
@@ -383,7 +431,8 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
                     // L2 loads in flight; the association is fixed, so the result
                     // is deterministic.
                     constexpr size_t kSlot = kSG * 16 * 8;
-                    for (int q = lane; q < nq_out; q += 32) {
+                    const int up_off = 4 * up4;
+                    for (int q = lane; q < 4 * nq4_out; q += 32) {
                         Acc a[4] = {0, 0, 0, 0}, u4[4] = {0, 0, 0, 0};
                         int c = 0;
                         for (; c + 4 <= total_p; c += 4) {
@@ -393,11 +442,15 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
                                 if (MODE == 1) u4[h] += __ldcg(&wsg[(size_t)(c + h) * kSlot + q + up_off]);
                             }
                         }
-                        for (; c < total_p; ++c) {
-                            a[c & 3] += __ldcg(&wsg[(size_t)c * kSlot + q]);
-                            if (MODE == 1) u4[c & 3] += __ldcg(&wsg[(size_t)c * kSlot + q + up_off]);
-                        }
-                        finalize(q, (a[0] + a[1]) + (a[2] + a[3]), (u4[0] + u4[1]) + (u4[2] + u4[3]));
+                        // the last (total_p % 4) slots go to sums 0, 1, 2 in order
+#pragma unroll
+                        for (int h = 0; h < 3; ++h)
+                            if (c + h < total_p) {
+                                a[h] += __ldcg(&wsg[(size_t)(c + h) * kSlot + q]);
+                                if (MODE == 1) u4[h] += __ldcg(&wsg[(size_t)(c + h) * kSlot + q + up_off]);
+                            }
+                        finalize_entry<LAYOUT, MODE, Acc>(p, sg, q, (a[0] + a[1]) + (a[2] + a[3]),
+                                                          (u4[0] + u4[1]) + (u4[2] + u4[3]));
                     }
                     __syncwarp();
                     if (lane == 0) atomicExch(&p.split_cnt[sg], 0u);
@@ -407,7 +460,28 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
     } else {
         // ---------------- MMA warps ----------------
         const int g = lane >> 2, t = lane & 3;
-        const bool has_x = g < M;
+        // Lane (g, t) supplies column g of the MMA's B operand: token g (XM 0, 1,
+        // S8 layout), or token g / 2, fp16 half g & 1 of the fp32 activation
+        // (XM 2; the two halves of one token meet again in d[0] + d[1]).  Lanes
+        // past the last column read 16 zero bytes (stride 0) instead.
+        constexpr bool PK = XM == 2;
+        const bool has_x = g < (PK ? 2 * M : M);
+        const uint8_t *xb0;
+        uint32_t xstr;  // bytes per fragment unit (k-step, k-step pair, or S8 chunk)
+        if (LAYOUT == kLayoutS8) {
+            xb0 = smem + L.xf + (g * 4 + t) * 8;
+            xstr = (uint32_t)M * 32;
+        } else if (PK) {
+            xb0 = smem + L.xf + ((g >> 1) * 4 + t) * 16 + (g & 1) * 8;
+            xstr = (uint32_t)M * 64;
+        } else {
+            xb0 = smem + L.xf + (g * 4 + t) * 16;
+            xstr = (uint32_t)M * 64;
+        }
+        if (!has_x) {
+            xb0 = smem + kZeroSlot;
+            xstr = 0;
+        }
         const float *xss = reinterpret_cast<const float *>(smem + L.xs);
         float zc24[kSG];
 #pragma unroll
@@ -437,12 +511,14 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
                 return false;
             }
             Acc *red = reinterpret_cast<Acc *>(smem + L.red) + ((size_t)b * kNW + warp) * kSG * 16 * M;
-            // lane (g, t) holds rows g (e = 0, 1) and g + 8 (e = 2, 3), tokens 2t + (e & 1)
+            // XM 2: lane (g, t) holds rows g (e = 0) and g + 8 (e = 1) of token t;
+            // otherwise rows g (e = 0, 1) and g + 8 (e = 2, 3), tokens 2t + (e & 1)
 #pragma unroll
             for (int i = 0; i < kSG; ++i)
 #pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const int tok = 2 * t + (e & 1), r = g + 8 * (e >> 1);
+                for (int e = 0; e < (PK ? 2 : 4); ++e) {
+                    const int tok = PK ? t : 2 * t + (e & 1);
+                    const int r = PK ? g + 8 * e : g + 8 * (e >> 1);
                     if (tok < M) red[(i * 16 + r) * M + tok] = acc[i][e];
                     acc[i][e] = 0;
                 }
@@ -471,8 +547,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
             for (int i = 0; i < kSG; ++i)
                 wv[i] = *reinterpret_cast<const uint4 *>(stg + (size_t)i * BB + warp * kChunkBytes + lane * 16);
             if constexpr (LAYOUT == kLayoutS8) {
-                uint2 b = make_uint2(0u, 0u);
-                if (has_x) b = reinterpret_cast<const uint2 *>(smem + L.xf)[((size_t)cs * M + g) * 4 + t];
+                const uint2 b = *reinterpret_cast<const uint2 *>(xb0 + (uint32_t)cs * xstr);
 #pragma unroll
                 for (int i = 0; i < kSG; ++i)
                     mma_s8_m16n8k32(reinterpret_cast<int *>(acc[i]), wv[i].x, wv[i].y, wv[i].z, wv[i].w, b.x, b.y);
@@ -482,7 +557,6 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
                 for (int i = 0; i < kSG; ++i)
                     w8[i] = (BITS == 8) ? wv[i]
                                         : make_uint4(wv[i].x >> 8, wv[i].y >> 8, wv[i].z >> 8, wv[i].w >> 8);
-                const uint4 *xu = reinterpret_cast<const uint4 *>(smem + L.xf);
 #pragma unroll
                 for (int eb = 0; eb < NE; ++eb) {
                     float d[kSG][4];
@@ -491,36 +565,58 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
 #pragma unroll
                         for (int e = 0; e < 4; ++e) d[i][e] = 0.0f;
 #pragma unroll
-                    for (int jj = 0; jj < SPE; jj += (XSPLIT ? 1 : 2)) {
+                    for (int jj = 0; jj < SPE; jj += (XM == 0 ? 2 : 1)) {
                         const int j = eb * SPE + jj;
                         const int kst = cs * S + j;
-                        uint4 bv = make_uint4(0u, 0u, 0u, 0u);
-                        if (has_x) bv = xu[((size_t)(XSPLIT ? kst : (kst >> 1)) * M + g) * 4 + t];
+                        if constexpr (XM == 2) {
+                            const uint2 bv = *reinterpret_cast<const uint2 *>(xb0 + (uint32_t)kst * xstr);
 #pragma unroll
-                        for (int i = 0; i < kSG; ++i) {
-                            mma_f16_m16n8k16(d[i], unpack_f16<BITS>(wv[i].x, w8[i].x, j),
-                                             unpack_f16<BITS>(wv[i].y, w8[i].y, j),
-                                             unpack_f16<BITS>(wv[i].z, w8[i].z, j),
-                                             unpack_f16<BITS>(wv[i].w, w8[i].w, j), bv.x, bv.y);
-                            const int j2 = XSPLIT ? j : j + 1;
-                            mma_f16_m16n8k16(d[i], unpack_f16<BITS>(wv[i].x, w8[i].x, j2),
-                                             unpack_f16<BITS>(wv[i].y, w8[i].y, j2),
-                                             unpack_f16<BITS>(wv[i].z, w8[i].z, j2),
-                                             unpack_f16<BITS>(wv[i].w, w8[i].w, j2), bv.z, bv.w);
+                            for (int i = 0; i < kSG; ++i)
+                                mma_f16_m16n8k16(d[i], unpack_f16<BITS>(wv[i].x, w8[i].x, j),
+                                                 unpack_f16<BITS>(wv[i].y, w8[i].y, j),
+                                                 unpack_f16<BITS>(wv[i].z, w8[i].z, j),
+                                                 unpack_f16<BITS>(wv[i].w, w8[i].w, j), bv.x, bv.y);
+                        } else {
+                            const uint4 bv =
+                                *reinterpret_cast<const uint4 *>(xb0 + (uint32_t)(XM == 1 ? kst : (kst >> 1)) * xstr);
+#pragma unroll
+                            for (int i = 0; i < kSG; ++i) {
+                                mma_f16_m16n8k16(d[i], unpack_f16<BITS>(wv[i].x, w8[i].x, j),
+                                                 unpack_f16<BITS>(wv[i].y, w8[i].y, j),
+                                                 unpack_f16<BITS>(wv[i].z, w8[i].z, j),
+                                                 unpack_f16<BITS>(wv[i].w, w8[i].w, j), bv.x, bv.y);
+                                const int j2 = XM == 1 ? j : j + 1;
+                                mma_f16_m16n8k16(d[i], unpack_f16<BITS>(wv[i].x, w8[i].x, j2),
+                                                 unpack_f16<BITS>(wv[i].y, w8[i].y, j2),
+                                                 unpack_f16<BITS>(wv[i].z, w8[i].z, j2),
+                                                 unpack_f16<BITS>(wv[i].w, w8[i].w, j2), bv.z, bv.w);
+                            }
                         }
                     }
                     const int kib = warp * KC + eb * E;  // column within the block
                     const int gib = gshift >= 0 ? (kib >> gshift) : 0;
-                    const float2 X = *reinterpret_cast<const float2 *>(xss + ((size_t)cs * NE + eb) * 8 + 2 * t);
+                    if constexpr (XM == 2) {
+                        const float X = xss[((size_t)cs * NE + eb) * 8 + t];
 #pragma unroll
-                    for (int i = 0; i < kSG; ++i) {
-                        float s0, o0, s1, o1;
-                        load_meta2<META>(stg + (size_t)i * BB + kBlockCodeBytes + (size_t)gib * 16 * MB, g, zc24[i],
-                                         s0, o0, s1, o1);
-                        acc[i][0] = fmaf(o0, X.x, fmaf(s0, d[i][0], acc[i][0]));
-                        acc[i][1] = fmaf(o0, X.y, fmaf(s0, d[i][1], acc[i][1]));
-                        acc[i][2] = fmaf(o1, X.x, fmaf(s1, d[i][2], acc[i][2]));
-                        acc[i][3] = fmaf(o1, X.y, fmaf(s1, d[i][3], acc[i][3]));
+                        for (int i = 0; i < kSG; ++i) {
+                            float s0, o0, s1, o1;
+                            load_meta2<META>(stg + (size_t)i * BB + kBlockCodeBytes + (size_t)gib * 16 * MB, g,
+                                             zc24[i], s0, o0, s1, o1);
+                            acc[i][0] = fmaf(o0, X, fmaf(s0, d[i][0] + d[i][1], acc[i][0]));
+                            acc[i][1] = fmaf(o1, X, fmaf(s1, d[i][2] + d[i][3], acc[i][1]));
+                        }
+                    } else {
+                        const float2 X = *reinterpret_cast<const float2 *>(xss + ((size_t)cs * NE + eb) * 8 + 2 * t);
+#pragma unroll
+                        for (int i = 0; i < kSG; ++i) {
+                            float s0, o0, s1, o1;
+                            load_meta2<META>(stg + (size_t)i * BB + kBlockCodeBytes + (size_t)gib * 16 * MB, g,
+                                             zc24[i], s0, o0, s1, o1);
+                            acc[i][0] = fmaf(o0, X.x, fmaf(s0, d[i][0], acc[i][0]));
+                            acc[i][1] = fmaf(o0, X.y, fmaf(s0, d[i][1], acc[i][1]));
+                            acc[i][2] = fmaf(o1, X.x, fmaf(s1, d[i][2], acc[i][2]));
+                            acc[i][3] = fmaf(o1, X.y, fmaf(s1, d[i][3], acc[i][3]));
+                        }
                     }
                 }
             }
@@ -539,9 +635,61 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
     __syncthreads();
 }
 
-template <int BITS, int LAYOUT, int E, bool XSPLIT, int MODE, int META>
-cudaError_t launch_gemv_t(const GemvPlan &plan, const GemvParams &p, cudaStream_t st) {
-    auto kern = gemv_kernel<BITS, LAYOUT, E, XSPLIT, MODE, META>;
+// rmode 1: sums the partial-sum slots of every strip group that the GEMV
+// kernel did not finish itself, in slot order (the same fixed association as
+// the in-kernel path: four running sums, then (a0 + a1) + (a2 + a3)), and
+// finalizes the outputs.  One CTA per strip group at a time; four entries per
+// thread and load.
+template <int LAYOUT, int MODE>
+__global__ void __launch_bounds__(128) gemv_reduce_kernel(const GemvParams p) {
+    using Acc = typename std::conditional<LAYOUT == kLayoutS8, int, float>::type;
+    using V4 = Vec4<Acc>;
+    using Acc4 = typename V4::T;
+    constexpr size_t kSlot = kSG * 16 * 8;
+    __shared__ int s_total;
+    grid_dependency_wait();
+    const int M = p.M;
+    const int nq4 = kSG * 16 * M / 4;
+    const int nq4_out = MODE == 1 ? nq4 / 2 : nq4;
+    const int up4 = 2 * 16 * M / 4;
+    const Acc *ws = static_cast<const Acc *>(p.ws);
+    for (int sg = blockIdx.x; sg < p.n_sg; sg += gridDim.x) {
+        __syncthreads();
+        if (threadIdx.x == 0) s_total = slot_count(p, sg);
+        __syncthreads();
+        const int total = s_total;
+        if (p.n_ks == 1 && total == 1) continue;  // finished by the GEMV kernel
+        const Acc4 *wsg = reinterpret_cast<const Acc4 *>(ws + (size_t)sg * p.maxp * kSlot);
+        for (int q4 = threadIdx.x; q4 < nq4_out; q4 += blockDim.x) {
+            Acc4 a[4] = {V4::zero(), V4::zero(), V4::zero(), V4::zero()};
+            Acc4 u[4] = {V4::zero(), V4::zero(), V4::zero(), V4::zero()};
+            int c = 0;
+            for (; c + 4 <= total; c += 4) {
+#pragma unroll
+                for (int h = 0; h < 4; ++h) {
+                    V4::add(a[h], __ldcg(&wsg[(size_t)(c + h) * (kSlot / 4) + q4]));
+                    if (MODE == 1) V4::add(u[h], __ldcg(&wsg[(size_t)(c + h) * (kSlot / 4) + q4 + up4]));
+                }
+            }
+#pragma unroll
+            for (int h = 0; h < 3; ++h)
+                if (c + h < total) {
+                    V4::add(a[h], __ldcg(&wsg[(size_t)(c + h) * (kSlot / 4) + q4]));
+                    if (MODE == 1) V4::add(u[h], __ldcg(&wsg[(size_t)(c + h) * (kSlot / 4) + q4 + up4]));
+                }
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                const Acc v = (comp(a[0], c) + comp(a[1], c)) + (comp(a[2], c) + comp(a[3], c));
+                const Acc vu = (comp(u[0], c) + comp(u[1], c)) + (comp(u[2], c) + comp(u[3], c));
+                finalize_entry<LAYOUT, MODE, Acc>(p, sg, 4 * q4 + c, v, vu);
+            }
+        }
+    }
+}
+
+template <int BITS, int LAYOUT, int E, int XM, int MODE, int META>
+cudaError_t launch_gemv_t(const GemvPlan &plan, const GemvParams &p_in, cudaStream_t st) {
+    auto kern = gemv_kernel<BITS, LAYOUT, E, XM, MODE, META>;
     static bool attr_set = false;
     if (!attr_set) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBudget);
@@ -569,6 +717,9 @@ cudaError_t launch_gemv_t(const GemvPlan &plan, const GemvParams &p, cudaStream_
     }
     long gk = std::min<long>((long)plan.sms * occ / plan.n_ks, plan.items_min);
     gk = std::max<long>(1, std::min<long>(gk, plan.grid / plan.n_ks));
+    GemvParams p = p_in;
+    p.gk = (int)gk;
+    p.rmode = plan.rmode;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)(gk * plan.n_ks));
     cfg.blockDim = dim3(kThreads);
@@ -580,27 +731,42 @@ cudaError_t launch_gemv_t(const GemvPlan &plan, const GemvParams &p, cudaStream_
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     note_launch();
-    return cudaLaunchKernelEx(&cfg, kern, p);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, p);
+    if (e != cudaSuccess || !plan.rmode) return e;
+    // the split-K partial sums, on the same stream right behind
+    cudaLaunchConfig_t rc = cfg;
+    rc.gridDim = dim3((unsigned)std::min<long>(p.n_sg, (long)plan.sms * 8));
+    rc.blockDim = dim3(128);
+    rc.dynamicSmemBytes = 0;
+    note_launch();
+    return cudaLaunchKernelEx(&rc, gemv_reduce_kernel<LAYOUT, MODE>, p);
 }
 
 // All variants of one code width / epilogue block, chosen at run time.
 template <int BITS, int LAYOUT, int E>
 cudaError_t launch_gemv_bits(const GemvPlan &plan, const GemvParams &p, int meta, cudaStream_t st) {
     if constexpr (LAYOUT == kLayoutS8) {
-        if (plan.mode == 0) return launch_gemv_t<BITS, LAYOUT, E, false, 0, kMetaNone>(plan, p, st);
-        return launch_gemv_t<BITS, LAYOUT, E, false, 1, kMetaNone>(plan, p, st);
+        if (plan.mode == 0) return launch_gemv_t<BITS, LAYOUT, E, 0, 0, kMetaNone>(plan, p, st);
+        return launch_gemv_t<BITS, LAYOUT, E, 0, 1, kMetaNone>(plan, p, st);
     } else {
-#define CHPE_META_CASES(XS, MD)                                                                 \
+#define CHPE_META_CASES(XM, MD)                                                                 \
     switch (meta) {                                                                             \
-    case kMetaS16: return launch_gemv_t<BITS, LAYOUT, E, XS, MD, kMetaS16>(plan, p, st);        \
-    case kMetaSZ16: return launch_gemv_t<BITS, LAYOUT, E, XS, MD, kMetaSZ16>(plan, p, st);      \
-    default: return launch_gemv_t<BITS, LAYOUT, E, XS, MD, kMetaF32>(plan, p, st);              \
+    case kMetaS16: return launch_gemv_t<BITS, LAYOUT, E, XM, MD, kMetaS16>(plan, p, st);        \
+    case kMetaSZ16: return launch_gemv_t<BITS, LAYOUT, E, XM, MD, kMetaSZ16>(plan, p, st);      \
+    default: return launch_gemv_t<BITS, LAYOUT, E, XM, MD, kMetaF32>(plan, p, st);              \
+    }
+#define CHPE_XM_CASES(MD)                                                                       \
+    switch (plan.xmode) {                                                                       \
+    case 2: CHPE_META_CASES(2, MD)                                                              \
+    case 1: CHPE_META_CASES(1, MD)                                                              \
+    default: CHPE_META_CASES(0, MD)                                                             \
     }
         if (plan.mode == 0) {
-            if (plan.xsplit) { CHPE_META_CASES(true, 0) } else { CHPE_META_CASES(false, 0) }
+            CHPE_XM_CASES(0)
         } else {
-            if (plan.xsplit) { CHPE_META_CASES(true, 1) } else { CHPE_META_CASES(false, 1) }
+            CHPE_XM_CASES(1)
         }
+#undef CHPE_XM_CASES
 #undef CHPE_META_CASES
     }
 }

@@ -58,8 +58,10 @@ struct GemvParams {
     float *y;
     int ldy;
     int accumulate;
-    void *ws;             // partial sums [n_sg][maxp][2][128]
+    void *ws;             // partial sums [n_sg][maxp][kSG * 16 * 8]
     unsigned *split_cnt;  // [n_sg] arrivals of partial sums (self-resetting)
+    int rmode;            // 0: last CTA to arrive sums the partials; 1: gemv_reduce_kernel does
+    int gk;               // CTAs per K-slice (set at launch)
     int *err;
 };
 
@@ -82,6 +84,11 @@ struct GemvPlan {
     int sms = 148;
     int e_cols = 0;  // epilogue block (columns)
     bool xsplit = false;
+    // activation operand: 0 fp16/bf16, two k-steps per fragment unit; 1 fp32
+    // as fp16 hi + lo, two MMAs per k-step; 2 fp32 as hi and lo in adjacent
+    // MMA columns, one MMA per k-step (M <= 4)
+    int xmode = 0;
+    int rmode = 0;  // split-K partials: 0 summed by the last CTA, 1 by a second kernel
     size_t smem = 0;
     size_t xf_bytes = 0, xs_bytes = 0, ws_bytes = 0;
     int split_counters = 0;

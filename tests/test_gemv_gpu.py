@@ -183,6 +183,48 @@ def test_gateup_swiglu_grouped(ctx):
     assert rel_l2(y, ref) < TOL
 
 
+@pytest.mark.parametrize("bits", [8, 4, 2])
+@pytest.mark.parametrize("M", [1, 2, 3, 4, 5, 8])
+def test_fp32_x_every_row_count_and_split(ctx, bits, M):
+    """fp32 activations at every row count: M <= 4 feeds each activation's two
+    fp16 halves to adjacent MMA columns, M > 4 to two MMAs; M > 2 sums split-K
+    partials in a second kernel.  K = 12288 forces several K-slices and
+    N = 520 leaves a ragged last strip group.  The fp32 split is exact up to
+    fp32 summation, so the bound is far tighter than the path's 1e-3.  Plain
+    GEMV, accumulate into y, and the fused gate/up SwiGLU."""
+    torch = torch_mod()
+    from chpe_qwen35_hybrid_engine_b200 import SCHEME_I8_GROUP_F16, SCHEME_U_GROUP_F16_ZERO
+    rng = np.random.default_rng(bits * 100 + M)
+    N, K = 520, 12288
+    tens, refs = [], []
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    for _ in range(2):
+        w = rng.normal(0, 0.02, (N, K)).astype(np.float32)
+        if bits == 8:
+            codes, s = O.quantize_sym8(w, 32)
+            tens.append(ctx.upload_matrix(8, SCHEME_I8_GROUP_F16, codes, s, rows=N, cols=K, group=32))
+            refs.append(O.gemv_grouped(codes, s, None, 32, x, num_workers=8))
+        else:
+            codes, s, z = O.quantize_asym(w, bits, 64)
+            tens.append(ctx.upload_matrix(bits, SCHEME_U_GROUP_F16_ZERO, pack_codes(codes, bits), s, z, rows=N,
+                                          cols=K, group=64))
+            refs.append(O.gemv_grouped(codes, s, z, 64, x, num_workers=8))
+    xd = torch.from_numpy(x).cuda()
+    y = ctx.gemv(tens[0], xd)
+    assert rel_l2(y.cpu().numpy(), refs[0]) < 1e-5
+    y0 = torch.from_numpy(rng.standard_normal((M, N)).astype(np.float32)).cuda()
+    y1 = y0.clone()
+    ctx.gemv(tens[0], xd, out=y1, accumulate=True)
+    assert rel_l2(y1.cpu().numpy(), y0.cpu().numpy() + refs[0]) < 1e-5
+    gu = ctx.gemv_gateup_swiglu(tens[0], tens[1], xd).cpu().numpy()
+    g, u = refs
+    assert rel_l2(gu, g / (1 + np.exp(-g)) * u) < 1e-5
+    # deterministic
+    assert torch.equal(ctx.gemv(tens[0], xd), y)
+    for t in tens:
+        t.free()
+
+
 # --- device quantizers: bit-exact with the oracle ---
 
 @pytest.mark.parametrize("bits,group,sym", [(4, 64, False), (2, 64, False), (8, 32, True), (4, 128, False)])

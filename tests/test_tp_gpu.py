@@ -1,0 +1,106 @@
+"""Tensor-parallel decode on 2 GPUs (NCCL) against the unsharded engine.
+
+Both ranks draw the same full random-init weights and keep their shard
+(column-split q/k/v/gate/up/LM head, row-split o/down).  The greedy tokens of
+16 steps must equal those of the single-GPU engine on the same weights, and
+the last step's logits must agree to fp32 summation-order noise (rel-L2 1e-5):
+the only difference is that o and down partial sums meet in an all-reduce.
+Needs 2 GPUs; skipped otherwise.
+"""
+import datetime
+import os
+import socket
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+def _geom():
+    from chpe_qwen35_hybrid_engine_b200.engine import Geometry
+    # 2 GQA layers, 4 q heads / 2 kv heads of 128, hidden 512, FFN 1024, vocab 1000
+    return Geometry(hidden=512, ffn=1024, vocab=1000, n_layers=2, attn_every=1, q_dim=512, kv_dim=256, ssm_qkv=0,
+                    ssm_z=0, head_dim=128, q_heads=4, kv_heads=2)
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _rank(rank, world, port, scheme, q):
+    import torch
+    import torch.distributed as dist
+    from chpe_qwen35_hybrid_engine_b200 import Context
+    from chpe_qwen35_hybrid_engine_b200.tp import TensorParallelEngine
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        ctx = Context(rank)
+        tp = TensorParallelEngine(ctx, _geom(), scheme, rank, world, seed=21, max_rows=8)
+        e = tp.eng
+        e.buf["tokens"][:1] = 33
+        toks = []
+        for _ in range(16):  # eager steps
+            tp.step(1)
+            toks.append(int(e.buf["argmax"][0]))
+            e.buf["tokens"][:1] = e.buf["argmax"][:1]
+        # the same 16 steps again, replaying a captured step
+        g = tp.capture(1)
+        gtoks = []
+        e.buf["tokens"][:1] = 33
+        for _ in range(16):
+            g.replay()
+            gtoks.append(int(e.buf["argmax"][0]))
+            e.buf["tokens"][:1] = e.buf["argmax"][:1]
+        torch.cuda.synchronize()
+        # logits shard of the step from token 33
+        e.buf["tokens"][:1] = 33
+        tp.step(1)
+        torch.cuda.synchronize()
+        shard = e.buf["logits"][0, :e.head.rows].clone()
+        parts = [torch.zeros(1000 // world, device=shard.device) for _ in range(world)]
+        dist.all_gather(parts, shard)
+        tp.graphs.clear()
+        del g
+        if rank == 0:
+            q.put((toks, gtoks, torch.cat(parts).cpu().numpy()))
+        ctx.close()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("scheme", ["q4g64", "q8g32"])
+def test_tp2_decode_matches_single_gpu(ctx, scheme):
+    import torch
+    import torch.multiprocessing as mp
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    from chpe_qwen35_hybrid_engine_b200.engine import build_random
+    mpc = mp.get_context("spawn")
+    q = mpc.Queue()
+    port = _port()
+    procs = [mpc.Process(target=_rank, args=(r, 2, port, scheme, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    try:
+        toks, gtoks, logits_tp = q.get(timeout=300)
+    finally:
+        for p in procs:
+            p.join(timeout=120)
+    assert all(p.exitcode == 0 for p in procs)
+    eng, _ = build_random(ctx, _geom(), scheme, seed=21, max_rows=8)
+    want = eng.decode_greedy([33], 16, M=1, use_graph=False)[:, 0].tolist()
+    assert toks == want
+    assert gtoks == want
+    eng.buf["tokens"][:1] = 33
+    eng.step(1)
+    torch.cuda.synchronize()
+    ref = eng.buf["logits"][0].cpu().numpy()
+    assert np.linalg.norm(logits_tp - ref) / np.linalg.norm(ref) < 1e-5
