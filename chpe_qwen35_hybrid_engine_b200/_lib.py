@@ -25,9 +25,17 @@ SCHEME_ROW_AFFINE_F32 = 6
 
 X_F32, X_BF16, X_F16, X_I8 = 0, 1, 2, 3
 
+XOP_PLAIN, XOP_RMSNORM, XOP_SILU_MUL, XOP_ATTN_STUB, XOP_SSM_STUB = 0, 1, 2, 3, 4
+
 
 class chpe_fmt(C.Structure):
     _fields_ = [("bits", C.c_int32), ("scheme", C.c_int32), ("group", C.c_int32), ("zero", C.c_float)]
+
+
+class chpe_xsrc(C.Structure):
+    _fields_ = [("op", C.c_int32), ("x", C.c_void_p), ("x_dtype", C.c_int32), ("ldx", C.c_int32),
+                ("aux", C.c_void_p), ("ld_aux", C.c_int32), ("eps", C.c_float), ("kv_dim", C.c_int32),
+                ("head_dim", C.c_int32), ("group", C.c_int32), ("qkv_dim", C.c_int32), ("silu_on_qkv", C.c_int32)]
 
 
 P = C.c_void_p
@@ -65,6 +73,7 @@ SIGNATURES = {
     "chpe_gemv_xfrag_dev": (I, [P, P, P, P, I, P]),
     "chpe_gemv_gateup_swiglu_xfrag_dev": (I, [P, P, P, P, P, P]),
     "chpe_xfrag_free": (I, [P, P]),
+    "chpe_xfrag_fill_op_dev": (I, [P, P, C.POINTER(chpe_xsrc), P]),
     "chpe_gemv_parallel": (I, [P, P, F, P, F, SZ, SZ, P]),
     "chpe_gemv_gate_up_swiglu_parallel": (I, [P, P, F, P, F, P, F, SZ, SZ, P]),
     "chpe_gemv_batch4_parallel": (I, [P, P, F, P, P, P, P, P, SZ, SZ, P, P, P, P]),

@@ -902,7 +902,8 @@ struct chpe_xfrag {
     Xfrag f;
     size_t xf_bytes = 0, xs_bytes = 0;
     float *sx = nullptr;
-    float *xrow = nullptr;
+    float *xrow = nullptr;  // fp32 rows (outlier columns; fused producers into int8 fragments)
+    bool outliers = false;  // created like a tensor with outlier columns
 };
 
 extern "C" int chpe_xfrag_create(chpe_ctx *ctx, const chpe_tensor *like, int M, int x_dtype, chpe_xfrag **out) {
@@ -913,10 +914,13 @@ extern "C" int chpe_xfrag_create(chpe_ctx *ctx, const chpe_tensor *like, int M, 
     cudaSetDevice(ctx->device);
     chpe_xfrag *h = new chpe_xfrag();
     h->f = xfrag_shape(like->m, M, x_dtype, &h->xf_bytes, &h->xs_bytes);
+    h->outliers = like->m.out_cols != nullptr;
     cudaError_t e = cudaMalloc(&h->f.xf, h->xf_bytes);
     if (e == cudaSuccess) e = cudaMalloc(reinterpret_cast<void **>(&h->f.xs), h->xs_bytes + 32);
     if (e == cudaSuccess) e = cudaMalloc(reinterpret_cast<void **>(&h->sx), 64 * sizeof(float));
-    if (e == cudaSuccess && x_dtype == CHPE_X_F32)
+    // fp32 rows are kept beside the fragments only for tensors with outlier
+    // columns, and for int8 tensors fed by a fused producer (quantized from them)
+    if (e == cudaSuccess && x_dtype == CHPE_X_F32 && (like->m.out_cols || like->m.layout == kLayoutS8))
         e = cudaMalloc(reinterpret_cast<void **>(&h->xrow), (size_t)M * like->m.K * sizeof(float));
     if (e != cudaSuccess) {
         cudaFree(h->f.xf);
@@ -936,7 +940,7 @@ extern "C" int chpe_xfrag_fill_dev(chpe_ctx *ctx, chpe_xfrag *xf, const void *x,
     if (!ctx || !xf || !x) return fail(ctx, CHPE_EINVAL, "null argument");
     if (xf->f.x_dtype == CHPE_X_I8 && !x_scales) return fail(ctx, CHPE_EINVAL, "int8 activations need x_scales");
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    if (xf->xrow) {
+    if (xf->outliers) {
         cudaError_t e = cudaMemcpyAsync(xf->xrow, x, (size_t)xf->f.M * xf->f.K * sizeof(float), cudaMemcpyDeviceToDevice, st);
         if (e != cudaSuccess) return fail(ctx, CHPE_ECUDA, "xfrag copy: %s", cudaGetErrorString(e));
         xf->f.xrow = xf->xrow;
@@ -944,9 +948,55 @@ extern "C" int chpe_xfrag_fill_dev(chpe_ctx *ctx, chpe_xfrag *xf, const void *x,
     return prep_x(ctx, xf->f, x, x_scales, xf->sx, st);
 }
 
+extern "C" int chpe_xfrag_fill_op_dev(chpe_ctx *ctx, chpe_xfrag *xf, const chpe_xsrc *src, void *stream) {
+    if (!ctx || !xf || !src || !src->x) return fail(ctx, CHPE_EINVAL, "null argument");
+    if (src->op < CHPE_XOP_PLAIN || src->op > CHPE_XOP_SSM_STUB) return fail(ctx, CHPE_EINVAL, "unknown op %d", src->op);
+    const Xfrag &f = xf->f;
+    if (src->op == CHPE_XOP_PLAIN && src->x_dtype != f.x_dtype)
+        return fail(ctx, CHPE_EINVAL, "x_dtype %d does not match the fragments (%d)", src->x_dtype, f.x_dtype);
+    if (src->op != CHPE_XOP_PLAIN && f.x_dtype != CHPE_X_F32)
+        return fail(ctx, CHPE_EINVAL, "fused producers need fragments created for fp32 activations");
+    if (src->op != CHPE_XOP_PLAIN && src->op != CHPE_XOP_ATTN_STUB && !src->aux)
+        return fail(ctx, CHPE_EINVAL, "op %d needs aux", src->op);
+    if (src->op == CHPE_XOP_ATTN_STUB &&
+        (src->kv_dim < 1 || (src->head_dim && (src->group < 1 ||
+                                               ((f.K / src->head_dim + src->group - 1) / src->group) * src->head_dim >
+                                                   src->ldx))))
+        return fail(ctx, CHPE_EINVAL, "attention stand-in shape");
+    if (src->op == CHPE_XOP_SSM_STUB && src->qkv_dim < 1) return fail(ctx, CHPE_EINVAL, "qkv_dim must be >= 1");
+    XSrc s;
+    s.op = src->op;
+    s.x = src->x;
+    s.dt = src->x_dtype;
+    s.ldx = src->ldx > 0 ? src->ldx : f.K;
+    s.aux = src->aux;
+    s.ld_aux = src->ld_aux > 0 ? src->ld_aux : f.K;
+    s.eps = src->eps;
+    s.kv_dim = src->kv_dim;
+    s.head_dim = src->head_dim;
+    s.group = src->group;
+    s.qkv_dim = src->qkv_dim;
+    s.silu_on_qkv = src->silu_on_qkv;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    cudaError_t e = cudaSuccess;
+    if (xf->xrow) {
+        // fp32 rows needed (outliers / int8 quantization): produce them once, then fill from them
+        e = launch_xmaterialize(s, f.M, f.K, xf->xrow, st);
+        if (e != cudaSuccess) return fail(ctx, CHPE_ECUDA, "xfrag producer: %s", cudaGetErrorString(e));
+        xf->f.xrow = xf->xrow;
+        return prep_x(ctx, xf->f, xf->xrow, nullptr, xf->sx, st);
+    }
+    if (f.layout != kLayoutF16) return fail(ctx, CHPE_EINVAL, "fused fill of int8 fragments needs fp32 rows");
+    e = launch_xfill_f16(s, f.M, f.K, f.Kp, f.e_cols, f.xsplit, f.bits, f.xf, f.xs, st);
+    if (e != cudaSuccess) return fail(ctx, CHPE_ECUDA, "xfrag fill: %s", cudaGetErrorString(e));
+    return CHPE_OK;
+}
+
 extern "C" int chpe_gemv_xfrag_dev(chpe_ctx *ctx, const chpe_tensor *w, const chpe_xfrag *xf, float *y,
                                    int accumulate, void *stream) {
     if (!ctx || !w || !xf || !y) return fail(ctx, CHPE_EINVAL, "null argument");
+    if (w->m.out_cols && !xf->f.xrow)
+        return fail(ctx, CHPE_EINVAL, "tensor has outlier columns: create the fragments like it (fp32)");
     return gemv_core(ctx, w->m, nullptr, 0, xf->f, y, w->m.N, accumulate, nullptr, nullptr,
                      static_cast<cudaStream_t>(stream));
 }

@@ -136,6 +136,36 @@ __device__ __forceinline__ void grid_dependents_launch() {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
+// Start of every small kernel of the library: let the next kernel on the
+// stream be scheduled right away (its own wait holds it back until this grid
+// has finished), then wait for the previous grid's results before touching
+// global memory.  The next kernel thereby launches, and a GEMV starts
+// fetching weights, while this one runs.
+__device__ __forceinline__ void pdl_begin() {
+    grid_dependents_launch();
+    grid_dependency_wait();
+}
+
+// Launch with programmatic stream serialization (the kernel calls pdl_begin
+// or grid_dependency_wait before it reads or writes anything another kernel
+// produces or consumes).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                       Args &&...args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    note_launch();
+    return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+
 __device__ __forceinline__ float silu_f(float g) { return g / (1.0f + expf(-g)); }
 
 }  // namespace chpe

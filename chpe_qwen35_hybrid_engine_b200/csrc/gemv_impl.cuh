@@ -286,6 +286,9 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
         }
         *reinterpret_cast<uint4 *>(smem + kZeroSlot) = make_uint4(0u, 0u, 0u, 0u);
         fence_barrier_init();
+        // the next kernel on the stream may be scheduled now: it waits for
+        // this grid before it touches anything this grid reads or writes
+        grid_dependents_launch();
     }
     __syncthreads();
 
@@ -364,6 +367,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
         // the last partial to arrive (atomic count) sums all slots in slot
         // order; with rmode 1 gemv_reduce_kernel does, after this kernel.
         // Runs behind the MMA warps, off the streaming path.
+        grid_dependency_wait();  // y, the workspace and the counters belong to the previous grid until it ends
         Acc *ws = static_cast<Acc *>(p.ws);
         const int nq = kSG * 16 * M;  // (strip, row, token) entries of a segment
         const int nq4 = nq / 4;       // nq is a multiple of 64
@@ -647,7 +651,7 @@ __global__ void __launch_bounds__(128) gemv_reduce_kernel(const GemvParams p) {
     using Acc4 = typename V4::T;
     constexpr size_t kSlot = kSG * 16 * 8;
     __shared__ int s_total;
-    grid_dependency_wait();
+    pdl_begin();
     const int M = p.M;
     const int nq4 = kSG * 16 * M / 4;
     const int nq4_out = MODE == 1 ? nq4 / 2 : nq4;

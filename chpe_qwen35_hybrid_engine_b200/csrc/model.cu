@@ -15,6 +15,7 @@ namespace chpe {
 // src/engine.zig:567-580 embedToken: hidden[i] = int8 row[i] * scale.
 __global__ void embed_i8_kernel(const int8_t *__restrict__ table, float scale, int hidden, int vocab,
                                 const int *__restrict__ tokens, float *__restrict__ out, int *__restrict__ err) {
+    pdl_begin();
     const int m = blockIdx.y;
     const int tok = tokens[m];
     if (tok < 0 || tok >= vocab) {
@@ -30,6 +31,7 @@ __global__ void embed_i8_kernel(const int8_t *__restrict__ table, float scale, i
 // not the reference's lane order, so the last bits may differ).
 __global__ void rmsnorm_kernel(const float *__restrict__ x, const float *__restrict__ gamma, int n, float eps,
                                float *__restrict__ y) {
+    pdl_begin();
     __shared__ float red[32];
     const float *xr = x + (size_t)blockIdx.x * n;
     float *yr = y + (size_t)blockIdx.x * n;
@@ -56,6 +58,7 @@ __global__ void rmsnorm_kernel(const float *__restrict__ x, const float *__restr
 // kv head h / group (what attention over a single position returns).
 __global__ void mix_attn_kernel(const float *__restrict__ v, int kv_dim, int out_dim, int head_dim, int group,
                                 float *__restrict__ out) {
+    pdl_begin();
     const int m = blockIdx.y;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < out_dim; i += gridDim.x * blockDim.x) {
         const int src = head_dim ? ((i / head_dim) / group) * head_dim + (i % head_dim) : (i % kv_dim);
@@ -67,6 +70,7 @@ __global__ void mix_attn_kernel(const float *__restrict__ v, int kv_dim, int out
 // src/engine.zig:813 / :988 (batch 4 / 8): out[i] = silu(qkv[i]) * z[i].
 __global__ void mix_ssm_kernel(const float *__restrict__ qkv, int qkv_dim, const float *__restrict__ z, int z_dim,
                                int out_dim, int silu_on_qkv, float *__restrict__ out) {
+    pdl_begin();
     const int m = blockIdx.y;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < out_dim; i += gridDim.x * blockDim.x) {
         const float q = qkv[(size_t)m * qkv_dim + (i % qkv_dim)];
@@ -78,6 +82,7 @@ __global__ void mix_ssm_kernel(const float *__restrict__ qkv, int qkv_dim, const
 // src/kernels/neon.zig:705-712 siluMul.
 __global__ void silu_mul_kernel(const float *__restrict__ g, const float *__restrict__ u, size_t n,
                                 float *__restrict__ out) {
+    pdl_begin();
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
         out[i] = silu_f(g[i]) * u[i];
 }
@@ -86,6 +91,7 @@ __global__ void silu_mul_kernel(const float *__restrict__ g, const float *__rest
 // (NaN never wins).  One block per row.
 __global__ void argmax_kernel(const float *__restrict__ logits, int n, int *__restrict__ idx,
                               float *__restrict__ maxv) {
+    pdl_begin();
     __shared__ float sv[32];
     __shared__ int si[32];
     const float *r = logits + (size_t)blockIdx.x * n;
@@ -154,18 +160,15 @@ extern "C" int chpe_embed_i8_dev(chpe_ctx *ctx, const int8_t *table, float scale
                                  const int *tokens, int M, float *out, void *stream) {
     if (!ctx || !table || !tokens || !out || M < 1 || hidden < 1) return CHPE_EINVAL;
     dim3 grid(grid_for(hidden, 256) < 16 ? grid_for(hidden, 256) : 16, M);
-    note_launch();
-    embed_i8_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(table, scale, hidden, vocab, tokens, out,
-                                                                          chpe_ctx_error_word(ctx));
-    return launched(cudaGetLastError());
+    return launched(launch_pdl(embed_i8_kernel, grid, dim3(256), 0, static_cast<cudaStream_t>(stream), table, scale,
+                               hidden, vocab, tokens, out, chpe_ctx_error_word(ctx)));
 }
 
 extern "C" int chpe_rmsnorm_dev(chpe_ctx *ctx, const float *x, const float *gamma, int M, int n, float eps, float *y,
                                 void *stream) {
     if (!ctx || !x || !gamma || !y || M < 1 || n < 1) return CHPE_EINVAL;
-    note_launch();
-    rmsnorm_kernel<<<M, 512, 0, static_cast<cudaStream_t>(stream)>>>(x, gamma, n, eps, y);
-    return launched(cudaGetLastError());
+    return launched(launch_pdl(rmsnorm_kernel, dim3(M), dim3(512), 0, static_cast<cudaStream_t>(stream), x, gamma, n,
+                               eps, y));
 }
 
 extern "C" int chpe_mix_attn_stub_dev(chpe_ctx *ctx, const float *v, int kv_dim, int M, int out_dim, int head_dim,
@@ -173,32 +176,27 @@ extern "C" int chpe_mix_attn_stub_dev(chpe_ctx *ctx, const float *v, int kv_dim,
     if (!ctx || !v || !out || M < 1 || kv_dim < 1) return CHPE_EINVAL;
     if (head_dim && (group < 1 || ((out_dim / head_dim + group - 1) / group) * head_dim > kv_dim)) return CHPE_EINVAL;
     dim3 grid(grid_for(out_dim, 256) < 16 ? grid_for(out_dim, 256) : 16, M);
-    note_launch();
-    mix_attn_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(v, kv_dim, out_dim, head_dim, group, out);
-    return launched(cudaGetLastError());
+    return launched(launch_pdl(mix_attn_kernel, grid, dim3(256), 0, static_cast<cudaStream_t>(stream), v, kv_dim,
+                               out_dim, head_dim, group, out));
 }
 
 extern "C" int chpe_mix_ssm_stub_dev(chpe_ctx *ctx, const float *qkv, int qkv_dim, const float *z, int z_dim, int M,
                                      int out_dim, int silu_on_qkv, float *out, void *stream) {
     if (!ctx || !qkv || !z || !out || M < 1 || qkv_dim < 1 || out_dim > z_dim) return CHPE_EINVAL;
     dim3 grid(grid_for(out_dim, 256) < 16 ? grid_for(out_dim, 256) : 16, M);
-    note_launch();
-    mix_ssm_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(qkv, qkv_dim, z, z_dim, out_dim, silu_on_qkv,
-                                                                         out);
-    return launched(cudaGetLastError());
+    return launched(launch_pdl(mix_ssm_kernel, grid, dim3(256), 0, static_cast<cudaStream_t>(stream), qkv, qkv_dim, z,
+                               z_dim, out_dim, silu_on_qkv, out));
 }
 
 extern "C" int chpe_silu_mul_dev(chpe_ctx *ctx, const float *g, const float *u, size_t n, float *out, void *stream) {
     if (!ctx || !g || !u || !out) return CHPE_EINVAL;
-    note_launch();
-    silu_mul_kernel<<<grid_for(n, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(g, u, n, out);
-    return launched(cudaGetLastError());
+    return launched(launch_pdl(silu_mul_kernel, dim3(grid_for(n, 256)), dim3(256), 0,
+                               static_cast<cudaStream_t>(stream), g, u, n, out));
 }
 
 extern "C" int chpe_argmax_dev(chpe_ctx *ctx, const float *logits, int M, int n, int *idx, float *maxv,
                                void *stream) {
     if (!ctx || !logits || !idx || M < 1 || n < 1) return CHPE_EINVAL;
-    note_launch();
-    argmax_kernel<<<M, 1024, 0, static_cast<cudaStream_t>(stream)>>>(logits, n, idx, maxv);
-    return launched(cudaGetLastError());
+    return launched(launch_pdl(argmax_kernel, dim3(M), dim3(1024), 0, static_cast<cudaStream_t>(stream), logits, n, idx,
+                               maxv));
 }

@@ -1,6 +1,8 @@
 // prep.cu -- activation-fragment preparation, dynamic int8 activation
 // quantization, weight repacking into the strip layout, and the GPU
 // quantizers used to build device tensors from fp32 weights.
+#include <algorithm>
+
 #include "common.cuh"
 #include "internal.h"
 
@@ -21,57 +23,136 @@ __device__ __forceinline__ uint32_t pack_h2(__half a, __half b) {
     return *reinterpret_cast<uint32_t *>(&h);
 }
 
-// One block per E-column block, one warp per activation row (8 warps).
-// Lane l < E/4 converts fragment entry (k-step e*E/16 + l/4, t = l%4).
-// Fragments are stored as 16-byte units so a consumer fetches two k-steps
-// (or, for fp32 input, the hi and lo parts of one k-step) with one load:
+// Value k of activation row tok, as produced by the source op (XSrc):
+//   kXPlain     x[tok][k] (fp32 / bf16 / fp16)
+//   kXRmsnorm   x[tok][k] * inv_rms(tok) * gamma[k]      (src/kernels/neon.zig:673-702)
+//   kXSiluMul   silu(x[tok][k]) * aux[tok][k]            (src/kernels/neon.zig:705-712)
+//   kXAttnStub  x[tok][src(k)]: the attention stand-in of src/engine.zig:619-623
+//               (src = k % kv_dim), or head-aligned (query head h takes kv head h / group)
+//   kXSsmStub   the Gated-DeltaNet stand-in, q = x[tok][k % qkv_dim], z = aux[tok][k]:
+//               q * silu(z) (batch 1, src/engine.zig:651-654) or silu(q) * z (:813, :988)
+__device__ __forceinline__ float xsrc_value(const XSrc &s, int tok, int k, float inv) {
+    switch (s.op) {
+    case kXRmsnorm: {
+        const float v = static_cast<const float *>(s.x)[(size_t)tok * s.ldx + k];
+        return __fmul_rn(__fmul_rn(v, inv), s.aux[k]);
+    }
+    case kXSiluMul:
+        return silu_f(static_cast<const float *>(s.x)[(size_t)tok * s.ldx + k]) * s.aux[(size_t)tok * s.ld_aux + k];
+    case kXAttnStub: {
+        const int src = s.head_dim ? ((k / s.head_dim) / s.group) * s.head_dim + (k % s.head_dim) : (k % s.kv_dim);
+        return static_cast<const float *>(s.x)[(size_t)tok * s.ldx + src];
+    }
+    case kXSsmStub: {
+        const float q = static_cast<const float *>(s.x)[(size_t)tok * s.ldx + (k % s.qkv_dim)];
+        const float z = s.aux[(size_t)tok * s.ld_aux + k];
+        return s.silu_on_qkv ? silu_f(q) * z : q * silu_f(z);
+    }
+    default:
+        return load_x(s.x, s.dt, (size_t)tok * s.ldx + k);
+    }
+}
+
+// 1 / sqrt(mean(x^2) + eps) of row tok, summed in a fixed order (strided by
+// the block, then a shuffle tree and the warp partials in order), so every
+// block of the row gets the same value.  Whole block; red: 32 floats.
+__device__ float row_inv_rms(const XSrc &s, int tok, int K, float *red) {
+    const float *row = static_cast<const float *>(s.x) + (size_t)tok * s.ldx;
+    float acc = 0.0f;
+    for (int k = threadIdx.x; k < K; k += blockDim.x) acc = fmaf(row[k], row[k], acc);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
+    __syncthreads();
+    float tot = 0.0f;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) tot += red[w];
+    __syncthreads();
+    return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)K), s.eps)));
+}
+
+// Activation fragments of the fp16 GEMV path.  Grid (units / 256, M): one
+// thread per fragment unit u = 4 * s + t of row tok (k-step s, lane column
+// t), i.e. columns 16s + 2t + {0, 1, 8, 9}.  Fragments are stored as 16-byte
+// units so a consumer fetches two k-steps (or, for fp32 input, the hi and lo
+// parts of one k-step) with one load:
 //   split (fp32 x):  unit (s, m, t) = {hi(16s+2t..), hi(16s+2t+8..), lo(..), lo(..)}
 //   fp16/bf16 x:     unit (s/2, m, t) = {step 2u: ..., step 2u+1: ...}
 // `bits` selects the per-k-step power-of-two pre-scale that matches where the
 // GEMV kernel reads the codes (unpack_f16): 4-bit odd k-steps of a chunk /16,
-// 2-bit k-step j of a chunk / 4^(j%4), 8-bit none.  Block sums stay unscaled.
-__global__ void xprep_f16_kernel(const void *__restrict__ x, int dt, int M, int K, int E, int split, int bits,
-                                 uint2 *__restrict__ xf, float *__restrict__ xs) {
-    const int eb = blockIdx.x, tok = threadIdx.x >> 5, lane = threadIdx.x & 31;
+// 2-bit k-step j of a chunk / 4^(j%4), 8-bit none.  The sum of each E-column
+// block (what the zero-point term multiplies) is taken over the values the
+// MMA sees, unscaled, from the E/4 consecutive threads that hold the block.
+__global__ void __launch_bounds__(256) xfill_f16_kernel(const XSrc s, int M, int K, int Kp, int E, int split,
+                                                        int bits, uint2 *__restrict__ xf, float *__restrict__ xs) {
+    __shared__ float red[32];
+    pdl_begin();
+    const int tok = blockIdx.y;
+    const float inv = s.op == kXRmsnorm ? row_inv_rms(s, tok, K, red) : 1.0f;
+    const int u = blockIdx.x * blockDim.x + threadIdx.x;
+    const int nunits = Kp / 4;
     float part = 0.0f;
-    if (lane < E / 4 && tok < M) {
-        const int s = eb * (E / 16) + lane / 4, t = lane & 3;
+    if (u < nunits) {
+        const int st = u >> 2, t = u & 3;
         const int steps = (256 / bits) / 16;  // k-steps per chunk
-        const int j = s % steps;
+        const int j = st % steps;
         const int sh = bits == 4 ? 4 * (j & 1) : bits == 2 ? 2 * (j & 3) : 0;
         const float down = __int_as_float((127 - sh) << 23), up = __int_as_float((127 + sh) << 23);
-        const int kb = 16 * s + 2 * t;
+        const int kb = 16 * st + 2 * t;
         const int kk[4] = {kb, kb + 1, kb + 8, kb + 9};
         __half h[4], l[4];
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-            const float v = (kk[q] < K ? load_x(x, dt, (size_t)tok * K + kk[q]) : 0.0f) * down;
+            const float v = (kk[q] < K ? xsrc_value(s, tok, kk[q], inv) : 0.0f) * down;
             h[q] = __float2half_rn(v);
             l[q] = split ? __float2half_rn(v - __half2float(h[q])) : __float2half_rn(0.0f);
             part += (__half2float(h[q]) + __half2float(l[q])) * up;
         }
         const uint2 hv = make_uint2(pack_h2(h[0], h[1]), pack_h2(h[2], h[3]));
         if (split) {
-            const size_t u = ((size_t)s * M + tok) * 4 + t;
-            xf[2 * u] = hv;
-            xf[2 * u + 1] = make_uint2(pack_h2(l[0], l[1]), pack_h2(l[2], l[3]));
+            const size_t v = ((size_t)st * M + tok) * 4 + t;
+            xf[2 * v] = hv;
+            xf[2 * v + 1] = make_uint2(pack_h2(l[0], l[1]), pack_h2(l[2], l[3]));
         } else {
-            const size_t u = ((size_t)(s >> 1) * M + tok) * 4 + t;
-            xf[2 * u + (s & 1)] = hv;
+            const size_t v = ((size_t)(st >> 1) * M + tok) * 4 + t;
+            xf[2 * v + (st & 1)] = hv;
         }
     }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) part += __shfl_xor_sync(0xffffffffu, part, off);
-    if (lane == 0) xs[(size_t)eb * 8 + tok] = part;
+    // E/4 consecutive threads (8, 16 or 32, aligned) hold one E-column block
+    for (int off = E / 8; off > 0; off >>= 1) part += __shfl_xor_sync(0xffffffffu, part, off);
+    if (u < nunits && (u % (E / 4)) == 0) xs[(size_t)(u / (E / 4)) * 8 + tok] = part;
+}
+
+cudaError_t launch_xfill_f16(const XSrc &s, int M, int K, int Kp, int e_cols, bool xsplit, int bits, void *xf,
+                             float *xs, cudaStream_t st) {
+    const int nunits = Kp / 4;
+    return launch_pdl(xfill_f16_kernel, dim3((nunits + 255) / 256, M), dim3(256), 0, st, s, M, K, Kp, e_cols,
+                      xsplit ? 1 : 0, bits, static_cast<uint2 *>(xf), xs);
 }
 
 cudaError_t launch_xprep_f16(const void *x, int x_dtype, int M, int K, int Kp, int e_cols, bool xsplit, int bits,
                              void *xf, float *xs, cudaStream_t st) {
-    const int nblk = Kp / e_cols;
-    note_launch();
-    xprep_f16_kernel<<<nblk, 256, 0, st>>>(x, x_dtype, M, K, e_cols, xsplit ? 1 : 0, bits, static_cast<uint2 *>(xf),
-                                           xs);
-    return cudaGetLastError();
+    XSrc s;
+    s.op = kXPlain;
+    s.x = x;
+    s.dt = x_dtype;
+    s.ldx = K;
+    return launch_xfill_f16(s, M, K, Kp, e_cols, xsplit, bits, xf, xs, st);
+}
+
+// The source op's values as fp32 rows [M][K] (for the int8 path, which
+// quantizes them per row, and for the outlier columns' fp32 activations).
+__global__ void __launch_bounds__(256) xmaterialize_kernel(const XSrc s, int K, float *__restrict__ out) {
+    __shared__ float red[32];
+    pdl_begin();
+    const int tok = blockIdx.y;
+    const float inv = s.op == kXRmsnorm ? row_inv_rms(s, tok, K, red) : 1.0f;
+    for (int k = blockIdx.x * blockDim.x + threadIdx.x; k < K; k += gridDim.x * blockDim.x)
+        out[(size_t)tok * K + k] = xsrc_value(s, tok, k, inv);
+}
+
+cudaError_t launch_xmaterialize(const XSrc &s, int M, int K, float *out, cudaStream_t st) {
+    const int gx = std::min(64, (K + 255) / 256);
+    return launch_pdl(xmaterialize_kernel, dim3(gx, M), dim3(256), 0, st, s, K, out);
 }
 
 __device__ __forceinline__ uint32_t pack4_i8(const int8_t *p, int k, int K) {
@@ -86,6 +167,7 @@ __device__ __forceinline__ uint32_t pack4_i8(const int8_t *p, int k, int K) {
 
 // int8 activations [M][K] -> fragments [kstep32][M][4] uint2.
 __global__ void xprep_s8_kernel(const int8_t *__restrict__ xq, int M, int K, int nsteps, uint2 *__restrict__ xf) {
+    pdl_begin();
     const size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     const size_t total = (size_t)nsteps * M * 4;
     if (idx >= total) return;
@@ -100,9 +182,8 @@ __global__ void xprep_s8_kernel(const int8_t *__restrict__ xq, int M, int K, int
 cudaError_t launch_xprep_s8(const int8_t *xq, int M, int K, int Kp, void *xf, cudaStream_t st) {
     const int nsteps = Kp / 32;
     const size_t total = (size_t)nsteps * M * 4;
-    note_launch();
-    xprep_s8_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(xq, M, K, nsteps, static_cast<uint2 *>(xf));
-    return cudaGetLastError();
+    return launch_pdl(xprep_s8_kernel, dim3((unsigned)((total + 255) / 256)), dim3(256), 0, st, xq, M, K, nsteps,
+                      static_cast<uint2 *>(xf));
 }
 
 // Per-row dynamic int8 quantization, bit-exact with the reference
@@ -112,6 +193,7 @@ __global__ void act_quant_s8_kernel(const float *__restrict__ x, int M, int K, i
                                     float *__restrict__ scales, uint2 *__restrict__ xf) {
     __shared__ float red[32];
     __shared__ float s_inv;
+    pdl_begin();
     const int tok = blockIdx.x;
     const float *row = x + (size_t)tok * K;
     float m = 0.0f;
@@ -154,9 +236,8 @@ __global__ void act_quant_s8_kernel(const float *__restrict__ x, int M, int K, i
 
 cudaError_t launch_act_quant_s8(const float *x, int M, int K, int Kp, int8_t *q, float *scales, void *xf,
                                 cudaStream_t st) {
-    note_launch();
-    act_quant_s8_kernel<<<M, 256, 0, st>>>(x, M, K, Kp / 32, q, scales, static_cast<uint2 *>(xf));
-    return cudaGetLastError();
+    return launch_pdl(act_quant_s8_kernel, dim3(M), dim3(256), 0, st, x, M, K, Kp / 32, q, scales,
+                      static_cast<uint2 *>(xf));
 }
 
 // ---------------------------------------------------------------------------

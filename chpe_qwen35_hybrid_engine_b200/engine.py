@@ -266,6 +266,7 @@ class HybridEngine:
         self.embed_scale = 1.0
         self.head: Tensor | None = None
         self.graphs = {}
+        self.xfrags = {}           # (input, rows) -> XFrag
         self.allreduce = None      # set by tensor parallelism: fn(tensor) summing across ranks
         g, Mx = geom, max_rows
         f32 = dict(dtype=torch.float32, device=self.dev)
@@ -288,69 +289,84 @@ class HybridEngine:
         self.ctx._check(rc)
 
     # -- one step ----------------------------------------------------------------
+    def _xf(self, key: str, like: Tensor, M: int):
+        """Activation fragments for the GEMVs of one input (created once per
+        row count; filled once per step and read by every GEMV of that input)."""
+        k = (key, M)
+        if k not in self.xfrags:
+            self.xfrags[k] = self.ctx.xfrag(like, M, L.X_F32)
+        return self.xfrags[k]
+
     def step(self, M: int, stream=None):
-        """Run one step over rows 0..M-1 of buf["tokens"]; leaves logits, argmax, maxv."""
+        """Run one step over rows 0..M-1 of buf["tokens"]; leaves logits, argmax, maxv.
+
+        Each GEMV input is produced straight into the MMA operand layout by a
+        fused fill (RMSNorm, the token-mixer stand-ins, SiLU * mul), so the
+        normalised hidden state and the mixer outputs never reach memory; the
+        Q/K/V (or DeltaNet qkv/z) projections, and gate/up, share one fill."""
         import torch
         g, ctx, lib = self.geom, self.ctx, self.ctx.lib
         b = self.buf
         st = stream or torch.cuda.current_stream(self.dev)
         sp = _stream_ptr(st)
-        H, F = g.hidden, g.ffn
-        xdt = L.X_F32
+        H = g.hidden
 
-        def gemv(t: Tensor, x, y, acc=False):
-            self._check(lib.chpe_gemv_dev(ctx.ptr, t.handle, _dev_ptr(x), xdt, None, M, _dev_ptr(y), int(acc), sp))
+        def gemv(t: Tensor, xf, y, acc=False):
+            self._check(lib.chpe_gemv_xfrag_dev(ctx.ptr, t.handle, xf.handle, _dev_ptr(y), int(acc), sp))
 
-        def gemv_res(t: Tensor, x, hidden):
+        def fill(xf, op, x, aux=None, ldx=0, ld_aux=0, **kw):
+            ctx.xfrag_fill_op(xf, op, x, aux, ldx=ldx, ld_aux=ld_aux, stream=sp.value, **kw)
+
+        def gemv_res(t: Tensor, xf, hidden):
             """hidden += x . W^T (the residual add of the block); with tensor
             parallelism the shard's partial sum goes through the all-reduce first."""
             if self.allreduce is None:
-                gemv(t, x, hidden, acc=True)
+                gemv(t, xf, hidden, acc=True)
             else:
                 part = b["mix_out"][:M]
-                gemv(t, x, part)
+                gemv(t, xf, part)
                 self.allreduce(part)
                 hidden[:M].add_(part)
 
         self._check(lib.chpe_embed_i8_dev(ctx.ptr, _dev_ptr(self.embed), C.c_float(self.embed_scale), H, g.vocab,
                                           _dev_ptr(b["tokens"]), M, _dev_ptr(b["hidden"]), sp))
-        hid, norm = b["hidden"], b["norm"]
+        hid = b["hidden"]
         for l, lw in enumerate(self.layers):
-            self._check(lib.chpe_rmsnorm_dev(ctx.ptr, _dev_ptr(hid), _dev_ptr(lw.in_gamma), M, H, C.c_float(g.eps),
-                                             _dev_ptr(norm), sp))
             p = lw.proj
+            xin = self._xf("in", p["gate"], M)
+            fill(xin, L.XOP_RMSNORM, hid, lw.in_gamma, ldx=H, eps=g.eps)
             if "q" in p:  # full attention (GQA) block; stand-in mixer = V broadcast
                 q_out, k_out, v_out = b["a"], b["b"], b["c"]
                 kv = p["v"].rows
-                gemv(p["q"], norm, q_out)
-                gemv(p["k"], norm, k_out)
-                gemv(p["v"], norm, v_out)
-                self._check(lib.chpe_mix_attn_stub_dev(ctx.ptr, _dev_ptr(v_out), kv, M, p["o"].cols, g.head_dim,
-                                                       g.q_heads // g.kv_heads, _dev_ptr(b["mix"]), sp))
-                gemv_res(p["o"], b["mix"], hid)
+                gemv(p["q"], xin, q_out)
+                gemv(p["k"], xin, k_out)
+                gemv(p["v"], xin, v_out)
+                xo = self._xf("o", p["o"], M)
+                fill(xo, L.XOP_ATTN_STUB, v_out, ldx=kv, kv_dim=kv, head_dim=g.head_dim,
+                     group=g.q_heads // g.kv_heads)
+                gemv_res(p["o"], xo, hid)
             else:  # Gated DeltaNet block; stand-in mixer = qkv gated by z
                 qkv_out, z_out = b["a"], b["b"]
-                gemv(p["qkv"], norm, qkv_out)
-                gemv(p["z"], norm, z_out)
-                self._check(lib.chpe_mix_ssm_stub_dev(ctx.ptr, _dev_ptr(qkv_out), p["qkv"].rows, _dev_ptr(z_out),
-                                                      p["z"].rows, M, p["out"].cols, int(M > 1), _dev_ptr(b["mix"]),
-                                                      sp))
-                gemv_res(p["out"], b["mix"], hid)
-            self._check(lib.chpe_rmsnorm_dev(ctx.ptr, _dev_ptr(hid), _dev_ptr(lw.post_gamma), M, H,
-                                             C.c_float(g.eps), _dev_ptr(norm), sp))
+                gemv(p["qkv"], xin, qkv_out)
+                gemv(p["z"], xin, z_out)
+                xo = self._xf("out", p["out"], M)
+                fill(xo, L.XOP_SSM_STUB, qkv_out, z_out, ldx=p["qkv"].rows, ld_aux=p["z"].rows,
+                     qkv_dim=p["qkv"].rows, silu_on_qkv=M > 1)
+                gemv_res(p["out"], xo, hid)
+            fill(xin, L.XOP_RMSNORM, hid, lw.post_gamma, ldx=H, eps=g.eps)
+            xd = self._xf("down", p["down"], M)
             if M == 1:  # src/engine.zig:682 fused gate/up SwiGLU
-                self._check(lib.chpe_gemv_gateup_swiglu_dev(ctx.ptr, p["gate"].handle, p["up"].handle,
-                                                            _dev_ptr(norm), xdt, None, M, _dev_ptr(b["a"]), sp))
+                self._check(lib.chpe_gemv_gateup_swiglu_xfrag_dev(ctx.ptr, p["gate"].handle, p["up"].handle,
+                                                                  xin.handle, _dev_ptr(b["a"]), sp))
+                fill(xd, L.XOP_PLAIN, b["a"], ldx=p["down"].cols)
             else:  # src/engine.zig:839-844 unfused gate, up, siluMul
-                gemv(p["gate"], norm, b["b"])
-                gemv(p["up"], norm, b["c"])
-                self._check(lib.chpe_silu_mul_dev(ctx.ptr, _dev_ptr(b["b"]), _dev_ptr(b["c"]), M * p["gate"].rows,
-                                                  _dev_ptr(b["a"]), sp))
-                # rows are [M][ffn_shard] contiguous in b/c: silu_mul ran on the first M*rows elements
-            gemv_res(p["down"], b["a"], hid)
-        self._check(lib.chpe_rmsnorm_dev(ctx.ptr, _dev_ptr(hid), _dev_ptr(self.final_gamma), M, H, C.c_float(g.eps),
-                                         _dev_ptr(norm), sp))
-        gemv(self.head, norm, b["logits"])
+                gemv(p["gate"], xin, b["b"])
+                gemv(p["up"], xin, b["c"])
+                fill(xd, L.XOP_SILU_MUL, b["b"], b["c"], ldx=p["gate"].rows, ld_aux=p["up"].rows)
+            gemv_res(p["down"], xd, hid)
+        xin = self._xf("in", self.layers[0].proj["gate"], M) if self.layers else self._xf("in", self.head, M)
+        fill(xin, L.XOP_RMSNORM, hid, self.final_gamma, ldx=H, eps=g.eps)
+        gemv(self.head, xin, b["logits"])
         self._check(lib.chpe_argmax_dev(ctx.ptr, _dev_ptr(b["logits"]), M, self.head.rows, _dev_ptr(b["argmax"]),
                                         _dev_ptr(b["maxv"]), sp))
 

@@ -203,6 +203,14 @@ class Context:
         self._check(self.lib.chpe_xfrag_fill_dev(self.ptr, xf.handle, _dev_ptr(x), _dev_ptr(x_scales),
                                                  _stream_ptr(stream)))
 
+    def xfrag_fill_op(self, xf: "XFrag", op: int, x, aux=None, ldx: int = 0, ld_aux: int = 0, eps: float = 0.0,
+                      x_dtype: int = L.X_F32, kv_dim: int = 1, head_dim: int = 0, group: int = 1, qkv_dim: int = 1,
+                      silu_on_qkv: bool = False, stream=None):
+        """Fill fragments from a fused producer (chpe_xfrag_fill_op_dev; L.XOP_*)."""
+        s = L.chpe_xsrc(op, _dev_ptr(x), x_dtype, ldx, _dev_ptr(aux), ld_aux, eps, kv_dim, head_dim, group, qkv_dim,
+                        int(silu_on_qkv))
+        self._check(self.lib.chpe_xfrag_fill_op_dev(self.ptr, xf.handle, C.byref(s), _stream_ptr(stream)))
+
     def gemv_xfrag(self, w: Tensor, xf: "XFrag", out, accumulate: bool = False, stream=None):
         self._check(self.lib.chpe_gemv_xfrag_dev(self.ptr, w.handle, xf.handle, _dev_ptr(out), int(accumulate),
                                                  _stream_ptr(stream)))

@@ -175,6 +175,39 @@ int chpe_gemv_gateup_swiglu_xfrag_dev(chpe_ctx *ctx, const chpe_tensor *gate, co
                                       const chpe_xfrag *xf, float *mlp_out, void *stream);
 int chpe_xfrag_free(chpe_ctx *ctx, chpe_xfrag *xf);
 
+/* Fill fragments from one of the step's elementwise producers, fused into the
+ * fill (one kernel instead of producer + fill; the producer's output never
+ * reaches memory).  M rows of `cols` values (the fragment's K):
+ *   CHPE_XOP_PLAIN      x[m][k] of x_dtype (as chpe_xfrag_fill_dev)
+ *   CHPE_XOP_RMSNORM    x[m][k] * 1/sqrt(mean_k(x[m]^2) + eps) * aux[k]
+ *                       (rmsnorm, src/kernels/neon.zig:673-702; aux = gamma)
+ *   CHPE_XOP_SILU_MUL   silu(x[m][k]) * aux[m][k]  (siluMul, neon.zig:705-712)
+ *   CHPE_XOP_ATTN_STUB  x[m][k % kv_dim], or head-aligned with head_dim/group
+ *                       (full-attention stand-in, src/engine.zig:619-623)
+ *   CHPE_XOP_SSM_STUB   q = x[m][k % qkv_dim], z = aux[m][k]: q * silu(z), or
+ *                       silu(q) * z when silu_on_qkv (Gated-DeltaNet stand-in,
+ *                       src/engine.zig:651-654 / :813 / :988)
+ * Row strides ldx / ld_aux are in elements; every op other than PLAIN reads
+ * fp32.  No counterpart in the reference, whose engine materialises each
+ * producer's output before quantizing it for the next gemvParallel. */
+#define CHPE_XOP_PLAIN 0
+#define CHPE_XOP_RMSNORM 1
+#define CHPE_XOP_SILU_MUL 2
+#define CHPE_XOP_ATTN_STUB 3
+#define CHPE_XOP_SSM_STUB 4
+typedef struct chpe_xsrc {
+    int op;
+    const void *x;
+    int x_dtype; /* CHPE_XOP_PLAIN only */
+    int ldx;
+    const float *aux;
+    int ld_aux;
+    float eps;
+    int kv_dim, head_dim, group; /* CHPE_XOP_ATTN_STUB */
+    int qkv_dim, silu_on_qkv;    /* CHPE_XOP_SSM_STUB */
+} chpe_xsrc;
+int chpe_xfrag_fill_op_dev(chpe_ctx *ctx, chpe_xfrag *xf, const chpe_xsrc *src, void *stream);
+
 /* Dynamic per-row int8 activation quantization (device): for each of M rows of
  * length n: s = max|x|/127 (1 if max <= 1e-9), q = clamp(round_half_away(x/s))
  * -- src/kernels/neon.zig:644-670 quantizeActivationInt8, bit-exact. */

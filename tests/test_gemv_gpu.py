@@ -189,9 +189,10 @@ def test_fp32_x_every_row_count_and_split(ctx, bits, M):
     """fp32 activations at every row count: M <= 4 feeds each activation's two
     fp16 halves to adjacent MMA columns, M > 4 to two MMAs; M > 2 sums split-K
     partials in a second kernel.  K = 12288 forces several K-slices and
-    N = 520 leaves a ragged last strip group.  The fp32 split is exact up to
-    fp32 summation, so the bound is far tighter than the path's 1e-3.  Plain
-    GEMV, accumulate into y, and the fused gate/up SwiGLU."""
+    N = 520 leaves a ragged last strip group.  The fp32 split keeps ~22 bits
+    (less where a 2-bit pre-scale pushes the lo half into fp16 subnormals), so
+    the bound, 1e-4, is far tighter than the path's 1e-3.  Plain GEMV,
+    accumulate into y, and the fused gate/up SwiGLU."""
     torch = torch_mod()
     from chpe_qwen35_hybrid_engine_b200 import SCHEME_I8_GROUP_F16, SCHEME_U_GROUP_F16_ZERO
     rng = np.random.default_rng(bits * 100 + M)
@@ -211,14 +212,14 @@ def test_fp32_x_every_row_count_and_split(ctx, bits, M):
             refs.append(O.gemv_grouped(codes, s, z, 64, x, num_workers=8))
     xd = torch.from_numpy(x).cuda()
     y = ctx.gemv(tens[0], xd)
-    assert rel_l2(y.cpu().numpy(), refs[0]) < 1e-5
+    assert rel_l2(y.cpu().numpy(), refs[0]) < 1e-4
     y0 = torch.from_numpy(rng.standard_normal((M, N)).astype(np.float32)).cuda()
     y1 = y0.clone()
     ctx.gemv(tens[0], xd, out=y1, accumulate=True)
-    assert rel_l2(y1.cpu().numpy(), y0.cpu().numpy() + refs[0]) < 1e-5
+    assert rel_l2(y1.cpu().numpy(), y0.cpu().numpy() + refs[0]) < 1e-4
     gu = ctx.gemv_gateup_swiglu(tens[0], tens[1], xd).cpu().numpy()
     g, u = refs
-    assert rel_l2(gu, g / (1 + np.exp(-g)) * u) < 1e-5
+    assert rel_l2(gu, g / (1 + np.exp(-g)) * u) < 1e-4
     # deterministic
     assert torch.equal(ctx.gemv(tens[0], xd), y)
     for t in tens:
