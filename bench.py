@@ -165,10 +165,15 @@ def gemv_step_profile(ctx, eng, M, reps, dev):
     step, GEMV launches per step)."""
     import torch
     from chpe_qwen35_hybrid_engine_b200 import X_F32
-    singles, fused = [], []
+    singles, fused, multis = [], [], []
     for lw in eng.layers:
         p = lw.proj
-        singles += [p[n] for n in ("q", "k", "v", "o", "qkv", "z", "out") if n in p]
+        if "q" in p:
+            multis.append([p["q"], p["k"], p["v"]])
+            singles.append(p["o"])
+        else:
+            multis.append([p["qkv"], p["z"]])
+            singles.append(p["out"])
         if M == 1:
             fused.append((p["gate"], p["up"]))
         else:
@@ -185,12 +190,15 @@ def gemv_step_profile(ctx, eng, M, reps, dev):
             xfs[key] = xf
         return xfs[key]
 
-    rows = max([t.rows for t in singles] + [g.rows for g, _ in fused])
+    rows = max([t.rows for t in singles] + [g.rows for g, _ in fused] + [t.rows for m in multis for t in m])
     y = torch.empty(M, rows, device=dev)
+    ys = [torch.empty(M, rows, device=dev) for _ in range(4)]
     st = torch.cuda.Stream(dev)
     st.wait_stream(torch.cuda.current_stream(dev))
 
     def issue():
+        for m in multis:
+            ctx.gemv_multi_xfrag(m, xf_for(m[0]), ys[:len(m)], stream=st)
         for t in singles:
             ctx.gemv_xfrag(t, xf_for(t), y, stream=st)
         for g, u in fused:
@@ -210,7 +218,8 @@ def gemv_step_profile(ctx, eng, M, reps, dev):
         xf.free()
     nbytes = sum(t.device_bytes + M * t.cols * 4 + M * t.rows * 4 for t in singles)
     nbytes += sum(g.device_bytes + u.device_bytes + M * g.cols * 4 + M * g.rows * 4 for g, u in fused)
-    return ms, nbytes, len(singles) + len(fused)
+    nbytes += sum(sum(t.device_bytes + M * t.rows * 4 for t in m) + M * m[0].cols * 4 for m in multis)
+    return ms, nbytes, len(singles) + len(fused) + len(multis)
 
 
 def decode_line(eng, stepper, M, args, world, dev, label, profile=True):

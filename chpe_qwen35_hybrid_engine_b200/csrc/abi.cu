@@ -292,30 +292,51 @@ int prep_x(chpe_ctx *ctx, Xfrag &f, const void *x, const float *x_scales, float 
     return CHPE_OK;
 }
 
-int gemv_core(chpe_ctx *ctx, const DevMatrix &w0, const DevMatrix *w1, int mode, const Xfrag &f, float *y, int ldy,
-              int accumulate, const float *scale_override0, const float *scale_override1, cudaStream_t st) {
-    GemvPlan P;
-    plan_gemv(w0, f.M, mode, f.xsplit, &P);
+int check_frag(chpe_ctx *ctx, const DevMatrix &w0, const GemvPlan &P, const Xfrag &f) {
     if (w0.layout != f.layout || w0.K != f.K || w_kp(w0) > f.Kp ||
         (w0.layout == kLayoutF16 && (P.e_cols != f.e_cols || w0.bits != f.bits)))
         return fail(ctx, CHPE_EINVAL,
                     "activation fragments do not match this tensor (K %d/%d, Kp %d/%d, block %d/%d, bits %d/%d)", w0.K,
                     f.K, w_kp(w0), f.Kp, P.e_cols, f.e_cols, w0.bits, f.bits);
-    int rc = ensure_scratch(ctx, P, st);
-    if (rc) return rc;
-    GemvParams p;
+    return CHPE_OK;
+}
+
+void set_src(GemvSrc &g, const DevMatrix &m, const float *scale_override) {
+    g.codes = m.codes;
+    g.bias = m.bias;
+    g.out_cols = m.out_cols;
+    g.out_w = m.out_w;
+    g.scale = scale_override ? *scale_override : m.scale;
+    g.zc = m.zc;
+}
+
+// Kernel parameters of one launch over `n` concatenated plain sources (mode 0)
+// or a gate/up pair (mode 1, ms[0] = gate, ms[1] = up), writing ys[r] rows of
+// ldys[r] (mode 1: ys[0], ldys[0]).
+void fill_params(GemvParams &p, int mode, const DevMatrix *const *ms, int n, const float *const *ovr,
+                 float *const *ys, const int *ldys, int accumulate, const GemvPlan &P, const Xfrag &f, void *ws,
+                 unsigned *counters, int *err) {
     memset(&p, 0, sizeof p);
-    const DevMatrix *ws[2] = {&w0, w1 ? w1 : &w0};
-    const float *ovr[2] = {scale_override0, scale_override1};
-    for (int i = 0; i < 2; ++i) {
-        p.src[i].codes = ws[i]->codes;
-        p.src[i].bias = ws[i]->bias;
-        p.src[i].out_cols = ws[i]->out_cols;
-        p.src[i].out_w = ws[i]->out_w;
-        p.src[i].scale = ovr[i] ? *ovr[i] : ws[i]->scale;
-        p.src[i].zc = ws[i]->zc;
+    const DevMatrix &w0 = *ms[0];
+    for (int i = 0; i < kMaxSrc; ++i) set_src(p.src[i], *ms[i < n ? i : 0], ovr ? ovr[i < n ? i : 0] : nullptr);
+    p.nsrc = mode == 1 ? 1 : n;
+    int sg = 0;
+    for (int r = 0; r <= kMaxSrc; ++r) {
+        if (mode == 1 || r >= n) {
+            p.sg0[r] = r == 0 ? 0 : (r == p.nsrc ? P.n_sg : 0x7fffffff);
+            continue;
+        }
+        p.sg0[r] = sg;
+        p.nstr[r] = ms[r]->n_strips;
+        p.rows[r] = ms[r]->N;
+        p.ys[r] = ys[r];
+        p.ldys[r] = ldys[r];
+        sg += ceil_div(ms[r]->n_strips, kSG);
     }
-    if (w0.out_cols && !f.xrow) return fail(ctx, CHPE_EINVAL, "outlier columns need fp32 activations");
+    if (mode == 0) {
+        for (int r = n + 1; r <= kMaxSrc; ++r) p.sg0[r] = 0x7fffffff;
+        p.sg0[n] = P.n_sg;
+    }
     p.N = w0.N;
     p.K = w0.K;
     p.M = f.M;
@@ -331,14 +352,61 @@ int gemv_core(chpe_ctx *ctx, const DevMatrix &w0, const DevMatrix *w1, int mode,
     p.xs = f.xs;
     p.sx = f.sx;
     p.xrow = f.xrow;
-    p.y = y;
-    p.ldy = ldy;
+    p.y = ys[0];
+    p.ldy = ldys[0];
     p.accumulate = accumulate;
-    p.ws = ctx->scr.ws;
-    p.split_cnt = ctx->scr.counters;
+    p.ws = ws;
+    p.split_cnt = counters;
     p.maxp = P.maxp;
-    p.err = ctx->d_err;
+    p.err = err;
+}
+
+int gemv_core(chpe_ctx *ctx, const DevMatrix &w0, const DevMatrix *w1, int mode, const Xfrag &f, float *y, int ldy,
+              int accumulate, const float *scale_override0, const float *scale_override1, cudaStream_t st) {
+    GemvPlan P;
+    plan_gemv(w0, f.M, mode, f.xsplit, &P);
+    int rc = check_frag(ctx, w0, P, f);
+    if (rc) return rc;
+    if ((rc = ensure_scratch(ctx, P, st))) return rc;
+    if (w0.out_cols && !f.xrow) return fail(ctx, CHPE_EINVAL, "outlier columns need fp32 activations");
+    const DevMatrix *ms[2] = {&w0, w1 ? w1 : &w0};
+    const float *ovr[2] = {scale_override0, scale_override1};
+    GemvParams p;
+    fill_params(p, mode, ms, mode == 1 ? 2 : 1, ovr, &y, &ldy, accumulate, P, f, ctx->scr.ws, ctx->scr.counters,
+                ctx->d_err);
     cudaError_t e = launch_gemv(w0, w1, P, p, st);
+    if (e != cudaSuccess) return fail(ctx, CHPE_ECUDA, "gemv launch: %s", cudaGetErrorString(e));
+    return CHPE_OK;
+}
+
+// One launch over n <= kMaxSrc plain sources with the same K and format.
+int gemv_multi_core(chpe_ctx *ctx, const DevMatrix *const *ms, int n, const Xfrag &f, float *const *ys,
+                    cudaStream_t st) {
+    const DevMatrix &w0 = *ms[0];
+    int total_sg = 0;
+    for (int r = 0; r < n; ++r) {
+        const DevMatrix &m = *ms[r];
+        if (m.K != w0.K || m.bits != w0.bits || m.layout != w0.layout || m.meta_kind != w0.meta_kind ||
+            m.group != w0.group || m.zc != w0.zc || m.n_blocks != w0.n_blocks || m.block_bytes != w0.block_bytes ||
+            m.gshift != w0.gshift)
+            return fail(ctx, CHPE_EINVAL, "tensor %d: all tensors of one launch need the same K and format", r);
+        if (m.out_cols) return fail(ctx, CHPE_EINVAL, "tensor %d has outlier columns (not fused)", r);
+        total_sg += ceil_div(m.n_strips, kSG);
+    }
+    // plan over the concatenation: one matrix of total_sg full strip groups
+    DevMatrix cat = w0;
+    cat.n_strips = total_sg * kSG;
+    cat.N = cat.n_strips * kStripRows;
+    GemvPlan P;
+    plan_gemv(cat, f.M, 0, f.xsplit, &P);
+    int rc = check_frag(ctx, w0, P, f);
+    if (rc) return rc;
+    if ((rc = ensure_scratch(ctx, P, st))) return rc;
+    int ldys[kMaxSrc];
+    for (int r = 0; r < n; ++r) ldys[r] = ms[r]->N;
+    GemvParams p;
+    fill_params(p, 0, ms, n, nullptr, ys, ldys, 0, P, f, ctx->scr.ws, ctx->scr.counters, ctx->d_err);
+    cudaError_t e = launch_gemv(w0, nullptr, P, p, st);
     if (e != cudaSuccess) return fail(ctx, CHPE_ECUDA, "gemv launch: %s", cudaGetErrorString(e));
     return CHPE_OK;
 }
@@ -1001,6 +1069,18 @@ extern "C" int chpe_gemv_xfrag_dev(chpe_ctx *ctx, const chpe_tensor *w, const ch
                      static_cast<cudaStream_t>(stream));
 }
 
+extern "C" int chpe_gemv_multi_xfrag_dev(chpe_ctx *ctx, int n, const chpe_tensor *const *ws, const chpe_xfrag *xf,
+                                         float *const *ys, void *stream) {
+    if (!ctx || !ws || !xf || !ys) return fail(ctx, CHPE_EINVAL, "null argument");
+    if (n < 1 || n > kMaxSrc) return fail(ctx, CHPE_EINVAL, "1..%d tensors per launch (got %d)", kMaxSrc, n);
+    const DevMatrix *ms[kMaxSrc];
+    for (int r = 0; r < n; ++r) {
+        if (!ws[r] || !ys[r]) return fail(ctx, CHPE_EINVAL, "null tensor or output %d", r);
+        ms[r] = &ws[r]->m;
+    }
+    return gemv_multi_core(ctx, ms, n, xf->f, ys, static_cast<cudaStream_t>(stream));
+}
+
 extern "C" int chpe_gemv_gateup_swiglu_xfrag_dev(chpe_ctx *ctx, const chpe_tensor *gate, const chpe_tensor *up,
                                                  const chpe_xfrag *xf, float *mlp_out, void *stream) {
     if (!ctx || !gate || !up || !xf || !mlp_out) return fail(ctx, CHPE_EINVAL, "null argument");
@@ -1103,37 +1183,10 @@ extern "C" int chpe_gemv_noalloc_dev(chpe_ctx *ctx, const chpe_tensor *w, const 
     if (m.out_cols && !f.xrow) return fail(ctx, CHPE_EINVAL, "outlier columns need fp32 activations");
 
     GemvParams p;
-    memset(&p, 0, sizeof p);
-    for (int i = 0; i < 2; ++i) {
-        p.src[i].codes = m.codes;
-        p.src[i].bias = m.bias;
-        p.src[i].out_cols = m.out_cols;
-        p.src[i].out_w = m.out_w;
-        p.src[i].scale = m.scale;
-        p.src[i].zc = m.zc;
-    }
-    p.N = m.N;
-    p.K = m.K;
-    p.M = M;
-    p.n_strips = m.n_strips;
-    p.n_blocks = m.n_blocks;
-    p.block_bytes = m.block_bytes;
-    p.gshift = m.gshift;
-    p.meta_kind = m.meta_kind;
-    p.n_sg = P.n_sg;
-    p.n_ks = P.n_ks;
-    p.bpk = P.bpk;
-    p.maxp = P.maxp;
-    p.xf = f.xf;
-    p.xs = f.xs;
-    p.sx = f.sx;
-    p.xrow = f.xrow;
-    p.y = y;
-    p.ldy = m.N;
-    p.accumulate = 0;
-    p.ws = base + off_ws;
-    p.split_cnt = reinterpret_cast<unsigned *>(base);
-    p.err = ctx->d_err;
+    const DevMatrix *ms[1] = {&m};
+    int ldy = m.N;
+    fill_params(p, 0, ms, 1, nullptr, &y, &ldy, 0, P, f, base + off_ws, reinterpret_cast<unsigned *>(base),
+                ctx->d_err);
     e = launch_gemv(m, nullptr, P, p, st);
     if (e != cudaSuccess) return fail(ctx, CHPE_ECUDA, "gemv launch: %s", cudaGetErrorString(e));
     return CHPE_OK;

@@ -35,9 +35,6 @@ int plan_gemv(const DevMatrix &w, int M, int mode, bool xsplit, GemvPlan *plan) 
     P.mode = mode;
     P.xsplit = xsplit;
     P.xmode = !xsplit ? 0 : (M <= 4 ? 2 : 1);
-    // with more than two rows the partial sums are too large for one warp to
-    // sum at the end of a CTA's range: a second, fully parallel kernel does
-    P.rmode = M > 2 ? 1 : 0;
     P.e_cols = epilogue_cols(w);
     const int kc = chunk_cols(w.bits);
     const int ne = w.layout == kLayoutS8 ? 0 : kc / P.e_cols;
@@ -65,6 +62,12 @@ int plan_gemv(const DevMatrix &w, int M, int mode, bool xsplit, GemvPlan *plan) 
     gk = std::min<long>(gk, std::max<long>(1, (long)P.n_sg * bpk / 4));
     gk = std::max<long>(1, gk);
     P.n_ks = n_ks;
+    // Split-K partials are summed by a second, fully parallel kernel: with
+    // several K-slices, or more than two rows, the sums at the end of a CTA's
+    // range would keep its epilogue warp (and then its MMA warps) waiting on
+    // L2 round trips.  With one slice only the few strip groups cut by range
+    // boundaries have partials; the last CTA to arrive sums those.
+    P.rmode = (M > 2 || n_ks > 1) ? 1 : 0;
     P.bpk = bpk;
     P.grid = (int)(gk * n_ks);
     P.smem = smem;

@@ -37,13 +37,13 @@ namespace chpe {
 
 constexpr int kNW = 8;      // MMA warps per CTA (one chunk of each block)
 constexpr int kStages = 4;  // ring depth (blocks per strip)
-constexpr int kSG = 4;      // strips per strip group
 constexpr int kProducerWarp = kNW, kEpilogueWarp = kNW + 1;
 constexpr int kThreads = (kNW + 2) * 32;
 // activation fragments staged per CTA: small enough for two CTAs per SM at
-// M <= 2; with more rows the reduction buffers already limit a CTA to one SM,
-// which then stages as much of K as fits (fewer K-slices, fewer partials)
-constexpr int kXMaxBytes = 20 * 1024;
+// M <= 2 (2 x (74 KB ring + 28 KB + reduction buffers) <= 220 KB); with more
+// rows the reduction buffers already limit a CTA to one SM, which then stages
+// as much of K as fits (fewer K-slices, fewer partials)
+constexpr int kXMaxBytes = 28 * 1024;
 constexpr int kXMaxBytesWide = 100 * 1024;
 constexpr int kSmemBudget = 220 * 1024;
 static_assert(kNW == kChunksPerBlock, "one block per stage, one chunk per warp");
@@ -159,16 +159,32 @@ __device__ __forceinline__ void load_meta2(const uint8_t *gbase, int g, float zc
     }
 }
 
-// Strip i (0..kSG-1) of strip group sg, and the weight source it comes from:
-// plain GEMV -> strips 4sg..4sg+3 of source 0; gate/up -> strips 2sg, 2sg+1 of
-// source 0 (gate, i = 0, 1) and of source 1 (up, i = 2, 3).
-template <int MODE>
-__host__ __device__ __forceinline__ int strip_of(int sg, int i) {
-    return MODE == 1 ? 2 * sg + (i & 1) : kSG * sg + i;
-}
+// Source of strip i (0..kSG-1) of a strip group for the scale/zero constants:
+// gate/up take strips 2sg, 2sg+1 of source 0 (gate, i = 0, 1) and of source 1
+// (up, i = 2, 3); concatenated plain sources share one format.
 template <int MODE>
 __host__ __device__ __forceinline__ int source_of(int i) {
     return MODE == 1 ? (i >> 1) : 0;
+}
+
+// Strip i of strip group sg as (source, strip within that source's matrix),
+// and whether it exists: plain GEMV -> strips 4(sg - sg0[r]) .. +3 of source r
+// (the sources concatenated along N); gate/up -> as source_of.
+struct StripRef {
+    int r, strip;
+    bool valid;
+};
+template <int MODE>
+__device__ __forceinline__ StripRef strip_ref(const GemvParams &p, int sg, int i) {
+    if (MODE == 1) {
+        const int strip = 2 * sg + (i & 1);
+        return StripRef{i >> 1, strip, strip < p.n_strips};
+    }
+    int r = 0;
+#pragma unroll
+    for (int k = 1; k < kMaxSrc; ++k) r += sg >= p.sg0[k];
+    const int strip = kSG * (sg - p.sg0[r]) + i;
+    return StripRef{r, strip, strip < p.nstr[r]};
 }
 
 // Output (or, for gate/up, the SwiGLU of the gate and up outputs) of entry
@@ -179,11 +195,11 @@ template <int LAYOUT, int MODE, typename Acc>
 __device__ __forceinline__ void finalize_entry(const GemvParams &p, int sg, int q, Acc v, Acc v_up) {
     const int M = p.M;
     const int tok = q % M, ir = q / M, r = ir & 15, i = ir >> 4;
-    const int strip = strip_of<MODE>(sg, i);
-    const int row = strip * kStripRows + r;
-    if (strip >= p.n_strips || row >= p.N) return;
+    const StripRef ref = strip_ref<MODE>(p, sg, i);
+    const int row = ref.strip * kStripRows + r;
+    if (!ref.valid || row >= (MODE == 1 ? p.N : p.rows[ref.r])) return;
     if (MODE == 0) {
-        const GemvSrc &sr = p.src[0];
+        const GemvSrc &sr = p.src[ref.r];
         float out = LAYOUT == kLayoutS8 ? (float)v * (sr.scale * p.sx[tok]) : (float)v * kTwo24;
         if (sr.bias) out += sr.bias[row];
         if (sr.out_cols) {
@@ -195,7 +211,7 @@ __device__ __forceinline__ void finalize_entry(const GemvParams &p, int sg, int 
             }
             out += os;
         }
-        float *yp = p.y + (size_t)tok * p.ldy + row;
+        float *yp = p.ys[ref.r] + (size_t)tok * p.ldys[ref.r] + row;
         *yp = p.accumulate ? *yp + out : out;
     } else {
         float gv, uv;
@@ -323,17 +339,18 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
                 tag_unit[slot] = sg;
                 tag_blk[slot] = bi;
                 tag_flags[slot] = ((i == i0 || bi == 0) ? kFirst : 0) | ((i == i1 - 1 || bi == nb - 1) ? kLast : 0);
+                StripRef ref[kSG];
                 uint32_t tx = 0;
 #pragma unroll
-                for (int q = 0; q < kSG; ++q)
-                    if (strip_of<MODE>(sg, q) < p.n_strips) tx += (uint32_t)BB;
+                for (int q = 0; q < kSG; ++q) {
+                    ref[q] = strip_ref<MODE>(p, sg, q);
+                    if (ref[q].valid) tx += (uint32_t)BB;
+                }
                 mbar_arrive_expect_tx(&full[slot], tx);
 #pragma unroll
                 for (int q = 0; q < kSG; ++q) {
-                    const int strip = strip_of<MODE>(sg, q);
-                    if (strip >= p.n_strips) continue;
-                    const uint8_t *src =
-                        p.src[source_of<MODE>(q)].codes + ((size_t)strip * p.n_blocks + b0 + bi) * BB;
+                    if (!ref[q].valid) continue;
+                    const uint8_t *src = p.src[ref[q].r].codes + ((size_t)ref[q].strip * p.n_blocks + b0 + bi) * BB;
                     bulk_g2s_hint(smem + L.ring + ((size_t)slot * kSG + q) * BB, src, (uint32_t)BB, &full[slot], pol);
                 }
                 // weights first, then (once) the upstream-dependent activations

@@ -42,8 +42,21 @@ struct GemvSrc {
     float zc;
 };
 
+constexpr int kSG = 4;      // strips per strip group (the GEMV's unit along N)
+constexpr int kMaxSrc = 4;  // matrices one plain GEMV launch can cover
+
 struct GemvParams {
-    GemvSrc src[2];
+    GemvSrc src[kMaxSrc];  // gate/up: src[0] = gate, src[1] = up
+    // Plain GEMV: up to kMaxSrc matrices with the same K and format (read from
+    // the same activation fragments) concatenated along N, each starting on a
+    // strip-group boundary: strip group sg belongs to source r with
+    // sg0[r] <= sg < sg0[r + 1] (sg0[r] = INT_MAX past nsrc).
+    int nsrc;
+    int sg0[kMaxSrc + 1];
+    int nstr[kMaxSrc];   // strips of each source
+    int rows[kMaxSrc];   // outputs of each source
+    float *ys[kMaxSrc];  // y of each source, rows [M][ldys[r]]
+    int ldys[kMaxSrc];
     int N, K, M;
     int n_strips, n_blocks, block_bytes, gshift;
     int meta_kind;

@@ -314,6 +314,12 @@ class HybridEngine:
         def gemv(t: Tensor, xf, y, acc=False):
             self._check(lib.chpe_gemv_xfrag_dev(ctx.ptr, t.handle, xf.handle, _dev_ptr(y), int(acc), sp))
 
+        def multi(ts, xf, ys):
+            """One launch for the projections that read the same input."""
+            hs = (C.c_void_p * len(ts))(*[t.handle for t in ts])
+            yp = (C.c_void_p * len(ts))(*[y.data_ptr() for y in ys])
+            self._check(lib.chpe_gemv_multi_xfrag_dev(ctx.ptr, len(ts), hs, xf.handle, yp, sp))
+
         def fill(xf, op, x, aux=None, ldx=0, ld_aux=0, **kw):
             ctx.xfrag_fill_op(xf, op, x, aux, ldx=ldx, ld_aux=ld_aux, stream=sp.value, **kw)
 
@@ -338,17 +344,14 @@ class HybridEngine:
             if "q" in p:  # full attention (GQA) block; stand-in mixer = V broadcast
                 q_out, k_out, v_out = b["a"], b["b"], b["c"]
                 kv = p["v"].rows
-                gemv(p["q"], xin, q_out)
-                gemv(p["k"], xin, k_out)
-                gemv(p["v"], xin, v_out)
+                multi([p["q"], p["k"], p["v"]], xin, [q_out, k_out, v_out])
                 xo = self._xf("o", p["o"], M)
                 fill(xo, L.XOP_ATTN_STUB, v_out, ldx=kv, kv_dim=kv, head_dim=g.head_dim,
                      group=g.q_heads // g.kv_heads)
                 gemv_res(p["o"], xo, hid)
             else:  # Gated DeltaNet block; stand-in mixer = qkv gated by z
                 qkv_out, z_out = b["a"], b["b"]
-                gemv(p["qkv"], xin, qkv_out)
-                gemv(p["z"], xin, z_out)
+                multi([p["qkv"], p["z"]], xin, [qkv_out, z_out])
                 xo = self._xf("out", p["out"], M)
                 fill(xo, L.XOP_SSM_STUB, qkv_out, z_out, ldx=p["qkv"].rows, ld_aux=p["z"].rows,
                      qkv_dim=p["qkv"].rows, silu_on_qkv=M > 1)

@@ -216,6 +216,15 @@ class Context:
                                                  _stream_ptr(stream)))
         return out
 
+    def gemv_multi_xfrag(self, tensors, xf: "XFrag", outs, stream=None):
+        """outs[r] = x . tensors[r]^T for up to 4 tensors of the same cols and
+        format, in one launch (chpe_gemv_multi_xfrag_dev)."""
+        n = len(tensors)
+        hs = (C.c_void_p * n)(*[t.handle for t in tensors])
+        ys = (C.c_void_p * n)(*[_dev_ptr(o).value for o in outs])
+        self._check(self.lib.chpe_gemv_multi_xfrag_dev(self.ptr, n, hs, xf.handle, ys, _stream_ptr(stream)))
+        return outs
+
     def gemv_gateup_swiglu_xfrag(self, gate: Tensor, up: Tensor, xf: "XFrag", out, stream=None):
         self._check(self.lib.chpe_gemv_gateup_swiglu_xfrag_dev(self.ptr, gate.handle, up.handle, xf.handle,
                                                                _dev_ptr(out), _stream_ptr(stream)))

@@ -173,6 +173,12 @@ int chpe_gemv_xfrag_dev(chpe_ctx *ctx, const chpe_tensor *w, const chpe_xfrag *x
                         void *stream);
 int chpe_gemv_gateup_swiglu_xfrag_dev(chpe_ctx *ctx, const chpe_tensor *gate, const chpe_tensor *up,
                                       const chpe_xfrag *xf, float *mlp_out, void *stream);
+/* ys[r][M, rows_r] = x . W_r^T for n = 1..4 tensors of the same cols and format
+ * in ONE launch (the Q, K, V projections, src/engine.zig:615-617, or the
+ * Gated-DeltaNet in-projections, :641-642, which the reference runs as
+ * separate gemvParallel calls on the same quantized x). */
+int chpe_gemv_multi_xfrag_dev(chpe_ctx *ctx, int n, const chpe_tensor *const *ws, const chpe_xfrag *xf,
+                              float *const *ys, void *stream);
 int chpe_xfrag_free(chpe_ctx *ctx, chpe_xfrag *xf);
 
 /* Fill fragments from one of the step's elementwise producers, fused into the

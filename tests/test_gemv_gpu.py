@@ -333,3 +333,44 @@ def test_bad_arguments_return_errors(ctx):
                           np.ones((16, 2), np.float16), rows=16, cols=100, group=64)
     with pytest.raises(ChpeError):  # fp16 cells are not quantized
         ctx.gemv_tile_polymorphic(make_cell(16, 4, 128, b""), np.ones(128, np.float32), np.zeros(4, np.float32))
+
+
+@pytest.mark.parametrize("bits", [8, 4])
+@pytest.mark.parametrize("M", [1, 3, 8])
+def test_multi_source_launch(ctx, bits, M):
+    """Three tensors of the same cols and format (q/k/v-like, ragged row
+    counts) in one launch: each output matches the oracle, and matches its own
+    single-tensor GEMV to fp32 summation order."""
+    torch = torch_mod()
+    from chpe_qwen35_hybrid_engine_b200 import SCHEME_I8_GROUP_F16, SCHEME_U_GROUP_F16_ZERO, X_F32
+    rng = np.random.default_rng(bits + 10 * M)
+    K = 4096
+    tens, refs = [], []
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    for N in (520, 100, 1000):
+        w = rng.normal(0, 0.02, (N, K)).astype(np.float32)
+        if bits == 8:
+            codes, s = O.quantize_sym8(w, 32)
+            tens.append(ctx.upload_matrix(8, SCHEME_I8_GROUP_F16, codes, s, rows=N, cols=K, group=32))
+            refs.append(O.gemv_grouped(codes, s, None, 32, x, num_workers=8))
+        else:
+            codes, s, z = O.quantize_asym(w, 4, 64)
+            tens.append(ctx.upload_matrix(4, SCHEME_U_GROUP_F16_ZERO, pack_codes(codes, 4), s, z, rows=N, cols=K,
+                                          group=64))
+            refs.append(O.gemv_grouped(codes, s, z, 64, x, num_workers=8))
+    xd = torch.from_numpy(x).cuda()
+    xf = ctx.xfrag(tens[0], M, X_F32)
+    ctx.xfrag_fill(xf, xd)
+    outs = [torch.full((M, t.rows), float("nan"), device="cuda") for t in tens]
+    ctx.gemv_multi_xfrag(tens, xf, outs)
+    for t, o, ref in zip(tens, outs, refs):
+        got = o.cpu().numpy()
+        assert np.isfinite(got).all()
+        assert rel_l2(got, ref) < 1e-4
+        single = torch.empty_like(o)
+        ctx.gemv_xfrag(t, xf, single)
+        assert rel_l2(got, single.cpu().numpy()) < 1e-6
+    xf.free()
+    for t in tens:
+        t.free()
+
