@@ -82,7 +82,7 @@ __device__ __forceinline__ uint64_t l2_policy_evict_first() {
 
 // 1-D bulk copy global -> this CTA's shared memory, completing `bytes`
 // transaction bytes on `bar`.  dst/src 16-byte aligned, bytes % 16 == 0.
-// No cluster multicast is used anywhere in this library.
+// Every bulk copy in this library fills only the issuing CTA's own shared memory.
 __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
     asm volatile(
         "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
