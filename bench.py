@@ -508,6 +508,82 @@ def run_gemv(args, rank, world, local_rank):
     return line
 
 
+def run_prefill(args, rank, world, local_rank):
+    """Prefill dequant-GEMM: y[M, N] = x[M, K] . dequant(W)^T on tcgen05 (bf16
+    activations N(0,1), the GemvCase weight formats); metric TFLOP/s."""
+    import torch
+    from chpe_qwen35_hybrid_engine_b200 import Context
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    ctx = Context(local_rank)
+    c = GemvCase(args.bits, args.rows, args.cols, 1, "bf16")
+    N, K, M = c.N, c.K, args.batch
+    flops = 2.0 * M * N * K
+    cd = torch.from_numpy(c.codes).to(dev)
+    sd = torch.from_numpy(c.scales).to(dev)
+    zd = torch.from_numpy(c.zeros).to(dev) if c.zeros is not None else None
+    n_copies = args.copies or max(2, int(np.ceil(3 * L2_BYTES / c.weight_bytes)))
+    tens = [ctx.upload_matrix(c.bits, c.scheme, cd, sd, zd, rows=N, cols=K, group=c.group) for _ in range(n_copies)]
+    del cd, sd, zd
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(0)
+    xd = torch.randn(M, K, device=dev, generator=gen).to(torch.bfloat16)
+    yd = torch.empty(M, N, device=dev)
+    st = torch.cuda.Stream(dev)
+    st.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(st):
+        for i in range(args.warmup):
+            ctx.gemm_prefill(tens[i % n_copies], xd, out=yd, stream=st)
+    torch.cuda.synchronize(dev)
+    clk = ClockSampler(local_rank).start()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=st):
+        for i in range(args.steps):
+            ctx.gemm_prefill(tens[i % n_copies], xd, out=yd, stream=st)
+    graph.replay()
+    ms_step = timed_replays(graph.replay, 1, world, dev) / args.steps
+    del graph
+    # end to end: x from pinned host memory, y back to the host
+    xh = xd.cpu().pin_memory()
+    yh = torch.empty(M, N).pin_memory()
+    xd2 = torch.empty_like(xd)
+    rst = torch.cuda.current_stream(dev)
+    it = [0]
+
+    def e2e_step():
+        xd2.copy_(xh, non_blocking=True)
+        ctx.gemm_prefill(tens[it[0] % n_copies], xd2, out=yd, stream=rst)
+        yh.copy_(yd, non_blocking=True)
+        it[0] += 1
+
+    for _ in range(args.warmup):
+        e2e_step()
+    e2e_ms = timed_replays(e2e_step, args.steps, world, dev) / args.steps
+    clk.stop()
+    ctx.sync()
+    peaks = measured_peaks()
+    tflops = flops / (ms_step * 1e-3) / 1e12
+    peak = peaks["bf16_tflops"]
+    cfg = {"workload": "prefill", "bits": c.bits, "N": N, "K": K, "M": M, "group": c.group, "x": "bf16",
+           "l2": f"weights rotate over {n_copies} copies", "parallelism": f"replicas{world}"}
+    line = {
+        "metric": f"prefill dequant-GEMM TFLOP/s ({c.bits}-bit g{c.group}, M={M}, K={K}, N={N})",
+        "value": round(world * tflops, 2), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "fp16 tensor-core operands (bf16 x, dequantized weights), fp32 accumulate",
+        "data": "synthetic (seeded uniform codes, lognormal fp16 group scales, x N(0,1))", "config": cfg,
+        "roofline": {"bound": "tensor", "achieved": round(tflops, 1), "peak": peak, "unit": "TFLOP/s",
+                     "frac": round(tflops / peak, 4), "traffic": None, "peak_source": peaks["source"] + " (bf16 burst)",
+                     "kernel": "prefill_gemm_kernel (+ activation tile prep)", "flops_per_step": flops},
+        "e2e": {"value": round(world * flops / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
+                "h2d_bytes_per_step": int(M * K * 2), "d2h_bytes_per_step": int(M * N * 4)},
+        "gpu_launches": 2 * args.steps,
+        "clocks": clk.summary(),
+    }
+    ctx.close()
+    return line
+
+
 # ----------------------------------------------------------------------------
 # CPU baselines: the oracle's C restatement of the reference path, host cores
 # ----------------------------------------------------------------------------
@@ -604,7 +680,20 @@ def run_reference(args, rank, world, workload):
     if rank != 0:
         return None
     threads = os.cpu_count() or 1
-    if workload == "gemv":
+    if workload == "prefill":
+        # a bounded sample: 8 activation rows through the oracle, scaled to M rows
+        c = GemvCase(args.bits, args.rows, args.cols, 8, "bf16")
+        for _ in range(args.warmup):
+            cpu_gemv_seconds(c, threads, reps=1)
+        dt, _ = cpu_gemv_seconds(c, threads, reps=args.steps)
+        step = dt * args.batch / 8
+        flops = 2.0 * args.batch * c.N * c.K
+        value, unit, ms = round(flops / step / 1e12, 5), "TFLOP/s", step * 1e3
+        metric = f"prefill dequant-GEMM TFLOP/s ({c.bits}-bit g{c.group}, M={args.batch}, K={c.K}, N={c.N})"
+        sample = f"8 of {args.batch} activation rows per step through the C oracle (fp64 accumulation), scaled"
+        cfg = {"workload": "prefill", "bits": c.bits, "N": c.N, "K": c.K, "M": args.batch, "group": c.group, "x": "bf16"}
+        scaling = "weak"
+    elif workload == "gemv":
         c = GemvCase(args.bits, args.rows, args.cols, args.batch, args.x)
         for _ in range(args.warmup):
             cpu_gemv_seconds(c, threads, reps=1)
@@ -638,12 +727,12 @@ def main():
     ap.add_argument("--steps", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="decode_72b", choices=["decode_72b", "decode_9b", "gemv", "q8_gemv"])
+    ap.add_argument("--workload", default="decode_72b", choices=["decode_72b", "decode_9b", "gemv", "q8_gemv", "prefill"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--bits", type=int, default=8, choices=[8, 4, 2], help="gemv: code width")
     ap.add_argument("--rows", type=int, default=12288, help="gemv: N (output columns)")
     ap.add_argument("--cols", type=int, default=4096, help="gemv: K (reduction length)")
-    ap.add_argument("--batch", type=int, default=1, help="gemv: M (activation rows, 1..8)")
+    ap.add_argument("--batch", type=int, default=1, help="gemv: M (activation rows, 1..8); prefill: M")
     ap.add_argument("--x", default="f32", choices=["f32", "bf16"], help="gemv: activation dtype")
     ap.add_argument("--copies", type=int, default=0, help="gemv: weight copies to rotate (default: > 3x L2)")
     args = ap.parse_args()
@@ -671,6 +760,8 @@ def main():
                                 device_id=torch.device("cuda", local_rank))
     if args.workload == "gemv":
         line = run_gemv(args, rank, world, local_rank)
+    elif args.workload == "prefill":
+        line = run_prefill(args, rank, world, local_rank)
     else:
         line = run_decode(args, rank, world, local_rank, args.workload)
     if rank == 0:

@@ -73,6 +73,7 @@ SIGNATURES = {
     "chpe_gemv_xfrag_dev": (I, [P, P, P, P, I, P]),
     "chpe_gemv_gateup_swiglu_xfrag_dev": (I, [P, P, P, P, P, P]),
     "chpe_gemv_multi_xfrag_dev": (I, [P, I, P, P, P, P]),
+    "chpe_gemm_prefill_dev": (I, [P, P, P, I, I, P, I, I, P]),
     "chpe_xfrag_free": (I, [P, P]),
     "chpe_xfrag_fill_op_dev": (I, [P, P, C.POINTER(chpe_xsrc), P]),
     "chpe_gemv_parallel": (I, [P, P, F, P, F, SZ, SZ, P]),

@@ -32,6 +32,8 @@ struct chpe_ctx {
     float *d_out = nullptr;
     size_t d_out_bytes = 0;
     float *d_scales = nullptr;
+    void *prefill_xt = nullptr;  // activation tiles of the prefill GEMM
+    size_t prefill_xt_bytes = 0;
     std::unordered_map<const void *, chpe_tensor *> registry;
     std::vector<chpe_tensor *> owned;
 };
@@ -558,6 +560,7 @@ extern "C" int chpe_destroy(chpe_ctx *ctx) {
     cudaFree(ctx->d_out);
     cudaFree(ctx->d_scales);
     cudaFree(ctx->d_err);
+    cudaFree(ctx->prefill_xt);
     cudaStreamDestroy(ctx->stream);
     delete ctx;
     return CHPE_OK;
@@ -1067,6 +1070,27 @@ extern "C" int chpe_gemv_xfrag_dev(chpe_ctx *ctx, const chpe_tensor *w, const ch
         return fail(ctx, CHPE_EINVAL, "tensor has outlier columns: create the fragments like it (fp32)");
     return gemv_core(ctx, w->m, nullptr, 0, xf->f, y, w->m.N, accumulate, nullptr, nullptr,
                      static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int chpe_gemm_prefill_dev(chpe_ctx *ctx, const chpe_tensor *w, const void *x, int x_dtype, int M, float *y,
+                                     int ldy, int accumulate, void *stream) {
+    if (!ctx || !w || !x || !y) return fail(ctx, CHPE_EINVAL, "null argument");
+    if (M < 1) return fail(ctx, CHPE_EINVAL, "M must be >= 1");
+    const DevMatrix &m = w->m;
+    if (ldy < m.N) return fail(ctx, CHPE_EINVAL, "ldy %d < rows %d", ldy, m.N);
+    if (x_dtype != CHPE_X_F32 && x_dtype != CHPE_X_BF16 && x_dtype != CHPE_X_F16)
+        return fail(ctx, CHPE_EINVAL, "prefill activations are fp32, bf16 or fp16");
+    if (!prefill_supported(m))
+        return fail(ctx, CHPE_ENOTSUP, "prefill GEMM: %d-bit codes with this scale layout (group %d) not supported",
+                    m.bits, m.group);
+    if (m.out_cols) return fail(ctx, CHPE_ENOTSUP, "prefill GEMM: outlier columns not supported");
+    cudaSetDevice(ctx->device);
+    int rc = grow(ctx, &ctx->prefill_xt, &ctx->prefill_xt_bytes, prefill_xt_bytes(M, m.K));
+    if (rc) return rc;
+    cudaError_t e = launch_prefill(m, x, x_dtype, M, ctx->prefill_xt, y, ldy, accumulate, ctx->d_err,
+                                   static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return fail(ctx, CHPE_ECUDA, "prefill launch: %s", cudaGetErrorString(e));
+    return CHPE_OK;
 }
 
 extern "C" int chpe_gemv_multi_xfrag_dev(chpe_ctx *ctx, int n, const chpe_tensor *const *ws, const chpe_xfrag *xf,

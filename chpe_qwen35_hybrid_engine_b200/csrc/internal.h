@@ -139,6 +139,12 @@ cudaError_t launch_act_quant_s8(const float *x, int M, int K, int Kp, int8_t *q,
 cudaError_t launch_gemv(const DevMatrix &w0, const DevMatrix *w1, const GemvPlan &plan, const GemvParams &p,
                         cudaStream_t st);
 
+// Prefill dequant-GEMM (prefill.cu).
+size_t prefill_xt_bytes(int M, int K);
+bool prefill_supported(const DevMatrix &w);
+cudaError_t launch_prefill(const DevMatrix &w, const void *x, int x_dtype, int M, void *xt, float *y, int ldy,
+                           int accumulate, int *err, cudaStream_t st);
+
 // Repack row-major codes of `src_bits` bits each (LSB first inside a byte;
 // src_bits = 8 for one byte per code) into the code area of the strip layout
 // of `m`, XOR-ing each code with `xorv` (F16 layout only).

@@ -1,0 +1,504 @@
+// prefill.cu -- dequant-GEMM for prefill (M >= 64 activation rows) on the
+// 5th-generation tensor cores: y[M, N] = x[M, K] . dequant(W)[N, K]^T.
+//
+// One CTA computes a 128 (tokens) x 256 (weight rows) tile of y over all of K
+// in steps of 64 columns (a "k-block"):
+//   * warp 0, one lane: 1-D bulk copies (TMA engine, mbarrier transaction
+//     counts) of the activation tile and of the packed weight codes and group
+//     metadata of the k-block into a 3-stage input ring.  The weights are read
+//     straight from the decode path's strip layout (one copy of the weights in
+//     HBM): per strip of 16 rows, the 1 or 2 chunks of codes and the group
+//     metadata that cover the k-block.
+//   * warps 4..11 (two warpgroups): dequantize the k-block's 256 x 64 weights
+//     into fp16 in shared memory, in the UMMA canonical K-major layout with the
+//     128-byte swizzle, into a 2-stage ring.  A code becomes an exact fp16
+//     integer with one byte-permute / LOP3 against the bit pattern of 1024
+//     (0x6400), one HSUB2 removes 1024 + 128 (signed int8) or 1024 + zero, and
+//     one HMUL2 applies the group scale: w = fp16(q * s), a single rounding.
+//   * warp 1, one lane: tcgen05.mma.cta_group::1.kind::f16 (A = activations,
+//     B = weights, both fp16 from shared memory, fp32 accumulator of 128 x 256
+//     in tensor memory), 4 instructions of K = 16 per k-block; tcgen05.commit
+//     frees the input and weight stages when the MMAs that read them finish.
+//   * warps 4..11 again, after the last k-block: tcgen05.ld the accumulator
+//     (warp 4 + q reads TMEM lanes 32q..32q+31, columns 0..127; warp 8 + q the
+//     columns 128..255) and store fp32 rows of y.
+// Activations are converted once per call into fp16 tiles of 128 x 64 already
+// in the swizzled layout (prefill_xprep_kernel), so each k-block's A operand
+// is one contiguous 16 KB copy.  Every wait is bounded: on a timeout the
+// kernel records an error code, stops issuing, waits (bounded) for the work it
+// issued, frees its tensor memory and returns.
+#include <algorithm>
+
+#include "../../include/chpe_b200.h"
+#include "common.cuh"
+#include "internal.h"
+
+namespace chpe {
+namespace {
+
+constexpr int kPM = 128;          // tokens per tile (UMMA M, cta_group::1)
+constexpr int kPN = 256;          // weight rows per tile (UMMA N)
+constexpr int kPK = 64;           // columns per k-block (one 128-byte swizzle atom of fp16)
+constexpr int kInStages = 3;      // activation + packed-weight ring
+constexpr int kBStages = 2;       // dequantized weight ring
+constexpr int kPThreads = 384;    // 12 warps
+constexpr int kDeqWarp0 = 4;      // first dequant / epilogue warp
+constexpr int kDeqWarps = 8;
+constexpr int kStripsPerTile = kPN / kStripRows;  // 16
+constexpr uint32_t kATileBytes = kPM * kPK * 2;   // 16 KB
+constexpr uint32_t kBTileBytes = kPN * kPK * 2;   // 32 KB
+constexpr uint32_t kTmemCols = 256;
+
+enum PrefillErr : int { kPErrInFull = 21, kPErrInEmpty = 22, kPErrBFull = 23, kPErrBEmpty = 24, kPErrAcc = 25 };
+
+// Byte offset of element (row, k) (k < 64) inside a K-major, 128-byte
+// swizzled fp16 tile: 8-row atoms of 1024 B, 16-byte chunk index XOR row.
+__host__ __device__ __forceinline__ uint32_t swz_off(int row, int k) {
+    return (uint32_t)((row >> 3) * 1024 + (row & 7) * 128 + ((((k >> 3) ^ (row & 7)) & 7) << 4) + (k & 7) * 2);
+}
+
+// UMMA shared-memory descriptor of a K-major, 128-byte swizzled operand
+// (sm_100 format: start >> 4 in [0,14), LBO >> 4 in [16,30), SBO >> 4 in
+// [32,46), version 1 at bit 46, layout type 2 = SWIZZLE_128B in [61,64)).
+__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t smem_addr) {
+    uint64_t d = (uint64_t)((smem_addr >> 4) & 0x3FFFu);
+    d |= (uint64_t)1u << 16;     // leading byte offset: 16 B (unused by the swizzled K-major layout)
+    d |= (uint64_t)64u << 32;    // stride byte offset: 1024 B between 8-row atoms
+    d |= (uint64_t)1u << 46;     // descriptor version for sm_100
+    d |= (uint64_t)2u << 61;     // SWIZZLE_128B
+    return d;
+}
+
+// Instruction descriptor of kind::f16: fp32 accumulator, fp16 A and B, both
+// K-major, M = 128, N = 256.
+constexpr uint32_t kIdesc = (1u << 4) | ((uint32_t)(kPN >> 3) << 17) | ((uint32_t)(kPM >> 4) << 24);
+
+__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate)
+        : "memory");
+}
+
+// Arrive on `bar` once every tcgen05.mma issued so far by this thread is done.
+__device__ __forceinline__ void umma_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld16(uint32_t addr, uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+        : "r"(addr));
+}
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t *>(&h); }
+__device__ __forceinline__ __half2 bits_h2(uint32_t u) { return *reinterpret_cast<__half2 *>(&u); }
+
+struct PrefillParams {
+    const uint8_t *codes;  // strip layout
+    const uint16_t *xt;    // activation tiles [m_tile][k_block][128 x 64 swizzled fp16]
+    float *y;
+    int ldy, M, N, K;
+    int n_strips, n_blocks, block_bytes, bits, meta_kind, group, span;
+    int n_kb;              // k-blocks (ceil(K / 64))
+    int n_mt;              // activation tiles along M
+    float zc;              // constant zero-point (meta S16 with zero)
+    int accumulate;
+    int *err;
+};
+
+// Packed bytes of one strip for one k-block: codes then metadata.
+struct KbSlice {
+    uint32_t code_off, code_bytes, meta_off, meta_bytes;
+    int g_first, g_per;    // first group of the k-block inside the block's metadata; columns per group (<= 64: group)
+};
+
+__host__ __device__ inline KbSlice kb_slice(const PrefillParams &p, int kb) {
+    KbSlice s;
+    const int k0 = kb * kPK;
+    const int kin = k0 % p.span;            // column inside the block
+    const int kc = 256 / p.bits;            // columns per chunk
+    s.code_off = (uint32_t)(kin / kc) * kChunkBytes;
+    s.code_bytes = (uint32_t)(kPK / kc > 0 ? kPK / kc : 1) * kChunkBytes;  // 8-bit: 2 chunks, 4-bit: 1
+    const int mb = meta_bytes(p.meta_kind);
+    const int gpb_cols = p.group <= p.span ? p.group : p.span;  // columns per stored group
+    s.g_first = kin / gpb_cols;
+    const int ng = gpb_cols >= kPK ? 1 : kPK / gpb_cols;
+    s.g_per = gpb_cols;
+    s.meta_off = (uint32_t)kBlockCodeBytes + (uint32_t)(s.g_first * 16 * mb);
+    s.meta_bytes = (uint32_t)(ng * 16 * mb);
+    return s;
+}
+
+struct PSmem {
+    uint32_t in_full, in_empty, b_full, b_empty, acc, tmem_slot, in_ring, b_ring, total;
+    uint32_t pk_stride;  // bytes of packed weights per input stage (16 strips)
+};
+
+__host__ __device__ inline PSmem psmem(uint32_t strip_bytes) {
+    PSmem L;
+    L.in_full = 0;
+    L.in_empty = L.in_full + 8 * kInStages;
+    L.b_full = L.in_empty + 8 * kInStages;
+    L.b_empty = L.b_full + 8 * kBStages;
+    L.acc = L.b_empty + 8 * kBStages;
+    L.tmem_slot = L.acc + 8;
+    L.pk_stride = kStripsPerTile * strip_bytes;
+    // input stage: activation tile (1024-aligned for the swizzle) then packed weights
+    const uint32_t in_stage = (kATileBytes + L.pk_stride + 1023u) & ~1023u;
+    L.in_ring = 1024;
+    L.b_ring = L.in_ring + kInStages * in_stage;
+    L.total = L.b_ring + kBStages * kBTileBytes;
+    return L;
+}
+
+__host__ __device__ inline uint32_t in_stage_bytes(uint32_t strip_bytes) {
+    return (kATileBytes + kStripsPerTile * strip_bytes + 1023u) & ~1023u;
+}
+
+template <int BITS, int META>
+__global__ void __launch_bounds__(kPThreads, 1) prefill_gemm_kernel(const PrefillParams p) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    // the swizzle is a function of the address: align the working area to 1024 B
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int mt = blockIdx.x % p.n_mt, nt = blockIdx.x / p.n_mt;  // tiles sharing weights run together
+    const int m0 = mt * kPM, strip0 = nt * kStripsPerTile;
+
+    // staged bytes per strip: codes + metadata of one k-block
+    const KbSlice s0 = kb_slice(p, 0);
+    const uint32_t strip_bytes = s0.code_bytes + s0.meta_bytes;
+    const PSmem L = psmem(strip_bytes);
+    const uint32_t in_stage = in_stage_bytes(strip_bytes);
+    uint64_t *in_full = reinterpret_cast<uint64_t *>(smem + L.in_full);
+    uint64_t *in_empty = reinterpret_cast<uint64_t *>(smem + L.in_empty);
+    uint64_t *b_full = reinterpret_cast<uint64_t *>(smem + L.b_full);
+    uint64_t *b_empty = reinterpret_cast<uint64_t *>(smem + L.b_empty);
+    uint64_t *acc_bar = reinterpret_cast<uint64_t *>(smem + L.acc);
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + L.tmem_slot);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kInStages; ++s) {
+            mbar_init(&in_full[s], 1);
+            mbar_init(&in_empty[s], 1 + kDeqWarps);  // MMA commit + every dequant warp
+        }
+        for (int s = 0; s < kBStages; ++s) {
+            mbar_init(&b_full[s], kDeqWarps);
+            mbar_init(&b_empty[s], 1);
+        }
+        mbar_init(acc_bar, 1);
+        fence_barrier_init();
+        grid_dependents_launch();
+    }
+    if (warp == 1) {  // the whole warp allocates the accumulator's tensor memory
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(kTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_d = *tmem_slot;
+    const int n_kb = p.n_kb;
+
+    if (warp == 0) {
+        // ---------------- producer ----------------
+        if (lane == 0) {
+            const uint64_t pol = l2_policy_evict_first();
+            int kb = 0;
+            bool waited = false;
+            for (; kb < n_kb; ++kb) {
+                const int s = kb % kInStages, use = kb / kInStages;
+                if (use > 0 && !mbar_wait_bounded(&in_empty[s], (use - 1) & 1)) {
+                    atomicExch(p.err, kPErrInEmpty);
+                    break;
+                }
+                uint8_t *stage = smem + L.in_ring + s * in_stage;
+                const KbSlice ks = kb_slice(p, kb);
+                const int blk = (kb * kPK) / p.span;
+                int nvalid = 0;
+                for (int i = 0; i < kStripsPerTile; ++i) nvalid += (strip0 + i) < p.n_strips;
+                mbar_arrive_expect_tx(&in_full[s], kATileBytes + (uint32_t)nvalid * (ks.code_bytes + ks.meta_bytes));
+                for (int i = 0; i < kStripsPerTile; ++i) {
+                    const int strip = strip0 + i;
+                    if (strip >= p.n_strips) continue;
+                    const uint8_t *src = p.codes + ((size_t)strip * p.n_blocks + blk) * p.block_bytes;
+                    uint8_t *dst = stage + kATileBytes + i * strip_bytes;
+                    bulk_g2s_hint(dst, src + ks.code_off, ks.code_bytes, &in_full[s], pol);
+                    bulk_g2s_hint(dst + ks.code_bytes, src + ks.meta_off, ks.meta_bytes, &in_full[s], pol);
+                }
+                if (!waited) {  // the activation tiles come from the previous kernel
+                    grid_dependency_wait();
+                    waited = true;
+                }
+                bulk_g2s(stage, p.xt + ((size_t)mt * n_kb + kb) * (kPM * kPK), kATileBytes, &in_full[s]);
+            }
+            // every issued copy has landed before the CTA may leave
+            for (int s = 0; s < kInStages && s < kb; ++s) {
+                const int last = s + ((kb - 1 - s) / kInStages) * kInStages;
+                if (!mbar_wait_bounded(&in_full[s], (last / kInStages) & 1)) atomicExch(p.err, kPErrInFull);
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issue ----------------
+        if (lane == 0) {
+            int kb = 0;
+            bool ok = true;
+            for (; kb < n_kb && ok; ++kb) {
+                const int s = kb % kInStages, bs = kb % kBStages;
+                if (!mbar_wait_bounded(&in_full[s], (kb / kInStages) & 1)) {
+                    atomicExch(p.err, kPErrInFull);
+                    ok = false;
+                    break;
+                }
+                if (!mbar_wait_bounded(&b_full[bs], (kb / kBStages) & 1)) {
+                    atomicExch(p.err, kPErrBFull);
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t a_base = smem_u32(smem + L.in_ring + s * in_stage);
+                const uint32_t b_base = smem_u32(smem + L.b_ring + bs * kBTileBytes);
+#pragma unroll
+                for (int kk = 0; kk < kPK / 16; ++kk)
+                    umma_f16(tmem_d, umma_desc_sw128(a_base + kk * 32), umma_desc_sw128(b_base + kk * 32),
+                             (kb > 0 || kk > 0) ? 1u : 0u);
+                umma_commit(&in_empty[s]);  // activation stage free once these MMAs are done
+                umma_commit(&b_empty[bs]);  // and the dequantized weight stage
+            }
+            umma_commit(acc_bar);  // the accumulator is complete (or this CTA gave up)
+            // the MMAs issued read shared memory: they finish before the CTA leaves
+            if (!mbar_wait_bounded(acc_bar, 0)) atomicExch(p.err, kPErrAcc);
+        }
+    } else if (warp >= kDeqWarp0) {
+        // ---------------- dequant, then epilogue ----------------
+        const int dw = warp - kDeqWarp0;  // 0..7: strips 2dw, 2dw+1 of the tile
+        const int g = lane >> 2, t = lane & 3;
+        bool ok = true;
+        for (int kb = 0; kb < n_kb; ++kb) {
+            const int s = kb % kInStages, bs = kb % kBStages;
+            if (!__all_sync(0xffffffffu, mbar_wait_bounded(&in_full[s], (kb / kInStages) & 1))) {
+                if (lane == 0) atomicExch(p.err, kPErrInFull);
+                ok = false;
+                break;
+            }
+            if (kb >= kBStages && !__all_sync(0xffffffffu, mbar_wait_bounded(&b_empty[bs], ((kb / kBStages) - 1) & 1))) {
+                if (lane == 0) atomicExch(p.err, kPErrBEmpty);
+                ok = false;
+                break;
+            }
+            const uint8_t *pk = smem + L.in_ring + s * in_stage + kATileBytes;
+            uint8_t *bt = smem + L.b_ring + bs * kBTileBytes;
+#pragma unroll
+            for (int ii = 0; ii < 2; ++ii) {
+                const int i = 2 * dw + ii;  // strip in the tile
+                const uint8_t *sp = pk + i * strip_bytes;
+                const int nb = i * kStripRows;  // first weight row of the strip in the tile
+                if constexpr (BITS == 8) {
+                    // two chunks of 32 columns; group 32 = one scale per chunk and row
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        const uint4 wv = *reinterpret_cast<const uint4 *>(sp + h * kChunkBytes + lane * 16);
+                        const uint32_t w4[4] = {wv.x, wv.y, wv.z, wv.w};
+                        const __half *meta = reinterpret_cast<const __half *>(sp + 2 * kChunkBytes);
+                        const int gl = (h * 32) / s0.g_per;  // group of this chunk inside the staged metadata
+#pragma unroll
+                        for (int r = 0; r < 4; ++r) {
+                            const int row = g + 8 * (r & 1);
+                            const int c = 32 * h + 2 * t + 8 * (r >> 1);
+                            const __half sc = meta[gl * 16 + 2 * g + (r & 1)];  // rows g, g+8 side by side
+                            const __half2 s2 = __halves2half2(sc, sc);
+                            const __half2 off = __float2half2_rn(1152.0f);  // 1024 + 128: u = q + 128
+                            const __half2 lo = __hmul2(__hsub2(bits_h2(__byte_perm(w4[r], 0x64646464u, 0x4140)), off), s2);
+                            const __half2 hi = __hmul2(__hsub2(bits_h2(__byte_perm(w4[r], 0x64646464u, 0x4342)), off), s2);
+                            *reinterpret_cast<uint32_t *>(bt + swz_off(nb + row, c)) = h2_bits(lo);
+                            *reinterpret_cast<uint32_t *>(bt + swz_off(nb + row, c + 16)) = h2_bits(hi);
+                        }
+                    }
+                } else {
+                    // one chunk of 64 columns; nibble j -> column 16j + c, nibble j+4 -> 16j + c + 1
+                    const uint4 wv = *reinterpret_cast<const uint4 *>(sp + lane * 16);
+                    const uint32_t w4[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+                    for (int r = 0; r < 4; ++r) {
+                        const int row = g + 8 * (r & 1);
+                        const int c = 2 * t + 8 * (r >> 1);
+                        __half2 s2, z2;
+                        // group metadata stores rows g and g + 8 side by side
+                        const int mi = 2 * g + (r & 1);
+                        if constexpr (META == kMetaSZ16) {
+                            const __half2 sz = *reinterpret_cast<const __half2 *>(sp + kChunkBytes + mi * 4);
+                            s2 = __low2half2(sz);
+                            z2 = __hadd2(__high2half2(sz), __float2half2_rn(1024.0f));  // 1024 + z (exact: z < 1024)
+                        } else {
+                            const __half sc = *reinterpret_cast<const __half *>(sp + kChunkBytes + mi * 2);
+                            s2 = __halves2half2(sc, sc);
+                            z2 = __float2half2_rn(1024.0f + p.zc);
+                        }
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            const uint32_t e = ((w4[r] >> (4 * j)) & 0x000F000Fu) | 0x64006400u;  // (1024+c_a, 1024+c_b)
+                            const __half2 v = __hmul2(__hsub2(bits_h2(e), z2), s2);
+                            *reinterpret_cast<uint32_t *>(bt + swz_off(nb + row, 16 * j + c)) = h2_bits(v);
+                        }
+                    }
+                }
+            }
+            fence_async_smem();  // the generic-proxy stores become visible to the tensor cores
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(&b_full[bs]);
+                mbar_arrive(&in_empty[s]);
+            }
+        }
+        // ---------------- epilogue ----------------
+        if (ok && __all_sync(0xffffffffu, mbar_wait_bounded(acc_bar, 0))) {
+            tc_fence_after();
+            grid_dependency_wait();  // y may still be read by the previous kernel
+            const int q = dw & 3;           // TMEM lanes 32q..32q+31
+            const int c0 = (dw >> 2) * 128;  // columns 0..127 or 128..255
+            const int m = m0 + 32 * q + lane;
+#pragma unroll 1
+            for (int cc = 0; cc < 128; cc += 16) {
+                uint32_t v[16];
+                tmem_ld16(tmem_d + ((uint32_t)(32 * q) << 16) + (uint32_t)(c0 + cc), v);
+                tmem_ld_wait();
+                const int n = strip0 * kStripRows + c0 + cc;
+                if (m < p.M) {
+                    float *yr = p.y + (size_t)m * p.ldy + n;
+#pragma unroll
+                    for (int e = 0; e < 16; ++e) {
+                        if (n + e < p.N) {
+                            const float val = __uint_as_float(v[e]);
+                            yr[e] = p.accumulate ? yr[e] + val : val;
+                        }
+                    }
+                }
+            }
+        } else if (lane == 0 && ok) {
+            atomicExch(p.err, kPErrAcc);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_d), "r"(kTmemCols) : "memory");
+    }
+}
+
+// Activations [M][K] (fp32 / bf16 / fp16) -> fp16 tiles [m_tile][k_block] of
+// 128 x 64, K-major with the 128-byte swizzle; zero outside [M, K).  One
+// thread per 8 consecutive columns (one 16-byte chunk of the tile).
+__global__ void prefill_xprep_kernel(const void *__restrict__ x, int dt, int M, int K, int n_mt, int n_kb,
+                                     uint16_t *__restrict__ xt) {
+    pdl_begin();
+    const size_t total = (size_t)n_mt * kPM * n_kb * (kPK / 8);
+    for (size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+         idx += (size_t)gridDim.x * blockDim.x) {
+        const int ch = (int)(idx % (kPK / 8));
+        const size_t rest = idx / (kPK / 8);
+        const int kb = (int)(rest % n_kb);
+        const int m = (int)(rest / n_kb);
+        const int k0 = kb * kPK + ch * 8;
+        uint32_t h[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            float a = 0.0f, b = 0.0f;
+            const int ka = k0 + 2 * e;
+            if (m < M) {
+                const size_t base = (size_t)m * K;
+                if (ka < K) {
+                    a = dt == CHPE_X_F32 ? static_cast<const float *>(x)[base + ka]
+                        : dt == CHPE_X_BF16 ? __bfloat162float(static_cast<const __nv_bfloat16 *>(x)[base + ka])
+                                            : __half2float(static_cast<const __half *>(x)[base + ka]);
+                }
+                if (ka + 1 < K) {
+                    b = dt == CHPE_X_F32 ? static_cast<const float *>(x)[base + ka + 1]
+                        : dt == CHPE_X_BF16 ? __bfloat162float(static_cast<const __nv_bfloat16 *>(x)[base + ka + 1])
+                                            : __half2float(static_cast<const __half *>(x)[base + ka + 1]);
+                }
+            }
+            h[e] = h2_bits(__floats2half2_rn(a, b));
+        }
+        const int mt = m / kPM, r = m % kPM;
+        uint8_t *tile = reinterpret_cast<uint8_t *>(xt) + ((size_t)mt * n_kb + kb) * kATileBytes;
+        *reinterpret_cast<uint4 *>(tile + swz_off(r, ch * 8)) = make_uint4(h[0], h[1], h[2], h[3]);
+    }
+}
+
+template <int BITS, int META>
+cudaError_t launch_prefill_t(const PrefillParams &p, size_t smem, cudaStream_t st) {
+    auto kern = prefill_gemm_kernel<BITS, META>;
+    static bool attr_set = false;
+    if (!attr_set) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        attr_set = true;
+    }
+    const int n_nt = (p.n_strips + kStripsPerTile - 1) / kStripsPerTile;
+    return launch_pdl(kern, dim3((unsigned)(p.n_mt * n_nt)), dim3(kPThreads), smem, st, p);
+}
+
+}  // namespace
+
+// Scratch bytes for the activation tiles of an M x K prefill.
+size_t prefill_xt_bytes(int M, int K) {
+    const size_t n_mt = (size_t)(M + kPM - 1) / kPM, n_kb = (size_t)(K + kPK - 1) / kPK;
+    return n_mt * n_kb * kATileBytes;
+}
+
+// Whether the prefill kernel handles this weight format.
+bool prefill_supported(const DevMatrix &w) {
+    if (w.layout != kLayoutF16) return false;
+    if (w.bits == 8) return w.meta_kind == kMetaS16 && w.group == 32;
+    if (w.bits == 4) return (w.meta_kind == kMetaSZ16 || w.meta_kind == kMetaS16) && w.group >= 64 &&
+                            (w.group % 64) == 0;
+    return false;
+}
+
+cudaError_t launch_prefill(const DevMatrix &w, const void *x, int x_dtype, int M, void *xt, float *y, int ldy,
+                           int accumulate, int *err, cudaStream_t st) {
+    PrefillParams p;
+    p.codes = w.codes;
+    p.xt = static_cast<const uint16_t *>(xt);
+    p.y = y;
+    p.ldy = ldy;
+    p.M = M;
+    p.N = w.N;
+    p.K = w.K;
+    p.n_strips = w.n_strips;
+    p.n_blocks = w.n_blocks;
+    p.block_bytes = w.block_bytes;
+    p.bits = w.bits;
+    p.meta_kind = w.meta_kind;
+    p.group = w.group;
+    p.span = w.span;
+    p.n_kb = (w.K + kPK - 1) / kPK;
+    p.n_mt = (M + kPM - 1) / kPM;
+    p.zc = w.zc;
+    p.accumulate = accumulate;
+    p.err = err;
+    const size_t total = (size_t)p.n_mt * kPM * p.n_kb * (kPK / 8);
+    cudaError_t e = launch_pdl(prefill_xprep_kernel, dim3((unsigned)std::min<size_t>((total + 255) / 256, 148 * 16)),
+                               dim3(256), 0, st, x, x_dtype, M, w.K, p.n_mt, p.n_kb, static_cast<uint16_t *>(xt));
+    if (e != cudaSuccess) return e;
+    const KbSlice s0 = kb_slice(p, 0);
+    const size_t smem = psmem(s0.code_bytes + s0.meta_bytes).total + 1024;  // + alignment slack
+    if (w.bits == 8) return launch_prefill_t<8, kMetaS16>(p, smem, st);
+    if (w.meta_kind == kMetaSZ16) return launch_prefill_t<4, kMetaSZ16>(p, smem, st);
+    return launch_prefill_t<4, kMetaS16>(p, smem, st);
+}
+
+}  // namespace chpe

@@ -216,6 +216,20 @@ class Context:
                                                  _stream_ptr(stream)))
         return out
 
+    def gemm_prefill(self, w: Tensor, x, out=None, accumulate: bool = False, stream=None):
+        """y[M, rows] = x[M, cols] . W^T on the tensor cores (chpe_gemm_prefill_dev);
+        x is a CUDA tensor (fp32 / bf16 / fp16)."""
+        import torch
+        M = x.shape[0]
+        if out is None:
+            out = torch.empty((M, w.rows), dtype=torch.float32, device=x.device)
+        dt = {torch.float32: L.X_F32, torch.bfloat16: L.X_BF16, torch.float16: L.X_F16}[x.dtype]
+        if stream is None:
+            stream = torch.cuda.current_stream(x.device)
+        self._check(self.lib.chpe_gemm_prefill_dev(self.ptr, w.handle, _dev_ptr(x.contiguous()), dt, M, _dev_ptr(out),
+                                                   out.stride(0), int(accumulate), _stream_ptr(stream)))
+        return out
+
     def gemv_multi_xfrag(self, tensors, xf: "XFrag", outs, stream=None):
         """outs[r] = x . tensors[r]^T for up to 4 tensors of the same cols and
         format, in one launch (chpe_gemv_multi_xfrag_dev)."""

@@ -214,6 +214,22 @@ typedef struct chpe_xsrc {
 } chpe_xsrc;
 int chpe_xfrag_fill_op_dev(chpe_ctx *ctx, chpe_xfrag *xf, const chpe_xsrc *src, void *stream);
 
+/* Prefill dequant-GEMM on the 5th-generation tensor cores (tcgen05, fp32
+ * accumulation in tensor memory): y[M, rows] (+)= x[M, cols] . dequant(W)^T
+ * for any M >= 1 (efficient from M = 64 up; tiles of 128 rows).
+ *   x: CHPE_X_BF16 / F16 / F32 device rows [M][cols], converted once to fp16
+ *      (bf16 and fp16 exactly); W is dequantized in shared memory to fp16
+ *      w = fp16(q * s) or fp16((c - z) * s) and never written back to HBM
+ *   W: the same resident tensor the GEMVs use; 8-bit with an fp16 scale per
+ *      32 columns (CHPE_SCHEME_I8_GROUP_F16, group 32), or 4-bit with fp16
+ *      scale (+ zero) per 64k columns (U_GROUP_F16_ZERO / _CONST_ZERO);
+ *      other formats return CHPE_ENOTSUP
+ *   y: fp32 rows [M][ldy] (ldy >= rows); accumulate != 0 adds into y
+ * No counterpart in the reference, whose engine runs every prompt token
+ * through the batch-1 step (src/main.zig:175-195). */
+int chpe_gemm_prefill_dev(chpe_ctx *ctx, const chpe_tensor *w, const void *x, int x_dtype, int M, float *y,
+                          int ldy, int accumulate, void *stream);
+
 /* Dynamic per-row int8 activation quantization (device): for each of M rows of
  * length n: s = max|x|/127 (1 if max <= 1e-9), q = clamp(round_half_away(x/s))
  * -- src/kernels/neon.zig:644-670 quantizeActivationInt8, bit-exact. */
