@@ -3,12 +3,13 @@
 //
 // One CTA computes a 128 (tokens) x 256 (weight rows) tile of y over all of K
 // in steps of 64 columns (a "k-block"):
-//   * warp 0, one lane: 1-D bulk copies (TMA engine, mbarrier transaction
-//     counts) of the activation tile and of the packed weight codes and group
-//     metadata of the k-block into a 3-stage input ring.  The weights are read
-//     straight from the decode path's strip layout (one copy of the weights in
-//     HBM): per strip of 16 rows, the 1 or 2 chunks of codes and the group
-//     metadata that cover the k-block.
+//   * warp 0, one lane: three copies per k-block on the TMA engine (mbarrier
+//     transaction counts) into a 4-stage input ring: the activation tile (1-D
+//     bulk copy) and, through two 3-D tensor maps over the decode path's strip
+//     layout (bytes of a block x blocks x strips; one copy of the weights in
+//     HBM), the 1 or 2 chunks of codes and the group metadata that cover the
+//     k-block for all 16 strips of the tile (strips past the matrix read as
+//     zeros).
 //   * warps 4..11 (two warpgroups): dequantize the k-block's 256 x 64 weights
 //     into fp16 in shared memory, in the UMMA canonical K-major layout with the
 //     128-byte swizzle, into a 2-stage ring.  A code becomes an exact fp16
@@ -27,6 +28,8 @@
 // is one contiguous 16 KB copy.  Every wait is bounded: on a timeout the
 // kernel records an error code, stops issuing, waits (bounded) for the work it
 // issued, frees its tensor memory and returns.
+#include <cuda.h>  // CUtensorMap and its enums (the encoder is fetched at run time)
+
 #include <algorithm>
 
 #include "../../include/chpe_b200.h"
@@ -39,7 +42,7 @@ namespace {
 constexpr int kPM = 128;          // tokens per tile (UMMA M, cta_group::1)
 constexpr int kPN = 256;          // weight rows per tile (UMMA N)
 constexpr int kPK = 64;           // columns per k-block (one 128-byte swizzle atom of fp16)
-constexpr int kInStages = 3;      // activation + packed-weight ring
+constexpr int kInStages = 4;      // activation + packed-weight ring
 constexpr int kBStages = 2;       // dequantized weight ring
 constexpr int kPThreads = 384;    // 12 warps
 constexpr int kDeqWarp0 = 4;      // first dequant / epilogue warp
@@ -101,6 +104,15 @@ __device__ __forceinline__ void tmem_ld16(uint32_t addr, uint32_t (&v)[16]) {
 }
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// Tiled copy of a box of a 3-D tensor map into this CTA's shared memory.
+__device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, int x, int y, int z, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+        "[%5];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+        : "memory");
+}
+
 __device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t *>(&h); }
 __device__ __forceinline__ __half2 bits_h2(uint32_t u) { return *reinterpret_cast<__half2 *>(&u); }
 
@@ -145,6 +157,7 @@ struct PSmem {
     uint32_t pk_stride;  // bytes of packed weights per input stage (16 strips)
 };
 
+// Input stage: [activation tile 16 KB][codes: 16 strips x code_bytes][metadata: 16 strips x meta_bytes].
 __host__ __device__ inline PSmem psmem(uint32_t strip_bytes) {
     PSmem L;
     L.in_full = 0;
@@ -167,7 +180,9 @@ __host__ __device__ inline uint32_t in_stage_bytes(uint32_t strip_bytes) {
 }
 
 template <int BITS, int META>
-__global__ void __launch_bounds__(kPThreads, 1) prefill_gemm_kernel(const PrefillParams p) {
+__global__ void __launch_bounds__(kPThreads, 1)
+    prefill_gemm_kernel(const PrefillParams p, const __grid_constant__ CUtensorMap tm_codes,
+                        const __grid_constant__ CUtensorMap tm_meta) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // the swizzle is a function of the address: align the working area to 1024 B
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -215,7 +230,6 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_gemm_kernel(const Prefil
     if (warp == 0) {
         // ---------------- producer ----------------
         if (lane == 0) {
-            const uint64_t pol = l2_policy_evict_first();
             int kb = 0;
             bool waited = false;
             for (; kb < n_kb; ++kb) {
@@ -227,17 +241,11 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_gemm_kernel(const Prefil
                 uint8_t *stage = smem + L.in_ring + s * in_stage;
                 const KbSlice ks = kb_slice(p, kb);
                 const int blk = (kb * kPK) / p.span;
-                int nvalid = 0;
-                for (int i = 0; i < kStripsPerTile; ++i) nvalid += (strip0 + i) < p.n_strips;
-                mbar_arrive_expect_tx(&in_full[s], kATileBytes + (uint32_t)nvalid * (ks.code_bytes + ks.meta_bytes));
-                for (int i = 0; i < kStripsPerTile; ++i) {
-                    const int strip = strip0 + i;
-                    if (strip >= p.n_strips) continue;
-                    const uint8_t *src = p.codes + ((size_t)strip * p.n_blocks + blk) * p.block_bytes;
-                    uint8_t *dst = stage + kATileBytes + i * strip_bytes;
-                    bulk_g2s_hint(dst, src + ks.code_off, ks.code_bytes, &in_full[s], pol);
-                    bulk_g2s_hint(dst + ks.code_bytes, src + ks.meta_off, ks.meta_bytes, &in_full[s], pol);
-                }
+                // full boxes land even for strips past the matrix (zero-filled)
+                mbar_arrive_expect_tx(&in_full[s], kATileBytes + kStripsPerTile * (ks.code_bytes + ks.meta_bytes));
+                tma_load_3d(stage + kATileBytes, &tm_codes, (int)(ks.code_off / 4), blk, strip0, &in_full[s]);
+                tma_load_3d(stage + kATileBytes + kStripsPerTile * ks.code_bytes, &tm_meta, (int)(ks.meta_off / 4), blk,
+                            strip0, &in_full[s]);
                 if (!waited) {  // the activation tiles come from the previous kernel
                     grid_dependency_wait();
                     waited = true;
@@ -299,11 +307,13 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_gemm_kernel(const Prefil
                 break;
             }
             const uint8_t *pk = smem + L.in_ring + s * in_stage + kATileBytes;
+            const uint8_t *pm = pk + kStripsPerTile * s0.code_bytes;  // metadata of the 16 strips
             uint8_t *bt = smem + L.b_ring + bs * kBTileBytes;
 #pragma unroll
             for (int ii = 0; ii < 2; ++ii) {
                 const int i = 2 * dw + ii;  // strip in the tile
-                const uint8_t *sp = pk + i * strip_bytes;
+                const uint8_t *sp = pk + i * s0.code_bytes;       // codes of strip i
+                const uint8_t *mp = pm + i * s0.meta_bytes;       // its group metadata
                 const int nb = i * kStripRows;  // first weight row of the strip in the tile
                 if constexpr (BITS == 8) {
                     // two chunks of 32 columns; group 32 = one scale per chunk and row
@@ -311,7 +321,7 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_gemm_kernel(const Prefil
                     for (int h = 0; h < 2; ++h) {
                         const uint4 wv = *reinterpret_cast<const uint4 *>(sp + h * kChunkBytes + lane * 16);
                         const uint32_t w4[4] = {wv.x, wv.y, wv.z, wv.w};
-                        const __half *meta = reinterpret_cast<const __half *>(sp + 2 * kChunkBytes);
+                        const __half *meta = reinterpret_cast<const __half *>(mp);
                         const int gl = (h * 32) / s0.g_per;  // group of this chunk inside the staged metadata
 #pragma unroll
                         for (int r = 0; r < 4; ++r) {
@@ -338,11 +348,11 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_gemm_kernel(const Prefil
                         // group metadata stores rows g and g + 8 side by side
                         const int mi = 2 * g + (r & 1);
                         if constexpr (META == kMetaSZ16) {
-                            const __half2 sz = *reinterpret_cast<const __half2 *>(sp + kChunkBytes + mi * 4);
+                            const __half2 sz = *reinterpret_cast<const __half2 *>(mp + mi * 4);
                             s2 = __low2half2(sz);
                             z2 = __hadd2(__high2half2(sz), __float2half2_rn(1024.0f));  // 1024 + z (exact: z < 1024)
                         } else {
-                            const __half sc = *reinterpret_cast<const __half *>(sp + kChunkBytes + mi * 2);
+                            const __half sc = *reinterpret_cast<const __half *>(mp + mi * 2);
                             s2 = __halves2half2(sc, sc);
                             z2 = __float2half2_rn(1024.0f + p.zc);
                         }
@@ -438,6 +448,38 @@ __global__ void prefill_xprep_kernel(const void *__restrict__ x, int dt, int M, 
     }
 }
 
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_tiled() {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void *ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(ptr);
+        else
+            cudaGetLastError();
+    }
+    return fn;
+}
+
+// The strip layout as a 3-D tensor of 32-bit words: (word of a block) x
+// blocks x strips; the box is one word range of every block of 16 strips.
+bool make_strip_map(CUtensorMap *map, const PrefillParams &p, uint32_t box_bytes) {
+    EncodeTiledFn fn = encode_tiled();
+    if (!fn) return false;
+    const cuuint64_t dims[3] = {(cuuint64_t)(p.block_bytes / 4), (cuuint64_t)p.n_blocks, (cuuint64_t)p.n_strips};
+    const cuuint64_t strides[2] = {(cuuint64_t)p.block_bytes, (cuuint64_t)p.block_bytes * (cuuint64_t)p.n_blocks};
+    const cuuint32_t box[3] = {box_bytes / 4, 1, (cuuint32_t)kStripsPerTile};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, const_cast<uint8_t *>(p.codes), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 template <int BITS, int META>
 cudaError_t launch_prefill_t(const PrefillParams &p, size_t smem, cudaStream_t st) {
     auto kern = prefill_gemm_kernel<BITS, META>;
@@ -447,8 +489,12 @@ cudaError_t launch_prefill_t(const PrefillParams &p, size_t smem, cudaStream_t s
         if (e != cudaSuccess) return e;
         attr_set = true;
     }
+    const KbSlice s0 = kb_slice(p, 0);
+    CUtensorMap tm_codes, tm_meta;
+    if (!make_strip_map(&tm_codes, p, s0.code_bytes) || !make_strip_map(&tm_meta, p, s0.meta_bytes))
+        return cudaErrorInvalidValue;
     const int n_nt = (p.n_strips + kStripsPerTile - 1) / kStripsPerTile;
-    return launch_pdl(kern, dim3((unsigned)(p.n_mt * n_nt)), dim3(kPThreads), smem, st, p);
+    return launch_pdl(kern, dim3((unsigned)(p.n_mt * n_nt)), dim3(kPThreads), smem, st, p, tm_codes, tm_meta);
 }
 
 }  // namespace
