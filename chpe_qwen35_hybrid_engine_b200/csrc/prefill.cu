@@ -1,31 +1,36 @@
 // prefill.cu -- dequant-GEMM for prefill (M >= 64 activation rows) on the
 // 5th-generation tensor cores: y[M, N] = x[M, K] . dequant(W)[N, K]^T.
 //
-// One CTA computes a 128 (tokens) x 256 (weight rows) tile of y over all of K
-// in steps of 64 columns (a "k-block"):
+// One CTA computes a tile of 128 weight rows x 256 tokens of y over all of K
+// in steps of 64 columns (a "k-block").  The weights are the MMA's M side, so
+// each dequantized weight tile serves 256 tokens and the accumulator's TMEM
+// lanes are weight rows (the epilogue's stores are 128-byte rows of y):
 //   * warp 0, one lane: three copies per k-block on the TMA engine (mbarrier
-//     transaction counts) into a 4-stage input ring: the activation tile (1-D
-//     bulk copy) and, through two 3-D tensor maps over the decode path's strip
-//     layout (bytes of a block x blocks x strips; one copy of the weights in
-//     HBM), the 1 or 2 chunks of codes and the group metadata that cover the
-//     k-block for all 16 strips of the tile (strips past the matrix read as
-//     zeros).
-//   * warps 4..11 (two warpgroups): dequantize the k-block's 256 x 64 weights
-//     into fp16 in shared memory, in the UMMA canonical K-major layout with the
+//     transaction counts) into a 4-stage input ring: the activation tile
+//     (1-D bulk copy of 256 x 64 fp16) and, through two 3-D tensor maps over
+//     the decode path's strip layout (words of a block x blocks x strips; one
+//     copy of the weights in HBM), the 1 or 2 chunks of codes and the group
+//     metadata that cover the k-block for the tile's 8 strips (strips past the
+//     matrix read as zeros).
+//   * warps 4..11: warp 4 + i dequantizes strip i (16 weight rows x 64) into
+//     fp16 in shared memory, in the UMMA canonical K-major layout with the
 //     128-byte swizzle, into a 2-stage ring.  A code becomes an exact fp16
 //     integer with one byte-permute / LOP3 against the bit pattern of 1024
 //     (0x6400), one HSUB2 removes 1024 + 128 (signed int8) or 1024 + zero, and
 //     one HMUL2 applies the group scale: w = fp16(q * s), a single rounding.
-//   * warp 1, one lane: tcgen05.mma.cta_group::1.kind::f16 (A = activations,
-//     B = weights, both fp16 from shared memory, fp32 accumulator of 128 x 256
-//     in tensor memory), 4 instructions of K = 16 per k-block; tcgen05.commit
-//     frees the input and weight stages when the MMAs that read them finish.
+//     The strip layout keeps each lane's codes in MMA-fragment register order,
+//     which is exactly what stmatrix takes: one stmatrix.x4 writes a 16 x 16
+//     block of the tile.
+//   * warp 1, one lane: tcgen05.mma.cta_group::1.kind::f16 (A = weights,
+//     B = activations, both fp16 from shared memory, fp32 accumulator of
+//     128 x 256 in tensor memory), 4 instructions of K = 16 per k-block;
+//     tcgen05.commit frees the stages once the MMAs that read them finish.
 //   * warps 4..11 again, after the last k-block: tcgen05.ld the accumulator
-//     (warp 4 + q reads TMEM lanes 32q..32q+31, columns 0..127; warp 8 + q the
-//     columns 128..255) and store fp32 rows of y.
-// Activations are converted once per call into fp16 tiles of 128 x 64 already
-// in the swizzled layout (prefill_xprep_kernel), so each k-block's A operand
-// is one contiguous 16 KB copy.  Every wait is bounded: on a timeout the
+//     (warp 4 + q, and 8 + q, read TMEM lanes 32q..32q+31 = weight rows,
+//     token columns 0..127 and 128..255) and store fp32 into y.
+// Activations are converted once per call into fp16 tiles of 256 x 64 already
+// in the swizzled layout (prefill_xprep_kernel), so each k-block's B operand
+// is one contiguous 32 KB copy.  Every wait is bounded: on a timeout the
 // kernel records an error code, stops issuing, waits (bounded) for the work it
 // issued, frees its tensor memory and returns.
 #include <cuda.h>  // CUtensorMap and its enums (the encoder is fetched at run time)
@@ -39,18 +44,19 @@
 namespace chpe {
 namespace {
 
-constexpr int kPM = 128;          // tokens per tile (UMMA M, cta_group::1)
-constexpr int kPN = 256;          // weight rows per tile (UMMA N)
+constexpr int kPM = 128;          // weight rows per tile (UMMA M, cta_group::1)
+constexpr int kPN = 256;          // tokens per tile (UMMA N)
 constexpr int kPK = 64;           // columns per k-block (one 128-byte swizzle atom of fp16)
 constexpr int kInStages = 4;      // activation + packed-weight ring
-constexpr int kBStages = 2;       // dequantized weight ring
+constexpr int kWStages = 2;       // dequantized weight ring
 constexpr int kPThreads = 384;    // 12 warps
 constexpr int kDeqWarp0 = 4;      // first dequant / epilogue warp
 constexpr int kDeqWarps = 8;
-constexpr int kStripsPerTile = kPN / kStripRows;  // 16
-constexpr uint32_t kATileBytes = kPM * kPK * 2;   // 16 KB
-constexpr uint32_t kBTileBytes = kPN * kPK * 2;   // 32 KB
+constexpr int kStripsPerTile = kPM / kStripRows;  // 8
+constexpr uint32_t kWTileBytes = kPM * kPK * 2;   // 16 KB of fp16 weights
+constexpr uint32_t kXTileBytes = kPN * kPK * 2;   // 32 KB of fp16 activations
 constexpr uint32_t kTmemCols = 256;
+static_assert(kDeqWarps == kStripsPerTile, "one dequant warp per strip");
 
 enum PrefillErr : int { kPErrInFull = 21, kPErrInEmpty = 22, kPErrBFull = 23, kPErrBEmpty = 24, kPErrAcc = 25 };
 
@@ -73,7 +79,7 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t smem_addr) {
 }
 
 // Instruction descriptor of kind::f16: fp32 accumulator, fp16 A and B, both
-// K-major, M = 128, N = 256.
+// K-major, M = 128 (weight rows), N = 256 (tokens).
 constexpr uint32_t kIdesc = (1u << 4) | ((uint32_t)(kPN >> 3) << 17) | ((uint32_t)(kPM >> 4) << 24);
 
 __device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
@@ -113,17 +119,26 @@ __device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, i
         : "memory");
 }
 
+// Four 8 x 8 fp16 matrices from MMA-fragment registers to shared memory: lane
+// i gives the address of row i % 8 of matrix i / 8; register j of every lane
+// holds (row lane / 4, columns 2 (lane % 4), +1) of matrix j.
+__device__ __forceinline__ void stmatrix_x4(uint32_t addr, uint32_t r0, uint32_t r1, uint32_t r2, uint32_t r3) {
+    asm volatile("stmatrix.sync.aligned.m8n8.x4.shared.b16 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(r0), "r"(r1),
+                 "r"(r2), "r"(r3)
+                 : "memory");
+}
+
 __device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t *>(&h); }
 __device__ __forceinline__ __half2 bits_h2(uint32_t u) { return *reinterpret_cast<__half2 *>(&u); }
 
 struct PrefillParams {
     const uint8_t *codes;  // strip layout
-    const uint16_t *xt;    // activation tiles [m_tile][k_block][128 x 64 swizzled fp16]
+    const uint16_t *xt;    // activation tiles [token_tile][k_block][256 x 64 swizzled fp16]
     float *y;
     int ldy, M, N, K;
     int n_strips, n_blocks, block_bytes, bits, meta_kind, group, span;
     int n_kb;              // k-blocks (ceil(K / 64))
-    int n_mt;              // activation tiles along M
+    int n_tt;              // token tiles (256 tokens each)
     float zc;              // constant zero-point (meta S16 with zero)
     int accumulate;
     int *err;
@@ -153,30 +168,23 @@ __host__ __device__ inline KbSlice kb_slice(const PrefillParams &p, int kb) {
 }
 
 struct PSmem {
-    uint32_t in_full, in_empty, b_full, b_empty, acc, tmem_slot, in_ring, b_ring, total;
-    uint32_t pk_stride;  // bytes of packed weights per input stage (16 strips)
+    uint32_t in_full, in_empty, w_full, w_empty, acc, tmem_slot, in_ring, in_stage, w_ring, total;
 };
 
-// Input stage: [activation tile 16 KB][codes: 16 strips x code_bytes][metadata: 16 strips x meta_bytes].
-__host__ __device__ inline PSmem psmem(uint32_t strip_bytes) {
+// Input stage: [activation tile 32 KB][codes: 8 strips x code_bytes][metadata: 8 strips x meta_bytes].
+__host__ __device__ inline PSmem psmem(uint32_t code_bytes, uint32_t meta_bytes) {
     PSmem L;
     L.in_full = 0;
     L.in_empty = L.in_full + 8 * kInStages;
-    L.b_full = L.in_empty + 8 * kInStages;
-    L.b_empty = L.b_full + 8 * kBStages;
-    L.acc = L.b_empty + 8 * kBStages;
+    L.w_full = L.in_empty + 8 * kInStages;
+    L.w_empty = L.w_full + 8 * kWStages;
+    L.acc = L.w_empty + 8 * kWStages;
     L.tmem_slot = L.acc + 8;
-    L.pk_stride = kStripsPerTile * strip_bytes;
-    // input stage: activation tile (1024-aligned for the swizzle) then packed weights
-    const uint32_t in_stage = (kATileBytes + L.pk_stride + 1023u) & ~1023u;
-    L.in_ring = 1024;
-    L.b_ring = L.in_ring + kInStages * in_stage;
-    L.total = L.b_ring + kBStages * kBTileBytes;
+    L.in_stage = (kXTileBytes + kStripsPerTile * (code_bytes + meta_bytes) + 1023u) & ~1023u;
+    L.in_ring = 1024;  // stages 1024-aligned (the swizzle is a function of the address)
+    L.w_ring = L.in_ring + kInStages * L.in_stage;
+    L.total = L.w_ring + kWStages * kWTileBytes;
     return L;
-}
-
-__host__ __device__ inline uint32_t in_stage_bytes(uint32_t strip_bytes) {
-    return (kATileBytes + kStripsPerTile * strip_bytes + 1023u) & ~1023u;
 }
 
 template <int BITS, int META>
@@ -187,18 +195,15 @@ __global__ void __launch_bounds__(kPThreads, 1)
     // the swizzle is a function of the address: align the working area to 1024 B
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int mt = blockIdx.x % p.n_mt, nt = blockIdx.x / p.n_mt;  // tiles sharing weights run together
-    const int m0 = mt * kPM, strip0 = nt * kStripsPerTile;
+    const int tt = blockIdx.x % p.n_tt, wt = blockIdx.x / p.n_tt;  // tiles sharing weights run together
+    const int tok0 = tt * kPN, strip0 = wt * kStripsPerTile;
 
-    // staged bytes per strip: codes + metadata of one k-block
-    const KbSlice s0 = kb_slice(p, 0);
-    const uint32_t strip_bytes = s0.code_bytes + s0.meta_bytes;
-    const PSmem L = psmem(strip_bytes);
-    const uint32_t in_stage = in_stage_bytes(strip_bytes);
+    const KbSlice s0 = kb_slice(p, 0);  // sizes are the same for every k-block
+    const PSmem L = psmem(s0.code_bytes, s0.meta_bytes);
     uint64_t *in_full = reinterpret_cast<uint64_t *>(smem + L.in_full);
     uint64_t *in_empty = reinterpret_cast<uint64_t *>(smem + L.in_empty);
-    uint64_t *b_full = reinterpret_cast<uint64_t *>(smem + L.b_full);
-    uint64_t *b_empty = reinterpret_cast<uint64_t *>(smem + L.b_empty);
+    uint64_t *w_full = reinterpret_cast<uint64_t *>(smem + L.w_full);
+    uint64_t *w_empty = reinterpret_cast<uint64_t *>(smem + L.w_empty);
     uint64_t *acc_bar = reinterpret_cast<uint64_t *>(smem + L.acc);
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + L.tmem_slot);
 
@@ -207,9 +212,9 @@ __global__ void __launch_bounds__(kPThreads, 1)
             mbar_init(&in_full[s], 1);
             mbar_init(&in_empty[s], 1 + kDeqWarps);  // MMA commit + every dequant warp
         }
-        for (int s = 0; s < kBStages; ++s) {
-            mbar_init(&b_full[s], kDeqWarps);
-            mbar_init(&b_empty[s], 1);
+        for (int s = 0; s < kWStages; ++s) {
+            mbar_init(&w_full[s], kDeqWarps);
+            mbar_init(&w_empty[s], 1);
         }
         mbar_init(acc_bar, 1);
         fence_barrier_init();
@@ -238,19 +243,19 @@ __global__ void __launch_bounds__(kPThreads, 1)
                     atomicExch(p.err, kPErrInEmpty);
                     break;
                 }
-                uint8_t *stage = smem + L.in_ring + s * in_stage;
+                uint8_t *stage = smem + L.in_ring + s * L.in_stage;
                 const KbSlice ks = kb_slice(p, kb);
                 const int blk = (kb * kPK) / p.span;
                 // full boxes land even for strips past the matrix (zero-filled)
-                mbar_arrive_expect_tx(&in_full[s], kATileBytes + kStripsPerTile * (ks.code_bytes + ks.meta_bytes));
-                tma_load_3d(stage + kATileBytes, &tm_codes, (int)(ks.code_off / 4), blk, strip0, &in_full[s]);
-                tma_load_3d(stage + kATileBytes + kStripsPerTile * ks.code_bytes, &tm_meta, (int)(ks.meta_off / 4), blk,
-                            strip0, &in_full[s]);
+                mbar_arrive_expect_tx(&in_full[s], kXTileBytes + kStripsPerTile * (ks.code_bytes + ks.meta_bytes));
+                tma_load_3d(stage + kXTileBytes, &tm_codes, (int)(ks.code_off / 4), blk, strip0, &in_full[s]);
+                tma_load_3d(stage + kXTileBytes + kStripsPerTile * ks.code_bytes, &tm_meta, (int)(ks.meta_off / 4),
+                            blk, strip0, &in_full[s]);
                 if (!waited) {  // the activation tiles come from the previous kernel
                     grid_dependency_wait();
                     waited = true;
                 }
-                bulk_g2s(stage, p.xt + ((size_t)mt * n_kb + kb) * (kPM * kPK), kATileBytes, &in_full[s]);
+                bulk_g2s(stage, p.xt + ((size_t)tt * n_kb + kb) * (kPN * kPK), kXTileBytes, &in_full[s]);
             }
             // every issued copy has landed before the CTA may leave
             for (int s = 0; s < kInStages && s < kb; ++s) {
@@ -261,29 +266,25 @@ __global__ void __launch_bounds__(kPThreads, 1)
     } else if (warp == 1) {
         // ---------------- MMA issue ----------------
         if (lane == 0) {
-            int kb = 0;
-            bool ok = true;
-            for (; kb < n_kb && ok; ++kb) {
-                const int s = kb % kInStages, bs = kb % kBStages;
+            for (int kb = 0; kb < n_kb; ++kb) {
+                const int s = kb % kInStages, ws = kb % kWStages;
                 if (!mbar_wait_bounded(&in_full[s], (kb / kInStages) & 1)) {
                     atomicExch(p.err, kPErrInFull);
-                    ok = false;
                     break;
                 }
-                if (!mbar_wait_bounded(&b_full[bs], (kb / kBStages) & 1)) {
+                if (!mbar_wait_bounded(&w_full[ws], (kb / kWStages) & 1)) {
                     atomicExch(p.err, kPErrBFull);
-                    ok = false;
                     break;
                 }
                 tc_fence_after();
-                const uint32_t a_base = smem_u32(smem + L.in_ring + s * in_stage);
-                const uint32_t b_base = smem_u32(smem + L.b_ring + bs * kBTileBytes);
+                const uint32_t x_base = smem_u32(smem + L.in_ring + s * L.in_stage);
+                const uint32_t w_base = smem_u32(smem + L.w_ring + ws * kWTileBytes);
 #pragma unroll
                 for (int kk = 0; kk < kPK / 16; ++kk)
-                    umma_f16(tmem_d, umma_desc_sw128(a_base + kk * 32), umma_desc_sw128(b_base + kk * 32),
+                    umma_f16(tmem_d, umma_desc_sw128(w_base + kk * 32), umma_desc_sw128(x_base + kk * 32),
                              (kb > 0 || kk > 0) ? 1u : 0u);
                 umma_commit(&in_empty[s]);  // activation stage free once these MMAs are done
-                umma_commit(&b_empty[bs]);  // and the dequantized weight stage
+                umma_commit(&w_empty[ws]);  // and the dequantized weight stage
             }
             umma_commit(acc_bar);  // the accumulator is complete (or this CTA gave up)
             // the MMAs issued read shared memory: they finish before the CTA leaves
@@ -291,84 +292,86 @@ __global__ void __launch_bounds__(kPThreads, 1)
         }
     } else if (warp >= kDeqWarp0) {
         // ---------------- dequant, then epilogue ----------------
-        const int dw = warp - kDeqWarp0;  // 0..7: strips 2dw, 2dw+1 of the tile
+        const int dw = warp - kDeqWarp0;  // 0..7: strip dw of the tile, weight rows 16dw..16dw+15
         const int g = lane >> 2, t = lane & 3;
+        // stmatrix address of this lane inside a 16 x 16 block: row (lane % 8) + 8 ((lane / 8) & 1) of the
+        // strip, columns 8 (lane / 16) .. +7 of the k-step
+        const int st_row = 16 * dw + (lane & 7) + 8 * ((lane >> 3) & 1);
+        const int st_col = 8 * (lane >> 4);
         bool ok = true;
         for (int kb = 0; kb < n_kb; ++kb) {
-            const int s = kb % kInStages, bs = kb % kBStages;
+            const int s = kb % kInStages, ws = kb % kWStages;
             if (!__all_sync(0xffffffffu, mbar_wait_bounded(&in_full[s], (kb / kInStages) & 1))) {
                 if (lane == 0) atomicExch(p.err, kPErrInFull);
                 ok = false;
                 break;
             }
-            if (kb >= kBStages && !__all_sync(0xffffffffu, mbar_wait_bounded(&b_empty[bs], ((kb / kBStages) - 1) & 1))) {
+            if (kb >= kWStages &&
+                !__all_sync(0xffffffffu, mbar_wait_bounded(&w_empty[ws], ((kb / kWStages) - 1) & 1))) {
                 if (lane == 0) atomicExch(p.err, kPErrBEmpty);
                 ok = false;
                 break;
             }
-            const uint8_t *pk = smem + L.in_ring + s * in_stage + kATileBytes;
-            const uint8_t *pm = pk + kStripsPerTile * s0.code_bytes;  // metadata of the 16 strips
-            uint8_t *bt = smem + L.b_ring + bs * kBTileBytes;
+            const uint8_t *stage = smem + L.in_ring + s * L.in_stage;
+            const uint8_t *sp = stage + kXTileBytes + dw * s0.code_bytes;                                // codes
+            const uint8_t *mp = stage + kXTileBytes + kStripsPerTile * s0.code_bytes + dw * s0.meta_bytes;  // metadata
+            const uint32_t wt_base = smem_u32(smem + L.w_ring + ws * kWTileBytes);
+            if constexpr (BITS == 8) {
+                // two chunks of 32 columns (2 k-steps each); group 32 = one scale per chunk and row
 #pragma unroll
-            for (int ii = 0; ii < 2; ++ii) {
-                const int i = 2 * dw + ii;  // strip in the tile
-                const uint8_t *sp = pk + i * s0.code_bytes;       // codes of strip i
-                const uint8_t *mp = pm + i * s0.meta_bytes;       // its group metadata
-                const int nb = i * kStripRows;  // first weight row of the strip in the tile
-                if constexpr (BITS == 8) {
-                    // two chunks of 32 columns; group 32 = one scale per chunk and row
-#pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        const uint4 wv = *reinterpret_cast<const uint4 *>(sp + h * kChunkBytes + lane * 16);
-                        const uint32_t w4[4] = {wv.x, wv.y, wv.z, wv.w};
-                        const __half *meta = reinterpret_cast<const __half *>(mp);
-                        const int gl = (h * 32) / s0.g_per;  // group of this chunk inside the staged metadata
-#pragma unroll
-                        for (int r = 0; r < 4; ++r) {
-                            const int row = g + 8 * (r & 1);
-                            const int c = 32 * h + 2 * t + 8 * (r >> 1);
-                            const __half sc = meta[gl * 16 + 2 * g + (r & 1)];  // rows g, g+8 side by side
-                            const __half2 s2 = __halves2half2(sc, sc);
-                            const __half2 off = __float2half2_rn(1152.0f);  // 1024 + 128: u = q + 128
-                            const __half2 lo = __hmul2(__hsub2(bits_h2(__byte_perm(w4[r], 0x64646464u, 0x4140)), off), s2);
-                            const __half2 hi = __hmul2(__hsub2(bits_h2(__byte_perm(w4[r], 0x64646464u, 0x4342)), off), s2);
-                            *reinterpret_cast<uint32_t *>(bt + swz_off(nb + row, c)) = h2_bits(lo);
-                            *reinterpret_cast<uint32_t *>(bt + swz_off(nb + row, c + 16)) = h2_bits(hi);
-                        }
-                    }
-                } else {
-                    // one chunk of 64 columns; nibble j -> column 16j + c, nibble j+4 -> 16j + c + 1
-                    const uint4 wv = *reinterpret_cast<const uint4 *>(sp + lane * 16);
+                for (int h = 0; h < 2; ++h) {
+                    const uint4 wv = *reinterpret_cast<const uint4 *>(sp + h * kChunkBytes + lane * 16);
                     const uint32_t w4[4] = {wv.x, wv.y, wv.z, wv.w};
+                    // scales of rows g and g + 8, stored side by side
+                    const __half2 sp2 = *reinterpret_cast<const __half2 *>(mp + ((h * 32) / s0.g_per) * 32 + 4 * g);
+                    const __half2 s_lo = __low2half2(sp2), s_hi = __high2half2(sp2);
+                    const __half2 off = __float2half2_rn(1152.0f);  // 1024 + 128: u = q + 128
+                    uint32_t a[2][4];
 #pragma unroll
                     for (int r = 0; r < 4; ++r) {
-                        const int row = g + 8 * (r & 1);
-                        const int c = 2 * t + 8 * (r >> 1);
-                        __half2 s2, z2;
-                        // group metadata stores rows g and g + 8 side by side
-                        const int mi = 2 * g + (r & 1);
-                        if constexpr (META == kMetaSZ16) {
-                            const __half2 sz = *reinterpret_cast<const __half2 *>(mp + mi * 4);
-                            s2 = __low2half2(sz);
-                            z2 = __hadd2(__high2half2(sz), __float2half2_rn(1024.0f));  // 1024 + z (exact: z < 1024)
-                        } else {
-                            const __half sc = *reinterpret_cast<const __half *>(mp + mi * 2);
-                            s2 = __halves2half2(sc, sc);
-                            z2 = __float2half2_rn(1024.0f + p.zc);
-                        }
-#pragma unroll
-                        for (int j = 0; j < 4; ++j) {
-                            const uint32_t e = ((w4[r] >> (4 * j)) & 0x000F000Fu) | 0x64006400u;  // (1024+c_a, 1024+c_b)
-                            const __half2 v = __hmul2(__hsub2(bits_h2(e), z2), s2);
-                            *reinterpret_cast<uint32_t *>(bt + swz_off(nb + row, 16 * j + c)) = h2_bits(v);
-                        }
+                        const __half2 sc = (r & 1) ? s_hi : s_lo;
+                        a[0][r] = h2_bits(__hmul2(__hsub2(bits_h2(__byte_perm(w4[r], 0x64646464u, 0x4140)), off), sc));
+                        a[1][r] = h2_bits(__hmul2(__hsub2(bits_h2(__byte_perm(w4[r], 0x64646464u, 0x4342)), off), sc));
                     }
+#pragma unroll
+                    for (int j = 0; j < 2; ++j)
+                        stmatrix_x4(wt_base + swz_off(st_row, 32 * h + 16 * j + st_col), a[j][0], a[j][1], a[j][2],
+                                    a[j][3]);
+                }
+            } else {
+                // one chunk of 64 columns (4 k-steps); nibble j -> k-step j, nibble j+4 -> its next column
+                const uint4 wv = *reinterpret_cast<const uint4 *>(sp + lane * 16);
+                const uint32_t w4[4] = {wv.x, wv.y, wv.z, wv.w};
+                __half2 s2[2], z2[2];
+                if constexpr (META == kMetaSZ16) {
+                    // (scale, zero) of rows g and g + 8, stored side by side
+                    const uint2 v = *reinterpret_cast<const uint2 *>(mp + 8 * g);
+                    const __half2 a0 = bits_h2(v.x), a1 = bits_h2(v.y);
+                    s2[0] = __low2half2(a0);
+                    s2[1] = __low2half2(a1);
+                    z2[0] = __hadd2(__high2half2(a0), __float2half2_rn(1024.0f));  // 1024 + z (exact: z < 1024)
+                    z2[1] = __hadd2(__high2half2(a1), __float2half2_rn(1024.0f));
+                } else {
+                    const __half2 sp2 = *reinterpret_cast<const __half2 *>(mp + 4 * g);
+                    s2[0] = __low2half2(sp2);
+                    s2[1] = __high2half2(sp2);
+                    z2[0] = z2[1] = __float2half2_rn(1024.0f + p.zc);
+                }
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    uint32_t a[4];
+#pragma unroll
+                    for (int r = 0; r < 4; ++r) {
+                        const uint32_t e = ((w4[r] >> (4 * j)) & 0x000F000Fu) | 0x64006400u;  // (1024+c_a, 1024+c_b)
+                        a[r] = h2_bits(__hmul2(__hsub2(bits_h2(e), z2[r & 1]), s2[r & 1]));
+                    }
+                    stmatrix_x4(wt_base + swz_off(st_row, 16 * j + st_col), a[0], a[1], a[2], a[3]);
                 }
             }
             fence_async_smem();  // the generic-proxy stores become visible to the tensor cores
             __syncwarp();
             if (lane == 0) {
-                mbar_arrive(&b_full[bs]);
+                mbar_arrive(&w_full[ws]);
                 mbar_arrive(&in_empty[s]);
             }
         }
@@ -376,22 +379,22 @@ __global__ void __launch_bounds__(kPThreads, 1)
         if (ok && __all_sync(0xffffffffu, mbar_wait_bounded(acc_bar, 0))) {
             tc_fence_after();
             grid_dependency_wait();  // y may still be read by the previous kernel
-            const int q = dw & 3;           // TMEM lanes 32q..32q+31
-            const int c0 = (dw >> 2) * 128;  // columns 0..127 or 128..255
-            const int m = m0 + 32 * q + lane;
+            const int q = dw & 3;            // TMEM lanes 32q..32q+31: weight rows
+            const int c0 = (dw >> 2) * 128;  // token columns 0..127 or 128..255
+            const int n = strip0 * kStripRows + 32 * q + lane;
 #pragma unroll 1
             for (int cc = 0; cc < 128; cc += 16) {
                 uint32_t v[16];
                 tmem_ld16(tmem_d + ((uint32_t)(32 * q) << 16) + (uint32_t)(c0 + cc), v);
                 tmem_ld_wait();
-                const int n = strip0 * kStripRows + c0 + cc;
-                if (m < p.M) {
-                    float *yr = p.y + (size_t)m * p.ldy + n;
+                if (n < p.N) {
 #pragma unroll
                     for (int e = 0; e < 16; ++e) {
-                        if (n + e < p.N) {
+                        const int m = tok0 + c0 + cc + e;
+                        if (m < p.M) {
+                            float *yp = p.y + (size_t)m * p.ldy + n;
                             const float val = __uint_as_float(v[e]);
-                            yr[e] = p.accumulate ? yr[e] + val : val;
+                            *yp = p.accumulate ? *yp + val : val;
                         }
                     }
                 }
@@ -408,13 +411,21 @@ __global__ void __launch_bounds__(kPThreads, 1)
     }
 }
 
-// Activations [M][K] (fp32 / bf16 / fp16) -> fp16 tiles [m_tile][k_block] of
-// 128 x 64, K-major with the 128-byte swizzle; zero outside [M, K).  One
-// thread per 8 consecutive columns (one 16-byte chunk of the tile).
-__global__ void prefill_xprep_kernel(const void *__restrict__ x, int dt, int M, int K, int n_mt, int n_kb,
+// Activations [M][K] (fp32 / bf16 / fp16) -> fp16 tiles [token_tile][k_block]
+// of 256 x 64, K-major with the 128-byte swizzle; zero outside [M, K).  One
+// thread per 8 consecutive columns (one 16-byte chunk of a tile row), read
+// with vector loads where the row allows.
+__device__ __forceinline__ float x_at(const void *x, int dt, size_t i) {
+    return dt == CHPE_X_F32 ? static_cast<const float *>(x)[i]
+           : dt == CHPE_X_BF16 ? __bfloat162float(static_cast<const __nv_bfloat16 *>(x)[i])
+                               : __half2float(static_cast<const __half *>(x)[i]);
+}
+
+__global__ void prefill_xprep_kernel(const void *__restrict__ x, int dt, int M, int K, int n_tt, int n_kb,
                                      uint16_t *__restrict__ xt) {
     pdl_begin();
-    const size_t total = (size_t)n_mt * kPM * n_kb * (kPK / 8);
+    const size_t total = (size_t)n_tt * kPN * n_kb * (kPK / 8);
+    const bool vec = (K % 8) == 0 && (reinterpret_cast<uintptr_t>(x) % 16) == 0;
     for (size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
          idx += (size_t)gridDim.x * blockDim.x) {
         const int ch = (int)(idx % (kPK / 8));
@@ -422,29 +433,39 @@ __global__ void prefill_xprep_kernel(const void *__restrict__ x, int dt, int M, 
         const int kb = (int)(rest % n_kb);
         const int m = (int)(rest / n_kb);
         const int k0 = kb * kPK + ch * 8;
-        uint32_t h[4];
+        uint4 out = make_uint4(0u, 0u, 0u, 0u);
+        if (m < M && k0 < K) {
+            const size_t base = (size_t)m * K + k0;
+            if (vec && dt == CHPE_X_F16) {
+                out = *reinterpret_cast<const uint4 *>(static_cast<const __half *>(x) + base);
+            } else if (vec && dt == CHPE_X_BF16) {
+                const uint4 v = *reinterpret_cast<const uint4 *>(static_cast<const __nv_bfloat16 *>(x) + base);
+                const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+                uint32_t h[4];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            float a = 0.0f, b = 0.0f;
-            const int ka = k0 + 2 * e;
-            if (m < M) {
-                const size_t base = (size_t)m * K;
-                if (ka < K) {
-                    a = dt == CHPE_X_F32 ? static_cast<const float *>(x)[base + ka]
-                        : dt == CHPE_X_BF16 ? __bfloat162float(static_cast<const __nv_bfloat16 *>(x)[base + ka])
-                                            : __half2float(static_cast<const __half *>(x)[base + ka]);
+                for (int e = 0; e < 4; ++e)
+                    h[e] = h2_bits(__float22half2_rn(__bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&w[e]))));
+                out = make_uint4(h[0], h[1], h[2], h[3]);
+            } else if (vec && dt == CHPE_X_F32) {
+                const float4 a = *reinterpret_cast<const float4 *>(static_cast<const float *>(x) + base);
+                const float4 b = *reinterpret_cast<const float4 *>(static_cast<const float *>(x) + base + 4);
+                out = make_uint4(h2_bits(__floats2half2_rn(a.x, a.y)), h2_bits(__floats2half2_rn(a.z, a.w)),
+                                 h2_bits(__floats2half2_rn(b.x, b.y)), h2_bits(__floats2half2_rn(b.z, b.w)));
+            } else {
+                uint32_t h[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int ka = k0 + 2 * e;
+                    const float va = ka < K ? x_at(x, dt, base + 2 * e) : 0.0f;
+                    const float vb = ka + 1 < K ? x_at(x, dt, base + 2 * e + 1) : 0.0f;
+                    h[e] = h2_bits(__floats2half2_rn(va, vb));
                 }
-                if (ka + 1 < K) {
-                    b = dt == CHPE_X_F32 ? static_cast<const float *>(x)[base + ka + 1]
-                        : dt == CHPE_X_BF16 ? __bfloat162float(static_cast<const __nv_bfloat16 *>(x)[base + ka + 1])
-                                            : __half2float(static_cast<const __half *>(x)[base + ka + 1]);
-                }
+                out = make_uint4(h[0], h[1], h[2], h[3]);
             }
-            h[e] = h2_bits(__floats2half2_rn(a, b));
         }
-        const int mt = m / kPM, r = m % kPM;
-        uint8_t *tile = reinterpret_cast<uint8_t *>(xt) + ((size_t)mt * n_kb + kb) * kATileBytes;
-        *reinterpret_cast<uint4 *>(tile + swz_off(r, ch * 8)) = make_uint4(h[0], h[1], h[2], h[3]);
+        const int tt = m / kPN, r = m % kPN;
+        uint8_t *tile = reinterpret_cast<uint8_t *>(xt) + ((size_t)tt * n_kb + kb) * kXTileBytes;
+        *reinterpret_cast<uint4 *>(tile + swz_off(r, ch * 8)) = out;
     }
 }
 
@@ -467,7 +488,7 @@ EncodeTiledFn encode_tiled() {
 }
 
 // The strip layout as a 3-D tensor of 32-bit words: (word of a block) x
-// blocks x strips; the box is one word range of every block of 16 strips.
+// blocks x strips; the box is one word range of one block of 8 strips.
 bool make_strip_map(CUtensorMap *map, const PrefillParams &p, uint32_t box_bytes) {
     EncodeTiledFn fn = encode_tiled();
     if (!fn) return false;
@@ -493,16 +514,16 @@ cudaError_t launch_prefill_t(const PrefillParams &p, size_t smem, cudaStream_t s
     CUtensorMap tm_codes, tm_meta;
     if (!make_strip_map(&tm_codes, p, s0.code_bytes) || !make_strip_map(&tm_meta, p, s0.meta_bytes))
         return cudaErrorInvalidValue;
-    const int n_nt = (p.n_strips + kStripsPerTile - 1) / kStripsPerTile;
-    return launch_pdl(kern, dim3((unsigned)(p.n_mt * n_nt)), dim3(kPThreads), smem, st, p, tm_codes, tm_meta);
+    const int n_wt = (p.n_strips + kStripsPerTile - 1) / kStripsPerTile;
+    return launch_pdl(kern, dim3((unsigned)(p.n_tt * n_wt)), dim3(kPThreads), smem, st, p, tm_codes, tm_meta);
 }
 
 }  // namespace
 
 // Scratch bytes for the activation tiles of an M x K prefill.
 size_t prefill_xt_bytes(int M, int K) {
-    const size_t n_mt = (size_t)(M + kPM - 1) / kPM, n_kb = (size_t)(K + kPK - 1) / kPK;
-    return n_mt * n_kb * kATileBytes;
+    const size_t n_tt = (size_t)(M + kPN - 1) / kPN, n_kb = (size_t)(K + kPK - 1) / kPK;
+    return n_tt * n_kb * kXTileBytes;
 }
 
 // Whether the prefill kernel handles this weight format.
@@ -532,16 +553,16 @@ cudaError_t launch_prefill(const DevMatrix &w, const void *x, int x_dtype, int M
     p.group = w.group;
     p.span = w.span;
     p.n_kb = (w.K + kPK - 1) / kPK;
-    p.n_mt = (M + kPM - 1) / kPM;
+    p.n_tt = (M + kPN - 1) / kPN;
     p.zc = w.zc;
     p.accumulate = accumulate;
     p.err = err;
-    const size_t total = (size_t)p.n_mt * kPM * p.n_kb * (kPK / 8);
+    const size_t total = (size_t)p.n_tt * kPN * p.n_kb * (kPK / 8);
     cudaError_t e = launch_pdl(prefill_xprep_kernel, dim3((unsigned)std::min<size_t>((total + 255) / 256, 148 * 16)),
-                               dim3(256), 0, st, x, x_dtype, M, w.K, p.n_mt, p.n_kb, static_cast<uint16_t *>(xt));
+                               dim3(256), 0, st, x, x_dtype, M, w.K, p.n_tt, p.n_kb, static_cast<uint16_t *>(xt));
     if (e != cudaSuccess) return e;
     const KbSlice s0 = kb_slice(p, 0);
-    const size_t smem = psmem(s0.code_bytes + s0.meta_bytes).total + 1024;  // + alignment slack
+    const size_t smem = psmem(s0.code_bytes, s0.meta_bytes).total + 1024;  // + alignment slack
     if (w.bits == 8) return launch_prefill_t<8, kMetaS16>(p, smem, st);
     if (w.meta_kind == kMetaSZ16) return launch_prefill_t<4, kMetaSZ16>(p, smem, st);
     return launch_prefill_t<4, kMetaS16>(p, smem, st);
