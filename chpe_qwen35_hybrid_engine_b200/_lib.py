@@ -74,6 +74,12 @@ SIGNATURES = {
     "chpe_gemv_gateup_swiglu_xfrag_dev": (I, [P, P, P, P, P, P]),
     "chpe_gemv_multi_xfrag_dev": (I, [P, I, P, P, P, P]),
     "chpe_gemm_prefill_dev": (I, [P, P, P, I, I, P, I, I, P]),
+    "chpe_comm_create": (I, [P, I, I, SZ, PP]),
+    "chpe_comm_handle_bytes": (SZ, []),
+    "chpe_comm_handle": (I, [P, P]),
+    "chpe_comm_open_peers": (I, [P, P]),
+    "chpe_allreduce_residual_dev": (I, [P, P, P, SZ, P]),
+    "chpe_comm_destroy": (I, [P]),
     "chpe_xfrag_free": (I, [P, P]),
     "chpe_xfrag_fill_op_dev": (I, [P, P, C.POINTER(chpe_xsrc), P]),
     "chpe_gemv_parallel": (I, [P, P, F, P, F, SZ, SZ, P]),

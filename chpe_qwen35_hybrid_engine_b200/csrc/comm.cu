@@ -1,0 +1,215 @@
+// comm.cu -- one-shot all-reduce over NVLink peer memory for tensor
+// parallelism (72B shape): after the O and down projections every rank holds
+// an fp32 partial [M][H] of the block output; the hidden state needs
+// hidden += sum over ranks of the partials.
+//
+// Each rank owns, in its own memory, a receive area of 2 x world slots of
+// Mmax x H floats plus world arrival flags, mapped into every peer with CUDA
+// IPC.  One kernel per all-reduce (one CTA of 1024 threads; M <= 8 rows of
+// H <= 8192 is at most 256 KB per rank):
+//   1. take the next epoch (a per-rank counter; every rank runs the same
+//      sequence of all-reduces, so epochs agree),
+//   2. store this rank's partial into slot [epoch & 1][rank] of every peer's
+//      receive area (P2P stores over NVLink; no TMA, no multicast),
+//   3. __threadfence_system, then store the epoch into the peer's flag [rank],
+//   4. wait until every flag of its own area reaches the epoch -- bounded by
+//      1 s of %globaltimer, after which it records an error and returns,
+//   5. hidden[m][i] += partial_0 + partial_1 + ... in rank order (its own
+//      partial read locally), so every rank computes the same bits.
+// Slots alternate with the epoch's parity: a rank can only rewrite a slot two
+// epochs later, after it has seen every peer's flag for the epoch in between,
+// which each peer sets only after it finished reading the older slot.
+#include <cstring>
+
+#include "../../include/chpe_b200.h"
+#include "common.cuh"
+#include "internal.h"
+
+namespace chpe {
+namespace {
+
+constexpr int kCommMaxRanks = 8;
+constexpr int kCommThreads = 1024;
+constexpr int kErrCommWait = 31;
+
+__device__ __forceinline__ void st_release_sys(unsigned *p, unsigned v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned *p) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+struct CommPeers {
+    float *recv[kCommMaxRanks];              // each rank's receive area (peer mappings; own one locally)
+    unsigned *flags[kCommMaxRanks];          // each rank's flags [world]
+};
+
+__global__ void __launch_bounds__(kCommThreads) allreduce_residual_kernel(const CommPeers peers, int world, int rank,
+                                                                          size_t slot_elems, const float *__restrict__ part,
+                                                                          float *__restrict__ hidden, int n,
+                                                                          unsigned *__restrict__ epoch_ctr,
+                                                                          int *__restrict__ err) {
+    __shared__ unsigned s_epoch;
+    __shared__ int s_ok;
+    pdl_begin();  // the partial is the previous kernel's output
+    if (threadIdx.x == 0) {
+        s_epoch = *epoch_ctr + 1u;
+        *epoch_ctr = s_epoch;
+        s_ok = 1;
+    }
+    __syncthreads();
+    const unsigned epoch = s_epoch;
+    const size_t slot = ((size_t)(epoch & 1u) * world + rank) * slot_elems;
+    // 2. push this rank's partial to every peer (float4 when aligned)
+    const int n4 = n / 4;
+    const float4 *p4 = reinterpret_cast<const float4 *>(part);
+    for (int r = 0; r < world; ++r) {
+        if (r == rank) continue;
+        float4 *dst = reinterpret_cast<float4 *>(peers.recv[r] + slot);
+        for (int i = threadIdx.x; i < n4; i += blockDim.x) dst[i] = p4[i];
+        for (int i = 4 * n4 + threadIdx.x; i < n; i += blockDim.x) peers.recv[r][slot + i] = part[i];
+    }
+    // 3. make the data visible system-wide, then raise this rank's flag in every peer
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x < world && threadIdx.x != rank) st_release_sys(peers.flags[threadIdx.x] + rank, epoch);
+    // 4. wait for every peer's flag in this rank's own area (bounded)
+    if (threadIdx.x < world && threadIdx.x != rank) {
+        const unsigned *f = peers.flags[rank] + threadIdx.x;
+        const unsigned long long t0 = global_timer_ns();
+        bool ok = false;
+        while (true) {
+            if ((int)(ld_acquire_sys(f) - epoch) >= 0) {
+                ok = true;
+                break;
+            }
+            if (global_timer_ns() - t0 > kWaitTimeoutNs) break;
+            __nanosleep(64);
+        }
+        if (!ok) {
+            atomicExch(err, kErrCommWait);
+            s_ok = 0;
+        }
+    }
+    __syncthreads();
+    if (!s_ok) return;
+    __threadfence_system();  // order the flag reads before the data reads
+    // 5. hidden += sum of the partials in rank order
+    const float *own = peers.recv[rank] + (size_t)(epoch & 1u) * world * slot_elems;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        float s = 0.0f;
+        for (int r = 0; r < world; ++r) s += (r == rank) ? part[i] : own[(size_t)r * slot_elems + i];
+        hidden[i] += s;
+    }
+}
+
+}  // namespace
+}  // namespace chpe
+
+using namespace chpe;
+
+struct chpe_comm {
+    chpe_ctx *ctx = nullptr;
+    int world = 0, rank = 0;
+    size_t max_elems = 0;  // Mmax * H
+    float *recv = nullptr;          // own receive area [2][world][max_elems]
+    unsigned *flags = nullptr;      // own flags [world]
+    unsigned *epoch = nullptr;      // own epoch counter
+    CommPeers peers;
+    bool opened[kCommMaxRanks] = {false};
+    cudaIpcMemHandle_t handle_recv, handle_flags;
+};
+
+int *chpe_ctx_error_word(chpe_ctx *ctx);
+
+extern "C" int chpe_comm_create(chpe_ctx *ctx, int world, int rank, size_t max_elems, chpe_comm **out) {
+    if (!ctx || !out) return CHPE_EINVAL;
+    *out = nullptr;
+    if (world < 1 || world > kCommMaxRanks || rank < 0 || rank >= world || max_elems < 1) return CHPE_EINVAL;
+    chpe_comm *c = new chpe_comm();
+    c->ctx = ctx;
+    c->world = world;
+    c->rank = rank;
+    c->max_elems = (max_elems + 3) / 4 * 4;
+    memset(&c->peers, 0, sizeof c->peers);
+    cudaError_t e = cudaMalloc(&c->recv, 2 * (size_t)world * c->max_elems * sizeof(float));
+    if (e == cudaSuccess) e = cudaMalloc(&c->flags, 256);
+    if (e == cudaSuccess) e = cudaMalloc(&c->epoch, 256);
+    if (e == cudaSuccess) e = cudaMemset(c->flags, 0, 256);
+    if (e == cudaSuccess) e = cudaMemset(c->epoch, 0, 256);
+    if (e == cudaSuccess) e = cudaIpcGetMemHandle(&c->handle_recv, c->recv);
+    if (e == cudaSuccess) e = cudaIpcGetMemHandle(&c->handle_flags, c->flags);
+    if (e != cudaSuccess) {
+        cudaFree(c->recv);
+        cudaFree(c->flags);
+        cudaFree(c->epoch);
+        delete c;
+        cudaGetLastError();
+        return CHPE_ECUDA;
+    }
+    c->peers.recv[rank] = c->recv;
+    c->peers.flags[rank] = c->flags;
+    *out = c;
+    return CHPE_OK;
+}
+
+extern "C" size_t chpe_comm_handle_bytes(void) { return 2 * sizeof(cudaIpcMemHandle_t); }
+
+extern "C" int chpe_comm_handle(const chpe_comm *c, void *out) {
+    if (!c || !out) return CHPE_EINVAL;
+    memcpy(out, &c->handle_recv, sizeof(cudaIpcMemHandle_t));
+    memcpy(static_cast<uint8_t *>(out) + sizeof(cudaIpcMemHandle_t), &c->handle_flags, sizeof(cudaIpcMemHandle_t));
+    return CHPE_OK;
+}
+
+extern "C" int chpe_comm_open_peers(chpe_comm *c, const void *handles) {
+    if (!c || !handles) return CHPE_EINVAL;
+    const size_t hb = chpe_comm_handle_bytes();
+    for (int r = 0; r < c->world; ++r) {
+        if (r == c->rank || c->opened[r]) continue;
+        cudaIpcMemHandle_t hr, hf;
+        memcpy(&hr, static_cast<const uint8_t *>(handles) + r * hb, sizeof hr);
+        memcpy(&hf, static_cast<const uint8_t *>(handles) + r * hb + sizeof hr, sizeof hf);
+        void *pr = nullptr, *pf = nullptr;
+        cudaError_t e = cudaIpcOpenMemHandle(&pr, hr, cudaIpcMemLazyEnablePeerAccess);
+        if (e == cudaSuccess) e = cudaIpcOpenMemHandle(&pf, hf, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) {
+            if (pr) cudaIpcCloseMemHandle(pr);
+            cudaGetLastError();
+            return CHPE_ECUDA;
+        }
+        c->peers.recv[r] = static_cast<float *>(pr);
+        c->peers.flags[r] = static_cast<unsigned *>(pf);
+        c->opened[r] = true;
+    }
+    return CHPE_OK;
+}
+
+extern "C" int chpe_allreduce_residual_dev(chpe_comm *c, const float *part, float *hidden, size_t n, void *stream) {
+    if (!c || !part || !hidden) return CHPE_EINVAL;
+    if (n > c->max_elems) return CHPE_EINVAL;
+    if (reinterpret_cast<uintptr_t>(part) % 16) return CHPE_EALIGN;  // read as float4
+    for (int r = 0; r < c->world; ++r)
+        if (!c->peers.recv[r] || !c->peers.flags[r]) return CHPE_ENOENT;  // peers not opened yet
+    cudaError_t e = launch_pdl(allreduce_residual_kernel, dim3(1), dim3(kCommThreads), 0,
+                               static_cast<cudaStream_t>(stream), c->peers, c->world, c->rank, c->max_elems, part,
+                               hidden, (int)n, c->epoch, chpe_ctx_error_word(c->ctx));
+    return e == cudaSuccess ? CHPE_OK : CHPE_ECUDA;
+}
+
+extern "C" int chpe_comm_destroy(chpe_comm *c) {
+    if (!c) return CHPE_EINVAL;
+    cudaDeviceSynchronize();
+    for (int r = 0; r < c->world; ++r) {
+        if (!c->opened[r]) continue;
+        cudaIpcCloseMemHandle(c->peers.recv[r]);
+        cudaIpcCloseMemHandle(c->peers.flags[r]);
+    }
+    cudaFree(c->recv);
+    cudaFree(c->flags);
+    cudaFree(c->epoch);
+    delete c;
+    return CHPE_OK;
+}

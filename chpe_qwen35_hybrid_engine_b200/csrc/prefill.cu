@@ -1,20 +1,24 @@
 // prefill.cu -- dequant-GEMM for prefill (M >= 64 activation rows) on the
 // 5th-generation tensor cores: y[M, N] = x[M, K] . dequant(W)[N, K]^T.
 //
-// One CTA computes a tile of 128 weight rows x 256 tokens of y over all of K
-// in steps of 64 columns (a "k-block").  The weights are the MMA's M side, so
-// each dequantized weight tile serves 256 tokens and the accumulator's TMEM
-// lanes are weight rows (the epilogue's stores are 128-byte rows of y):
+// One CTA computes a tile of 256 weight rows x 256 tokens of y over all of K
+// in steps of 64 columns (a "k-block"), as two 128 x 256 MMA accumulators
+// (all 512 TMEM columns) that share each activation tile.  The weights are the
+// MMA's M side, so each dequantized weight tile serves 256 tokens and the
+// accumulators' TMEM lanes are weight rows (the epilogue's stores are 128-byte
+// rows of y); sharing the activation tile between two weight halves halves
+// the operand bytes each MMA cycle needs, which is what lets a 3-stage ring
+// cover the L2 / HBM latency:
 //   * warp 0, one lane: three copies per k-block on the TMA engine (mbarrier
-//     transaction counts) into a 4-stage input ring: the activation tile
+//     transaction counts) into a 3-stage input ring: the activation tile
 //     (1-D bulk copy of 256 x 64 fp16) and, through two 3-D tensor maps over
 //     the decode path's strip layout (words of a block x blocks x strips; one
 //     copy of the weights in HBM), the 1 or 2 chunks of codes and the group
-//     metadata that cover the k-block for the tile's 8 strips (strips past the
-//     matrix read as zeros).
-//   * warps 4..11: warp 4 + i dequantizes strip i (16 weight rows x 64) into
+//     metadata that cover the k-block for the tile's 16 strips (strips past
+//     the matrix read as zeros).
+//   * warps 4..19: warp 4 + i dequantizes strip i (16 weight rows x 64) into
 //     fp16 in shared memory, in the UMMA canonical K-major layout with the
-//     128-byte swizzle, into a 2-stage ring.  A code becomes an exact fp16
+//     128-byte swizzle (two 128-row tiles stacked), into a 2-stage ring.  A code becomes an exact fp16
 //     integer with one byte-permute / LOP3 against the bit pattern of 1024
 //     (0x6400), one HSUB2 removes 1024 + 128 (signed int8) or 1024 + zero, and
 //     one HMUL2 applies the group scale: w = fp16(q * s), a single rounding.
@@ -22,12 +26,12 @@
 //     which is exactly what stmatrix takes: one stmatrix.x4 writes a 16 x 16
 //     block of the tile.
 //   * warp 1, one lane: tcgen05.mma.cta_group::1.kind::f16 (A = weights,
-//     B = activations, both fp16 from shared memory, fp32 accumulator of
-//     128 x 256 in tensor memory), 4 instructions of K = 16 per k-block;
+//     B = activations, both fp16 from shared memory, fp32 accumulators of
+//     128 x 256 in tensor memory), 2 x 4 instructions of K = 16 per k-block;
 //     tcgen05.commit frees the stages once the MMAs that read them finish.
-//   * warps 4..11 again, after the last k-block: tcgen05.ld the accumulator
-//     (warp 4 + q, and 8 + q, read TMEM lanes 32q..32q+31 = weight rows,
-//     token columns 0..127 and 128..255) and store fp32 into y.
+//   * warps 4..19 again, after the last k-block: tcgen05.ld the accumulators
+//     (warp 4 + 4c + q reads TMEM lanes 32q..32q+31 = weight rows of half
+//     c & 1, token columns 128 (c >> 1) .. +127) and store fp32 into y.
 // Activations are converted once per call into fp16 tiles of 256 x 64 already
 // in the swizzled layout (prefill_xprep_kernel), so each k-block's B operand
 // is one contiguous 32 KB copy.  Every wait is bounded: on a timeout the
@@ -44,18 +48,20 @@
 namespace chpe {
 namespace {
 
-constexpr int kPM = 128;          // weight rows per tile (UMMA M, cta_group::1)
+constexpr int kPM = 128;          // weight rows per MMA (UMMA M, cta_group::1)
+constexpr int kPHalves = 2;       // MMA accumulators (weight halves) per CTA
 constexpr int kPN = 256;          // tokens per tile (UMMA N)
 constexpr int kPK = 64;           // columns per k-block (one 128-byte swizzle atom of fp16)
-constexpr int kInStages = 4;      // activation + packed-weight ring
+constexpr int kInStages = 3;      // activation + packed-weight ring
 constexpr int kWStages = 2;       // dequantized weight ring
-constexpr int kPThreads = 384;    // 12 warps
+constexpr int kPThreads = 640;    // 20 warps
 constexpr int kDeqWarp0 = 4;      // first dequant / epilogue warp
-constexpr int kDeqWarps = 8;
-constexpr int kStripsPerTile = kPM / kStripRows;  // 8
-constexpr uint32_t kWTileBytes = kPM * kPK * 2;   // 16 KB of fp16 weights
-constexpr uint32_t kXTileBytes = kPN * kPK * 2;   // 32 KB of fp16 activations
-constexpr uint32_t kTmemCols = 256;
+constexpr int kDeqWarps = 16;
+constexpr int kStripsPerTile = kPHalves * kPM / kStripRows;  // 16
+constexpr uint32_t kWHalfBytes = kPM * kPK * 2;              // 16 KB of fp16 weights per MMA
+constexpr uint32_t kWTileBytes = kPHalves * kWHalfBytes;     // 32 KB
+constexpr uint32_t kXTileBytes = kPN * kPK * 2;              // 32 KB of fp16 activations
+constexpr uint32_t kTmemCols = kPHalves * kPN;               // 512: the whole tensor memory
 static_assert(kDeqWarps == kStripsPerTile, "one dequant warp per strip");
 
 enum PrefillErr : int { kPErrInFull = 21, kPErrInEmpty = 22, kPErrBFull = 23, kPErrBEmpty = 24, kPErrAcc = 25 };
@@ -281,8 +287,10 @@ __global__ void __launch_bounds__(kPThreads, 1)
                 const uint32_t w_base = smem_u32(smem + L.w_ring + ws * kWTileBytes);
 #pragma unroll
                 for (int kk = 0; kk < kPK / 16; ++kk)
-                    umma_f16(tmem_d, umma_desc_sw128(w_base + kk * 32), umma_desc_sw128(x_base + kk * 32),
-                             (kb > 0 || kk > 0) ? 1u : 0u);
+#pragma unroll
+                    for (int a = 0; a < kPHalves; ++a)
+                        umma_f16(tmem_d + (uint32_t)(a * kPN), umma_desc_sw128(w_base + a * kWHalfBytes + kk * 32),
+                                 umma_desc_sw128(x_base + kk * 32), (kb > 0 || kk > 0) ? 1u : 0u);
                 umma_commit(&in_empty[s]);  // activation stage free once these MMAs are done
                 umma_commit(&w_empty[ws]);  // and the dequantized weight stage
             }
@@ -292,7 +300,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
         }
     } else if (warp >= kDeqWarp0) {
         // ---------------- dequant, then epilogue ----------------
-        const int dw = warp - kDeqWarp0;  // 0..7: strip dw of the tile, weight rows 16dw..16dw+15
+        const int dw = warp - kDeqWarp0;  // 0..15: strip dw of the tile, weight rows 16dw..16dw+15
         const int g = lane >> 2, t = lane & 3;
         // stmatrix address of this lane inside a 16 x 16 block: row (lane % 8) + 8 ((lane / 8) & 1) of the
         // strip, columns 8 (lane / 16) .. +7 of the k-step
@@ -379,13 +387,14 @@ __global__ void __launch_bounds__(kPThreads, 1)
         if (ok && __all_sync(0xffffffffu, mbar_wait_bounded(acc_bar, 0))) {
             tc_fence_after();
             grid_dependency_wait();  // y may still be read by the previous kernel
-            const int q = dw & 3;            // TMEM lanes 32q..32q+31: weight rows
-            const int c0 = (dw >> 2) * 128;  // token columns 0..127 or 128..255
-            const int n = strip0 * kStripRows + 32 * q + lane;
+            const int q = dw & 3;                   // TMEM lanes 32q..32q+31: weight rows of half `a`
+            const int a = (dw >> 2) & 1;            // accumulator (weight half)
+            const int c0 = (dw >> 3) * 128;         // token columns 0..127 or 128..255
+            const int n = strip0 * kStripRows + a * kPM + 32 * q + lane;
 #pragma unroll 1
             for (int cc = 0; cc < 128; cc += 16) {
                 uint32_t v[16];
-                tmem_ld16(tmem_d + ((uint32_t)(32 * q) << 16) + (uint32_t)(c0 + cc), v);
+                tmem_ld16(tmem_d + ((uint32_t)(32 * q) << 16) + (uint32_t)(a * kPN + c0 + cc), v);
                 tmem_ld_wait();
                 if (n < p.N) {
 #pragma unroll
@@ -488,7 +497,7 @@ EncodeTiledFn encode_tiled() {
 }
 
 // The strip layout as a 3-D tensor of 32-bit words: (word of a block) x
-// blocks x strips; the box is one word range of one block of 8 strips.
+// blocks x strips; the box is one word range of one block of 16 strips.
 bool make_strip_map(CUtensorMap *map, const PrefillParams &p, uint32_t box_bytes) {
     EncodeTiledFn fn = encode_tiled();
     if (!fn) return false;

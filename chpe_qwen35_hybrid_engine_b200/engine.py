@@ -267,7 +267,8 @@ class HybridEngine:
         self.head: Tensor | None = None
         self.graphs = {}
         self.xfrags = {}           # (input, rows) -> XFrag
-        self.allreduce = None      # set by tensor parallelism: fn(tensor) summing across ranks
+        self.allreduce = None      # set by tensor parallelism: fn(tensor) summing across ranks (NCCL)
+        self.comm = None           # or the NVLink one-shot all-reduce (ops.Comm)
         g, Mx = geom, max_rows
         f32 = dict(dtype=torch.float32, device=self.dev)
         widest = max(g.hidden, g.q_dim, g.ssm_qkv or 1, g.ffn)
@@ -325,8 +326,14 @@ class HybridEngine:
 
         def gemv_res(t: Tensor, xf, hidden):
             """hidden += x . W^T (the residual add of the block); with tensor
-            parallelism the shard's partial sum goes through the all-reduce first."""
-            if self.allreduce is None:
+            parallelism the shard's partial sum is summed over the ranks first:
+            one NVLink all-reduce kernel that also adds into hidden (comm), or
+            an NCCL all-reduce and an add."""
+            if self.comm is not None:
+                part = b["mix_out"][:M]
+                gemv(t, xf, part)
+                self.comm.allreduce_residual(part, hidden, M * H, stream=sp.value)
+            elif self.allreduce is None:
                 gemv(t, xf, hidden, acc=True)
             else:
                 part = b["mix_out"][:M]

@@ -86,6 +86,46 @@ class XFrag:
             self.handle = None
 
 
+class Comm:
+    """One-shot NVLink all-reduce of a tensor-parallel group (chpe_comm_*): one
+    per rank; `exchange` swaps the IPC handles over any host transport
+    (torch.distributed here) and maps every peer's receive area."""
+
+    def __init__(self, ctx: "Context", world: int, rank: int, max_elems: int):
+        self.ctx, self.world, self.rank = ctx, world, rank
+        h = C.c_void_p()
+        ctx._check(ctx.lib.chpe_comm_create(ctx.ptr, world, rank, max_elems, C.byref(h)))
+        self.handle = h
+
+    def local_handle(self) -> bytes:
+        n = self.ctx.lib.chpe_comm_handle_bytes()
+        buf = (C.c_char * n)()
+        self.ctx._check(self.ctx.lib.chpe_comm_handle(self.handle, buf))
+        return bytes(buf)
+
+    def open_peers(self, handles):
+        blob = b"".join(handles)
+        buf = (C.c_char * len(blob)).from_buffer_copy(blob)
+        self.ctx._check(self.ctx.lib.chpe_comm_open_peers(self.handle, buf))
+
+    def exchange(self, group=None):
+        import torch.distributed as dist
+        hs = [None] * self.world
+        dist.all_gather_object(hs, self.local_handle(), group=group)
+        self.open_peers(hs)
+        dist.barrier(group=group)
+
+    def allreduce_residual(self, part, hidden, n: int, stream=None):
+        """hidden[:n] += sum over ranks of part[:n] (device pointers)."""
+        self.ctx._check(self.ctx.lib.chpe_allreduce_residual_dev(self.handle, _dev_ptr(part), _dev_ptr(hidden), n,
+                                                                  _stream_ptr(stream)))
+
+    def close(self):
+        if self.handle:
+            self.ctx.lib.chpe_comm_destroy(self.handle)
+            self.handle = None
+
+
 class Context:
     def __init__(self, device: int = 0):
         self.lib = L.load()

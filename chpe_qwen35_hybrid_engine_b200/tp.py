@@ -7,8 +7,10 @@ Partition (one exchange per block, as the model's structure allows):
     down projection's K split, so SwiGLU stays rank-local;
   * o, down: row (K) split on group boundaries (down's 462 groups split
     unevenly at 4 and 8 ranks: 115/116 and 57/58 groups);
-  * after o and after down, the [M, hidden] fp32 partial sums are summed with
-    an NCCL all-reduce over NVLink, then added to the replicated hidden state;
+  * after o and after down, the [M, hidden] fp32 partial sums are summed over
+    the ranks and added to the replicated hidden state: by the library's
+    one-shot NVLink all-reduce kernel (every rank pushes its partial into every
+    peer's memory, then sums in rank order), or by NCCL;
   * the LM head is column split over the vocabulary; each rank takes its local
     argmax and the (value, index) pairs are all-gathered and reduced, ties to
     the smaller index as in src/engine.zig:1098-1110.
@@ -66,7 +68,9 @@ def partition(geom: Geometry, world: int, rank: int, group: int) -> dict:
 
 class TensorParallelEngine:
     def __init__(self, ctx, geom: Geometry, scheme: str, rank: int, world: int, seed: int = 0, max_rows: int = 8,
-                 process_group=None, random_codes: bool = False):
+                 process_group=None, random_codes: bool = False, allreduce: str = "p2p"):
+        """allreduce: "p2p" -- the library's one-shot NVLink all-reduce kernel
+        (adds into the hidden state as well); "nccl" -- torch.distributed."""
         import torch
         import torch.distributed as dist
         self.rank, self.world, self.geom = rank, world, geom
@@ -75,7 +79,14 @@ class TensorParallelEngine:
             self.eng = build_random_codes(ctx, geom, scheme, seed=seed, max_rows=max_rows, shard=(rank, world))
         else:
             self.eng, _ = build_random(ctx, geom, scheme, seed=seed, max_rows=max_rows, shard=(rank, world))
-        self.eng.allreduce = (lambda t: dist.all_reduce(t, group=self.pg)) if world > 1 else None
+        self.comm = None
+        if world > 1 and allreduce == "p2p":
+            from .ops import Comm
+            self.comm = Comm(ctx, world, rank, max_rows * geom.hidden)
+            self.comm.exchange(self.pg)
+            self.eng.comm = self.comm
+        elif world > 1:
+            self.eng.allreduce = lambda t: dist.all_reduce(t, group=self.pg)
         self.v0 = rank * geom.vocab // world  # first vocabulary row of this rank's LM-head shard
         dev = self.eng.dev
         self.gather_v = torch.zeros(world, max_rows, dtype=torch.float32, device=dev)

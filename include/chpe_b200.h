@@ -230,6 +230,25 @@ int chpe_xfrag_fill_op_dev(chpe_ctx *ctx, chpe_xfrag *xf, const chpe_xsrc *src, 
 int chpe_gemm_prefill_dev(chpe_ctx *ctx, const chpe_tensor *w, const void *x, int x_dtype, int M, float *y,
                           int ldy, int accumulate, void *stream);
 
+/* ---- tensor parallelism: one-shot all-reduce over NVLink peer memory ------
+ * hidden[i] += sum over the `world` ranks of part_r[i], i < n, after the O and
+ * down projections of a tensor-parallel block.  Each rank pushes its partial
+ * into every peer's receive area (P2P stores through CUDA IPC mappings), raises
+ * a flag there, waits (bounded: 1 s, then CHPE_ETIMEOUT at chpe_sync) for every
+ * peer's flag and sums the partials in rank order -- identical bits on every
+ * rank.  One kernel, no NCCL on this path.  Setup: chpe_comm_create on every
+ * rank, exchange the chpe_comm_handle_bytes() handle of every rank (any host
+ * transport), chpe_comm_open_peers with all ranks' handles in rank order.
+ * Every rank must issue the same sequence of all-reduces.  No counterpart in
+ * the single-process reference. */
+typedef struct chpe_comm chpe_comm;
+int chpe_comm_create(chpe_ctx *ctx, int world, int rank, size_t max_elems, chpe_comm **out);
+size_t chpe_comm_handle_bytes(void);
+int chpe_comm_handle(const chpe_comm *comm, void *out);
+int chpe_comm_open_peers(chpe_comm *comm, const void *handles);
+int chpe_allreduce_residual_dev(chpe_comm *comm, const float *part, float *hidden, size_t n, void *stream);
+int chpe_comm_destroy(chpe_comm *comm);
+
 /* Dynamic per-row int8 activation quantization (device): for each of M rows of
  * length n: s = max|x|/127 (1 if max <= 1e-9), q = clamp(round_half_away(x/s))
  * -- src/kernels/neon.zig:644-670 quantizeActivationInt8, bit-exact. */

@@ -32,7 +32,7 @@ def _port():
     return p
 
 
-def _rank(rank, world, port, scheme, q):
+def _rank(rank, world, port, scheme, q, allreduce="nccl"):
     import torch
     import torch.distributed as dist
     from chpe_qwen35_hybrid_engine_b200 import Context
@@ -43,7 +43,7 @@ def _rank(rank, world, port, scheme, q):
                             device_id=torch.device("cuda", rank))
     try:
         ctx = Context(rank)
-        tp = TensorParallelEngine(ctx, _geom(), scheme, rank, world, seed=21, max_rows=8)
+        tp = TensorParallelEngine(ctx, _geom(), scheme, rank, world, seed=21, max_rows=8, allreduce=allreduce)
         e = tp.eng
         e.buf["tokens"][:1] = 33
         toks = []
@@ -69,15 +69,19 @@ def _rank(rank, world, port, scheme, q):
         dist.all_gather(parts, shard)
         tp.graphs.clear()
         del g
+        assert ctx.lib.chpe_sync(ctx.ptr) == 0  # no kernel recorded a timeout
         if rank == 0:
             q.put((toks, gtoks, torch.cat(parts).cpu().numpy()))
+        dist.barrier()
+        if tp.comm is not None:
+            tp.comm.close()
         ctx.close()
     finally:
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("scheme", ["q4g64", "q8g32"])
-def test_tp2_decode_matches_single_gpu(ctx, scheme):
+@pytest.mark.parametrize("scheme,allreduce", [("q4g64", "p2p"), ("q4g64", "nccl"), ("q8g32", "p2p")])
+def test_tp2_decode_matches_single_gpu(ctx, scheme, allreduce):
     import torch
     import torch.multiprocessing as mp
     if torch.cuda.device_count() < 2:
@@ -86,7 +90,7 @@ def test_tp2_decode_matches_single_gpu(ctx, scheme):
     mpc = mp.get_context("spawn")
     q = mpc.Queue()
     port = _port()
-    procs = [mpc.Process(target=_rank, args=(r, 2, port, scheme, q)) for r in range(2)]
+    procs = [mpc.Process(target=_rank, args=(r, 2, port, scheme, q, allreduce)) for r in range(2)]
     for p in procs:
         p.start()
     try:
@@ -104,3 +108,75 @@ def test_tp2_decode_matches_single_gpu(ctx, scheme):
     torch.cuda.synchronize()
     ref = eng.buf["logits"][0].cpu().numpy()
     assert np.linalg.norm(logits_tp - ref) / np.linalg.norm(ref) < 1e-5
+
+
+def _comm_rank(rank, world, port, q, skip_rank):
+    import torch
+    import torch.distributed as dist
+    from chpe_qwen35_hybrid_engine_b200 import Context
+    from chpe_qwen35_hybrid_engine_b200.ops import Comm
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        ctx = Context(rank)
+        n = 8 * 8192
+        comm = Comm(ctx, world, rank, n)
+        comm.exchange()
+        g = torch.Generator().manual_seed(5)
+        parts = [torch.randn(n, generator=g) for _ in range(world)]
+        h0 = torch.randn(n, generator=g)
+        want = h0.clone()
+        s = torch.zeros(n)
+        for r in range(world):  # the kernel's order: sum of the partials in rank order, then add
+            s = s + parts[r]
+        want = h0 + s
+        part = parts[rank].cuda()
+        hidden = h0.cuda()
+        for it in range(3):  # three epochs in a row (both slot parities)
+            if it > 0:
+                hidden.copy_(h0.cuda())
+            if rank != skip_rank:
+                comm.allreduce_residual(part, hidden, n)
+            torch.cuda.synchronize()
+        rc = ctx.lib.chpe_sync(ctx.ptr)
+        out = (rank, rc, torch.equal(hidden.cpu(), want))
+        dist.barrier()  # peers keep their receive areas mapped until everyone is done
+        comm.close()
+        ctx.close()
+        q.put(out)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("skip_rank", [None, 1])
+def test_p2p_allreduce_exact_and_timeout(ctx, skip_rank):
+    """The one-shot NVLink all-reduce: every rank's hidden state equals
+    h0 + (sum of the partials in rank order) bit for bit, over three epochs.
+    With skip_rank = 1 that rank never joins: rank 0's bounded wait runs out
+    (about 1 s per epoch), the kernel returns, and chpe_sync reports
+    CHPE_ETIMEOUT -- no GPU fault, the context stays usable."""
+    import torch
+    import torch.multiprocessing as mp
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    mpc = mp.get_context("spawn")
+    q = mpc.Queue()
+    port = _port()
+    procs = [mpc.Process(target=_comm_rank, args=(r, 2, port, q, skip_rank)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {}
+    try:
+        for _ in range(2):
+            rank, rc, equal = q.get(timeout=120)
+            res[rank] = (rc, equal)
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+    assert all(p.exitcode == 0 for p in procs)
+    if skip_rank is None:
+        assert res[0] == (0, True) and res[1] == (0, True)
+    else:
+        assert res[0][0] == -5  # CHPE_ETIMEOUT from rank 0's expired wait
+
