@@ -4,21 +4,24 @@
 // hidden += sum over ranks of the partials.
 //
 // Each rank owns, in its own memory, a receive area of 2 x world slots of
-// Mmax x H floats plus world arrival flags, mapped into every peer with CUDA
-// IPC.  One kernel per all-reduce (one CTA of 1024 threads; M <= 8 rows of
-// H <= 8192 is at most 256 KB per rank):
-//   1. take the next epoch (a per-rank counter; every rank runs the same
-//      sequence of all-reduces, so epochs agree),
-//   2. store this rank's partial into slot [epoch & 1][rank] of every peer's
-//      receive area (P2P stores over NVLink; no TMA, no multicast),
-//   3. __threadfence_system, then store the epoch into the peer's flag [rank],
-//   4. wait until every flag of its own area reaches the epoch -- bounded by
-//      1 s of %globaltimer, after which it records an error and returns,
-//   5. hidden[m][i] += partial_0 + partial_1 + ... in rank order (its own
+// Mmax x H floats plus arrival flags [world][chunks], mapped into every peer
+// with CUDA IPC.  One kernel per all-reduce, one CTA per chunk of 1024 floats
+// (M = 1, H = 8192: 8 CTAs); CTA c, independently of the others:
+//   1. reads the epoch (a per-rank counter advanced at the end of every
+//      all-reduce; every rank runs the same sequence, so epochs agree),
+//   2. stores chunk c of this rank's partial into slot [epoch & 1][rank] of
+//      every peer's receive area (P2P stores over NVLink; no TMA, no
+//      multicast), then one thread per peer raises flag [rank][c] there with a
+//      system-scope release store,
+//   3. waits until flag [r][c] of its own area reaches the epoch for every
+//      peer r -- bounded by 1 s of %globaltimer, after which it records an
+//      error and returns,
+//   4. hidden[i] += partial_0[i] + partial_1[i] + ... in rank order (its own
 //      partial read locally), so every rank computes the same bits.
-// Slots alternate with the epoch's parity: a rank can only rewrite a slot two
-// epochs later, after it has seen every peer's flag for the epoch in between,
-// which each peer sets only after it finished reading the older slot.
+// Slots alternate with the epoch's parity: a rank can only rewrite a chunk's
+// slot two epochs later, after it has seen every peer's flag for that chunk in
+// the epoch in between, which each peer raises only after it finished reading
+// the older slot.
 #include <cstring>
 
 #include "../../include/chpe_b200.h"
@@ -29,7 +32,8 @@ namespace chpe {
 namespace {
 
 constexpr int kCommMaxRanks = 8;
-constexpr int kCommThreads = 1024;
+constexpr int kCommThreads = 256;
+constexpr int kCommChunk = 1024;  // floats per CTA
 constexpr int kErrCommWait = 31;
 
 __device__ __forceinline__ void st_release_sys(unsigned *p, unsigned v) {
@@ -42,42 +46,40 @@ __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned *p) {
 }
 
 struct CommPeers {
-    float *recv[kCommMaxRanks];              // each rank's receive area (peer mappings; own one locally)
-    unsigned *flags[kCommMaxRanks];          // each rank's flags [world]
+    float *recv[kCommMaxRanks];      // each rank's receive area (peer mappings; own one locally)
+    unsigned *flags[kCommMaxRanks];  // each rank's flags [world][max_chunks]
 };
 
 __global__ void __launch_bounds__(kCommThreads) allreduce_residual_kernel(const CommPeers peers, int world, int rank,
-                                                                          size_t slot_elems, const float *__restrict__ part,
+                                                                          size_t slot_elems, int max_chunks,
+                                                                          const float *__restrict__ part,
                                                                           float *__restrict__ hidden, int n,
-                                                                          unsigned *__restrict__ epoch_ctr,
+                                                                          unsigned *__restrict__ ctr,
                                                                           int *__restrict__ err) {
-    __shared__ unsigned s_epoch;
     __shared__ int s_ok;
     pdl_begin();  // the partial is the previous kernel's output
-    if (threadIdx.x == 0) {
-        s_epoch = *epoch_ctr + 1u;
-        *epoch_ctr = s_epoch;
-        s_ok = 1;
-    }
-    __syncthreads();
-    const unsigned epoch = s_epoch;
+    const int c = blockIdx.x;
+    const unsigned epoch = ctr[0] + 1u;  // ctr[0] advances only after every CTA of this launch read it
+    if (threadIdx.x == 0) s_ok = 1;
+    const int i0 = c * kCommChunk, i1 = min(n, i0 + kCommChunk);
     const size_t slot = ((size_t)(epoch & 1u) * world + rank) * slot_elems;
-    // 2. push this rank's partial to every peer (float4 when aligned)
-    const int n4 = n / 4;
-    const float4 *p4 = reinterpret_cast<const float4 *>(part);
+    // 2. push chunk c of this rank's partial to every peer, then raise the flags
     for (int r = 0; r < world; ++r) {
         if (r == rank) continue;
-        float4 *dst = reinterpret_cast<float4 *>(peers.recv[r] + slot);
-        for (int i = threadIdx.x; i < n4; i += blockDim.x) dst[i] = p4[i];
-        for (int i = 4 * n4 + threadIdx.x; i < n; i += blockDim.x) peers.recv[r][slot + i] = part[i];
+        float *dst = peers.recv[r] + slot;
+        if (i1 - i0 == kCommChunk) {
+            const float4 v = reinterpret_cast<const float4 *>(part + i0)[threadIdx.x];
+            reinterpret_cast<float4 *>(dst + i0)[threadIdx.x] = v;
+        } else {
+            for (int i = i0 + threadIdx.x; i < i1; i += blockDim.x) dst[i] = part[i];
+        }
     }
-    // 3. make the data visible system-wide, then raise this rank's flag in every peer
-    __threadfence_system();
     __syncthreads();
-    if (threadIdx.x < world && threadIdx.x != rank) st_release_sys(peers.flags[threadIdx.x] + rank, epoch);
-    // 4. wait for every peer's flag in this rank's own area (bounded)
+    if (threadIdx.x < world && threadIdx.x != rank)
+        st_release_sys(peers.flags[threadIdx.x] + (size_t)rank * max_chunks + c, epoch);
+    // 3. wait for every peer's flag of this chunk (bounded)
     if (threadIdx.x < world && threadIdx.x != rank) {
-        const unsigned *f = peers.flags[rank] + threadIdx.x;
+        const unsigned *f = peers.flags[rank] + (size_t)threadIdx.x * max_chunks + c;
         const unsigned long long t0 = global_timer_ns();
         bool ok = false;
         while (true) {
@@ -86,7 +88,7 @@ __global__ void __launch_bounds__(kCommThreads) allreduce_residual_kernel(const 
                 break;
             }
             if (global_timer_ns() - t0 > kWaitTimeoutNs) break;
-            __nanosleep(64);
+            __nanosleep(32);
         }
         if (!ok) {
             atomicExch(err, kErrCommWait);
@@ -94,14 +96,22 @@ __global__ void __launch_bounds__(kCommThreads) allreduce_residual_kernel(const 
         }
     }
     __syncthreads();
-    if (!s_ok) return;
-    __threadfence_system();  // order the flag reads before the data reads
-    // 5. hidden += sum of the partials in rank order
-    const float *own = peers.recv[rank] + (size_t)(epoch & 1u) * world * slot_elems;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
-        float s = 0.0f;
-        for (int r = 0; r < world; ++r) s += (r == rank) ? part[i] : own[(size_t)r * slot_elems + i];
-        hidden[i] += s;
+    if (s_ok) {
+        // 4. hidden += sum of the partials in rank order
+        const float *own = peers.recv[rank] + (size_t)(epoch & 1u) * world * slot_elems;
+        for (int i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
+            float s = 0.0f;
+            for (int r = 0; r < world; ++r) s += (r == rank) ? part[i] : own[(size_t)r * slot_elems + i];
+            hidden[i] += s;
+        }
+    }
+    // the last CTA to finish advances the epoch for the next all-reduce
+    if (threadIdx.x == 0) {
+        __threadfence();
+        if (atomicAdd(&ctr[1], 1u) == gridDim.x - 1) {
+            ctr[1] = 0u;
+            ctr[0] = epoch;
+        }
     }
 }
 
@@ -115,8 +125,9 @@ struct chpe_comm {
     int world = 0, rank = 0;
     size_t max_elems = 0;  // Mmax * H
     float *recv = nullptr;          // own receive area [2][world][max_elems]
-    unsigned *flags = nullptr;      // own flags [world]
-    unsigned *epoch = nullptr;      // own epoch counter
+    unsigned *flags = nullptr;      // own flags [world][max_chunks]
+    unsigned *epoch = nullptr;      // own epoch counter and arrival ticket
+    int max_chunks = 0;
     CommPeers peers;
     bool opened[kCommMaxRanks] = {false};
     cudaIpcMemHandle_t handle_recv, handle_flags;
@@ -132,12 +143,14 @@ extern "C" int chpe_comm_create(chpe_ctx *ctx, int world, int rank, size_t max_e
     c->ctx = ctx;
     c->world = world;
     c->rank = rank;
-    c->max_elems = (max_elems + 3) / 4 * 4;
+    c->max_elems = (max_elems + kCommChunk - 1) / kCommChunk * kCommChunk;
+    c->max_chunks = (int)(c->max_elems / kCommChunk);
     memset(&c->peers, 0, sizeof c->peers);
+    const size_t flag_bytes = (size_t)kCommMaxRanks * c->max_chunks * sizeof(unsigned);
     cudaError_t e = cudaMalloc(&c->recv, 2 * (size_t)world * c->max_elems * sizeof(float));
-    if (e == cudaSuccess) e = cudaMalloc(&c->flags, 256);
+    if (e == cudaSuccess) e = cudaMalloc(&c->flags, flag_bytes);
     if (e == cudaSuccess) e = cudaMalloc(&c->epoch, 256);
-    if (e == cudaSuccess) e = cudaMemset(c->flags, 0, 256);
+    if (e == cudaSuccess) e = cudaMemset(c->flags, 0, flag_bytes);
     if (e == cudaSuccess) e = cudaMemset(c->epoch, 0, 256);
     if (e == cudaSuccess) e = cudaIpcGetMemHandle(&c->handle_recv, c->recv);
     if (e == cudaSuccess) e = cudaIpcGetMemHandle(&c->handle_flags, c->flags);
@@ -193,9 +206,11 @@ extern "C" int chpe_allreduce_residual_dev(chpe_comm *c, const float *part, floa
     if (reinterpret_cast<uintptr_t>(part) % 16) return CHPE_EALIGN;  // read as float4
     for (int r = 0; r < c->world; ++r)
         if (!c->peers.recv[r] || !c->peers.flags[r]) return CHPE_ENOENT;  // peers not opened yet
-    cudaError_t e = launch_pdl(allreduce_residual_kernel, dim3(1), dim3(kCommThreads), 0,
-                               static_cast<cudaStream_t>(stream), c->peers, c->world, c->rank, c->max_elems, part,
-                               hidden, (int)n, c->epoch, chpe_ctx_error_word(c->ctx));
+    if (n == 0) return CHPE_OK;
+    const unsigned chunks = (unsigned)((n + kCommChunk - 1) / kCommChunk);
+    cudaError_t e = launch_pdl(allreduce_residual_kernel, dim3(chunks), dim3(kCommThreads), 0,
+                               static_cast<cudaStream_t>(stream), c->peers, c->world, c->rank, c->max_elems,
+                               c->max_chunks, part, hidden, (int)n, c->epoch, chpe_ctx_error_word(c->ctx));
     return e == cudaSuccess ? CHPE_OK : CHPE_ECUDA;
 }
 
