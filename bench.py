@@ -48,6 +48,19 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 L2_BYTES = 126 * 1024 * 1024
+
+# DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of the dominant
+# kernel, from the ncu captures summarised under profiles/ (per launch; per
+# decode step for the decode workloads).  The 72B-shape step is too large to
+# capture whole: its traffic is the step's algorithmic bytes times the
+# traffic / algorithmic ratio of the captured 29568 x 8192 Q4 GEMV.
+NCU_TRAFFIC = {
+    ("gemv", 8, 12288, 4096, 1, "f32"): 53_560_320,
+    ("gemv", 4, 29568, 8192, 1, "f32"): 141_244_416,
+    ("prefill", 8, 12288, 4096, 2048): 138_023_168,
+    ("decode_9b", 1): 7_385_932_800,
+}
+Q4_TRAFFIC_RATIO = 141_244_416 / 136_400_384
 DECODE_METRIC = "decode tokens/s (quantized GEMV path; GEMV HBM GB/s vs peak in roofline)"
 
 
@@ -330,6 +343,10 @@ def run_decode(args, rank, world, local_rank, which):
         ctx9.close()
     achieved = main["gemv_gbs"]
     n_launch = main["kernel_launches_per_step"] * args.steps
+    if which == "decode_9b":
+        traffic = NCU_TRAFFIC[("decode_9b", 1)]
+    else:
+        traffic = int(main["gemv_bytes_per_step"] * Q4_TRAFFIC_RATIO)
     line = {
         "metric": DECODE_METRIC, "value": round(main["tok_s"] * units, 2), "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": main["ms_per_step"], "higher_is_better": True,
@@ -338,7 +355,8 @@ def run_decode(args, rank, world, local_rank, which):
         "data": "synthetic (seeded random-init weights, seeded uniform token ids)",
         "config": config,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                     "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": None,
+                     "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": traffic,
+                     "traffic_unit": "bytes per step (all GEMV launches of one step, per GPU)",
                      "peak_source": peaks["source"],
                      "kernel": "gemv_kernel: all GEMVs of one step on one GPU, bytes / GEMV time",
                      "algorithmic_bytes_per_step": main["gemv_bytes_per_step"],
@@ -494,7 +512,8 @@ def run_gemv(args, rank, world, local_rank):
         "data": "synthetic (seeded uniform codes, lognormal fp16 group scales, x N(0,1))",
         "config": cfg,
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                     "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": None,
+                     "frac": round(achieved / peaks["hbm_gbs"], 4),
+                     "traffic": NCU_TRAFFIC.get(("gemv", c.bits, N, K, M, c.xdtype)),
                      "peak_source": peaks["source"], "kernel": "gemv_kernel", "kernel_us": round(kern_ms * 1e3, 3),
                      "algorithmic_bytes": algo},
         "e2e": {"value": round(world * algo / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
@@ -573,7 +592,8 @@ def run_prefill(args, rank, world, local_rank):
         "vs_baseline": None, "dtype": "fp16 tensor-core operands (bf16 x, dequantized weights), fp32 accumulate",
         "data": "synthetic (seeded uniform codes, lognormal fp16 group scales, x N(0,1))", "config": cfg,
         "roofline": {"bound": "tensor", "achieved": round(tflops, 1), "peak": peak, "unit": "TFLOP/s",
-                     "frac": round(tflops / peak, 4), "traffic": None, "peak_source": peaks["source"] + " (bf16 burst)",
+                     "frac": round(tflops / peak, 4), "traffic": NCU_TRAFFIC.get(("prefill", c.bits, N, K, M)),
+                     "peak_source": peaks["source"] + " (bf16 burst)",
                      "kernel": "prefill_gemm_kernel (+ activation tile prep)", "flops_per_step": flops},
         "e2e": {"value": round(world * flops / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
                 "h2d_bytes_per_step": int(M * K * 2), "d2h_bytes_per_step": int(M * N * 4)},
