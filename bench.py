@@ -172,50 +172,42 @@ def timed_replays(replay, steps, world, dev):
 # ----------------------------------------------------------------------------
 
 def gemv_step_profile(ctx, eng, M, reps, dev):
-    """Every GEMV of one step (as the engine issues them at this row count),
-    with activation fragments prepared beforehand, captured as one graph and
-    replayed `reps` times.  Returns (GEMV ms per step, algorithmic bytes per
-    step, GEMV launches per step)."""
+    """Every GEMV of one step as the engine issues it at this row count
+    (activation fragments prepared beforehand, one fragment set per input),
+    captured as one graph and replayed `reps` times.  Returns (GEMV ms per
+    step, algorithmic bytes per step, GEMV launches per step)."""
     import torch
     from chpe_qwen35_hybrid_engine_b200 import X_F32
-    singles, fused, multis = [], [], []
+    groups = []  # (tensors, mode)
     for lw in eng.layers:
         p = lw.proj
-        if "q" in p:
-            multis.append([p["q"], p["k"], p["v"]])
-            singles.append(p["o"])
-        else:
-            multis.append([p["qkv"], p["z"]])
-            singles.append(p["out"])
-        if M == 1:
-            fused.append((p["gate"], p["up"]))
-        else:
-            singles += [p["gate"], p["up"]]
-        singles.append(p["down"])
-    singles.append(eng.head)
+        groups.append(([p["q"], p["k"], p["v"]] if "q" in p else [p["qkv"], p["z"]], 0))
+        groups.append(([p["o"] if "q" in p else p["out"]], 0))
+        groups.append(([p["gate"], p["up"]], 1 if M == 1 else 0))
+        groups.append(([p["down"]], 0))
+    groups.append(([eng.head], 0))
+    rows = max(t.rows for ts, _ in groups for t in ts)
+    ys = [torch.empty(M, rows, device=dev) for _ in range(3)]
     xfs = {}
-
-    def xf_for(t):
-        key = (t.cols, t.bits)
+    for ts, _ in groups:
+        key = (ts[0].cols, ts[0].bits)
         if key not in xfs:
-            xf = ctx.xfrag(t, M, X_F32)
-            ctx.xfrag_fill(xf, torch.randn(M, t.cols, device=dev))
+            xf = ctx.xfrag(ts[0], M, X_F32)
+            ctx.xfrag_fill(xf, torch.randn(M, ts[0].cols, device=dev))
             xfs[key] = xf
-        return xfs[key]
-
-    rows = max([t.rows for t in singles] + [g.rows for g, _ in fused] + [t.rows for m in multis for t in m])
-    y = torch.empty(M, rows, device=dev)
-    ys = [torch.empty(M, rows, device=dev) for _ in range(4)]
+    torch.cuda.synchronize(dev)
     st = torch.cuda.Stream(dev)
     st.wait_stream(torch.cuda.current_stream(dev))
 
     def issue():
-        for m in multis:
-            ctx.gemv_multi_xfrag(m, xf_for(m[0]), ys[:len(m)], stream=st)
-        for t in singles:
-            ctx.gemv_xfrag(t, xf_for(t), y, stream=st)
-        for g, u in fused:
-            ctx.gemv_gateup_swiglu_xfrag(g, u, xf_for(g), y, stream=st)
+        for ts, mode in groups:
+            xf = xfs[(ts[0].cols, ts[0].bits)]
+            if mode == 1:
+                ctx.gemv_gateup_swiglu_xfrag(ts[0], ts[1], xf, ys[0], stream=st)
+            elif len(ts) > 1:
+                ctx.gemv_multi_xfrag(ts, xf, ys[:len(ts)], stream=st)
+            else:
+                ctx.gemv_xfrag(ts[0], xf, ys[0], stream=st)
 
     with torch.cuda.stream(st):
         issue()
@@ -229,10 +221,12 @@ def gemv_step_profile(ctx, eng, M, reps, dev):
     del graph
     for xf in xfs.values():
         xf.free()
-    nbytes = sum(t.device_bytes + M * t.cols * 4 + M * t.rows * 4 for t in singles)
-    nbytes += sum(g.device_bytes + u.device_bytes + M * g.cols * 4 + M * g.rows * 4 for g, u in fused)
-    nbytes += sum(sum(t.device_bytes + M * t.rows * 4 for t in m) + M * m[0].cols * 4 for m in multis)
-    return ms, nbytes, len(singles) + len(fused) + len(multis)
+    nbytes = 0
+    for ts, mode in groups:
+        nbytes += sum(t.device_bytes + M * t.rows * 4 for t in ts) + M * ts[0].cols * 4
+        if mode == 1:
+            nbytes -= M * ts[1].rows * 4  # one output for gate and up
+    return ms, nbytes, len(groups)
 
 
 def decode_line(eng, stepper, M, args, world, dev, label, profile=True):

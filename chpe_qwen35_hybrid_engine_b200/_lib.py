@@ -82,6 +82,7 @@ SIGNATURES = {
     "chpe_comm_destroy": (I, [P]),
     "chpe_xfrag_free": (I, [P, P]),
     "chpe_xfrag_fill_op_dev": (I, [P, P, C.POINTER(chpe_xsrc), P]),
+    "chpe_gemv_src_dev": (I, [P, I, I, P, C.POINTER(chpe_xsrc), I, P, I, P]),
     "chpe_gemv_parallel": (I, [P, P, F, P, F, SZ, SZ, P]),
     "chpe_gemv_gate_up_swiglu_parallel": (I, [P, P, F, P, F, P, F, SZ, SZ, P]),
     "chpe_gemv_batch4_parallel": (I, [P, P, F, P, P, P, P, P, SZ, SZ, P, P, P, P]),

@@ -364,7 +364,8 @@ void fill_params(GemvParams &p, int mode, const DevMatrix *const *ms, int n, con
 }
 
 int gemv_core(chpe_ctx *ctx, const DevMatrix &w0, const DevMatrix *w1, int mode, const Xfrag &f, float *y, int ldy,
-              int accumulate, const float *scale_override0, const float *scale_override1, cudaStream_t st) {
+              int accumulate, const float *scale_override0, const float *scale_override1, cudaStream_t st,
+              const XSrc *src = nullptr) {
     GemvPlan P;
     plan_gemv(w0, f.M, mode, f.xsplit, &P);
     int rc = check_frag(ctx, w0, P, f);
@@ -376,14 +377,19 @@ int gemv_core(chpe_ctx *ctx, const DevMatrix &w0, const DevMatrix *w1, int mode,
     GemvParams p;
     fill_params(p, mode, ms, mode == 1 ? 2 : 1, ovr, &y, &ldy, accumulate, P, f, ctx->scr.ws, ctx->scr.counters,
                 ctx->d_err);
+    if (src) {
+        p.xsrc = *src;
+        p.fused = 1;
+    }
     cudaError_t e = launch_gemv(w0, w1, P, p, st);
     if (e != cudaSuccess) return fail(ctx, CHPE_ECUDA, "gemv launch: %s", cudaGetErrorString(e));
     return CHPE_OK;
 }
 
-// One launch over n <= kMaxSrc plain sources with the same K and format.
+// One launch over n <= kMaxSrc plain sources with the same K and format;
+// with `src`, every CTA builds its activation fragments from it (fused fill).
 int gemv_multi_core(chpe_ctx *ctx, const DevMatrix *const *ms, int n, const Xfrag &f, float *const *ys,
-                    cudaStream_t st) {
+                    cudaStream_t st, const XSrc *src = nullptr, int accumulate = 0) {
     const DevMatrix &w0 = *ms[0];
     int total_sg = 0;
     for (int r = 0; r < n; ++r) {
@@ -407,7 +413,11 @@ int gemv_multi_core(chpe_ctx *ctx, const DevMatrix *const *ms, int n, const Xfra
     int ldys[kMaxSrc];
     for (int r = 0; r < n; ++r) ldys[r] = ms[r]->N;
     GemvParams p;
-    fill_params(p, 0, ms, n, nullptr, ys, ldys, 0, P, f, ctx->scr.ws, ctx->scr.counters, ctx->d_err);
+    fill_params(p, 0, ms, n, nullptr, ys, ldys, accumulate, P, f, ctx->scr.ws, ctx->scr.counters, ctx->d_err);
+    if (src) {
+        p.xsrc = *src;
+        p.fused = 1;
+    }
     cudaError_t e = launch_gemv(w0, nullptr, P, p, st);
     if (e != cudaSuccess) return fail(ctx, CHPE_ECUDA, "gemv launch: %s", cudaGetErrorString(e));
     return CHPE_OK;
@@ -1070,6 +1080,69 @@ extern "C" int chpe_gemv_xfrag_dev(chpe_ctx *ctx, const chpe_tensor *w, const ch
         return fail(ctx, CHPE_EINVAL, "tensor has outlier columns: create the fragments like it (fp32)");
     return gemv_core(ctx, w->m, nullptr, 0, xf->f, y, w->m.N, accumulate, nullptr, nullptr,
                      static_cast<cudaStream_t>(stream));
+}
+
+// XSrc from the C struct (shared with chpe_xfrag_fill_op_dev), validated.
+int make_xsrc(chpe_ctx *ctx, const chpe_xsrc *src, int K, XSrc *out) {
+    if (src->op < CHPE_XOP_PLAIN || src->op > CHPE_XOP_SSM_STUB) return fail(ctx, CHPE_EINVAL, "unknown op %d", src->op);
+    if (src->op == CHPE_XOP_PLAIN && src->x_dtype != CHPE_X_F32)
+        return fail(ctx, CHPE_EINVAL, "fused fills read fp32 activations");
+    if (src->op != CHPE_XOP_PLAIN && src->op != CHPE_XOP_ATTN_STUB && !src->aux)
+        return fail(ctx, CHPE_EINVAL, "op %d needs aux", src->op);
+    if (src->op == CHPE_XOP_ATTN_STUB &&
+        (src->kv_dim < 1 ||
+         (src->head_dim && (src->group < 1 || ((K / src->head_dim + src->group - 1) / src->group) * src->head_dim >
+                                                      (src->ldx > 0 ? src->ldx : K)))))
+        return fail(ctx, CHPE_EINVAL, "attention stand-in shape");
+    if (src->op == CHPE_XOP_SSM_STUB && src->qkv_dim < 1) return fail(ctx, CHPE_EINVAL, "qkv_dim must be >= 1");
+    XSrc s;
+    s.op = src->op;
+    s.x = src->x;
+    s.dt = CHPE_X_F32;
+    s.ldx = src->ldx > 0 ? src->ldx : K;
+    s.aux = src->aux;
+    s.ld_aux = src->ld_aux > 0 ? src->ld_aux : K;
+    s.eps = src->eps;
+    s.kv_dim = src->kv_dim;
+    s.head_dim = src->head_dim;
+    s.group = src->group;
+    s.qkv_dim = src->qkv_dim;
+    s.silu_on_qkv = src->silu_on_qkv;
+    *out = s;
+    return CHPE_OK;
+}
+
+extern "C" int chpe_gemv_src_dev(chpe_ctx *ctx, int mode, int n, const chpe_tensor *const *ws, const chpe_xsrc *src,
+                                 int M, float *const *ys, int accumulate, void *stream) {
+    if (!ctx || !ws || !src || !src->x || !ys) return fail(ctx, CHPE_EINVAL, "null argument");
+    if (M < 1 || M > kMaxTokens) return fail(ctx, CHPE_EINVAL, "fused GEMV takes 1..%d rows (got %d)", kMaxTokens, M);
+    if (mode != 0 && mode != 1) return fail(ctx, CHPE_EINVAL, "mode 0 (plain) or 1 (gate/up SwiGLU)");
+    if (mode == 1 ? n != 2 : (n < 1 || n > kMaxSrc)) return fail(ctx, CHPE_EINVAL, "tensor count %d for mode %d", n, mode);
+    for (int r = 0; r < n; ++r)
+        if (!ws[r] || (r < (mode == 1 ? 1 : n) && !ys[r])) return fail(ctx, CHPE_EINVAL, "null tensor or output %d", r);
+    const DevMatrix &w0 = ws[0]->m;
+    if (w0.layout != kLayoutF16)
+        return fail(ctx, CHPE_ENOTSUP, "fused fills feed the fp16 tensor-core path (not int8 x int8 W8A8)");
+    for (int r = 0; r < n; ++r)
+        if (ws[r]->m.out_cols) return fail(ctx, CHPE_ENOTSUP, "fused fills do not cover outlier columns");
+    XSrc s;
+    int rc = make_xsrc(ctx, src, w0.K, &s);
+    if (rc) return rc;
+    cudaSetDevice(ctx->device);
+    size_t xfb, xsb;
+    Xfrag f = xfrag_shape(w0, M, CHPE_X_F32, &xfb, &xsb);  // shape only: the kernel builds the fragments
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (mode == 1) {
+        const DevMatrix &g = ws[0]->m, &u = ws[1]->m;
+        if (g.N != u.N || g.K != u.K || g.bits != u.bits || g.layout != u.layout || g.meta_kind != u.meta_kind ||
+            g.group != u.group || g.zc != u.zc)
+            return fail(ctx, CHPE_EINVAL, "gate and up must share shape and format");
+        return gemv_core(ctx, g, &u, 1, f, ys[0], g.N, 0, nullptr, nullptr, st, &s);
+    }
+    if (n == 1) return gemv_core(ctx, w0, nullptr, 0, f, ys[0], w0.N, accumulate, nullptr, nullptr, st, &s);
+    const DevMatrix *ms[kMaxSrc];
+    for (int r = 0; r < n; ++r) ms[r] = &ws[r]->m;
+    return gemv_multi_core(ctx, ms, n, f, ys, st, &s, accumulate);
 }
 
 extern "C" int chpe_gemm_prefill_dev(chpe_ctx *ctx, const chpe_tensor *w, const void *x, int x_dtype, int M, float *y,

@@ -32,6 +32,7 @@
 
 #include "common.cuh"
 #include "internal.h"
+#include "xsrc.cuh"
 
 namespace chpe {
 
@@ -251,6 +252,108 @@ template <typename V> __device__ __forceinline__ auto comp(const V &v, int c) {
     return c == 0 ? v.x : c == 1 ? v.y : c == 2 ? v.z : v.w;
 }
 
+// Value k of row m of a fused fill's source, specialised by op (the switch of
+// xsrc_value resolved at compile time, so the loads of a unit can be issued
+// together).
+// (RMSNorm, the op of every block's first GEMV, is resolved at compile time;
+// the other ops go through xsrc_value.)
+template <int OP>
+__device__ __forceinline__ float fused_src(const XSrc &s, int m, int k, float inv) {
+    if constexpr (OP == kXRmsnorm) {
+        return __fmul_rn(__fmul_rn(static_cast<const float *>(s.x)[(size_t)m * s.ldx + k], inv), s.aux[k]);
+    } else {
+        return xsrc_value(s, m, k, inv);
+    }
+}
+
+// Fused fill (fp32 activations split into fp16 hi + lo, F16 layout): the 256
+// threads of the MMA warps build this CTA's K-slice of activation fragments
+// and epilogue-block sums in shared memory, in the layout the bulk-copied
+// fragments have (xfill_f16_kernel, same bits), straight from the source op --
+// RMSNorm statistics included, so no fill kernel runs between two GEMVs.
+// Ends with a barrier of the MMA warps.
+template <int BITS, int E, int OP>
+__device__ __forceinline__ void fused_fill_op(const GemvParams &p, uint8_t *xf_s, float *xs_s, float *scratch,
+                                              int b0, int nb, int span) {
+    constexpr int S = (256 / BITS) / 16;  // k-steps per chunk
+    const int tid = threadIdx.x;           // 0..255 (MMA warps)
+    const int lane = tid & 31, warp = tid >> 5;
+    const int M = p.M, K = p.K;
+    const XSrc &xs = p.xsrc;
+    float inv[kMaxTokens];
+#pragma unroll
+    for (int m = 0; m < kMaxTokens; ++m) inv[m] = 1.0f;
+    if constexpr (OP == kXRmsnorm) {
+        // 1 / sqrt(mean(x^2) + eps) per row in the order of row_inv_rms
+#pragma unroll
+        for (int m = 0; m < kMaxTokens; ++m) {
+            if (m >= M) break;
+            float acc = row_sumsq_part(static_cast<const float *>(xs.x) + (size_t)m * xs.ldx, K, tid, kNW * 32);
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+            if (lane == 0) scratch[warp * kMaxTokens + m] = acc;
+        }
+        named_bar_sync(1, kNW * 32);
+#pragma unroll
+        for (int m = 0; m < kMaxTokens; ++m) {
+            if (m >= M) break;
+            float tot = 0.0f;
+#pragma unroll
+            for (int w = 0; w < kNW; ++w) tot += scratch[w * kMaxTokens + m];
+            inv[m] = inv_rms_of(tot, K, xs.eps);
+        }
+    }
+    const int units = nb * kChunksPerBlock * S * 4;  // a multiple of 32: whole warps take part below
+    const int k_base = b0 * span;
+#pragma unroll 2
+    for (int u = tid; u < units; u += kNW * 32) {
+        const int sr = u >> 2, t = u & 3;
+        const int j = sr % S;
+        const int sh = BITS == 4 ? 4 * (j & 1) : BITS == 2 ? 2 * (j & 3) : 0;
+        const float down = __int_as_float((127 - sh) << 23), up = __int_as_float((127 + sh) << 23);
+        const int kb = k_base + 16 * sr + 2 * t;
+        const int kk[4] = {kb, kb + 1, kb + 8, kb + 9};
+        float part[kMaxTokens];
+#pragma unroll
+        for (int m = 0; m < kMaxTokens; ++m) {
+            part[m] = 0.0f;
+            if (m < M) {
+                float v[4];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) v[q] = kk[q] < K ? fused_src<OP>(xs, m, kk[q], inv[m]) : 0.0f;
+                __half h[4], l[4];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const float w = v[q] * down;
+                    h[q] = __float2half_rn(w);
+                    l[q] = __float2half_rn(w - __half2float(h[q]));
+                    part[m] += (__half2float(h[q]) + __half2float(l[q])) * up;
+                }
+                *reinterpret_cast<uint4 *>(xf_s + ((size_t)(sr * M + m) * 4 + t) * 16) =
+                    make_uint4(pack_h2(h[0], h[1]), pack_h2(h[2], h[3]), pack_h2(l[0], l[1]), pack_h2(l[2], l[3]));
+            }
+        }
+        // E/4 consecutive threads hold one epilogue block
+#pragma unroll
+        for (int m = 0; m < kMaxTokens; ++m) {
+            if (m >= M) break;
+            float v = part[m];
+            for (int off = E / 8; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+            if ((u % (E / 4)) == 0) xs_s[(size_t)(u / (E / 4)) * 8 + m] = v;
+        }
+    }
+    named_bar_sync(1, kNW * 32);
+}
+
+template <int BITS, int E>
+__device__ __forceinline__ void fused_fill(const GemvParams &p, uint8_t *xf_s, float *xs_s, float *scratch, int b0,
+                                           int nb, int span) {
+    if (p.xsrc.op == kXRmsnorm)
+        fused_fill_op<BITS, E, kXRmsnorm>(p, xf_s, xs_s, scratch, b0, nb, span);
+    else
+        fused_fill_op<BITS, E, -1>(p, xf_s, xs_s, scratch, b0, nb, span);
+}
+
 // XM: how the activation operand is fed (GemvPlan::xmode).
 template <int BITS, int LAYOUT, int E, int XM, int MODE, int META>
 __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
@@ -354,13 +457,13 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
                     bulk_g2s_hint(smem + L.ring + ((size_t)slot * kSG + q) * BB, src, (uint32_t)BB, &full[slot], pol);
                 }
                 // weights first, then (once) the upstream-dependent activations
-                if (!x_issued && it + 1 >= kStages) issue_x();
+                if (!p.fused && !x_issued && it + 1 >= kStages) issue_x();
                 if (++bi == nb) {
                     bi = 0;
                     ++sg;
                 }
             }
-            if (!x_issued) issue_x();
+            if (!p.fused && !x_issued) issue_x();
             // end-of-work marker in the next slot
             {
                 const int slot = it % kStages, use = it / kStages;
@@ -374,7 +477,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
                 const int last = s + ((it - 1 - s) / kStages) * kStages;
                 if (!mbar_wait_bounded(&full[s], (last / kStages) & 1)) atomicExch(p.err, kErrWaitFull);
             }
-            if (!mbar_wait_bounded(xbar, 0)) atomicExch(p.err, kErrWaitPrologue);
+            if (!p.fused && !mbar_wait_bounded(xbar, 0)) atomicExch(p.err, kErrWaitPrologue);
         }
     } else if (warp == kEpilogueWarp) {
         // ---------------- epilogue warp ----------------
@@ -510,13 +613,22 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
         const int gshift = p.gshift;
 
         bool aborted = false;
-        // A timed-out wait ends this warp's work; decisions are taken per warp
-        // (__all_sync) and every wait is bounded, so no warp can be left stuck.
-        if (!__all_sync(0xffffffffu, mbar_wait_bounded(xbar, 0))) {
-            if (lane == 0) atomicExch(p.err, kErrWaitPrologue);
-            aborted = true;
+        if constexpr (LAYOUT == kLayoutF16 && XSPLIT) {
+            if (p.fused) {
+                grid_dependency_wait();  // the source rows are the previous kernel's output
+                fused_fill<BITS, E>(p, smem + L.xf, reinterpret_cast<float *>(smem + L.xs),
+                                    reinterpret_cast<float *>(smem + L.red), b0, nb, KC * kChunksPerBlock);
+            }
         }
-        grid_dependency_wait();
+        if (!p.fused) {
+            // A timed-out wait ends this warp's work; decisions are taken per warp
+            // (__all_sync) and every wait is bounded, so no warp can be left stuck.
+            if (!__all_sync(0xffffffffu, mbar_wait_bounded(xbar, 0))) {
+                if (lane == 0) atomicExch(p.err, kErrWaitPrologue);
+                aborted = true;
+            }
+            grid_dependency_wait();
+        }
 
         Acc acc[kSG][4];
 #pragma unroll

@@ -33,6 +33,20 @@ struct DevMatrix {
     size_t bytes = 0;
 };
 
+// Where the activations of a fragment fill come from (xfill / xmaterialize):
+// the plain rows x, or one of the step's elementwise producers fused in.
+enum XSrcOp : int { kXPlain = 0, kXRmsnorm = 1, kXSiluMul = 2, kXAttnStub = 3, kXSsmStub = 4 };
+struct XSrc {
+    int op = kXPlain;
+    const void *x = nullptr;  // rows [M][ldx] (fp32 except for kXPlain)
+    int dt = 0;               // kXPlain: CHPE_X_* of x
+    int ldx = 0;
+    const float *aux = nullptr;  // gamma [K] (rmsnorm), up [M][ld_aux] (silu*mul), z [M][ld_aux] (ssm)
+    int ld_aux = 0;
+    float eps = 0.0f;
+    int kv_dim = 1, head_dim = 0, group = 1;  // attention stand-in
+    int qkv_dim = 1, silu_on_qkv = 0;         // Gated-DeltaNet stand-in
+};
 struct GemvSrc {
     const uint8_t *codes;
     const float *bias;
@@ -75,6 +89,11 @@ struct GemvParams {
     unsigned *split_cnt;  // [n_sg] arrivals of partial sums (self-resetting)
     int rmode;            // 0: last CTA to arrive sums the partials; 1: gemv_reduce_kernel does
     int gk;               // CTAs per K-slice (set at launch)
+    // fused fill: with `fused` set, every CTA builds the activation fragments
+    // of its K-slice in shared memory from `xsrc` (fp32 rows [M][K]) instead
+    // of copying prepared ones (xf / xs unused)
+    XSrc xsrc;
+    int fused;
     int *err;
 };
 
@@ -109,20 +128,6 @@ struct GemvPlan {
 
 int plan_gemv(const DevMatrix &w, int M, int mode, bool xsplit, GemvPlan *plan);
 
-// Where the activations of a fragment fill come from (xfill / xmaterialize):
-// the plain rows x, or one of the step's elementwise producers fused in.
-enum XSrcOp : int { kXPlain = 0, kXRmsnorm = 1, kXSiluMul = 2, kXAttnStub = 3, kXSsmStub = 4 };
-struct XSrc {
-    int op = kXPlain;
-    const void *x = nullptr;  // rows [M][ldx] (fp32 except for kXPlain)
-    int dt = 0;               // kXPlain: CHPE_X_* of x
-    int ldx = 0;
-    const float *aux = nullptr;  // gamma [K] (rmsnorm), up [M][ld_aux] (silu*mul), z [M][ld_aux] (ssm)
-    int ld_aux = 0;
-    float eps = 0.0f;
-    int kv_dim = 1, head_dim = 0, group = 1;  // attention stand-in
-    int qkv_dim = 1, silu_on_qkv = 0;         // Gated-DeltaNet stand-in
-};
 cudaError_t launch_xfill_f16(const XSrc &s, int M, int K, int Kp, int e_cols, bool xsplit, int bits, void *xf,
                              float *xs, cudaStream_t st);
 cudaError_t launch_xmaterialize(const XSrc &s, int M, int K, float *out, cudaStream_t st);

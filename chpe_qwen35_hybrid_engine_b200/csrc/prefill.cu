@@ -301,7 +301,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
     } else if (warp >= kDeqWarp0) {
         // ---------------- dequant, then epilogue ----------------
         const int dw = warp - kDeqWarp0;  // 0..15: strip dw of the tile, weight rows 16dw..16dw+15
-        const int g = lane >> 2, t = lane & 3;
+        const int g = lane >> 2;
         // stmatrix address of this lane inside a 16 x 16 block: row (lane % 8) + 8 ((lane / 8) & 1) of the
         // strip, columns 8 (lane / 16) .. +7 of the k-step
         const int st_row = 16 * dw + (lane & 7) + 8 * ((lane >> 3) & 1);

@@ -5,6 +5,7 @@
 
 #include "common.cuh"
 #include "internal.h"
+#include "xsrc.cuh"
 
 namespace chpe {
 
@@ -12,54 +13,12 @@ namespace chpe {
 // activations
 // ---------------------------------------------------------------------------
 
-__device__ __forceinline__ float load_x(const void *x, int dt, size_t i) {
-    if (dt == 0) return static_cast<const float *>(x)[i];
-    if (dt == 1) return __bfloat162float(static_cast<const __nv_bfloat16 *>(x)[i]);
-    return __half2float(static_cast<const __half *>(x)[i]);
-}
-
-__device__ __forceinline__ uint32_t pack_h2(__half a, __half b) {
-    __half2 h = __halves2half2(a, b);
-    return *reinterpret_cast<uint32_t *>(&h);
-}
-
-// Value k of activation row tok, as produced by the source op (XSrc):
-//   kXPlain     x[tok][k] (fp32 / bf16 / fp16)
-//   kXRmsnorm   x[tok][k] * inv_rms(tok) * gamma[k]      (src/kernels/neon.zig:673-702)
-//   kXSiluMul   silu(x[tok][k]) * aux[tok][k]            (src/kernels/neon.zig:705-712)
-//   kXAttnStub  x[tok][src(k)]: the attention stand-in of src/engine.zig:619-623
-//               (src = k % kv_dim), or head-aligned (query head h takes kv head h / group)
-//   kXSsmStub   the Gated-DeltaNet stand-in, q = x[tok][k % qkv_dim], z = aux[tok][k]:
-//               q * silu(z) (batch 1, src/engine.zig:651-654) or silu(q) * z (:813, :988)
-__device__ __forceinline__ float xsrc_value(const XSrc &s, int tok, int k, float inv) {
-    switch (s.op) {
-    case kXRmsnorm: {
-        const float v = static_cast<const float *>(s.x)[(size_t)tok * s.ldx + k];
-        return __fmul_rn(__fmul_rn(v, inv), s.aux[k]);
-    }
-    case kXSiluMul:
-        return silu_f(static_cast<const float *>(s.x)[(size_t)tok * s.ldx + k]) * s.aux[(size_t)tok * s.ld_aux + k];
-    case kXAttnStub: {
-        const int src = s.head_dim ? ((k / s.head_dim) / s.group) * s.head_dim + (k % s.head_dim) : (k % s.kv_dim);
-        return static_cast<const float *>(s.x)[(size_t)tok * s.ldx + src];
-    }
-    case kXSsmStub: {
-        const float q = static_cast<const float *>(s.x)[(size_t)tok * s.ldx + (k % s.qkv_dim)];
-        const float z = s.aux[(size_t)tok * s.ld_aux + k];
-        return s.silu_on_qkv ? silu_f(q) * z : q * silu_f(z);
-    }
-    default:
-        return load_x(s.x, s.dt, (size_t)tok * s.ldx + k);
-    }
-}
-
-// 1 / sqrt(mean(x^2) + eps) of row tok, summed in a fixed order (strided by
-// the block, then a shuffle tree and the warp partials in order), so every
-// block of the row gets the same value.  Whole block; red: 32 floats.
+// 1 / sqrt(mean(x^2) + eps) of row tok (blocks of 256 threads): per-thread
+// partials in the fixed order of row_sumsq_part, a shuffle tree, the warp
+// partials in order -- the same bits as the GEMV kernel's fused fill.
 __device__ float row_inv_rms(const XSrc &s, int tok, int K, float *red) {
     const float *row = static_cast<const float *>(s.x) + (size_t)tok * s.ldx;
-    float acc = 0.0f;
-    for (int k = threadIdx.x; k < K; k += blockDim.x) acc = fmaf(row[k], row[k], acc);
+    float acc = row_sumsq_part(row, K, threadIdx.x, blockDim.x);
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
     if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
@@ -67,7 +26,7 @@ __device__ float row_inv_rms(const XSrc &s, int tok, int K, float *red) {
     float tot = 0.0f;
     for (int w = 0; w < (int)(blockDim.x >> 5); ++w) tot += red[w];
     __syncthreads();
-    return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)K), s.eps)));
+    return inv_rms_of(tot, K, s.eps);
 }
 
 // Activation fragments of the fp16 GEMV path.  Grid (units / 256, M): one

@@ -269,6 +269,7 @@ class HybridEngine:
         self.xfrags = {}           # (input, rows) -> XFrag
         self.allreduce = None      # set by tensor parallelism: fn(tensor) summing across ranks (NCCL)
         self.comm = None           # or the NVLink one-shot all-reduce (ops.Comm)
+        self.fuse_fills = False    # GEMVs build their own fragments (chpe_gemv_src_dev) instead of a shared fill
         g, Mx = geom, max_rows
         f32 = dict(dtype=torch.float32, device=self.dev)
         widest = max(g.hidden, g.q_dim, g.ssm_qkv or 1, g.ffn)
@@ -301,82 +302,78 @@ class HybridEngine:
     def step(self, M: int, stream=None):
         """Run one step over rows 0..M-1 of buf["tokens"]; leaves logits, argmax, maxv.
 
-        Each GEMV input is produced straight into the MMA operand layout by a
-        fused fill (RMSNorm, the token-mixer stand-ins, SiLU * mul), so the
-        normalised hidden state and the mixer outputs never reach memory; the
-        Q/K/V (or DeltaNet qkv/z) projections, and gate/up, share one fill."""
+        Each GEMV input is produced straight into the MMA operand layout by one
+        fused fill (RMSNorm of the hidden state, the token-mixer stand-ins, SiLU
+        * mul), shared by the GEMVs of that input, so the normalised hidden
+        state and the mixer outputs never reach memory; the Q/K/V (or DeltaNet
+        qkv/z) projections share one launch, gate/up another.  With fuse_fills
+        each GEMV builds its fragments in its own CTAs instead."""
         import torch
         g, ctx, lib = self.geom, self.ctx, self.ctx.lib
         b = self.buf
         st = stream or torch.cuda.current_stream(self.dev)
         sp = _stream_ptr(st)
         H = g.hidden
+        # fused fills only on request: every CTA of a K-slice builds the same
+        # fragments, which on B200 costs more than the fill kernel it saves
+        fused = self.fuse_fills and self.scheme != "w8a8"
 
-        def gemv(t: Tensor, xf, y, acc=False):
-            self._check(lib.chpe_gemv_xfrag_dev(ctx.ptr, t.handle, xf.handle, _dev_ptr(y), int(acc), sp))
+        def run(ts, ys, op, x, aux=None, mode=0, acc=False, **kw):
+            """ys (+)= op(x, aux) . W^T for the tensors ts (one launch)."""
+            if fused:
+                ctx.gemv_src(ts, ys, op, x, aux, M=M, mode=mode, accumulate=acc, stream=sp.value, **kw)
+                return
+            xf = self._xf(("in", ts[0].cols), ts[0], M)
+            ctx.xfrag_fill_op(xf, op, x, aux, stream=sp.value, **kw)
+            if mode == 1:
+                self._check(lib.chpe_gemv_gateup_swiglu_xfrag_dev(ctx.ptr, ts[0].handle, ts[1].handle, xf.handle,
+                                                                  _dev_ptr(ys[0]), sp))
+            elif len(ts) > 1:
+                ctx.gemv_multi_xfrag(ts, xf, ys, stream=sp.value)
+            else:
+                ctx.gemv_xfrag(ts[0], xf, ys[0], accumulate=acc, stream=sp.value)
 
-        def multi(ts, xf, ys):
-            """One launch for the projections that read the same input."""
-            hs = (C.c_void_p * len(ts))(*[t.handle for t in ts])
-            yp = (C.c_void_p * len(ts))(*[y.data_ptr() for y in ys])
-            self._check(lib.chpe_gemv_multi_xfrag_dev(ctx.ptr, len(ts), hs, xf.handle, yp, sp))
-
-        def fill(xf, op, x, aux=None, ldx=0, ld_aux=0, **kw):
-            ctx.xfrag_fill_op(xf, op, x, aux, ldx=ldx, ld_aux=ld_aux, stream=sp.value, **kw)
-
-        def gemv_res(t: Tensor, xf, hidden):
-            """hidden += x . W^T (the residual add of the block); with tensor
+        def run_res(t: Tensor, op, x, aux=None, **kw):
+            """hidden += op(x) . W^T (the residual add of the block); with tensor
             parallelism the shard's partial sum is summed over the ranks first:
             one NVLink all-reduce kernel that also adds into hidden (comm), or
             an NCCL all-reduce and an add."""
+            hidden = b["hidden"]
+            if self.comm is None and self.allreduce is None:
+                run([t], [hidden], op, x, aux, acc=True, **kw)
+                return
+            part = b["mix_out"][:M]
+            run([t], [part], op, x, aux, **kw)
             if self.comm is not None:
-                part = b["mix_out"][:M]
-                gemv(t, xf, part)
                 self.comm.allreduce_residual(part, hidden, M * H, stream=sp.value)
-            elif self.allreduce is None:
-                gemv(t, xf, hidden, acc=True)
             else:
-                part = b["mix_out"][:M]
-                gemv(t, xf, part)
                 self.allreduce(part)
                 hidden[:M].add_(part)
 
         self._check(lib.chpe_embed_i8_dev(ctx.ptr, _dev_ptr(self.embed), C.c_float(self.embed_scale), H, g.vocab,
                                           _dev_ptr(b["tokens"]), M, _dev_ptr(b["hidden"]), sp))
         hid = b["hidden"]
+        norm = dict(ldx=H, eps=g.eps)
         for l, lw in enumerate(self.layers):
             p = lw.proj
-            xin = self._xf("in", p["gate"], M)
-            fill(xin, L.XOP_RMSNORM, hid, lw.in_gamma, ldx=H, eps=g.eps)
             if "q" in p:  # full attention (GQA) block; stand-in mixer = V broadcast
                 q_out, k_out, v_out = b["a"], b["b"], b["c"]
                 kv = p["v"].rows
-                multi([p["q"], p["k"], p["v"]], xin, [q_out, k_out, v_out])
-                xo = self._xf("o", p["o"], M)
-                fill(xo, L.XOP_ATTN_STUB, v_out, ldx=kv, kv_dim=kv, head_dim=g.head_dim,
-                     group=g.q_heads // g.kv_heads)
-                gemv_res(p["o"], xo, hid)
+                run([p["q"], p["k"], p["v"]], [q_out, k_out, v_out], L.XOP_RMSNORM, hid, lw.in_gamma, **norm)
+                run_res(p["o"], L.XOP_ATTN_STUB, v_out, ldx=kv, kv_dim=kv, head_dim=g.head_dim,
+                        group=g.q_heads // g.kv_heads)
             else:  # Gated DeltaNet block; stand-in mixer = qkv gated by z
                 qkv_out, z_out = b["a"], b["b"]
-                multi([p["qkv"], p["z"]], xin, [qkv_out, z_out])
-                xo = self._xf("out", p["out"], M)
-                fill(xo, L.XOP_SSM_STUB, qkv_out, z_out, ldx=p["qkv"].rows, ld_aux=p["z"].rows,
-                     qkv_dim=p["qkv"].rows, silu_on_qkv=M > 1)
-                gemv_res(p["out"], xo, hid)
-            fill(xin, L.XOP_RMSNORM, hid, lw.post_gamma, ldx=H, eps=g.eps)
-            xd = self._xf("down", p["down"], M)
+                run([p["qkv"], p["z"]], [qkv_out, z_out], L.XOP_RMSNORM, hid, lw.in_gamma, **norm)
+                run_res(p["out"], L.XOP_SSM_STUB, qkv_out, z_out, ldx=p["qkv"].rows, ld_aux=p["z"].rows,
+                        qkv_dim=p["qkv"].rows, silu_on_qkv=M > 1)
             if M == 1:  # src/engine.zig:682 fused gate/up SwiGLU
-                self._check(lib.chpe_gemv_gateup_swiglu_xfrag_dev(ctx.ptr, p["gate"].handle, p["up"].handle,
-                                                                  xin.handle, _dev_ptr(b["a"]), sp))
-                fill(xd, L.XOP_PLAIN, b["a"], ldx=p["down"].cols)
+                run([p["gate"], p["up"]], [b["a"]], L.XOP_RMSNORM, hid, lw.post_gamma, mode=1, **norm)
+                run_res(p["down"], L.XOP_PLAIN, b["a"], ldx=p["down"].cols)
             else:  # src/engine.zig:839-844 unfused gate, up, siluMul
-                gemv(p["gate"], xin, b["b"])
-                gemv(p["up"], xin, b["c"])
-                fill(xd, L.XOP_SILU_MUL, b["b"], b["c"], ldx=p["gate"].rows, ld_aux=p["up"].rows)
-            gemv_res(p["down"], xd, hid)
-        xin = self._xf("in", self.layers[0].proj["gate"], M) if self.layers else self._xf("in", self.head, M)
-        fill(xin, L.XOP_RMSNORM, hid, self.final_gamma, ldx=H, eps=g.eps)
-        gemv(self.head, xin, b["logits"])
+                run([p["gate"], p["up"]], [b["b"], b["c"]], L.XOP_RMSNORM, hid, lw.post_gamma, **norm)
+                run_res(p["down"], L.XOP_SILU_MUL, b["b"], b["c"], ldx=p["gate"].rows, ld_aux=p["up"].rows)
+        run([self.head], [b["logits"]], L.XOP_RMSNORM, hid, self.final_gamma, **norm)
         self._check(lib.chpe_argmax_dev(ctx.ptr, _dev_ptr(b["logits"]), M, self.head.rows, _dev_ptr(b["argmax"]),
                                         _dev_ptr(b["maxv"]), sp))
 

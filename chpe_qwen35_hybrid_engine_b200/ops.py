@@ -251,6 +251,21 @@ class Context:
                         int(silu_on_qkv))
         self._check(self.lib.chpe_xfrag_fill_op_dev(self.ptr, xf.handle, C.byref(s), _stream_ptr(stream)))
 
+    def gemv_src(self, tensors, outs, op: int, x, aux=None, M: int = 1, mode: int = 0, accumulate: bool = False,
+                 ldx: int = 0, ld_aux: int = 0, eps: float = 0.0, kv_dim: int = 1, head_dim: int = 0, group: int = 1,
+                 qkv_dim: int = 1, silu_on_qkv: bool = False, stream=None):
+        """GEMV(s) with the activation producer fused in (chpe_gemv_src_dev):
+        mode 0: outs[r] (+)= src . tensors[r]^T; mode 1: outs[0] = SwiGLU of
+        tensors (gate, up).  src = op(x, aux) as in xfrag_fill_op."""
+        s = L.chpe_xsrc(op, _dev_ptr(x), L.X_F32, ldx, _dev_ptr(aux), ld_aux, eps, kv_dim, head_dim, group, qkv_dim,
+                        int(silu_on_qkv))
+        n = len(tensors)
+        hs = (C.c_void_p * n)(*[t.handle for t in tensors])
+        ys = (C.c_void_p * n)(*[(_dev_ptr(outs[i]).value if i < len(outs) else None) for i in range(n)])
+        self._check(self.lib.chpe_gemv_src_dev(self.ptr, mode, n, hs, C.byref(s), M, ys, int(accumulate),
+                                               _stream_ptr(stream)))
+        return outs
+
     def gemv_xfrag(self, w: Tensor, xf: "XFrag", out, accumulate: bool = False, stream=None):
         self._check(self.lib.chpe_gemv_xfrag_dev(self.ptr, w.handle, xf.handle, _dev_ptr(out), int(accumulate),
                                                  _stream_ptr(stream)))

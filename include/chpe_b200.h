@@ -213,6 +213,15 @@ typedef struct chpe_xsrc {
     int qkv_dim, silu_on_qkv;    /* CHPE_XOP_SSM_STUB */
 } chpe_xsrc;
 int chpe_xfrag_fill_op_dev(chpe_ctx *ctx, chpe_xfrag *xf, const chpe_xsrc *src, void *stream);
+/* GEMV with the producer fused into it: every CTA builds the activation
+ * fragments of its own K-slice from `src` (fp32 rows; RMSNorm statistics
+ * computed in the CTA), so no fill kernel or fragment buffer sits between two
+ * GEMVs.  mode 0: ys[r][M, rows_r] (+)= x . W_r^T for n = 1..4 tensors of the
+ * same cols and format (accumulate != 0 adds into y); mode 1: n = 2 (gate,
+ * up), ys[0] = silu(x.Wg^T) * (x.Wu^T).  fp16-path tensors only (not W8A8),
+ * M = 1..8.  Same results as chpe_xfrag_fill_op_dev + the _xfrag_ GEMVs. */
+int chpe_gemv_src_dev(chpe_ctx *ctx, int mode, int n, const chpe_tensor *const *ws, const chpe_xsrc *src, int M,
+                      float *const *ys, int accumulate, void *stream);
 
 /* Prefill dequant-GEMM on the 5th-generation tensor cores (tcgen05, fp32
  * accumulation in tensor memory): y[M, rows] (+)= x[M, cols] . dequant(W)^T

@@ -109,3 +109,60 @@ def test_fill_op_errors(ctx):
         ctx.xfrag_fill_op(xf, 99, x)
     xf.free()
     t.free()
+
+
+@pytest.mark.parametrize("bits", [8, 4])
+@pytest.mark.parametrize("M", [1, 3, 8])
+def test_fused_fill_gemv_equals_fill_then_gemv(ctx, bits, M):
+    """chpe_gemv_src_dev (each GEMV CTA builds its fragments from the source op,
+    RMSNorm statistics included) gives the same bits as chpe_xfrag_fill_op_dev
+    followed by the fragment GEMVs: plain, accumulate, three tensors in one
+    launch, and gate/up SwiGLU."""
+    import torch
+    from chpe_qwen35_hybrid_engine_b200 import X_F32, _lib as L
+    rng = np.random.default_rng(100 + bits * 10 + M)
+    K = 4096
+    t0, _ = _tensor(ctx, rng, bits, 520, K)
+    t1, _ = _tensor(ctx, rng, bits, 100, K)
+    t2, _ = _tensor(ctx, rng, bits, 520, K)
+    xf = ctx.xfrag(t0, M, X_F32)
+    dev = "cuda"
+    x = torch.from_numpy((rng.standard_normal((M, K + 32)) * 2).astype(np.float32)).to(dev)
+    gamma = torch.from_numpy((1 + 0.1 * rng.standard_normal(K)).astype(np.float32)).to(dev)
+    u = torch.from_numpy(rng.standard_normal((M, K)).astype(np.float32)).to(dev)
+    v = torch.from_numpy(rng.standard_normal((M, 1024)).astype(np.float32)).to(dev)
+    cases = [dict(op=L.XOP_RMSNORM, x=x, aux=gamma, ldx=K + 32, eps=1e-6),
+             dict(op=L.XOP_SILU_MUL, x=x, aux=u, ldx=K + 32, ld_aux=K),
+             dict(op=L.XOP_ATTN_STUB, x=v, ldx=1024, kv_dim=1024, head_dim=128, group=4),
+             dict(op=L.XOP_SSM_STUB, x=v, aux=u, ldx=1024, ld_aux=K, qkv_dim=768, silu_on_qkv=M > 1),
+             dict(op=L.XOP_PLAIN, x=x[:, :K].contiguous())]
+    for kw in cases:
+        ctx.xfrag_fill_op(xf, kw["op"], kw["x"], kw.get("aux"), ldx=kw.get("ldx", 0), ld_aux=kw.get("ld_aux", 0),
+                          eps=kw.get("eps", 0.0), kv_dim=kw.get("kv_dim", 1), head_dim=kw.get("head_dim", 0),
+                          group=kw.get("group", 1), qkv_dim=kw.get("qkv_dim", 1),
+                          silu_on_qkv=kw.get("silu_on_qkv", False))
+        ref = [torch.empty(M, t.rows, device=dev) for t in (t0, t1)]
+        ctx.gemv_multi_xfrag([t0, t1], xf, ref)
+        ref_gu = torch.empty(M, 520, device=dev)
+        ctx.gemv_gateup_swiglu_xfrag(t0, t2, xf, ref_gu)
+        base = torch.from_numpy(rng.standard_normal((M, 520)).astype(np.float32)).to(dev)
+        ref_acc = base.clone()
+        ctx.gemv_xfrag(t0, xf, ref_acc, accumulate=True)
+        op = kw.pop("op")
+        xx = kw.pop("x")
+        aux = kw.pop("aux", None)
+        got = [torch.empty(M, t.rows, device=dev) for t in (t0, t1)]
+        ctx.gemv_src([t0, t1], got, op, xx, aux, M=M, **kw)
+        got_gu = torch.empty(M, 520, device=dev)
+        ctx.gemv_src([t0, t2], [got_gu], op, xx, aux, M=M, mode=1, **kw)
+        got_acc = base.clone()
+        ctx.gemv_src([t0], [got_acc], op, xx, aux, M=M, accumulate=True, **kw)
+        torch.cuda.synchronize()
+        assert torch.equal(got[0], ref[0]) and torch.equal(got[1], ref[1]), op
+        assert torch.equal(got_gu, ref_gu), op
+        assert torch.equal(got_acc, ref_acc), op
+    assert ctx.lib.chpe_sync(ctx.ptr) == 0
+    xf.free()
+    for t in (t0, t1, t2):
+        t.free()
+
