@@ -37,14 +37,14 @@
 namespace chpe {
 
 constexpr int kNW = 8;      // MMA warps per CTA (one chunk of each block)
-constexpr int kStages = 4;  // ring depth (blocks per strip)
+constexpr int kStages = 3;  // ring depth (blocks per strip)
 constexpr int kProducerWarp = kNW, kEpilogueWarp = kNW + 1;
 constexpr int kThreads = (kNW + 2) * 32;
 // activation fragments staged per CTA: small enough for two CTAs per SM at
 // M <= 2 (2 x (74 KB ring + 28 KB + reduction buffers) <= 220 KB); with more
 // rows the reduction buffers already limit a CTA to one SM, which then stages
 // as much of K as fits (fewer K-slices, fewer partials)
-constexpr int kXMaxBytes = 28 * 1024;
+constexpr int kXMaxBytes = 40 * 1024;
 constexpr int kXMaxBytesWide = 100 * 1024;
 constexpr int kSmemBudget = 220 * 1024;
 static_assert(kNW == kChunksPerBlock, "one block per stage, one chunk per warp");
