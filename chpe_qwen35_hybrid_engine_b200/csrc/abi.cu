@@ -359,7 +359,12 @@ void fill_params(GemvParams &p, int mode, const DevMatrix *const *ms, int n, con
     p.accumulate = accumulate;
     p.ws = ws;
     p.split_cnt = counters;
-    p.maxp = P.maxp;
+    p.work_ctr = counters + P.n_sg;
+    p.n_whole = P.n_whole;
+    p.bc = P.bc;
+    p.cfull = P.cfull;
+    p.ctot = P.ctot;
+    p.pref = P.pref;
     p.err = err;
 }
 
@@ -489,6 +494,8 @@ int finish(chpe_ctx *ctx) {
     CK(cudaMemcpy(&h_err, ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost));
     if (h_err) {
         cudaMemset(ctx->d_err, 0, sizeof(int));
+        // a kernel that gave up may have left arrival / work counters set
+        if (ctx->scr.counters) cudaMemset(ctx->scr.counters, 0, ctx->scr.counters_n * sizeof(unsigned));
         return fail(ctx, CHPE_ETIMEOUT, "kernel bounded wait expired (code %d)", h_err);
     }
     return CHPE_OK;

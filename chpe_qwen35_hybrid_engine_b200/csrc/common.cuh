@@ -130,6 +130,16 @@ __device__ __forceinline__ void mma_s8_m16n8k32(int d[4], uint32_t a0, uint32_t 
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+// Atomic add at GPU scope with acquire-release semantics; returns the old
+// value.  The release half publishes the writes that the issuing warp made
+// before a __syncwarp; the acquire half makes the other CTAs' writes that
+// preceded their own releases visible to this warp (after a __syncwarp).
+__device__ __forceinline__ unsigned atom_add_acq_rel_gpu(unsigned *p, unsigned v) {
+    unsigned old;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
+
 // Programmatic dependent launch: wait for the upstream grid's memory.
 __device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void grid_dependents_launch() {

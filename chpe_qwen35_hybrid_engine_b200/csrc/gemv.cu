@@ -44,39 +44,54 @@ int plan_gemv(const DevMatrix &w, int M, int mode, bool xsplit, GemvPlan *plan) 
     const size_t xmax = M <= 2 ? kXMaxBytes : kXMaxBytesWide;
     const int bpk_max = (int)std::max<size_t>(1, xmax / x_per_block);
     // Fewest K-slices whose activation fragments fit the staging budget, with
-    // equal slices; the stream-K partition balances the work, not the slicing.
+    // equal slices; the work counters balance the work, not the slicing.
     int n_ks = std::min(ceil_div(w.n_blocks, std::min(bpk_max, w.n_blocks)), kMaxKs);
     const int bpk = ceil_div(w.n_blocks, n_ks);
     n_ks = ceil_div(w.n_blocks, bpk);
     const size_t smem = smem_layout(w.layout, w.bits, bpk, M, xsplit, P.e_cols, w.block_bytes).total;
-    const int per_sm = std::max(1, (int)std::min<size_t>(4, kSmemBudget / (smem + 1024)));
-    // no CTA may get an empty range (the partial counts assume none): at most
-    // as many CTAs per slice as the shortest slice has items
+    // at most two CTAs per SM (the kernel's registers: __launch_bounds__(kThreads, 2))
+    const int per_sm = std::max(1, (int)std::min<size_t>(2, kSmemBudget / (smem + 1024)));
     const int nb_last = w.n_blocks - (n_ks - 1) * bpk;
-    const long items = (long)P.n_sg * nb_last;
-    P.items_min = items;
     P.sms = num_sms();
     // upper bound here; the launch recomputes the grid from the kernel's occupancy
-    long gk = std::min<long>((long)P.sms * per_sm / n_ks, items);
-    // at least ~4 items per CTA: small matrices get fewer, longer ranges
-    gk = std::min<long>(gk, std::max<long>(1, (long)P.n_sg * bpk / 4));
-    gk = std::max<long>(1, gk);
+    long gk = (long)P.sms * per_sm / n_ks;
+    // at least ~4 blocks of work per CTA: small matrices get fewer CTAs
+    gk = std::max<long>(1, std::min<long>(gk, std::max<long>(1, (long)P.n_sg * bpk / 4)));
+    // Work units.  Whole strip groups (per K-slice) stream fastest -- long
+    // runs per strip, no partial sums -- but balance poorly, so they come in
+    // rounds of one per CTA covering about 70 % of a CTA's share, with at
+    // least one whole strip group's worth of chunks left after a second
+    // round (a CTA that draws a whole strip group late then still ends with
+    // the others).  The rest is cut into chunks of bc blocks.  Units of one
+    // or two blocks cost more in hand-offs and arrival counts than they gain
+    // in balance, so chunks are four blocks unless a CTA has fewer than six
+    // blocks of work.
+    const long per_cta = (long)P.n_sg * bpk / gk;
+    P.bc = per_cta >= 6 ? 4 : per_cta >= 3 ? 2 : 1;
+    long rounds = per_cta * 7 / (10 * bpk);
+    if (rounds >= 2 && per_cta - rounds * bpk < bpk) --rounds;
+    P.n_whole = (int)std::min<long>(P.n_sg, rounds * gk);
+    // More than two rows: one CTA per SM, each with many blocks of work, so
+    // whole strip groups alone balance well enough; partial sums only across
+    // K-slices, summed by gemv_reduce_kernel.
+    if (M > 2) {
+        P.rmode = 1;
+        P.n_whole = P.n_sg;
+    }
+    P.cfull = ceil_div(bpk, P.bc);
+    P.ctot = std::max((n_ks - 1) * P.cfull + ceil_div(nb_last, P.bc), n_ks);
+    // static units cover the ring's first fill (fetched before the upstream kernel ends)
+    P.pref = ceil_div(kStages, P.bc);
+    P.items_min = slice_units(P.n_sg, P.n_whole, ceil_div(nb_last, P.bc));
+    gk = std::min<long>(gk, P.items_min);
     P.n_ks = n_ks;
-    // Split-K partials are summed by a second, fully parallel kernel: with
-    // several K-slices, or more than two rows, the sums at the end of a CTA's
-    // range would keep its epilogue warp (and then its MMA warps) waiting on
-    // L2 round trips.  With one slice only the few strip groups cut by range
-    // boundaries have partials; the last CTA to arrive sums those.
-    P.rmode = (M > 2 || n_ks > 1) ? 1 : 0;
     P.bpk = bpk;
     P.grid = (int)(gk * n_ks);
     P.smem = smem;
-    // CTAs of one slice touching one strip group: at most gk / n_sg + 2
-    P.maxp = n_ks * (int)(gk / P.n_sg + 2);
     P.xf_bytes = (size_t)w.n_blocks * xfrag_bytes_per_block(w.layout, w.bits, M, xsplit);
     P.xs_bytes = w.layout == kLayoutF16 ? (size_t)w.n_blocks * kChunksPerBlock * ne * 32 : 0;
-    P.ws_bytes = (size_t)P.n_sg * P.maxp * kSG * 16 * 8 * 4;
-    P.split_counters = P.n_sg;
+    P.ws_bytes = P.ctot > 1 ? (size_t)P.n_sg * P.ctot * kSG * 16 * M * 4 : 0;
+    P.split_counters = P.n_sg + n_ks;
     *plan = P;
     return 0;
 }

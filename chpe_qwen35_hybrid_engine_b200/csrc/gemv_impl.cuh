@@ -3,15 +3,19 @@
 // code width in gemv_b8.cu / gemv_b4.cu / gemv_b2.cu / gemv_s8.cu; planned and
 // dispatched in gemv.cu.
 //
-// Persistent, warp-specialised kernel.  A CTA (8 consumer warps + 1 producer
-// warp) is bound to one K-slice for its lifetime: its activation fragments are
-// bulk-copied into shared memory once.  The (strip group, block) items of the
-// slice are split stream-K style into one equal contiguous range per CTA.  The
-// producer thread streams its range -- per strip and stage one block, 4 KiB of
-// codes plus the block's group metadata, in one 1-D bulk copy (TMA engine,
-// mbarrier completion, L2 evict-first) -- through a 4-stage shared-memory
-// ring.  A strip group is four 16-row strips, or for the fused gate/up SwiGLU
-// the same two strips of the gate and of the up matrix.
+// Persistent, warp-specialised kernel.  A CTA (8 MMA warps, 1 producer warp,
+// 1 epilogue warp) is bound to one K-slice for its lifetime: its activation
+// fragments are bulk-copied into shared memory once.  The slice's work is cut
+// into units (strip groups, whole or in chunks of blocks; see unit_of).
+// Every CTA takes its first units statically, so it can start fetching
+// weights before the upstream kernel has finished, and the rest from a
+// per-slice atomic work counter, so CTAs that stream faster take more units
+// and all of them finish within about one unit of each other.  The producer
+// warp streams each unit -- per strip and stage one block, 4 KiB of codes plus
+// the block's group metadata, in one 1-D bulk copy (TMA engine, mbarrier
+// completion, L2 evict-first) -- through a 3-stage shared-memory ring.  A
+// strip group is four 16-row strips, or for the fused gate/up SwiGLU the same
+// two strips of the gate and of the up matrix.
 //
 // Each MMA warp takes one chunk of every block, turns codes into fp16 MMA
 // operands in registers with one LOP3 / PRMT per pair (the code as an exact
@@ -21,11 +25,13 @@
 // per-group scale / zero-point into fp32 register accumulators:
 //     acc += s * D + (-z * s * 2^-24) * sum(x over the block),  y = 2^24 * acc.
 // The int8 x int8 path (W8A8) feeds raw codes to m16n8k32 integer MMAs and
-// keeps exact int32 sums.  When a CTA's range leaves a strip group, its warps
-// reduce through shared memory in a fixed order; a strip group covered by
-// several CTAs (range boundaries, K-slices) collects one partial sum per CTA
-// in a workspace slot numbered by slice and range, and the last CTA to arrive
-// (atomic count) sums the slots in slot order, so results are deterministic.
+// keeps exact int32 sums.  At the end of a unit the MMA warps hand their
+// accumulators to the epilogue warp (shared memory, fixed warp order).  A
+// strip group that is one unit over its whole K is finished there; otherwise
+// the unit's sum goes to the workspace slot of its chunk, and the CTA that
+// brings the last chunk of the strip group (acquire-release arrival count)
+// sums all slots in chunk order.  The sum of a chunk does not depend on which
+// CTA computed it, so results are deterministic.
 #pragma once
 #include <algorithm>
 #include <type_traits>
@@ -54,13 +60,16 @@ constexpr size_t kZeroSlot = 496;
 
 struct SmemLayout {
     size_t bar, tags, ring, xf, xs, red, info, total;
+    int nbuf;  // accumulator hand-off buffers (2 or 4)
 };
 
-// Hand-off of one finished segment from the MMA warps to the epilogue warp.
+// Hand-off of one finished unit from the MMA warps to the epilogue warp.
 struct SegInfo {
-    int sg;     // strip group, -1 = no more segments
-    int whole;  // the segment covers the strip group's whole K
+    int sg;  // strip group, -1 = no more units
+    int gc;  // chunk of the strip group's K
 };
+
+constexpr int kMaxRedBufs = 4;
 
 __host__ __device__ inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
@@ -73,34 +82,61 @@ __host__ __device__ inline size_t xfrag_bytes_per_block(int layout, int bits, in
 __host__ __device__ inline SmemLayout smem_layout(int layout, int bits, int bpk, int M, bool xsplit, int e_cols,
                                                   int block_bytes) {
     SmemLayout L;
-    L.bar = 0;    // full[kStages], empty[kStages], xbar, rfull[2], rempty[2]
+    // hand-off buffers: four at M <= 2 (the epilogue warp may spend an L2
+    // round trip per unit without holding up the MMA warps), two above
+    L.nbuf = M <= 2 ? kMaxRedBufs : 2;
+    L.bar = 0;    // full[kStages], empty[kStages], xbar, rfull[kMaxRedBufs], rempty[kMaxRedBufs]
     L.tags = 256; // unit / block / flag tag per ring slot; 16 zero bytes at kZeroSlot
     size_t o = 512;
-    static_assert((2 * kStages + 5) * 8 <= 256 && 256 + 3 * kStages * 4 <= kZeroSlot, "barrier / tag area");
+    static_assert((2 * kStages + 1 + 2 * kMaxRedBufs) * 8 <= 256 && 256 + 3 * kStages * 4 <= kZeroSlot,
+                  "barrier / tag area");
     L.ring = o;
     o += align_up((size_t)kStages * kSG * block_bytes, 128);
     L.xf = o;
     o = align_up(o + (size_t)bpk * xfrag_bytes_per_block(layout, bits, M, xsplit), 128);
     L.xs = o;
     if (layout == kLayoutF16) o = align_up(o + (size_t)bpk * kChunksPerBlock * ((256 / bits) / e_cols) * 32, 128);
-    L.red = o;  // two buffers of per-warp accumulators [warp][strip][16 rows][M]
-    o += 2 * (size_t)kNW * kSG * 16 * M * 4;
+    L.red = o;  // nbuf buffers of per-warp accumulators [warp][strip][16 rows][M]
+    o += (size_t)L.nbuf * kNW * kSG * 16 * M * 4;
     L.info = o;
-    o += 2 * sizeof(SegInfo);
+    o += kMaxRedBufs * sizeof(SegInfo);
     L.total = align_up(o, 128);
     return L;
 }
 
-// Stream-K partition of the (strip group, block) items of one K-slice over the
-// Gk CTAs that work on it: CTA j owns items [start(j), start(j+1)).
-__host__ __device__ inline long part_start(long T, int Gk, int j) { return (long)j * T / Gk; }
-__host__ __device__ inline int part_owner(long T, int Gk, long x) { return (int)(((x + 1) * Gk - 1) / T); }
+// Work units of one K-slice with nbk blocks.  Strip groups below n_whole are
+// one unit each (all nbk blocks: long contiguous runs per strip, no partial
+// sums within the slice); the others are cut into C chunks of bc blocks, so
+// the last units handed out are short.  Unit u < n_whole is strip group u;
+// unit n_whole + v is chunk v % C of strip group n_whole + v / C.  A CTA of the
+// slice takes units j, j + Gk, ... (P of them) statically, then units
+// P * Gk + g for the values g it draws from the slice's work counter, until
+// one is past the last unit.  Each CTA draws exactly one such past-the-end
+// value; the draw that returns the last value of the launch
+// (grabs_total - 1) resets the counter for the next launch.
+__host__ __device__ inline int unit_chunks(int nbk, int bc) { return (nbk + bc - 1) / bc; }
 
-// Number of CTAs of a slice with nbk blocks whose range touches strip group sg.
-__host__ __device__ inline int part_count(int sg, int nbk, long n_sg, int Gk) {
-    const long T = n_sg * nbk;
-    return part_owner(T, Gk, (long)sg * nbk + nbk - 1) - part_owner(T, Gk, (long)sg * nbk) + 1;
+struct Unit {
+    int sg, bs, be;  // strip group, blocks [bs, be) of the slice
+    int gc, ctot;    // chunk index within the strip group's whole K, and its chunk count
+};
+// (32-bit arithmetic: a 64-bit division costs the producer a few hundred
+// dependent instructions per unit, time in which no copy is issued)
+__host__ __device__ inline Unit unit_of(int u, int nbk, int C, int ks, int n_ks, int n_whole, int bc, int cfull,
+                                        int ctot_split) {
+    if (u < n_whole) return Unit{u, 0, nbk, ks, n_ks};
+    const unsigned v = (unsigned)(u - n_whole);
+    const unsigned q = v / (unsigned)C;
+    const int c = (int)(v - q * (unsigned)C);
+    const int be = c * bc + bc < nbk ? c * bc + bc : nbk;
+    return Unit{n_whole + (int)q, c * bc, be, ks * cfull + c, ctot_split};
 }
+__host__ __device__ inline int slice_units(int n_sg, int n_whole, int C) { return n_whole + (n_sg - n_whole) * C; }
+// Static units per CTA: enough blocks to fill the ring before the first draw.
+__host__ __device__ inline int static_units(int n_whole, int Gk, int nbk, int pref) {
+    return n_whole >= Gk ? (kStages + nbk - 1) / nbk : pref;
+}
+__host__ __device__ inline int grabs_total(int U, int pref, int Gk) { return (U > pref * Gk ? U - pref * Gk : 0) + Gk; }
 
 // Codes become fp16 operands with the exponent field left at zero: the bit
 // pattern `code` is the fp16 subnormal code * 2^-24, exact for every code
@@ -229,14 +265,6 @@ __device__ __forceinline__ void finalize_entry(const GemvParams &p, int sg, int 
     }
 }
 
-// Workspace slots of strip group sg: one per (K-slice, CTA of that slice whose
-// range touches sg), numbered slice by slice in CTA order.
-__host__ __device__ inline int slot_count(const GemvParams &p, int sg) {
-    int total = 0;
-    for (int kk = 0; kk < p.n_ks; ++kk) total += part_count(sg, min(p.bpk, p.n_blocks - kk * p.bpk), p.n_sg, p.gk);
-    return total;
-}
-
 template <typename Acc> struct Vec4;
 template <> struct Vec4<float> {
     using T = float4;
@@ -248,6 +276,62 @@ template <> struct Vec4<int> {
     __device__ static T zero() { return make_int4(0, 0, 0, 0); }
     __device__ static void add(T &a, const T &b) { a.x += b.x; a.y += b.y; a.z += b.z; a.w += b.w; }
 };
+template <typename Acc> struct Vec2;
+template <> struct Vec2<float> {
+    using T = float2;
+    __device__ static T zero() { return make_float2(0.f, 0.f); }
+    __device__ static void add(T &a, const T &b) { a.x += b.x; a.y += b.y; }
+    __device__ static T sum(const T &a, const T &b) { return make_float2(a.x + b.x, a.y + b.y); }
+};
+template <> struct Vec2<int> {
+    using T = int2;
+    __device__ static T zero() { return make_int2(0, 0); }
+    __device__ static void add(T &a, const T &b) { a.x += b.x; a.y += b.y; }
+    __device__ static T sum(const T &a, const T &b) { return make_int2(a.x + b.x, a.y + b.y); }
+};
+
+// Final sum of the ctot chunk slots of strip group sg (slots [ctot][nq]
+// entries, nq = kSG * 16 * M), finalized into y: eight running sums over the
+// chunks (chunk c into sum c % 8), combined as
+// ((s0 + s1) + (s2 + s3)) + ((s4 + s5) + (s6 + s7)).  The association depends
+// only on ctot, so the result does not depend on which CTA runs it.  Two
+// entries per lane and load.
+template <int LAYOUT, int MODE, typename Acc>
+__device__ __forceinline__ void reduce_slots(const GemvParams &p, const Acc *slots, int ctot, int sg, int lane) {
+    using V2 = Vec2<Acc>;
+    using T2 = typename V2::T;
+    const int M = p.M;
+    const int nq2 = kSG * 16 * M / 2;             // float2 units of a slot
+    const int nout2 = MODE == 1 ? nq2 / 2 : nq2;  // units finalized (gate/up: the gate half)
+    const int up2 = 16 * M;                       // gate/up: up entries follow two strips later
+    const T2 *s2 = reinterpret_cast<const T2 *>(slots);
+    for (int q2 = lane; q2 < nout2; q2 += 32) {
+        T2 a[8], u[8];
+#pragma unroll
+        for (int h = 0; h < 8; ++h) a[h] = u[h] = V2::zero();
+        int c = 0;
+        for (; c + 8 <= ctot; c += 8) {
+#pragma unroll
+            for (int h = 0; h < 8; ++h) {
+                V2::add(a[h], __ldcg(&s2[(size_t)(c + h) * nq2 + q2]));
+                if (MODE == 1) V2::add(u[h], __ldcg(&s2[(size_t)(c + h) * nq2 + q2 + up2]));
+            }
+        }
+#pragma unroll
+        for (int h = 0; h < 7; ++h)
+            if (c + h < ctot) {
+                V2::add(a[h], __ldcg(&s2[(size_t)(c + h) * nq2 + q2]));
+                if (MODE == 1) V2::add(u[h], __ldcg(&s2[(size_t)(c + h) * nq2 + q2 + up2]));
+            }
+        const T2 v = V2::sum(V2::sum(V2::sum(a[0], a[1]), V2::sum(a[2], a[3])),
+                             V2::sum(V2::sum(a[4], a[5]), V2::sum(a[6], a[7])));
+        const T2 vu = V2::sum(V2::sum(V2::sum(u[0], u[1]), V2::sum(u[2], u[3])),
+                              V2::sum(V2::sum(u[4], u[5]), V2::sum(u[6], u[7])));
+        finalize_entry<LAYOUT, MODE, Acc>(p, sg, 2 * q2, v.x, vu.x);
+        finalize_entry<LAYOUT, MODE, Acc>(p, sg, 2 * q2 + 1, v.y, vu.y);
+    }
+}
+
 template <typename V> __device__ __forceinline__ auto comp(const V &v, int c) {
     return c == 0 ? v.x : c == 1 ? v.y : c == 2 ? v.z : v.w;
 }
@@ -366,7 +450,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
     constexpr int NE = (LAYOUT == kLayoutS8) ? 1 : KC / E;
     constexpr int SPE = (LAYOUT == kLayoutS8) ? 1 : E / 16;
     constexpr int MB = META == kMetaS16 ? 2 : META == kMetaSZ16 ? 4 : 8;
-    constexpr int kFirst = 1, kLast = 2;
+    constexpr int kLast = 1;  // ring tag: last block of a unit (the chunk index in the bits above)
 
     extern __shared__ __align__(128) uint8_t smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -376,8 +460,9 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
     const int b0 = ks * p.bpk;
     const int b1 = min(b0 + p.bpk, p.n_blocks);
     const int nb = b1 - b0;
-    const long T = (long)p.n_sg * nb;
-    const long i0 = part_start(T, Gk, jk), i1 = part_start(T, Gk, jk + 1);
+    const int C = unit_chunks(nb, p.bc);                      // chunks per chunked strip group in this slice
+    const int U = slice_units(p.n_sg, p.n_whole, C);          // units of this slice
+    const int PS = static_units(p.n_whole, Gk, nb, p.pref);  // static units per CTA
     const int M = p.M;
     const int BB = p.block_bytes;
     const SmemLayout L = smem_layout(LAYOUT, BITS, p.bpk, M, XSPLIT, E, BB);
@@ -385,8 +470,10 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + L.bar);
     uint64_t *empty = full + kStages;
     uint64_t *xbar = empty + kStages;
-    uint64_t *rfull = xbar + 1;   // [2] MMA warps -> epilogue warp: accumulators written
-    uint64_t *rempty = rfull + 2; // [2] epilogue warp -> MMA warps: buffer free again
+    uint64_t *rfull = xbar + 1;              // [nbuf] MMA warps -> epilogue warp: accumulators written
+    uint64_t *rempty = rfull + kMaxRedBufs;  // [nbuf] epilogue warp -> MMA warps: buffer free again
+    const int nbuf = L.nbuf;                 // 2 or 4
+    const int nbuf_log = nbuf >> 1;          // log2(nbuf)
     int *tag_unit = reinterpret_cast<int *>(smem + L.tags);
     int *tag_blk = tag_unit + kStages;
     int *tag_flags = tag_blk + kStages;
@@ -399,8 +486,8 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
             mbar_init(&empty[s], kNW);
         }
         mbar_init(xbar, 1);
-        for (int b = 0; b < 2; ++b) {
-            mbar_init(&rfull[b], kNW * 32);
+        for (int b = 0; b < nbuf; ++b) {
+            mbar_init(&rfull[b], kNW);  // one arrival per MMA warp
             mbar_init(&rempty[b], 1);
         }
         *reinterpret_cast<uint4 *>(smem + kZeroSlot) = make_uint4(0u, 0u, 0u, 0u);
@@ -412,66 +499,104 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
     __syncthreads();
 
     if (warp == kProducerWarp) {
-        // ---------------- producer ----------------
-        if (lane == 0) {
-            const uint64_t pol = l2_policy_evict_first();
-            int it = 0;
-            bool x_issued = false;
-            auto issue_x = [&]() {
-                grid_dependency_wait();
-                const uint32_t xb = (uint32_t)(nb * xfrag_bytes_per_block(LAYOUT, BITS, M, XSPLIT));
-                uint32_t tx = xb;
-                const uint32_t xsb = (uint32_t)nb * kChunksPerBlock * NE * 32;
-                if (LAYOUT == kLayoutF16) tx += xsb;
-                mbar_arrive_expect_tx(xbar, tx);
-                bulk_g2s(smem + L.xf,
-                         static_cast<const uint8_t *>(p.xf) + (size_t)b0 * xfrag_bytes_per_block(LAYOUT, BITS, M, XSPLIT),
-                         xb, xbar);
-                if (LAYOUT == kLayoutF16)
-                    bulk_g2s(smem + L.xs, reinterpret_cast<const uint8_t *>(p.xs) + (size_t)b0 * kChunksPerBlock * NE * 32,
-                             xsb, xbar);
-                x_issued = true;
-            };
-            int sg = (int)(i0 / nb), bi = (int)(i0 - (long)sg * nb);
-            for (long i = i0; i < i1; ++i, ++it) {
-                const int slot = it % kStages, use = it / kStages;
-                if (use > 0 && !mbar_wait_bounded(&empty[slot], (use - 1) & 1)) {
-                    atomicExch(p.err, kErrWaitEmpty);
+        // ---------------- producer warp ----------------
+        // The whole warp runs the loop (uniform control flow): lane 0 draws
+        // units, arms the stage barriers and writes the ring tags; lane q < kSG
+        // sets up strip q of each unit and issues its copies, so the copies of
+        // a stage go out as one warp instruction.  A single thread doing all of
+        // it falls behind the MMA warps when units are short.
+        const uint64_t pol = l2_policy_evict_first();
+        unsigned *wctr = p.work_ctr + ks;
+        const int n_grabs = grabs_total(U, PS, Gk);
+        int it = 0, slot = 0, use = 0;  // ring position: items issued, slot, pass
+        bool x_issued = false;
+        // After the upstream grid has finished: the activations (unless the
+        // MMA warps build them) and, from then on, the work counter.
+        auto issue_x = [&]() {
+            grid_dependency_wait();
+            x_issued = true;
+            if (p.fused || lane != 0) return;
+            const uint32_t xb = (uint32_t)(nb * xfrag_bytes_per_block(LAYOUT, BITS, M, XSPLIT));
+            uint32_t tx = xb;
+            const uint32_t xsb = (uint32_t)nb * kChunksPerBlock * NE * 32;
+            if (LAYOUT == kLayoutF16) tx += xsb;
+            mbar_arrive_expect_tx(xbar, tx);
+            bulk_g2s(smem + L.xf,
+                     static_cast<const uint8_t *>(p.xf) + (size_t)b0 * xfrag_bytes_per_block(LAYOUT, BITS, M, XSPLIT), xb,
+                     xbar);
+            if (LAYOUT == kLayoutF16)
+                bulk_g2s(smem + L.xs, reinterpret_cast<const uint8_t *>(p.xs) + (size_t)b0 * kChunksPerBlock * NE * 32,
+                         xsb, xbar);
+        };
+        int pi = 0;            // static units taken
+        bool pending = false;  // a draw is in flight (lane 0 holds its value)
+        unsigned drawn = 0;
+        auto draw = [&]() {
+            if (pending) return;
+            if (!x_issued) issue_x();
+            if (lane == 0) drawn = atomicAdd(wctr, 1u);
+            pending = true;
+        };
+        auto static_left = [&]() { return pi < PS && jk + pi * Gk < U; };
+        auto next_unit = [&]() -> int {
+            if (static_left()) return jk + (pi++) * Gk;
+            pi = PS;
+            draw();
+            pending = false;
+            const int d = (int)__shfl_sync(0xffffffffu, drawn, 0);
+            const int u = PS * Gk + d;
+            if (u < U) return u;
+            if (lane == 0 && d == n_grabs - 1) atomicExch(wctr, 0u);  // the launch's last draw
+            return -1;
+        };
+        bool stop = false;
+        while (!stop) {
+            const int u = next_unit();
+            if (u < 0) break;
+            const Unit un = unit_of(u, nb, C, ks, p.n_ks, p.n_whole, p.bc, p.cfull, p.ctot);
+            const uint8_t *src = nullptr;  // lane q < kSG: strip q, block bs of the unit
+            bool valid = false;
+            if (lane < kSG) {
+                const StripRef r = strip_ref<MODE>(p, un.sg, lane);
+                valid = r.valid;
+                if (valid) src = p.src[r.r].codes + ((size_t)r.strip * p.n_blocks + b0 + un.bs) * BB;
+            }
+            const uint32_t tx = (uint32_t)__popc(__ballot_sync(0xffffffffu, valid)) * (uint32_t)BB;
+            uint8_t *dst = smem + L.ring + (size_t)lane * BB;
+            for (int bi = un.bs; bi < un.be; ++bi, ++it) {
+                // the next unit's draw goes out with the first copy of this one,
+                // so its L2 round trip overlaps the whole unit
+                if (bi == un.bs && !static_left()) draw();
+                if (use > 0 && !__all_sync(0xffffffffu, mbar_wait_bounded(&empty[slot], (use - 1) & 1))) {
+                    if (lane == 0) atomicExch(p.err, kErrWaitEmpty);
+                    stop = true;
                     break;
                 }
-                tag_unit[slot] = sg;
-                tag_blk[slot] = bi;
-                tag_flags[slot] = ((i == i0 || bi == 0) ? kFirst : 0) | ((i == i1 - 1 || bi == nb - 1) ? kLast : 0);
-                StripRef ref[kSG];
-                uint32_t tx = 0;
-#pragma unroll
-                for (int q = 0; q < kSG; ++q) {
-                    ref[q] = strip_ref<MODE>(p, sg, q);
-                    if (ref[q].valid) tx += (uint32_t)BB;
+                if (lane == 0) {
+                    tag_unit[slot] = un.sg;
+                    tag_blk[slot] = bi;
+                    tag_flags[slot] = (bi == un.be - 1 ? kLast : 0) | (un.gc << 1);
+                    mbar_arrive_expect_tx(&full[slot], tx);
                 }
-                mbar_arrive_expect_tx(&full[slot], tx);
-#pragma unroll
-                for (int q = 0; q < kSG; ++q) {
-                    if (!ref[q].valid) continue;
-                    const uint8_t *src = p.src[ref[q].r].codes + ((size_t)ref[q].strip * p.n_blocks + b0 + bi) * BB;
-                    bulk_g2s_hint(smem + L.ring + ((size_t)slot * kSG + q) * BB, src, (uint32_t)BB, &full[slot], pol);
+                __syncwarp();
+                if (valid)
+                    bulk_g2s_hint(dst + (size_t)slot * kSG * BB, src + (size_t)(bi - un.bs) * BB, (uint32_t)BB,
+                                  &full[slot], pol);
+                if (++slot == kStages) {
+                    slot = 0;
+                    ++use;
                 }
                 // weights first, then (once) the upstream-dependent activations
-                if (!p.fused && !x_issued && it + 1 >= kStages) issue_x();
-                if (++bi == nb) {
-                    bi = 0;
-                    ++sg;
-                }
+                if (!x_issued && it + 1 >= kStages) issue_x();
             }
-            if (!p.fused && !x_issued) issue_x();
+        }
+        if (!x_issued) issue_x();
+        if (lane == 0) {
             // end-of-work marker in the next slot
-            {
-                const int slot = it % kStages, use = it / kStages;
-                if (use > 0 && !mbar_wait_bounded(&empty[slot], (use - 1) & 1)) atomicExch(p.err, kErrWaitEmpty);
-                tag_unit[slot] = -1;
-                mbar_arrive(&full[slot]);
-                ++it;
-            }
+            if (use > 0 && !mbar_wait_bounded(&empty[slot], (use - 1) & 1)) atomicExch(p.err, kErrWaitEmpty);
+            tag_unit[slot] = -1;
+            mbar_arrive(&full[slot]);
+            ++it;
             // every issued copy has landed before the CTA may exit
             for (int s = 0; s < kStages && s < it; ++s) {
                 const int last = s + ((it - 1 - s) / kStages) * kStages;
@@ -481,18 +606,19 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
         }
     } else if (warp == kEpilogueWarp) {
         // ---------------- epilogue warp ----------------
-        // Sums the MMA warps' accumulators of each finished segment (fixed warp
-        // order, four entries per load), writes the outputs of a whole strip
-        // group, or parks a partial sum in its workspace slot.  With rmode 0
-        // the last partial to arrive (atomic count) sums all slots in slot
-        // order; with rmode 1 gemv_reduce_kernel does, after this kernel.
+        // Sums the MMA warps' accumulators of each finished unit (fixed warp
+        // order, four entries per load).  A strip group whose K is one unit is
+        // written out here; otherwise the sum goes to the unit's chunk slot and
+        // the arrival count of the strip group is raised (acquire-release); the
+        // arrival that completes the count sums all chunk slots and writes the
+        // outputs (with rmode 1 gemv_reduce_kernel does, after this kernel).
         // Runs behind the MMA warps, off the streaming path.
         grid_dependency_wait();  // y, the workspace and the counters belong to the previous grid until it ends
         Acc *ws = static_cast<Acc *>(p.ws);
-        const int nq = kSG * 16 * M;  // (strip, row, token) entries of a segment
+        const int nq = kSG * 16 * M;  // (strip, row, token) entries of a unit
         const int nq4 = nq / 4;       // nq is a multiple of 64
         for (int k = 0;; ++k) {
-            const int b = k & 1, u = k >> 1;
+            const int b = k & (nbuf - 1), u = k >> nbuf_log;
             if (!__all_sync(0xffffffffu, mbar_wait_bounded(&rfull[b], u & 1))) {
                 if (lane == 0) atomicExch(p.err, kErrWaitFull);
                 break;
@@ -501,85 +627,51 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
             if (si.sg < 0) break;
             const int sg = si.sg;
             const Acc4 *red4 = reinterpret_cast<const Acc4 *>(smem + L.red) + (size_t)b * kNW * nq4;
-            // gate/up: entry q of a gate strip pairs with q + 2*16*M of the up strip
-            const int nq4_out = MODE == 1 ? nq4 / 2 : nq4;
-            const int up4 = 2 * 16 * M / 4;
-            int slot_p = 0, total_p = 1;
-            if (!si.whole) {
-                // partial slot: partials of earlier K-slices first, then this slice's CTAs in order
-                total_p = 0;
-                for (int kk = 0; kk < p.n_ks; ++kk) {
-                    const int nbk = min(p.bpk, p.n_blocks - kk * p.bpk);
-                    const int cnt = part_count(sg, nbk, p.n_sg, Gk);
-                    if (kk < ks) slot_p += cnt;
-                    total_p += cnt;
+            const int ctot = sg < p.n_whole ? p.n_ks : p.ctot;  // chunks of this strip group
+            if (ctot == 1) {
+                // gate/up: entry q of a gate strip pairs with q + 2*16*M of the up strip
+                const int nq4_out = MODE == 1 ? nq4 / 2 : nq4;
+                const int up4 = 2 * 16 * M / 4;
+                for (int q4 = lane; q4 < nq4_out; q4 += 32) {
+                    Acc4 sum = V4::zero(), su = V4::zero();
+#pragma unroll
+                    for (int w = 0; w < kNW; ++w) {
+                        V4::add(sum, red4[(size_t)w * nq4 + q4]);
+                        if (MODE == 1) V4::add(su, red4[(size_t)w * nq4 + q4 + up4]);
+                    }
+#pragma unroll
+                    for (int c = 0; c < 4; ++c)
+                        finalize_entry<LAYOUT, MODE, Acc>(p, sg, 4 * q4 + c, comp(sum, c), comp(su, c));
                 }
-                slot_p += jk - part_owner(T, Gk, (long)sg * nb);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&rempty[b]);  // accumulator buffer consumed
+                continue;
             }
-            Acc4 *wslot4 = reinterpret_cast<Acc4 *>(ws + ((size_t)sg * p.maxp + slot_p) * (kSG * 16 * 8));
+            Acc *slots = ws + (size_t)sg * p.ctot * nq;
+            Acc4 *wslot4 = reinterpret_cast<Acc4 *>(slots + (size_t)si.gc * nq);
             for (int q4 = lane; q4 < nq4; q4 += 32) {
                 Acc4 sum = V4::zero();
 #pragma unroll
                 for (int w = 0; w < kNW; ++w) V4::add(sum, red4[(size_t)w * nq4 + q4]);
-                if (si.whole) {
-                    if (MODE == 0) {
-#pragma unroll
-                        for (int c = 0; c < 4; ++c) finalize_entry<LAYOUT, MODE, Acc>(p, sg, 4 * q4 + c, comp(sum, c), 0);
-                    } else if (q4 < nq4_out) {
-                        Acc4 su = V4::zero();
-#pragma unroll
-                        for (int w = 0; w < kNW; ++w) V4::add(su, red4[(size_t)w * nq4 + q4 + up4]);
-#pragma unroll
-                        for (int c = 0; c < 4; ++c)
-                            finalize_entry<LAYOUT, MODE, Acc>(p, sg, 4 * q4 + c, comp(sum, c), comp(su, c));
-                    }
-                } else {
-                    wslot4[q4] = sum;
-                }
+                wslot4[q4] = sum;
             }
             __syncwarp();
-            if (lane == 0) mbar_arrive(&rempty[b]);  // accumulator buffer consumed
-            if (!si.whole && p.rmode == 0) {
-                __threadfence();  // this CTA's partial sums visible before its arrival is counted
-                __syncwarp();
-                int last = 0;
-                if (lane == 0) {
-                    const unsigned old = atomicAdd(&p.split_cnt[sg], 1u);
-                    last = old == (unsigned)(total_p - 1);
-                    if (last) __threadfence();  // ... and the other CTAs' partial sums visible here
-                }
-                last = __shfl_sync(0xffffffffu, last, 0);
-                if (last) {
-                    const Acc *wsg = ws + (size_t)sg * p.maxp * (kSG * 16 * 8);
-                    // Four independent partial sums over the slots keep several
-                    // L2 loads in flight; the association is fixed, so the result
-                    // is deterministic.
-                    constexpr size_t kSlot = kSG * 16 * 8;
-                    const int up_off = 4 * up4;
-                    for (int q = lane; q < 4 * nq4_out; q += 32) {
-                        Acc a[4] = {0, 0, 0, 0}, u4[4] = {0, 0, 0, 0};
-                        int c = 0;
-                        for (; c + 4 <= total_p; c += 4) {
-#pragma unroll
-                            for (int h = 0; h < 4; ++h) {
-                                a[h] += __ldcg(&wsg[(size_t)(c + h) * kSlot + q]);
-                                if (MODE == 1) u4[h] += __ldcg(&wsg[(size_t)(c + h) * kSlot + q + up_off]);
-                            }
-                        }
-                        // the last (total_p % 4) slots go to sums 0, 1, 2 in order
-#pragma unroll
-                        for (int h = 0; h < 3; ++h)
-                            if (c + h < total_p) {
-                                a[h] += __ldcg(&wsg[(size_t)(c + h) * kSlot + q]);
-                                if (MODE == 1) u4[h] += __ldcg(&wsg[(size_t)(c + h) * kSlot + q + up_off]);
-                            }
-                        finalize_entry<LAYOUT, MODE, Acc>(p, sg, q, (a[0] + a[1]) + (a[2] + a[3]),
-                                                          (u4[0] + u4[1]) + (u4[2] + u4[3]));
-                    }
-                    __syncwarp();
-                    if (lane == 0) atomicExch(&p.split_cnt[sg], 0u);
-                }
+            if (p.rmode == 1) {  // gemv_reduce_kernel sums the slots after this kernel
+                if (lane == 0) mbar_arrive(&rempty[b]);
+                continue;
             }
+            unsigned old = 0;
+            if (lane == 0) {
+                mbar_arrive(&rempty[b]);  // accumulator buffer consumed
+                old = atom_add_acq_rel_gpu(&p.split_cnt[sg], 1u);
+            }
+            old = __shfl_sync(0xffffffffu, old, 0);
+            if (old != (unsigned)(ctot - 1)) continue;
+            __syncwarp();
+            // the last chunk of strip group sg to arrive: every slot is written
+            reduce_slots<LAYOUT, MODE, Acc>(p, slots, ctot, sg, lane);
+            __syncwarp();
+            if (lane == 0) p.split_cnt[sg] = 0u;  // clean for the next launch
         }
     } else {
         // ---------------- MMA warps ----------------
@@ -635,10 +727,10 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
         for (int i = 0; i < kSG; ++i)
 #pragma unroll
             for (int e = 0; e < 4; ++e) acc[i][e] = 0;
-        int seg_first = 0, nseg = 0;
+        int nseg = 0;
         // Hands the accumulators (or the end-of-work mark, sg < 0) to the epilogue warp.
-        auto hand_off = [&](int sg, int whole) -> bool {
-            const int b = nseg & 1, u = nseg >> 1;
+        auto hand_off = [&](int sg, int gc) -> bool {
+            const int b = nseg & (nbuf - 1), u = nseg >> nbuf_log;
             if (u > 0 && !__all_sync(0xffffffffu, mbar_wait_bounded(&rempty[b], (u - 1) & 1))) {
                 if (lane == 0) atomicExch(p.err, kErrWaitEmpty);
                 return false;
@@ -655,8 +747,10 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
                     if (tok < M) red[(i * 16 + r) * M + tok] = acc[i][e];
                     acc[i][e] = 0;
                 }
-            if (warp == 0 && lane == 0) info[b] = SegInfo{sg, whole};
-            mbar_arrive(&rfull[b]);
+            if (warp == 0 && lane == 0) info[b] = SegInfo{sg, gc};
+            // one arrival per warp, after its stores
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&rfull[b]);
             ++nseg;
             return true;
         };
@@ -672,7 +766,6 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
             if (sg < 0) break;
             const int bi = tag_blk[slot];
             const int flags = tag_flags[slot];
-            if (flags & kFirst) seg_first = bi;
             const uint8_t *stg = smem + L.ring + (size_t)slot * kSG * BB;
             const int cs = bi * kChunksPerBlock + warp;  // chunk in slice
             uint4 wv[kSG];
@@ -756,8 +849,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);
             if (flags & kLast) {
-                const int whole = p.n_ks == 1 && seg_first == 0 && bi == nb - 1;
-                if (!hand_off(sg, whole)) {
+                if (!hand_off(sg, flags >> 1)) {
                     aborted = true;
                     break;
                 }
@@ -768,55 +860,22 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
     __syncthreads();
 }
 
-// rmode 1: sums the partial-sum slots of every strip group that the GEMV
-// kernel did not finish itself, in slot order (the same fixed association as
-// the in-kernel path: four running sums, then (a0 + a1) + (a2 + a3)), and
-// finalizes the outputs.  One CTA per strip group at a time; four entries per
-// thread and load.
+// rmode 1: sums the chunk slots of every chunked strip group in chunk order
+// (reduce_slots: the association of the in-kernel path) and writes its
+// outputs; one warp per strip group.  With more than two rows an arrival
+// count per unit would keep the epilogue warp waiting on L2 round trips,
+// and through it the MMA warps.
 template <int LAYOUT, int MODE>
 __global__ void __launch_bounds__(128) gemv_reduce_kernel(const GemvParams p) {
     using Acc = typename std::conditional<LAYOUT == kLayoutS8, int, float>::type;
-    using V4 = Vec4<Acc>;
-    using Acc4 = typename V4::T;
-    constexpr size_t kSlot = kSG * 16 * 8;
-    __shared__ int s_total;
     pdl_begin();
-    const int M = p.M;
-    const int nq4 = kSG * 16 * M / 4;
-    const int nq4_out = MODE == 1 ? nq4 / 2 : nq4;
-    const int up4 = 2 * 16 * M / 4;
-    const Acc *ws = static_cast<const Acc *>(p.ws);
-    for (int sg = blockIdx.x; sg < p.n_sg; sg += gridDim.x) {
-        __syncthreads();
-        if (threadIdx.x == 0) s_total = slot_count(p, sg);
-        __syncthreads();
-        const int total = s_total;
-        if (p.n_ks == 1 && total == 1) continue;  // finished by the GEMV kernel
-        const Acc4 *wsg = reinterpret_cast<const Acc4 *>(ws + (size_t)sg * p.maxp * kSlot);
-        for (int q4 = threadIdx.x; q4 < nq4_out; q4 += blockDim.x) {
-            Acc4 a[4] = {V4::zero(), V4::zero(), V4::zero(), V4::zero()};
-            Acc4 u[4] = {V4::zero(), V4::zero(), V4::zero(), V4::zero()};
-            int c = 0;
-            for (; c + 4 <= total; c += 4) {
-#pragma unroll
-                for (int h = 0; h < 4; ++h) {
-                    V4::add(a[h], __ldcg(&wsg[(size_t)(c + h) * (kSlot / 4) + q4]));
-                    if (MODE == 1) V4::add(u[h], __ldcg(&wsg[(size_t)(c + h) * (kSlot / 4) + q4 + up4]));
-                }
-            }
-#pragma unroll
-            for (int h = 0; h < 3; ++h)
-                if (c + h < total) {
-                    V4::add(a[h], __ldcg(&wsg[(size_t)(c + h) * (kSlot / 4) + q4]));
-                    if (MODE == 1) V4::add(u[h], __ldcg(&wsg[(size_t)(c + h) * (kSlot / 4) + q4 + up4]));
-                }
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                const Acc v = (comp(a[0], c) + comp(a[1], c)) + (comp(a[2], c) + comp(a[3], c));
-                const Acc vu = (comp(u[0], c) + comp(u[1], c)) + (comp(u[2], c) + comp(u[3], c));
-                finalize_entry<LAYOUT, MODE, Acc>(p, sg, 4 * q4 + c, v, vu);
-            }
-        }
+    const int lane = threadIdx.x & 31;
+    const int nq = kSG * 16 * p.M;
+    for (int sg = blockIdx.x * 4 + (threadIdx.x >> 5); sg < p.n_sg; sg += gridDim.x * 4) {
+        const int ctot = sg < p.n_whole ? p.n_ks : p.ctot;
+        if (ctot == 1) continue;  // finished by the GEMV kernel
+        reduce_slots<LAYOUT, MODE, Acc>(p, static_cast<const Acc *>(p.ws) + (size_t)sg * p.ctot * nq, ctot, sg,
+                                        lane);
     }
 }
 
@@ -865,10 +924,10 @@ cudaError_t launch_gemv_t(const GemvPlan &plan, const GemvParams &p_in, cudaStre
     cfg.numAttrs = 1;
     note_launch();
     cudaError_t e = cudaLaunchKernelEx(&cfg, kern, p);
-    if (e != cudaSuccess || !plan.rmode) return e;
-    // the split-K partial sums, on the same stream right behind
+    if (e != cudaSuccess || !plan.rmode || plan.ctot == 1) return e;
+    // the chunk sums, on the same stream right behind
     cudaLaunchConfig_t rc = cfg;
-    rc.gridDim = dim3((unsigned)std::min<long>(p.n_sg, (long)plan.sms * 8));
+    rc.gridDim = dim3((unsigned)std::min<long>((p.n_sg + 3) / 4, (long)plan.sms * 4));
     rc.blockDim = dim3(128);
     rc.dynamicSmemBytes = 0;
     note_launch();

@@ -77,7 +77,11 @@ struct GemvParams {
     int n_sg;  // strip groups (units along N)
     int n_ks;  // K-slices; CTA b works on slice b % n_ks
     int bpk;   // blocks per K-slice
-    int maxp;  // workspace slots per strip group (upper bound on partials)
+    // work units: strip groups below n_whole whole per K-slice, the others in
+    // chunks of bc blocks; cfull chunks per full K-slice, ctot chunks over the
+    // whole K (= workspace slots per strip group); pref static units per CTA
+    // when the first units are chunks; the rest are drawn from work_ctr
+    int n_whole, bc, cfull, ctot, pref;
     const void *xf;
     const float *xs;
     const float *sx;
@@ -85,9 +89,10 @@ struct GemvParams {
     float *y;
     int ldy;
     int accumulate;
-    void *ws;             // partial sums [n_sg][maxp][kSG * 16 * 8]
-    unsigned *split_cnt;  // [n_sg] arrivals of partial sums (self-resetting)
-    int rmode;            // 0: last CTA to arrive sums the partials; 1: gemv_reduce_kernel does
+    void *ws;             // chunk sums [n_sg][ctot][kSG * 16 * M]
+    unsigned *split_cnt;  // [n_sg] arrivals of chunk sums (self-resetting)
+    unsigned *work_ctr;   // [n_ks] work counters (self-resetting)
+    int rmode;            // chunk sums: 0 by the last chunk's CTA, 1 by gemv_reduce_kernel (set at launch)
     int gk;               // CTAs per K-slice (set at launch)
     // fused fill: with `fused` set, every CTA builds the activation fragments
     // of its K-slice in shared memory from `xsrc` (fp32 rows [M][K]) instead
@@ -102,7 +107,7 @@ struct GemvScratch {
     void *xf = nullptr, *xlo = nullptr;
     float *xs = nullptr, *sx = nullptr;
     void *ws = nullptr;
-    unsigned *counters = nullptr;  // split counters, one per strip group
+    unsigned *counters = nullptr;  // arrival counters (one per strip group), then work counters
     size_t xf_bytes = 0, xlo_bytes = 0, xs_bytes = 0, sx_bytes = 0, ws_bytes = 0, counters_n = 0;
 };
 
@@ -111,8 +116,10 @@ constexpr int kMaxKs = 256;
 // Launch plan of one GEMV (computed on the host).
 struct GemvPlan {
     int mode = 0;  // 0 plain, 1 gate/up SwiGLU
-    int n_sg = 0, n_ks = 0, bpk = 0, grid = 0, maxp = 0;
-    long items_min = 0;  // items of the shortest K-slice (bound on CTAs per slice)
+    int n_sg = 0, n_ks = 0, bpk = 0, grid = 0;
+    int n_whole = 0, bc = 1, cfull = 1, ctot = 1, pref = 1;  // work units (GemvParams)
+    long items_min = 0;  // units of the shortest K-slice (bound on CTAs per slice)
+    int rmode = 0;       // chunk sums: 0 in the GEMV kernel, 1 by a second kernel (more than two rows)
     int sms = 148;
     int e_cols = 0;  // epilogue block (columns)
     bool xsplit = false;
@@ -120,7 +127,6 @@ struct GemvPlan {
     // as fp16 hi + lo, two MMAs per k-step; 2 fp32 as hi and lo in adjacent
     // MMA columns, one MMA per k-step (M <= 4)
     int xmode = 0;
-    int rmode = 0;  // split-K partials: 0 summed by the last CTA, 1 by a second kernel
     size_t smem = 0;
     size_t xf_bytes = 0, xs_bytes = 0, ws_bytes = 0;
     int split_counters = 0;

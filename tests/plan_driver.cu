@@ -2,6 +2,7 @@
 // sweep of shapes, formats and activation counts it checks that planning ends
 // and that every plan is consistent.  Built and run by tests/test_plan.py.
 #include <cstdio>
+#include <vector>
 #include "../chpe_qwen35_hybrid_engine_b200/csrc/gemv.cu"
 
 using namespace chpe;
@@ -48,25 +49,66 @@ int main() {
             bool ok = P.n_ks >= 1 && P.n_ks <= kMaxKs && P.bpk >= 1 && (long)P.bpk * P.n_ks >= m.n_blocks &&
                       (long)P.bpk * (P.n_ks - 1) < m.n_blocks && P.grid >= P.n_ks && P.grid % P.n_ks == 0 &&
                       P.smem <= (size_t)kSmemBudget;
-            // the stream-K partition covers every item once and no strip group
-            // collects more partial sums than its workspace slots
+            // the work units (static ones, then drawn ones, CTAs interleaved
+            // in a fixed pseudo-random order) cover every block of every strip
+            // group exactly once, every strip group's arrival count reaches its
+            // chunk count exactly, and the last draw of each slice is the one
+            // that resets its counter
+            ok = ok && P.bc >= 1 && P.pref * P.bc >= kStages && P.ctot >= P.n_ks && P.n_whole >= 0 &&
+                 P.n_whole <= P.n_sg && (P.ctot == 1 || P.ws_bytes >= (size_t)P.n_sg * P.ctot * kSG * 16 * M * 4) &&
+                 P.split_counters == P.n_sg + P.n_ks;
             const int Gk = P.grid / P.n_ks;
+            const bool deep = (N * (long)K) <= (1L << 26);  // full coverage check on the smaller shapes
+            std::vector<int> seen, arrivals(P.n_sg, 0);
+            if (ok && deep) seen.assign((size_t)P.n_sg * m.n_blocks, 0);
             for (int k = 0; k < P.n_ks && ok; ++k) {
                 const int nbk = std::min(P.bpk, m.n_blocks - k * P.bpk);
-                const long T = (long)P.n_sg * nbk;
-                ok = part_start(T, Gk, 0) == 0 && part_start(T, Gk, Gk) == T;
-                for (int j = 0; j < Gk && ok; ++j) ok = part_start(T, Gk, j) < part_start(T, Gk, j + 1);
-                for (long x = 0; x < T && ok; x += std::max<long>(1, T / 97)) {
-                    const int o = part_owner(T, Gk, x);
-                    ok = part_start(T, Gk, o) <= x && x < part_start(T, Gk, o + 1);
+                const int C = unit_chunks(nbk, P.bc);
+                const int U = slice_units(P.n_sg, P.n_whole, C);
+                const int PS = static_units(P.n_whole, Gk, nbk, P.pref);
+                const long ntot = grabs_total(U, PS, Gk);
+                ok = Gk <= U;
+                auto take = [&](long u) {
+                    const Unit un = unit_of((int)u, nbk, C, k, P.n_ks, P.n_whole, P.bc, P.cfull, P.ctot);
+                    ok = un.sg < P.n_sg && un.gc < un.ctot && un.ctot <= P.ctot && un.bs < un.be && un.be <= nbk &&
+                         (un.sg < P.n_whole ? un.ctot == P.n_ks : un.ctot == P.ctot);
+                    if (ok) arrivals[un.sg]++;
+                    if (ok && deep)
+                        for (int b = un.bs; b < un.be; ++b) seen[(size_t)un.sg * m.n_blocks + k * P.bpk + b]++;
+                };
+
+                long ctr = 0, draws = 0;
+                int resets = 0;
+                std::vector<int> pi(Gk, 0);
+                std::vector<char> done(Gk, 0);
+                int left = Gk;
+                unsigned rng = 12345u + k;
+                while (left > 0 && ok) {
+                    rng = rng * 1103515245u + 12345u;
+                    int j = (int)((rng >> 8) % (unsigned)Gk);
+                    while (done[j]) j = (j + 1) % Gk;
+                    long u;
+                    if (pi[j] < PS && j + (long)pi[j] * Gk < U) {
+                        u = j + (long)(pi[j]++) * Gk;
+                    } else {
+                        pi[j] = PS;
+                        const long d = ctr++;
+                        ++draws;
+                        u = (long)PS * Gk + d;
+                        if (u >= U) {
+                            if (d == ntot - 1) { ++resets; ctr = 0; }
+                            done[j] = 1;
+                            --left;
+                            continue;
+                        }
+                    }
+                    take(u);
                 }
+                ok = ok && resets == 1 && ctr == 0 && draws == ntot;
             }
-            for (int sg = 0; sg < P.n_sg && ok; sg += std::max(1, P.n_sg / 61)) {
-                int tot = 0;
-                for (int k = 0; k < P.n_ks; ++k)
-                    tot += part_count(sg, std::min(P.bpk, m.n_blocks - k * P.bpk), P.n_sg, Gk);
-                ok = tot <= P.maxp;
-            }
+            if (ok && deep)
+                for (int v : seen) ok = ok && v == 1;
+            for (int sg = 0; sg < P.n_sg && ok; ++sg) ok = arrivals[sg] == (sg < P.n_whole ? P.n_ks : P.ctot);
             if (!ok) {
                 ++bad;
                 if (bad < 20) printf("BAD N=%d K=%d bits=%d M=%d mode=%d n_ks=%d bpk=%d grid=%d smem=%zu\n", N, K, f.bits,
