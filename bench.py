@@ -55,12 +55,12 @@ L2_BYTES = 126 * 1024 * 1024
 # capture whole: its traffic is the step's algorithmic bytes times the
 # traffic / algorithmic ratio of the captured 29568 x 8192 Q4 GEMV.
 NCU_TRAFFIC = {
-    ("gemv", 8, 12288, 4096, 1, "f32"): 53_560_320,
-    ("gemv", 4, 29568, 8192, 1, "f32"): 141_244_416,
+    ("gemv", 8, 12288, 4096, 1, "f32"): 53_589_504,
+    ("gemv", 4, 29568, 8192, 1, "f32"): 140_035_584,
     ("prefill", 8, 12288, 4096, 2048): 138_023_168,
-    ("decode_9b", 1): 7_385_932_800,
+    ("decode_9b", 1): 7_399_503_104,
 }
-Q4_TRAFFIC_RATIO = 141_244_416 / 136_400_384
+Q4_TRAFFIC_RATIO = 140_035_584 / 136_400_384
 DECODE_METRIC = "decode tokens/s (quantized GEMV path; GEMV HBM GB/s vs peak in roofline)"
 
 
