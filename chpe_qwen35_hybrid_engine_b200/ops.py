@@ -172,6 +172,11 @@ class Context:
         f = L.chpe_fmt(bits, scheme, group, zero)
         h = C.c_void_p()
         keep = [codes, scales, zeros, bias]  # noqa: F841  (keep buffers alive during the call)
+        # The library reads device inputs on its own stream: whatever torch
+        # queued to produce them must have finished first.
+        if any(getattr(t, "is_cuda", False) for t in keep):
+            import torch
+            torch.cuda.current_stream().synchronize()
         self._check(self.lib.chpe_upload_matrix(self.ptr, C.byref(f), _dev_ptr(codes), row_stride, _dev_ptr(scales),
                                                 _dev_ptr(zeros), _dev_ptr(bias), rows, cols, C.byref(h)))
         return Tensor(self, h)

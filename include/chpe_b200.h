@@ -111,7 +111,9 @@ int chpe_sync(chpe_ctx *ctx);
  *           (ROW_AFFINE_F32), else NULL
  *   bias:   fp32 [rows] added once per output row, or NULL
  * Pointers may be host or device memory (detected).  The device copy is
- * repacked into the strip layout and owned by the context.
+ * repacked into the strip layout and owned by the context.  Device inputs are
+ * read on the context's stream: work on other streams that writes them must
+ * be complete before the call.  The call returns after the repack finished.
  * Replaces: archive.getTileU16Direct(lmap.*_tile) + the per-tensor scales of
  * LayerTensorMap (src/engine.zig:609-612, src/tensor_map.zig:7-51). */
 int chpe_upload_matrix(chpe_ctx *ctx, const chpe_fmt *fmt, const void *codes, size_t row_stride, const void *scales,
