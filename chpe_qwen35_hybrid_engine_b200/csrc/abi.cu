@@ -1215,8 +1215,8 @@ extern "C" int chpe_xfrag_free(chpe_ctx *ctx, chpe_xfrag *xf) {
 // not be issued during capture), and host engines whose device memory is
 // carved out of one region reserved up front.  chpe_gemv_dev may grow the
 // context's scratch with cudaMalloc on first use of a larger shape; this entry
-// point never does.  Its scratch -- activation fragments, block sums, split-K
-// partial sums and their arrival counters -- lives in one file-scope device
+// point never does.  Its scratch -- activation fragments, block sums, chunk
+// sums and the arrival and work counters -- lives in one file-scope device
 // array of kNoAllocScratchBytes, which every GPU that loads this library holds
 // until the process exits.  All calls share the array (it keeps the last
 // call's contents), so calls that overlap on the GPU race on it.
@@ -1266,7 +1266,7 @@ extern "C" int chpe_gemv_noalloc_dev(chpe_ctx *ctx, const chpe_tensor *w, const 
     Xfrag f = xfrag_shape(m, M, x_dtype, &xfb, &xsb);
     GemvPlan P;
     plan_gemv(m, M, 0, f.xsplit, &P);
-    // [split counters | activation fragments | block sums | activation scales | partial sums]
+    // [arrival + work counters | activation fragments | block sums | activation scales | chunk sums]
     auto al = [](size_t v) { return (v + 255) / 256 * 256; };
     const size_t cnt_bytes = al((size_t)P.split_counters * sizeof(unsigned));
     const size_t off_xf = cnt_bytes, off_xs = off_xf + al(xfb), off_sx = off_xs + al(xsb + 32),
@@ -1275,7 +1275,7 @@ extern "C" int chpe_gemv_noalloc_dev(chpe_ctx *ctx, const chpe_tensor *w, const 
         return fail(ctx, CHPE_EINVAL,
                     "shape [%d x %d], M = %d needs %zu bytes of scratch; the allocation-free GEMV has %zu", m.N, m.K, M,
                     need, kNoAllocScratchBytes);
-    // arrival counters start at zero (they also reset themselves after a clean call)
+    // arrival and work counters start at zero (they also reset themselves after a clean call)
     e = cudaMemsetAsync(base, 0, cnt_bytes, st);
     if (e != cudaSuccess) return fail(ctx, CHPE_ECUDA, "clear counters: %s", cudaGetErrorString(e));
     f.xf = base + off_xf;

@@ -300,8 +300,9 @@ int chpe_argmax_dev(chpe_ctx *ctx, const float *logits, int M, int n, int *idx, 
  * routine.  Its scratch is one static device array of 16 MiB that every GPU
  * loading the library holds until exit; a shape whose scratch needs more
  * returns CHPE_EINVAL with the required size.  All calls share that array and
- * it keeps the last call's contents (its arrival counters are cleared with a
- * memset at the start of every call), so calls that overlap on the GPU race.
+ * it keeps the last call's contents (its arrival and work counters are
+ * cleared with a memset at the start of every call), so calls that overlap on
+ * the GPU race.
  * The first call on each device looks up the array's device address; make
  * that first call before any stream capture. */
 int chpe_gemv_noalloc_dev(chpe_ctx *ctx, const chpe_tensor *w, const void *x, int x_dtype, const float *x_scales,
