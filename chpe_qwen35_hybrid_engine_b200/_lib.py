@@ -58,6 +58,7 @@ SIGNATURES = {
     "chpe_tensor_free": (I, [P, P]),
     "chpe_tensor_info": (I, [P, C.POINTER(SZ), C.POINTER(SZ), C.POINTER(I), C.POINTER(SZ)]),
     "chpe_register_i8": (I, [P, P, SZ, SZ]),
+    "chpe_tensor_unpack": (I, [P, P, P, P, P]),
     "chpe_gemv_dev": (I, [P, P, P, I, P, I, P, I, P]),
     "chpe_gemv_gateup_swiglu_dev": (I, [P, P, P, P, I, P, I, P, P]),
     "chpe_quantize_act_i8_dev": (I, [P, P, I, SZ, P, P, P]),
@@ -79,6 +80,8 @@ SIGNATURES = {
     "chpe_comm_handle": (I, [P, P]),
     "chpe_comm_open_peers": (I, [P, P]),
     "chpe_allreduce_residual_dev": (I, [P, P, P, SZ, P]),
+    "chpe_comm_failed": (I, [P]),
+    "chpe_comm_reset": (I, [P]),
     "chpe_comm_destroy": (I, [P]),
     "chpe_xfrag_free": (I, [P, P]),
     "chpe_xfrag_fill_op_dev": (I, [P, P, C.POINTER(chpe_xsrc), P]),

@@ -32,6 +32,7 @@ struct chpe_ctx {
     float *d_out = nullptr;
     size_t d_out_bytes = 0;
     float *d_scales = nullptr;
+    float *d_xe = nullptr;  // row unscale factors of the GEMV's fused fill
     void *prefill_xt = nullptr;  // activation tiles of the prefill GEMM
     size_t prefill_xt_bytes = 0;
     std::unordered_map<const void *, chpe_tensor *> registry;
@@ -148,6 +149,7 @@ int build_matrix(chpe_ctx *ctx, const UploadSpec &u, const uint8_t *d_codes, siz
     m.block_bytes = kBlockCodeBytes + 16 * m.gpb * meta_bytes(u.meta_kind);
     m.scale = u.scale;
     m.zc = u.zc;
+    m.xorv = u.xorv;
     m.bytes = (size_t)m.n_strips * m.n_blocks * m.block_bytes;
     cudaError_t e = cudaMalloc(&m.codes, m.bytes);
     if (e != cudaSuccess) return fail(ctx, CHPE_ENOMEM, "cudaMalloc weights (%zu B): %s", m.bytes, cudaGetErrorString(e));
@@ -250,12 +252,16 @@ int ensure_scratch(chpe_ctx *ctx, const GemvPlan &P, cudaStream_t st) {
     return CHPE_OK;
 }
 
+// Bytes after the block sums that hold the fill's row unscale factors xe[8].
+constexpr size_t kXeBytes = 64;
+
 // Activation fragments of one block of <= 8 rows, ready for the GEMV kernel.
 struct Xfrag {
     int layout = kLayoutF16, bits = 8, M = 0, K = 0, Kp = 0, e_cols = 0, x_dtype = 0;
     bool xsplit = false;
-    void *xf = nullptr, *xlo = nullptr;
-    float *xs = nullptr;
+    void *xf = nullptr;
+    float *xs = nullptr;  // block sums, then the row unscale factors xe[8]
+    float *xe = nullptr;
     const float *sx = nullptr;
     const float *xrow = nullptr;  // fp32 rows for outlier columns
 };
@@ -288,7 +294,7 @@ int prep_x(chpe_ctx *ctx, Xfrag &f, const void *x, const float *x_scales, float 
             f.sx = sx_buf;
         }
     } else {
-        e = launch_xprep_f16(x, f.x_dtype, f.M, f.K, f.Kp, f.e_cols, f.xsplit, f.bits, f.xf, f.xs, st);
+        e = launch_xprep_f16(x, f.x_dtype, f.M, f.K, f.Kp, f.e_cols, f.xsplit, f.bits, f.xf, f.xs, f.xe, st);
     }
     if (e != cudaSuccess) return fail(ctx, CHPE_ECUDA, "activation prep: %s", cudaGetErrorString(e));
     return CHPE_OK;
@@ -352,6 +358,7 @@ void fill_params(GemvParams &p, int mode, const DevMatrix *const *ms, int n, con
     p.bpk = P.bpk;
     p.xf = f.xf;
     p.xs = f.xs;
+    p.xe = f.xe;
     p.sx = f.sx;
     p.xrow = f.xrow;
     p.y = ys[0];
@@ -385,6 +392,7 @@ int gemv_core(chpe_ctx *ctx, const DevMatrix &w0, const DevMatrix *w1, int mode,
     if (src) {
         p.xsrc = *src;
         p.fused = 1;
+        p.xe = ctx->d_xe;  // written by the kernel's fused fill (for the chunk-sum kernel)
     }
     cudaError_t e = launch_gemv(w0, w1, P, p, st);
     if (e != cudaSuccess) return fail(ctx, CHPE_ECUDA, "gemv launch: %s", cudaGetErrorString(e));
@@ -422,6 +430,7 @@ int gemv_multi_core(chpe_ctx *ctx, const DevMatrix *const *ms, int n, const Xfra
     if (src) {
         p.xsrc = *src;
         p.fused = 1;
+        p.xe = ctx->d_xe;
     }
     cudaError_t e = launch_gemv(w0, nullptr, P, p, st);
     if (e != cudaSuccess) return fail(ctx, CHPE_ECUDA, "gemv launch: %s", cudaGetErrorString(e));
@@ -460,11 +469,11 @@ int run_gemv(chpe_ctx *ctx, const DevMatrix &w0, const DevMatrix *w1, int mode, 
         size_t xfb, xsb;
         Xfrag f = xfrag_shape(w0, Mb, x_dtype, &xfb, &xsb);
         if ((rc = grow(ctx, &ctx->scr.xf, &ctx->scr.xf_bytes, xfb))) return rc;
-        if ((rc = grow(ctx, reinterpret_cast<void **>(&ctx->scr.xs), &ctx->scr.xs_bytes, xsb + 32))) return rc;
+        if ((rc = grow(ctx, reinterpret_cast<void **>(&ctx->scr.xs), &ctx->scr.xs_bytes, xsb + kXeBytes))) return rc;
         if ((rc = grow(ctx, reinterpret_cast<void **>(&ctx->scr.sx), &ctx->scr.sx_bytes, 64 * sizeof(float)))) return rc;
         f.xf = ctx->scr.xf;
-        f.xlo = ctx->scr.xlo;
         f.xs = ctx->scr.xs;
+        f.xe = ctx->scr.xs + xsb / sizeof(float);
         f.xrow = xrow ? xrow + (size_t)m0 * w0.K : nullptr;
         const void *xb = static_cast<const uint8_t *>(x) + (size_t)m0 * w0.K * elt;
         if ((rc = prep_x(ctx, f, xb, x_scales ? x_scales + m0 : nullptr,
@@ -551,6 +560,7 @@ extern "C" int chpe_init(int device, chpe_ctx **out) {
     if (e == cudaSuccess) e = cudaMalloc(&ctx->d_err, sizeof(int));
     if (e == cudaSuccess) e = cudaMemset(ctx->d_err, 0, sizeof(int));
     if (e == cudaSuccess) e = cudaMalloc(reinterpret_cast<void **>(&ctx->d_scales), 64 * sizeof(float));
+    if (e == cudaSuccess) e = cudaMalloc(reinterpret_cast<void **>(&ctx->d_xe), 64 * sizeof(float));
     if (e != cudaSuccess) {
         delete ctx;
         return CHPE_ECUDA;
@@ -568,7 +578,6 @@ extern "C" int chpe_destroy(chpe_ctx *ctx) {
         delete t;
     }
     cudaFree(ctx->scr.xf);
-    cudaFree(ctx->scr.xlo);
     cudaFree(ctx->scr.xs);
     cudaFree(ctx->scr.sx);
     cudaFree(ctx->scr.ws);
@@ -576,6 +585,7 @@ extern "C" int chpe_destroy(chpe_ctx *ctx) {
     cudaFree(ctx->d_in);
     cudaFree(ctx->d_out);
     cudaFree(ctx->d_scales);
+    cudaFree(ctx->d_xe);
     cudaFree(ctx->d_err);
     cudaFree(ctx->prefill_xt);
     cudaStreamDestroy(ctx->stream);
@@ -805,6 +815,31 @@ extern "C" int chpe_tensor_info(const chpe_tensor *t, size_t *rows, size_t *cols
     return CHPE_OK;
 }
 
+extern "C" int chpe_tensor_unpack(chpe_ctx *ctx, const chpe_tensor *t, void *codes, void *scales, void *zeros) {
+    if (!ctx || !t || !codes) return fail(ctx, CHPE_EINVAL, "null argument");
+    const DevMatrix &m = t->m;
+    if (zeros && m.meta_kind != kMetaSZ16) return fail(ctx, CHPE_ENOTSUP, "this tensor stores no zero-points");
+    cudaSetDevice(ctx->device);
+    const size_t row_bytes = ((size_t)m.K * m.bits + 7) / 8;
+    const size_t ng = m.meta_kind == kMetaF32 ? 1 : (size_t)m.n_groups;
+    const size_t meta_elt = m.meta_kind == kMetaF32 ? 4 : 2;
+    const size_t code_bytes = (size_t)m.N * row_bytes, meta_bytes = m.meta_kind == kMetaNone ? 0 : (size_t)m.N * ng * meta_elt;
+    uint8_t *d = nullptr;
+    CK(cudaMalloc(&d, code_bytes + 2 * meta_bytes + 256));
+    uint8_t *ds = d + (code_bytes + 127) / 128 * 128;
+    uint8_t *dz = ds + (meta_bytes + 127) / 128 * 128;
+    cudaError_t e = launch_unpack(m, m.xorv, row_bytes, d, m.meta_kind == kMetaF32 ? nullptr : reinterpret_cast<__half *>(ds),
+                                  m.meta_kind == kMetaSZ16 ? reinterpret_cast<__half *>(dz) : nullptr,
+                                  m.meta_kind == kMetaF32 ? reinterpret_cast<float *>(ds) : nullptr, ctx->stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(codes, d, code_bytes, cudaMemcpyDefault, ctx->stream);
+    if (e == cudaSuccess && scales && meta_bytes) e = cudaMemcpyAsync(scales, ds, meta_bytes, cudaMemcpyDefault, ctx->stream);
+    if (e == cudaSuccess && zeros) e = cudaMemcpyAsync(zeros, dz, meta_bytes, cudaMemcpyDefault, ctx->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+    cudaFree(d);
+    if (e != cudaSuccess) return fail(ctx, CHPE_ECUDA, "unpack: %s", cudaGetErrorString(e));
+    return CHPE_OK;
+}
+
 static void drop_registered(chpe_ctx *ctx, const void *key) {
     chpe_tensor *t = lookup(ctx, key);
     if (!t) return;
@@ -1004,7 +1039,8 @@ extern "C" int chpe_xfrag_create(chpe_ctx *ctx, const chpe_tensor *like, int M, 
     h->f = xfrag_shape(like->m, M, x_dtype, &h->xf_bytes, &h->xs_bytes);
     h->outliers = like->m.out_cols != nullptr;
     cudaError_t e = cudaMalloc(&h->f.xf, h->xf_bytes);
-    if (e == cudaSuccess) e = cudaMalloc(reinterpret_cast<void **>(&h->f.xs), h->xs_bytes + 32);
+    if (e == cudaSuccess) e = cudaMalloc(reinterpret_cast<void **>(&h->f.xs), h->xs_bytes + kXeBytes);
+    if (e == cudaSuccess) h->f.xe = h->f.xs + h->xs_bytes / sizeof(float);
     if (e == cudaSuccess) e = cudaMalloc(reinterpret_cast<void **>(&h->sx), 64 * sizeof(float));
     // fp32 rows are kept beside the fragments only for tensors with outlier
     // columns, and for int8 tensors fed by a fused producer (quantized from them)
@@ -1012,7 +1048,6 @@ extern "C" int chpe_xfrag_create(chpe_ctx *ctx, const chpe_tensor *like, int M, 
         e = cudaMalloc(reinterpret_cast<void **>(&h->xrow), (size_t)M * like->m.K * sizeof(float));
     if (e != cudaSuccess) {
         cudaFree(h->f.xf);
-        cudaFree(h->f.xlo);
         cudaFree(h->f.xs);
         cudaFree(h->sx);
         cudaFree(h->xrow);
@@ -1069,13 +1104,13 @@ extern "C" int chpe_xfrag_fill_op_dev(chpe_ctx *ctx, chpe_xfrag *xf, const chpe_
     cudaError_t e = cudaSuccess;
     if (xf->xrow) {
         // fp32 rows needed (outliers / int8 quantization): produce them once, then fill from them
-        e = launch_xmaterialize(s, f.M, f.K, xf->xrow, st);
+        e = launch_xmaterialize(s, f.M, f.K, f.Kp, xf->xrow, st);
         if (e != cudaSuccess) return fail(ctx, CHPE_ECUDA, "xfrag producer: %s", cudaGetErrorString(e));
         xf->f.xrow = xf->xrow;
         return prep_x(ctx, xf->f, xf->xrow, nullptr, xf->sx, st);
     }
     if (f.layout != kLayoutF16) return fail(ctx, CHPE_EINVAL, "fused fill of int8 fragments needs fp32 rows");
-    e = launch_xfill_f16(s, f.M, f.K, f.Kp, f.e_cols, f.xsplit, f.bits, f.xf, f.xs, st);
+    e = launch_xfill_f16(s, f.M, f.K, f.Kp, f.e_cols, f.xsplit, f.bits, f.xf, f.xs, f.xe, st);
     if (e != cudaSuccess) return fail(ctx, CHPE_ECUDA, "xfrag fill: %s", cudaGetErrorString(e));
     return CHPE_OK;
 }
@@ -1199,7 +1234,6 @@ extern "C" int chpe_xfrag_free(chpe_ctx *ctx, chpe_xfrag *xf) {
     if (!ctx || !xf) return fail(ctx, CHPE_EINVAL, "null argument");
     cudaStreamSynchronize(ctx->stream);
     cudaFree(xf->f.xf);
-    cudaFree(xf->f.xlo);
     cudaFree(xf->f.xs);
     cudaFree(xf->sx);
     cudaFree(xf->xrow);
@@ -1211,15 +1245,16 @@ extern "C" int chpe_xfrag_free(chpe_ctx *ctx, chpe_xfrag *xf) {
 // allocation-free GEMV
 // ---------------------------------------------------------------------------
 // Some callers cannot allocate device memory at the moment they run a GEMV:
-// code recording a CUDA graph (cudaMalloc is not a stream operation and may
-// not be issued during capture), and host engines whose device memory is
-// carved out of one region reserved up front.  chpe_gemv_dev may grow the
-// context's scratch with cudaMalloc on first use of a larger shape; this entry
-// point never does.  Its scratch -- activation fragments, block sums, chunk
-// sums and the arrival and work counters -- lives in one file-scope device
-// array of kNoAllocScratchBytes, which every GPU that loads this library holds
-// until the process exits.  All calls share the array (it keeps the last
-// call's contents), so calls that overlap on the GPU race on it.
+// host engines that reserve all the device memory they use once at start-up
+// (one arena on a GPU shared with other jobs) and treat any later cudaMalloc
+// as a failure, and decode loops that cannot take cudaMalloc's implicit
+// device synchronisation.  chpe_gemv_dev may grow the context's scratch with
+// cudaMalloc on first use of a larger shape; this entry point never does.
+// Its scratch -- activation fragments, block sums, chunk sums and the arrival
+// and work counters -- lives in one file-scope device array of
+// kNoAllocScratchBytes, which every GPU that loads this library holds until
+// the process exits.  All calls share the array (it keeps the last call's
+// contents), so calls that overlap on the GPU race on it.
 
 constexpr size_t kNoAllocScratchBytes = 16u << 20;  // 16 MiB
 static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
@@ -1229,19 +1264,44 @@ namespace {
 constexpr int kNoAllocMaxDevices = 64;
 std::mutex g_noalloc_mu;
 void *g_noalloc_ptr[kNoAllocMaxDevices] = {nullptr};
+void *g_noalloc_owner[kNoAllocMaxDevices] = {nullptr};  // the device context the address belongs to
 
-// Device address of the static scratch on the current device (looked up once
-// per device with that device current: in host code the array's name is only
-// a host-side stand-in, not a device address).
+// The current CUDA context (driver handle), through the runtime's driver
+// entry point; null when unavailable.
+void *current_cu_context() {
+    using Fn = int (*)(void **);
+    static Fn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<Fn>(p);
+        else
+            cudaGetLastError();
+    });
+    void *c = nullptr;
+    if (fn && fn(&c) != 0) c = nullptr;
+    return c;
+}
+
+// Device address of the static scratch on the current device (looked up with
+// that device current -- in host code the array's name is only a host-side
+// stand-in, not a device address -- once per device and device context: a
+// context destroyed and re-created, e.g. by cudaDeviceReset, gets a fresh
+// lookup instead of a stale address).
 int noalloc_scratch(chpe_ctx *ctx, uint8_t **out) {
     if (ctx->device < 0 || ctx->device >= kNoAllocMaxDevices) return fail(ctx, CHPE_EINVAL, "device index");
+    void *owner = current_cu_context();
     std::lock_guard<std::mutex> lock(g_noalloc_mu);
-    if (!g_noalloc_ptr[ctx->device]) {
+    if (!g_noalloc_ptr[ctx->device] || g_noalloc_owner[ctx->device] != owner) {
         void *ptr = nullptr;
         cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
         if (e != cudaSuccess || !ptr)
             return fail(ctx, CHPE_ECUDA, "cudaGetSymbolAddress(static scratch): %s", cudaGetErrorString(e));
         g_noalloc_ptr[ctx->device] = ptr;
+        g_noalloc_owner[ctx->device] = owner;
     }
     *out = static_cast<uint8_t *>(g_noalloc_ptr[ctx->device]);
     return CHPE_OK;
@@ -1269,7 +1329,7 @@ extern "C" int chpe_gemv_noalloc_dev(chpe_ctx *ctx, const chpe_tensor *w, const 
     // [arrival + work counters | activation fragments | block sums | activation scales | chunk sums]
     auto al = [](size_t v) { return (v + 255) / 256 * 256; };
     const size_t cnt_bytes = al((size_t)P.split_counters * sizeof(unsigned));
-    const size_t off_xf = cnt_bytes, off_xs = off_xf + al(xfb), off_sx = off_xs + al(xsb + 32),
+    const size_t off_xf = cnt_bytes, off_xs = off_xf + al(xfb), off_sx = off_xs + al(xsb + kXeBytes),
                  off_ws = off_sx + al(kMaxTokens * sizeof(float)), need = off_ws + al(P.ws_bytes);
     if (need > kNoAllocScratchBytes)
         return fail(ctx, CHPE_EINVAL,
@@ -1280,6 +1340,7 @@ extern "C" int chpe_gemv_noalloc_dev(chpe_ctx *ctx, const chpe_tensor *w, const 
     if (e != cudaSuccess) return fail(ctx, CHPE_ECUDA, "clear counters: %s", cudaGetErrorString(e));
     f.xf = base + off_xf;
     f.xs = reinterpret_cast<float *>(base + off_xs);
+    f.xe = f.xs + xsb / sizeof(float);
     f.xrow = x_dtype == CHPE_X_F32 ? static_cast<const float *>(x) : nullptr;
     float *sx_buf = reinterpret_cast<float *>(base + off_sx);
     if ((rc = prep_x(ctx, f, x, x_scales, (m.layout == kLayoutS8 && x_dtype == CHPE_X_F32) ? sx_buf : nullptr, st)))

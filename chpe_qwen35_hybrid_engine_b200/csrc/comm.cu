@@ -22,6 +22,16 @@
 // slot two epochs later, after it has seen every peer's flag for that chunk in
 // the epoch in between, which each peer raises only after it finished reading
 // the older slot.
+//
+// A wait that expires leaves the ranks' epochs out of step, and a later
+// exchange could pair slots of different epochs without noticing.  So a CTA
+// whose wait expires marks the comm object failed -- in its device memory and
+// in a mapped host word -- and the epoch stops advancing; every later
+// all-reduce on a failed object returns at once with an error, on the host
+// (chpe_allreduce_residual_dev refuses) and on the device (a launch already
+// queued, e.g. in a CUDA graph, skips the exchange and records the error).
+// chpe_comm_reset, called on every rank between two host barriers, clears the
+// epochs, the flags and the mark.
 #include <cstring>
 
 #include "../../include/chpe_b200.h"
@@ -35,6 +45,7 @@ constexpr int kCommMaxRanks = 8;
 constexpr int kCommThreads = 256;
 constexpr int kCommChunk = 1024;  // floats per CTA
 constexpr int kErrCommWait = 31;
+constexpr int kErrCommFailed = 32;  // an all-reduce issued on a comm object that failed before
 
 __device__ __forceinline__ void st_release_sys(unsigned *p, unsigned v) {
     asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
@@ -50,15 +61,21 @@ struct CommPeers {
     unsigned *flags[kCommMaxRanks];  // each rank's flags [world][max_chunks]
 };
 
-__global__ void __launch_bounds__(kCommThreads) allreduce_residual_kernel(const CommPeers peers, int world, int rank,
+__global__ void __launch_bounds__(kCommThreads) chpe_allreduce_residual_kernel(const CommPeers peers, int world, int rank,
                                                                           size_t slot_elems, int max_chunks,
                                                                           const float *__restrict__ part,
                                                                           float *__restrict__ hidden, int n,
                                                                           unsigned *__restrict__ ctr,
+                                                                          volatile unsigned *host_failed,
                                                                           int *__restrict__ err) {
     __shared__ int s_ok;
     pdl_begin();  // the partial is the previous kernel's output
     const int c = blockIdx.x;
+    // ctr[0] epoch, ctr[1] arrival ticket, ctr[2] failed mark
+    if (*reinterpret_cast<volatile unsigned *>(&ctr[2])) {
+        if (threadIdx.x == 0) atomicExch(err, kErrCommFailed);
+        return;
+    }
     const unsigned epoch = ctr[0] + 1u;  // ctr[0] advances only after every CTA of this launch read it
     if (threadIdx.x == 0) s_ok = 1;
     const int i0 = c * kCommChunk, i1 = min(n, i0 + kCommChunk);
@@ -92,6 +109,8 @@ __global__ void __launch_bounds__(kCommThreads) allreduce_residual_kernel(const 
         }
         if (!ok) {
             atomicExch(err, kErrCommWait);
+            atomicExch(&ctr[2], 1u);  // failed: no later exchange on this object until a reset
+            *host_failed = 1u;
             s_ok = 0;
         }
     }
@@ -105,12 +124,13 @@ __global__ void __launch_bounds__(kCommThreads) allreduce_residual_kernel(const 
             hidden[i] += s;
         }
     }
-    // the last CTA to finish advances the epoch for the next all-reduce
+    // the last CTA to finish advances the epoch for the next all-reduce (not
+    // after a failure: the object then stays failed until chpe_comm_reset)
     if (threadIdx.x == 0) {
         __threadfence();
         if (atomicAdd(&ctr[1], 1u) == gridDim.x - 1) {
             ctr[1] = 0u;
-            ctr[0] = epoch;
+            if (!atomicAdd(&ctr[2], 0u)) ctr[0] = epoch;
         }
     }
 }
@@ -126,7 +146,9 @@ struct chpe_comm {
     size_t max_elems = 0;  // Mmax * H
     float *recv = nullptr;          // own receive area [2][world][max_elems]
     unsigned *flags = nullptr;      // own flags [world][max_chunks]
-    unsigned *epoch = nullptr;      // own epoch counter and arrival ticket
+    unsigned *epoch = nullptr;      // own epoch counter, arrival ticket and failed mark
+    unsigned *host_failed = nullptr;  // mapped pinned host word: set by a kernel whose wait expired
+    unsigned *host_failed_dev = nullptr;
     int max_chunks = 0;
     CommPeers peers;
     bool opened[kCommMaxRanks] = {false};
@@ -152,12 +174,19 @@ extern "C" int chpe_comm_create(chpe_ctx *ctx, int world, int rank, size_t max_e
     if (e == cudaSuccess) e = cudaMalloc(&c->epoch, 256);
     if (e == cudaSuccess) e = cudaMemset(c->flags, 0, flag_bytes);
     if (e == cudaSuccess) e = cudaMemset(c->epoch, 0, 256);
+    if (e == cudaSuccess) e = cudaHostAlloc(reinterpret_cast<void **>(&c->host_failed), sizeof(unsigned),
+                                            cudaHostAllocMapped);
+    if (e == cudaSuccess) {
+        *c->host_failed = 0u;
+        e = cudaHostGetDevicePointer(reinterpret_cast<void **>(&c->host_failed_dev), c->host_failed, 0);
+    }
     if (e == cudaSuccess) e = cudaIpcGetMemHandle(&c->handle_recv, c->recv);
     if (e == cudaSuccess) e = cudaIpcGetMemHandle(&c->handle_flags, c->flags);
     if (e != cudaSuccess) {
         cudaFree(c->recv);
         cudaFree(c->flags);
         cudaFree(c->epoch);
+        if (c->host_failed) cudaFreeHost(c->host_failed);
         delete c;
         cudaGetLastError();
         return CHPE_ECUDA;
@@ -206,12 +235,36 @@ extern "C" int chpe_allreduce_residual_dev(chpe_comm *c, const float *part, floa
     if (reinterpret_cast<uintptr_t>(part) % 16) return CHPE_EALIGN;  // read as float4
     for (int r = 0; r < c->world; ++r)
         if (!c->peers.recv[r] || !c->peers.flags[r]) return CHPE_ENOENT;  // peers not opened yet
+    // a failed object (a bounded wait expired) takes no exchange until chpe_comm_reset
+    if (*reinterpret_cast<volatile unsigned *>(c->host_failed)) return CHPE_ETIMEOUT;
     if (n == 0) return CHPE_OK;
     const unsigned chunks = (unsigned)((n + kCommChunk - 1) / kCommChunk);
-    cudaError_t e = launch_pdl(allreduce_residual_kernel, dim3(chunks), dim3(kCommThreads), 0,
+    cudaError_t e = launch_pdl(chpe_allreduce_residual_kernel, dim3(chunks), dim3(kCommThreads), 0,
                                static_cast<cudaStream_t>(stream), c->peers, c->world, c->rank, c->max_elems,
-                               c->max_chunks, part, hidden, (int)n, c->epoch, chpe_ctx_error_word(c->ctx));
+                               c->max_chunks, part, hidden, (int)n, c->epoch, c->host_failed_dev,
+                               chpe_ctx_error_word(c->ctx));
     return e == cudaSuccess ? CHPE_OK : CHPE_ECUDA;
+}
+
+extern "C" int chpe_comm_failed(const chpe_comm *c) {
+    if (!c) return CHPE_EINVAL;
+    return *reinterpret_cast<volatile unsigned *>(c->host_failed) ? 1 : 0;
+}
+
+extern "C" int chpe_comm_reset(chpe_comm *c) {
+    if (!c) return CHPE_EINVAL;
+    // every kernel of this process that may touch the object has finished
+    cudaError_t e = cudaDeviceSynchronize();
+    const size_t flag_bytes = (size_t)kCommMaxRanks * c->max_chunks * sizeof(unsigned);
+    if (e == cudaSuccess) e = cudaMemset(c->flags, 0, flag_bytes);
+    if (e == cudaSuccess) e = cudaMemset(c->epoch, 0, 256);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return CHPE_ECUDA;
+    }
+    *reinterpret_cast<volatile unsigned *>(c->host_failed) = 0u;
+    return CHPE_OK;
 }
 
 extern "C" int chpe_comm_destroy(chpe_comm *c) {
@@ -225,6 +278,7 @@ extern "C" int chpe_comm_destroy(chpe_comm *c) {
     cudaFree(c->recv);
     cudaFree(c->flags);
     cudaFree(c->epoch);
+    cudaFreeHost(c->host_failed);
     delete c;
     return CHPE_OK;
 }

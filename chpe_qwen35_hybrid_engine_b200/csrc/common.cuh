@@ -7,6 +7,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <mutex>
+
 namespace chpe {
 
 // A bounded wait gives up after this many nanoseconds of %globaltimer, records
@@ -18,6 +20,60 @@ enum KernelError : int { kErrNone = 0, kErrWaitFull = 1, kErrWaitEmpty = 2, kErr
 // Host side: every kernel launch of the library is counted (process-wide,
 // relaxed atomic; defined in abi.cu, read through chpe_kernel_launches).
 void note_launch();
+
+// Host side: per-device launch state of one kernel.  A kernel's dynamic
+// shared-memory limit (cudaFuncSetAttribute) and its occupancy belong to a
+// device context, so a process that launches on several GPUs sets and
+// queries them once per device; the lock serialises host threads.
+constexpr int kMaxDevices = 64;
+struct KernelDeviceState {
+    std::mutex mu;
+    bool attr_set[kMaxDevices] = {};
+    size_t occ_smem[kMaxDevices][8] = {};
+    int occ_val[kMaxDevices][8] = {};
+};
+// The current device (0 when the runtime cannot say; the device's calls then fail anyway).
+inline int current_device() {
+    int d = 0;
+    if (cudaGetDevice(&d) != cudaSuccess) {
+        cudaGetLastError();
+        d = 0;
+    }
+    return d;
+}
+// Sets the kernel's dynamic shared-memory limit to `smem` bytes on the current
+// device once, and returns (through *occ, when non-null) its resident blocks
+// per SM for `threads` threads and `smem` bytes, cached per device and size.
+template <typename Kern>
+cudaError_t kernel_prepare(KernelDeviceState &st, Kern kern, int threads, size_t smem_limit, size_t smem, int *occ) {
+    const int dev = current_device();
+    if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> lock(st.mu);
+    if (!st.attr_set[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_limit);
+        if (e != cudaSuccess) return e;
+        st.attr_set[dev] = true;
+    }
+    if (!occ) return cudaSuccess;
+    *occ = 0;
+    for (int i = 0; i < 8 && st.occ_smem[dev][i]; ++i)
+        if (st.occ_smem[dev][i] == smem) *occ = st.occ_val[dev][i];
+    if (!*occ) {
+        int o = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, kern, threads, smem) != cudaSuccess || o < 1) {
+            cudaGetLastError();
+            o = 1;
+        }
+        for (int i = 0; i < 8; ++i)
+            if (!st.occ_smem[dev][i]) {
+                st.occ_smem[dev][i] = smem;
+                st.occ_val[dev][i] = o;
+                break;
+            }
+        *occ = o;
+    }
+    return cudaSuccess;
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -172,6 +228,28 @@ cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t sme
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
+    note_launch();
+    return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+
+// As launch_pdl, for a kernel whose CTAs form clusters of cluster_x along x.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl_cluster(void (*kern)(KArgs...), dim3 grid, dim3 block, unsigned cluster_x, size_t smem,
+                               cudaStream_t st, Args &&...args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = cluster_x;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
     note_launch();
     return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
 }

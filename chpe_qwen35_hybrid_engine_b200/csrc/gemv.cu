@@ -1,5 +1,7 @@
 // gemv.cu -- launch planning and dispatch of the decode/verify GEMV
 // (kernel in gemv_impl.cuh, instantiated per code width in gemv_b*.cu).
+#include <atomic>
+
 #include "gemv_impl.cuh"
 
 namespace chpe {
@@ -10,15 +12,18 @@ cudaError_t launch_gemv_b4(const GemvPlan &plan, const GemvParams &p, int meta, 
 cudaError_t launch_gemv_b2(const GemvPlan &plan, const GemvParams &p, int meta, cudaStream_t st);
 cudaError_t launch_gemv_s8(const GemvPlan &plan, const GemvParams &p, int meta, cudaStream_t st);
 
+// SMs of the current device (cached per device).
 static int num_sms() {
-    static int n = 0;
+    static std::atomic<int> cache[kMaxDevices];
+    const int dev = current_device();
+    if (dev < 0 || dev >= kMaxDevices) return 148;
+    int n = cache[dev].load(std::memory_order_relaxed);
     if (!n) {
-        int dev = 0;
-        cudaGetDevice(&dev);
         if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) {
             cudaGetLastError();
             n = 148;
         }
+        cache[dev].store(n, std::memory_order_relaxed);
     }
     return n;
 }
@@ -73,7 +78,7 @@ int plan_gemv(const DevMatrix &w, int M, int mode, bool xsplit, GemvPlan *plan) 
     P.n_whole = (int)std::min<long>(P.n_sg, rounds * gk);
     // More than two rows: one CTA per SM, each with many blocks of work, so
     // whole strip groups alone balance well enough; partial sums only across
-    // K-slices, summed by gemv_reduce_kernel.
+    // K-slices, summed by chpe_qgemv_reduce_kernel.
     if (M > 2) {
         P.rmode = 1;
         P.n_whole = P.n_sg;

@@ -59,7 +59,7 @@ static_assert(kNW == kChunksPerBlock, "one block per stage, one chunk per warp")
 constexpr size_t kZeroSlot = 496;
 
 struct SmemLayout {
-    size_t bar, tags, ring, xf, xs, red, info, total;
+    size_t bar, tags, ring, xf, xs, red, info, xe, total;
     int nbuf;  // accumulator hand-off buffers (2 or 4)
 };
 
@@ -100,6 +100,8 @@ __host__ __device__ inline SmemLayout smem_layout(int layout, int bits, int bpk,
     o += (size_t)L.nbuf * kNW * kSG * 16 * M * 4;
     L.info = o;
     o += kMaxRedBufs * sizeof(SegInfo);
+    L.xe = o;  // row unscale factors of a fused fill [kMaxTokens]
+    o += kMaxTokens * sizeof(float);
     L.total = align_up(o, 128);
     return L;
 }
@@ -226,10 +228,11 @@ __device__ __forceinline__ StripRef strip_ref(const GemvParams &p, int sg, int i
 
 // Output (or, for gate/up, the SwiGLU of the gate and up outputs) of entry
 // q = (i * 16 + r) * M + tok of strip group sg from its summed accumulator(s):
-// scales the integer (W8A8) or 2^-24-scaled (fp16 path) sum, adds the bias and
-// the outlier columns, and writes or accumulates into y.
+// scales the integer (W8A8) sum, or the fp16 path's sum by 2^24 and by the
+// row's unscale factor xe[tok] (the fill's power-of-two row scaling), adds
+// the bias and the outlier columns, and writes or accumulates into y.
 template <int LAYOUT, int MODE, typename Acc>
-__device__ __forceinline__ void finalize_entry(const GemvParams &p, int sg, int q, Acc v, Acc v_up) {
+__device__ __forceinline__ void finalize_entry(const GemvParams &p, int sg, int q, Acc v, Acc v_up, const float *xe) {
     const int M = p.M;
     const int tok = q % M, ir = q / M, r = ir & 15, i = ir >> 4;
     const StripRef ref = strip_ref<MODE>(p, sg, i);
@@ -237,7 +240,7 @@ __device__ __forceinline__ void finalize_entry(const GemvParams &p, int sg, int 
     if (!ref.valid || row >= (MODE == 1 ? p.N : p.rows[ref.r])) return;
     if (MODE == 0) {
         const GemvSrc &sr = p.src[ref.r];
-        float out = LAYOUT == kLayoutS8 ? (float)v * (sr.scale * p.sx[tok]) : (float)v * kTwo24;
+        float out = LAYOUT == kLayoutS8 ? (float)v * (sr.scale * p.sx[tok]) : ((float)v * kTwo24) * xe[tok];
         if (sr.bias) out += sr.bias[row];
         if (sr.out_cols) {
             float os = 0.0f;
@@ -256,8 +259,8 @@ __device__ __forceinline__ void finalize_entry(const GemvParams &p, int sg, int 
             gv = (float)v * (p.src[0].scale * p.sx[tok]);
             uv = (float)v_up * (p.src[1].scale * p.sx[tok]);
         } else {
-            gv = (float)v * kTwo24;
-            uv = (float)v_up * kTwo24;
+            gv = ((float)v * kTwo24) * xe[tok];
+            uv = ((float)v_up * kTwo24) * xe[tok];
         }
         if (p.src[0].bias) gv += p.src[0].bias[row];
         if (p.src[1].bias) uv += p.src[1].bias[row];
@@ -297,7 +300,8 @@ template <> struct Vec2<int> {
 // only on ctot, so the result does not depend on which CTA runs it.  Two
 // entries per lane and load.
 template <int LAYOUT, int MODE, typename Acc>
-__device__ __forceinline__ void reduce_slots(const GemvParams &p, const Acc *slots, int ctot, int sg, int lane) {
+__device__ __forceinline__ void reduce_slots(const GemvParams &p, const Acc *slots, int ctot, int sg, int lane,
+                                             const float *xe) {
     using V2 = Vec2<Acc>;
     using T2 = typename V2::T;
     const int M = p.M;
@@ -327,8 +331,8 @@ __device__ __forceinline__ void reduce_slots(const GemvParams &p, const Acc *slo
                              V2::sum(V2::sum(a[4], a[5]), V2::sum(a[6], a[7])));
         const T2 vu = V2::sum(V2::sum(V2::sum(u[0], u[1]), V2::sum(u[2], u[3])),
                               V2::sum(V2::sum(u[4], u[5]), V2::sum(u[6], u[7])));
-        finalize_entry<LAYOUT, MODE, Acc>(p, sg, 2 * q2, v.x, vu.x);
-        finalize_entry<LAYOUT, MODE, Acc>(p, sg, 2 * q2 + 1, v.y, vu.y);
+        finalize_entry<LAYOUT, MODE, Acc>(p, sg, 2 * q2, v.x, vu.x, xe);
+        finalize_entry<LAYOUT, MODE, Acc>(p, sg, 2 * q2 + 1, v.y, vu.y, xe);
     }
 }
 
@@ -353,38 +357,52 @@ __device__ __forceinline__ float fused_src(const XSrc &s, int m, int k, float in
 // Fused fill (fp32 activations split into fp16 hi + lo, F16 layout): the 256
 // threads of the MMA warps build this CTA's K-slice of activation fragments
 // and epilogue-block sums in shared memory, in the layout the bulk-copied
-// fragments have (xfill_f16_kernel, same bits), straight from the source op --
+// fragments have (chpe_xfill_f16_kernel, same bits), straight from the source op --
 // RMSNorm statistics included, so no fill kernel runs between two GEMVs.
 // Ends with a barrier of the MMA warps.
 template <int BITS, int E, int OP>
 __device__ __forceinline__ void fused_fill_op(const GemvParams &p, uint8_t *xf_s, float *xs_s, float *scratch,
-                                              int b0, int nb, int span) {
+                                              float *xe_s, int b0, int nb, int span) {
     constexpr int S = (256 / BITS) / 16;  // k-steps per chunk
     const int tid = threadIdx.x;           // 0..255 (MMA warps)
-    const int lane = tid & 31, warp = tid >> 5;
     const int M = p.M, K = p.K;
     const XSrc &xs = p.xsrc;
-    float inv[kMaxTokens];
+    // Row statistics over the whole row, in the fill kernel's order (the
+    // fill ranges one after the other): the RMSNorm scale and the row's
+    // power-of-two scale 2^e, so the fragments are the fill kernel's bits.
+    float inv[kMaxTokens], scl[kMaxTokens];
+    const int nunits = (p.n_blocks * span) / 4;
+    const int C = fill_ctas(nunits);
 #pragma unroll
-    for (int m = 0; m < kMaxTokens; ++m) inv[m] = 1.0f;
-    if constexpr (OP == kXRmsnorm) {
-        // 1 / sqrt(mean(x^2) + eps) per row in the order of row_inv_rms
-#pragma unroll
-        for (int m = 0; m < kMaxTokens; ++m) {
-            if (m >= M) break;
-            float acc = row_sumsq_part(static_cast<const float *>(xs.x) + (size_t)m * xs.ldx, K, tid, kNW * 32);
-#pragma unroll
-            for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
-            if (lane == 0) scratch[warp * kMaxTokens + m] = acc;
-        }
-        named_bar_sync(1, kNW * 32);
-#pragma unroll
-        for (int m = 0; m < kMaxTokens; ++m) {
-            if (m >= M) break;
+    for (int m = 0; m < kMaxTokens; ++m) {
+        inv[m] = 1.0f;
+        scl[m] = 1.0f;
+        if (m >= M) continue;
+        float am = 0.0f;
+        if constexpr (OP == kXRmsnorm) {
+            const float *row = static_cast<const float *>(xs.x) + (size_t)m * xs.ldx;
             float tot = 0.0f;
-#pragma unroll
-            for (int w = 0; w < kNW; ++w) tot += scratch[w * kMaxTokens + m];
+            for (int c = 0; c < C; ++c) {
+                int u0, u1;
+                fill_range(nunits, C, c, u0, u1);
+                tot += block_range_sumsq(row, min(4 * u0, K), min(4 * u1, K), tid, kNW * 32, scratch, 1);
+            }
             inv[m] = inv_rms_of(tot, K, xs.eps);
+        }
+        am = range_absmax(xs, m, 0, K, tid, kNW * 32);
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, off));
+        if ((tid & 31) == 0) scratch[tid >> 5] = am;
+        named_bar_sync(1, kNW * 32);
+        float mx = 0.0f;
+#pragma unroll
+        for (int w = 0; w < kNW; ++w) mx = fmaxf(mx, scratch[w]);
+        named_bar_sync(1, kNW * 32);
+        const int e = row_scale_exp(OP == kXRmsnorm ? mx * inv[m] : mx);
+        scl[m] = pow2_of(e);
+        if (tid == 0) {
+            xe_s[m] = pow2_of(-e);
+            if (blockIdx.x == 0) const_cast<float *>(p.xe)[m] = pow2_of(-e);  // for the chunk-sum kernel
         }
     }
     const int units = nb * kChunksPerBlock * S * 4;  // a multiple of 32: whole warps take part below
@@ -394,7 +412,7 @@ __device__ __forceinline__ void fused_fill_op(const GemvParams &p, uint8_t *xf_s
         const int sr = u >> 2, t = u & 3;
         const int j = sr % S;
         const int sh = BITS == 4 ? 4 * (j & 1) : BITS == 2 ? 2 * (j & 3) : 0;
-        const float down = __int_as_float((127 - sh) << 23), up = __int_as_float((127 + sh) << 23);
+        const float down = pow2_of(-sh), up = pow2_of(sh);
         const int kb = k_base + 16 * sr + 2 * t;
         const int kk[4] = {kb, kb + 1, kb + 8, kb + 9};
         float part[kMaxTokens];
@@ -406,9 +424,10 @@ __device__ __forceinline__ void fused_fill_op(const GemvParams &p, uint8_t *xf_s
 #pragma unroll
                 for (int q = 0; q < 4; ++q) v[q] = kk[q] < K ? fused_src<OP>(xs, m, kk[q], inv[m]) : 0.0f;
                 __half h[4], l[4];
+                const float dn = scl[m] * down;  // 2^(e - sh), as the fill kernel's pre-scale
 #pragma unroll
                 for (int q = 0; q < 4; ++q) {
-                    const float w = v[q] * down;
+                    const float w = v[q] * dn;
                     h[q] = __float2half_rn(w);
                     l[q] = __float2half_rn(w - __half2float(h[q]));
                     part[m] += (__half2float(h[q]) + __half2float(l[q])) * up;
@@ -430,17 +449,17 @@ __device__ __forceinline__ void fused_fill_op(const GemvParams &p, uint8_t *xf_s
 }
 
 template <int BITS, int E>
-__device__ __forceinline__ void fused_fill(const GemvParams &p, uint8_t *xf_s, float *xs_s, float *scratch, int b0,
-                                           int nb, int span) {
+__device__ __forceinline__ void fused_fill(const GemvParams &p, uint8_t *xf_s, float *xs_s, float *scratch,
+                                           float *xe_s, int b0, int nb, int span) {
     if (p.xsrc.op == kXRmsnorm)
-        fused_fill_op<BITS, E, kXRmsnorm>(p, xf_s, xs_s, scratch, b0, nb, span);
+        fused_fill_op<BITS, E, kXRmsnorm>(p, xf_s, xs_s, scratch, xe_s, b0, nb, span);
     else
-        fused_fill_op<BITS, E, -1>(p, xf_s, xs_s, scratch, b0, nb, span);
+        fused_fill_op<BITS, E, -1>(p, xf_s, xs_s, scratch, xe_s, b0, nb, span);
 }
 
 // XM: how the activation operand is fed (GemvPlan::xmode).
 template <int BITS, int LAYOUT, int E, int XM, int MODE, int META>
-__global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
+__global__ void __launch_bounds__(kThreads, 2) chpe_qgemv_kernel(const GemvParams p) {
     using Acc = typename std::conditional<LAYOUT == kLayoutS8, int, float>::type;
     using V4 = Vec4<Acc>;
     using Acc4 = typename V4::T;
@@ -611,10 +630,13 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
         // written out here; otherwise the sum goes to the unit's chunk slot and
         // the arrival count of the strip group is raised (acquire-release); the
         // arrival that completes the count sums all chunk slots and writes the
-        // outputs (with rmode 1 gemv_reduce_kernel does, after this kernel).
+        // outputs (with rmode 1 chpe_qgemv_reduce_kernel does, after this kernel).
         // Runs behind the MMA warps, off the streaming path.
         grid_dependency_wait();  // y, the workspace and the counters belong to the previous grid until it ends
         Acc *ws = static_cast<Acc *>(p.ws);
+        // row unscale factors: the fill's (global), or this CTA's fused fill's
+        // (shared; written before the first unit is handed over)
+        const float *xe = p.fused ? reinterpret_cast<const float *>(smem + L.xe) : p.xe;
         const int nq = kSG * 16 * M;  // (strip, row, token) entries of a unit
         const int nq4 = nq / 4;       // nq is a multiple of 64
         for (int k = 0;; ++k) {
@@ -641,7 +663,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
                     }
 #pragma unroll
                     for (int c = 0; c < 4; ++c)
-                        finalize_entry<LAYOUT, MODE, Acc>(p, sg, 4 * q4 + c, comp(sum, c), comp(su, c));
+                        finalize_entry<LAYOUT, MODE, Acc>(p, sg, 4 * q4 + c, comp(sum, c), comp(su, c), xe);
                 }
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&rempty[b]);  // accumulator buffer consumed
@@ -656,7 +678,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
                 wslot4[q4] = sum;
             }
             __syncwarp();
-            if (p.rmode == 1) {  // gemv_reduce_kernel sums the slots after this kernel
+            if (p.rmode == 1) {  // chpe_qgemv_reduce_kernel sums the slots after this kernel
                 if (lane == 0) mbar_arrive(&rempty[b]);
                 continue;
             }
@@ -669,7 +691,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
             if (old != (unsigned)(ctot - 1)) continue;
             __syncwarp();
             // the last chunk of strip group sg to arrive: every slot is written
-            reduce_slots<LAYOUT, MODE, Acc>(p, slots, ctot, sg, lane);
+            reduce_slots<LAYOUT, MODE, Acc>(p, slots, ctot, sg, lane, xe);
             __syncwarp();
             if (lane == 0) p.split_cnt[sg] = 0u;  // clean for the next launch
         }
@@ -709,7 +731,8 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
             if (p.fused) {
                 grid_dependency_wait();  // the source rows are the previous kernel's output
                 fused_fill<BITS, E>(p, smem + L.xf, reinterpret_cast<float *>(smem + L.xs),
-                                    reinterpret_cast<float *>(smem + L.red), b0, nb, KC * kChunksPerBlock);
+                                    reinterpret_cast<float *>(smem + L.red), reinterpret_cast<float *>(smem + L.xe),
+                                    b0, nb, KC * kChunksPerBlock);
             }
         }
         if (!p.fused) {
@@ -866,7 +889,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
 // count per unit would keep the epilogue warp waiting on L2 round trips,
 // and through it the MMA warps.
 template <int LAYOUT, int MODE>
-__global__ void __launch_bounds__(128) gemv_reduce_kernel(const GemvParams p) {
+__global__ void __launch_bounds__(128) chpe_qgemv_reduce_kernel(const GemvParams p) {
     using Acc = typename std::conditional<LAYOUT == kLayoutS8, int, float>::type;
     pdl_begin();
     const int lane = threadIdx.x & 31;
@@ -875,38 +898,19 @@ __global__ void __launch_bounds__(128) gemv_reduce_kernel(const GemvParams p) {
         const int ctot = sg < p.n_whole ? p.n_ks : p.ctot;
         if (ctot == 1) continue;  // finished by the GEMV kernel
         reduce_slots<LAYOUT, MODE, Acc>(p, static_cast<const Acc *>(p.ws) + (size_t)sg * p.ctot * nq, ctot, sg,
-                                        lane);
+                                        lane, p.xe);
     }
 }
 
 template <int BITS, int LAYOUT, int E, int XM, int MODE, int META>
 cudaError_t launch_gemv_t(const GemvPlan &plan, const GemvParams &p_in, cudaStream_t st) {
-    auto kern = gemv_kernel<BITS, LAYOUT, E, XM, MODE, META>;
-    static bool attr_set = false;
-    if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBudget);
-        if (e != cudaSuccess) return e;
-        attr_set = true;
-    }
+    auto kern = chpe_qgemv_kernel<BITS, LAYOUT, E, XM, MODE, META>;
     // one wave of resident CTAs: the planned grid capped by the real occupancy
-    // (queried once per shared-memory size; the kernel's registers are fixed)
-    static size_t occ_smem[8] = {0};
-    static int occ_val[8] = {0};
-    int occ = 0;
-    for (int i = 0; i < 8 && occ_smem[i]; ++i)
-        if (occ_smem[i] == plan.smem) occ = occ_val[i];
-    if (!occ) {
-        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kThreads, plan.smem) != cudaSuccess || occ < 1) {
-            cudaGetLastError();
-            occ = 1;
-        }
-        for (int i = 0; i < 8; ++i)
-            if (!occ_smem[i]) {
-                occ_smem[i] = plan.smem;
-                occ_val[i] = occ;
-                break;
-            }
-    }
+    // (queried once per device and shared-memory size; the registers are fixed)
+    static KernelDeviceState kstate;
+    int occ = 1;
+    cudaError_t pe = kernel_prepare(kstate, kern, kThreads, kSmemBudget, plan.smem, &occ);
+    if (pe != cudaSuccess) return pe;
     long gk = std::min<long>((long)plan.sms * occ / plan.n_ks, plan.items_min);
     gk = std::max<long>(1, std::min<long>(gk, plan.grid / plan.n_ks));
     GemvParams p = p_in;
@@ -931,7 +935,7 @@ cudaError_t launch_gemv_t(const GemvPlan &plan, const GemvParams &p_in, cudaStre
     rc.blockDim = dim3(128);
     rc.dynamicSmemBytes = 0;
     note_launch();
-    return cudaLaunchKernelEx(&rc, gemv_reduce_kernel<LAYOUT, MODE>, p);
+    return cudaLaunchKernelEx(&rc, chpe_qgemv_reduce_kernel<LAYOUT, MODE>, p);
 }
 
 // All variants of one code width / epilogue block, chosen at run time.

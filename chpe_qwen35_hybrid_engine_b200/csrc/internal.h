@@ -26,6 +26,7 @@ struct DevMatrix {
     int n_groups = 0;     // groups per row
     float scale = 1.0f;   // per-tensor scale (S8 layout)
     float zc = 0.0f;      // constant zero-point (kMetaS16)
+    uint32_t xorv = 0;    // XOR applied to every stored code (F16 layout: int8 ^ 0x80, 2-bit codebook ^ 2)
     uint8_t *codes = nullptr;  // n_strips * n_blocks * block_bytes
     float *bias = nullptr;
     int *out_cols = nullptr;  // [N][8] outlier columns, -1 = none
@@ -84,6 +85,7 @@ struct GemvParams {
     int n_whole, bc, cfull, ctot, pref;
     const void *xf;
     const float *xs;
+    const float *xe;  // row unscale factors [M] (2^-e of the fill's row scaling); fp16 path
     const float *sx;
     const float *xrow;  // fp32 activations [M][K] (outlier columns), or null
     float *y;
@@ -92,7 +94,7 @@ struct GemvParams {
     void *ws;             // chunk sums [n_sg][ctot][kSG * 16 * M]
     unsigned *split_cnt;  // [n_sg] arrivals of chunk sums (self-resetting)
     unsigned *work_ctr;   // [n_ks] work counters (self-resetting)
-    int rmode;            // chunk sums: 0 by the last chunk's CTA, 1 by gemv_reduce_kernel (set at launch)
+    int rmode;            // chunk sums: 0 by the last chunk's CTA, 1 by chpe_qgemv_reduce_kernel (set at launch)
     int gk;               // CTAs per K-slice (set at launch)
     // fused fill: with `fused` set, every CTA builds the activation fragments
     // of its K-slice in shared memory from `xsrc` (fp32 rows [M][K]) instead
@@ -104,11 +106,11 @@ struct GemvParams {
 
 // Scratch a GEMV call needs, owned by the caller (context).
 struct GemvScratch {
-    void *xf = nullptr, *xlo = nullptr;
+    void *xf = nullptr;
     float *xs = nullptr, *sx = nullptr;
     void *ws = nullptr;
     unsigned *counters = nullptr;  // arrival counters (one per strip group), then work counters
-    size_t xf_bytes = 0, xlo_bytes = 0, xs_bytes = 0, sx_bytes = 0, ws_bytes = 0, counters_n = 0;
+    size_t xf_bytes = 0, xs_bytes = 0, sx_bytes = 0, ws_bytes = 0, counters_n = 0;
 };
 
 constexpr int kMaxKs = 256;
@@ -134,13 +136,15 @@ struct GemvPlan {
 
 int plan_gemv(const DevMatrix &w, int M, int mode, bool xsplit, GemvPlan *plan);
 
+// Fragment fills write the row unscale factors xe[M] (2^-e of the row's
+// power-of-two scaling) beside the block sums.
 cudaError_t launch_xfill_f16(const XSrc &s, int M, int K, int Kp, int e_cols, bool xsplit, int bits, void *xf,
-                             float *xs, cudaStream_t st);
-cudaError_t launch_xmaterialize(const XSrc &s, int M, int K, float *out, cudaStream_t st);
+                             float *xs, float *xe, cudaStream_t st);
+cudaError_t launch_xmaterialize(const XSrc &s, int M, int K, int Kp, float *out, cudaStream_t st);
 
 // x-fragment preparation (fp activations -> fp16 fragments + block sums).
 cudaError_t launch_xprep_f16(const void *x, int x_dtype, int M, int K, int Kp, int e_cols, bool xsplit, int bits,
-                             void *xf, float *xs, cudaStream_t st);
+                             void *xf, float *xs, float *xe, cudaStream_t st);
 // int8 activations -> int8 fragments.
 cudaError_t launch_xprep_s8(const int8_t *xq, int M, int K, int Kp, void *xf, cudaStream_t st);
 // fp32 activations -> per-row dynamic int8 quantization (+ fragments).
@@ -161,6 +165,11 @@ cudaError_t launch_prefill(const DevMatrix &w, const void *x, int x_dtype, int M
 // of `m`, XOR-ing each code with `xorv` (F16 layout only).
 cudaError_t launch_repack_codes(const uint8_t *src, size_t row_stride, int src_bits, uint32_t xorv,
                                 const DevMatrix &m, cudaStream_t st);
+// Read-back of a matrix in strip layout: row-major codes packed LSB first
+// (row_bytes per row, the stored XOR undone) and its group metadata (fp16
+// scales / zeros [N][n_groups], or the fp32 per-row scale of kMetaF32).
+cudaError_t launch_unpack(const DevMatrix &m, uint32_t xorv, size_t row_bytes, uint8_t *codes, __half *s, __half *z,
+                          float *fs, cudaStream_t st);
 // Grouped quantization of fp32 weights [N][K] (one code byte per weight).
 cudaError_t launch_quant_group(const float *w, int N, int K, int group, int bits, int symmetric, uint8_t *codes,
                                __half *scales, __half *zeros, cudaStream_t st);

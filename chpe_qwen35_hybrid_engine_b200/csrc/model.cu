@@ -13,7 +13,7 @@
 namespace chpe {
 
 // src/engine.zig:567-580 embedToken: hidden[i] = int8 row[i] * scale.
-__global__ void embed_i8_kernel(const int8_t *__restrict__ table, float scale, int hidden, int vocab,
+__global__ void chpe_embed_i8_kernel(const int8_t *__restrict__ table, float scale, int hidden, int vocab,
                                 const int *__restrict__ tokens, float *__restrict__ out, int *__restrict__ err) {
     pdl_begin();
     const int m = blockIdx.y;
@@ -29,7 +29,7 @@ __global__ void embed_i8_kernel(const int8_t *__restrict__ table, float scale, i
 // src/kernels/neon.zig:673-702 rmsnorm: y = x * (1/sqrt(mean(x^2) + eps)) * gamma.
 // One block per row; the sum of squares is a fixed-order tree (deterministic,
 // not the reference's lane order, so the last bits may differ).
-__global__ void rmsnorm_kernel(const float *__restrict__ x, const float *__restrict__ gamma, int n, float eps,
+__global__ void chpe_rmsnorm_kernel(const float *__restrict__ x, const float *__restrict__ gamma, int n, float eps,
                                float *__restrict__ y) {
     pdl_begin();
     __shared__ float red[32];
@@ -56,7 +56,7 @@ __global__ void rmsnorm_kernel(const float *__restrict__ x, const float *__restr
 // src/engine.zig:619-623: attention stand-in, out[i] = v[i % kv_dim]
 // (head_dim = 0); or, head-aligned, each query head h of head_dim columns takes
 // kv head h / group (what attention over a single position returns).
-__global__ void mix_attn_kernel(const float *__restrict__ v, int kv_dim, int out_dim, int head_dim, int group,
+__global__ void chpe_mix_attn_kernel(const float *__restrict__ v, int kv_dim, int out_dim, int head_dim, int group,
                                 float *__restrict__ out) {
     pdl_begin();
     const int m = blockIdx.y;
@@ -68,7 +68,7 @@ __global__ void mix_attn_kernel(const float *__restrict__ v, int kv_dim, int out
 
 // src/engine.zig:651-654 (batch 1): out[i] = qkv[i % qkv_dim] * silu(z[i]);
 // src/engine.zig:813 / :988 (batch 4 / 8): out[i] = silu(qkv[i]) * z[i].
-__global__ void mix_ssm_kernel(const float *__restrict__ qkv, int qkv_dim, const float *__restrict__ z, int z_dim,
+__global__ void chpe_mix_ssm_kernel(const float *__restrict__ qkv, int qkv_dim, const float *__restrict__ z, int z_dim,
                                int out_dim, int silu_on_qkv, float *__restrict__ out) {
     pdl_begin();
     const int m = blockIdx.y;
@@ -80,7 +80,7 @@ __global__ void mix_ssm_kernel(const float *__restrict__ qkv, int qkv_dim, const
 }
 
 // src/kernels/neon.zig:705-712 siluMul.
-__global__ void silu_mul_kernel(const float *__restrict__ g, const float *__restrict__ u, size_t n,
+__global__ void chpe_silu_mul_kernel(const float *__restrict__ g, const float *__restrict__ u, size_t n,
                                 float *__restrict__ out) {
     pdl_begin();
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
@@ -89,7 +89,7 @@ __global__ void silu_mul_kernel(const float *__restrict__ g, const float *__rest
 
 // src/engine.zig:1098-1110 computeArgmax: first index of the largest value
 // (NaN never wins).  One block per row.
-__global__ void argmax_kernel(const float *__restrict__ logits, int n, int *__restrict__ idx,
+__global__ void chpe_argmax_kernel(const float *__restrict__ logits, int n, int *__restrict__ idx,
                               float *__restrict__ maxv) {
     pdl_begin();
     __shared__ float sv[32];
@@ -160,14 +160,14 @@ extern "C" int chpe_embed_i8_dev(chpe_ctx *ctx, const int8_t *table, float scale
                                  const int *tokens, int M, float *out, void *stream) {
     if (!ctx || !table || !tokens || !out || M < 1 || hidden < 1) return CHPE_EINVAL;
     dim3 grid(grid_for(hidden, 256) < 16 ? grid_for(hidden, 256) : 16, M);
-    return launched(launch_pdl(embed_i8_kernel, grid, dim3(256), 0, static_cast<cudaStream_t>(stream), table, scale,
+    return launched(launch_pdl(chpe_embed_i8_kernel, grid, dim3(256), 0, static_cast<cudaStream_t>(stream), table, scale,
                                hidden, vocab, tokens, out, chpe_ctx_error_word(ctx)));
 }
 
 extern "C" int chpe_rmsnorm_dev(chpe_ctx *ctx, const float *x, const float *gamma, int M, int n, float eps, float *y,
                                 void *stream) {
     if (!ctx || !x || !gamma || !y || M < 1 || n < 1) return CHPE_EINVAL;
-    return launched(launch_pdl(rmsnorm_kernel, dim3(M), dim3(512), 0, static_cast<cudaStream_t>(stream), x, gamma, n,
+    return launched(launch_pdl(chpe_rmsnorm_kernel, dim3(M), dim3(512), 0, static_cast<cudaStream_t>(stream), x, gamma, n,
                                eps, y));
 }
 
@@ -176,7 +176,7 @@ extern "C" int chpe_mix_attn_stub_dev(chpe_ctx *ctx, const float *v, int kv_dim,
     if (!ctx || !v || !out || M < 1 || kv_dim < 1) return CHPE_EINVAL;
     if (head_dim && (group < 1 || ((out_dim / head_dim + group - 1) / group) * head_dim > kv_dim)) return CHPE_EINVAL;
     dim3 grid(grid_for(out_dim, 256) < 16 ? grid_for(out_dim, 256) : 16, M);
-    return launched(launch_pdl(mix_attn_kernel, grid, dim3(256), 0, static_cast<cudaStream_t>(stream), v, kv_dim,
+    return launched(launch_pdl(chpe_mix_attn_kernel, grid, dim3(256), 0, static_cast<cudaStream_t>(stream), v, kv_dim,
                                out_dim, head_dim, group, out));
 }
 
@@ -184,19 +184,19 @@ extern "C" int chpe_mix_ssm_stub_dev(chpe_ctx *ctx, const float *qkv, int qkv_di
                                      int out_dim, int silu_on_qkv, float *out, void *stream) {
     if (!ctx || !qkv || !z || !out || M < 1 || qkv_dim < 1 || out_dim > z_dim) return CHPE_EINVAL;
     dim3 grid(grid_for(out_dim, 256) < 16 ? grid_for(out_dim, 256) : 16, M);
-    return launched(launch_pdl(mix_ssm_kernel, grid, dim3(256), 0, static_cast<cudaStream_t>(stream), qkv, qkv_dim, z,
+    return launched(launch_pdl(chpe_mix_ssm_kernel, grid, dim3(256), 0, static_cast<cudaStream_t>(stream), qkv, qkv_dim, z,
                                z_dim, out_dim, silu_on_qkv, out));
 }
 
 extern "C" int chpe_silu_mul_dev(chpe_ctx *ctx, const float *g, const float *u, size_t n, float *out, void *stream) {
     if (!ctx || !g || !u || !out) return CHPE_EINVAL;
-    return launched(launch_pdl(silu_mul_kernel, dim3(grid_for(n, 256)), dim3(256), 0,
+    return launched(launch_pdl(chpe_silu_mul_kernel, dim3(grid_for(n, 256)), dim3(256), 0,
                                static_cast<cudaStream_t>(stream), g, u, n, out));
 }
 
 extern "C" int chpe_argmax_dev(chpe_ctx *ctx, const float *logits, int M, int n, int *idx, float *maxv,
                                void *stream) {
     if (!ctx || !logits || !idx || M < 1 || n < 1) return CHPE_EINVAL;
-    return launched(launch_pdl(argmax_kernel, dim3(M), dim3(1024), 0, static_cast<cudaStream_t>(stream), logits, n, idx,
+    return launched(launch_pdl(chpe_argmax_kernel, dim3(M), dim3(1024), 0, static_cast<cudaStream_t>(stream), logits, n, idx,
                                maxv));
 }

@@ -33,7 +33,7 @@
 //     (warp 4 + 4c + q reads TMEM lanes 32q..32q+31 = weight rows of half
 //     c & 1, token columns 128 (c >> 1) .. +127) and store fp32 into y.
 // Activations are converted once per call into fp16 tiles of 256 x 64 already
-// in the swizzled layout (prefill_xprep_kernel), so each k-block's B operand
+// in the swizzled layout (chpe_prefill_xprep_kernel), so each k-block's B operand
 // is one contiguous 32 KB copy.  Every wait is bounded: on a timeout the
 // kernel records an error code, stops issuing, waits (bounded) for the work it
 // issued, frees its tensor memory and returns.
@@ -44,6 +44,7 @@
 #include "../../include/chpe_b200.h"
 #include "common.cuh"
 #include "internal.h"
+#include "xsrc.cuh"
 
 namespace chpe {
 namespace {
@@ -140,6 +141,7 @@ __device__ __forceinline__ __half2 bits_h2(uint32_t u) { return *reinterpret_cas
 struct PrefillParams {
     const uint8_t *codes;  // strip layout
     const uint16_t *xt;    // activation tiles [token_tile][k_block][256 x 64 swizzled fp16]
+    const float2 *rs;      // per token (2^e, 2^-e): the row scaling applied before the fp16 conversion
     float *y;
     int ldy, M, N, K;
     int n_strips, n_blocks, block_bytes, bits, meta_kind, group, span;
@@ -195,7 +197,7 @@ __host__ __device__ inline PSmem psmem(uint32_t code_bytes, uint32_t meta_bytes)
 
 template <int BITS, int META>
 __global__ void __launch_bounds__(kPThreads, 1)
-    prefill_gemm_kernel(const PrefillParams p, const __grid_constant__ CUtensorMap tm_codes,
+    chpe_prefill_gemm_kernel(const PrefillParams p, const __grid_constant__ CUtensorMap tm_codes,
                         const __grid_constant__ CUtensorMap tm_meta) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // the swizzle is a function of the address: align the working area to 1024 B
@@ -402,7 +404,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
                         const int m = tok0 + c0 + cc + e;
                         if (m < p.M) {
                             float *yp = p.y + (size_t)m * p.ldy + n;
-                            const float val = __uint_as_float(v[e]);
+                            const float val = __uint_as_float(v[e]) * p.rs[m].y;  // undo the row scaling
                             *yp = p.accumulate ? *yp + val : val;
                         }
                     }
@@ -430,8 +432,31 @@ __device__ __forceinline__ float x_at(const void *x, int dt, size_t i) {
                                : __half2float(static_cast<const __half *>(x)[i]);
 }
 
-__global__ void prefill_xprep_kernel(const void *__restrict__ x, int dt, int M, int K, int n_tt, int n_kb,
-                                     uint16_t *__restrict__ xt) {
+// Row scaling of the prefill activations: one block per token row computes
+// max |x| and stores (2^e, 2^-e) with max |x| * 2^e in [2^14, 2^15)
+// (row_scale_exp), so the fp16 tiles hold every row whatever its magnitude;
+// the epilogue multiplies the row's sums by 2^-e (powers of two are exact).
+__global__ void __launch_bounds__(256) chpe_prefill_rowscale_kernel(const void *__restrict__ x, int dt, int K,
+                                                                   float2 *__restrict__ rs) {
+    __shared__ float red[8];
+    pdl_begin();
+    const int m = blockIdx.x;
+    float am = 0.0f;
+    for (int k = threadIdx.x; k < K; k += blockDim.x) am = fmaxf(am, fabsf(x_at(x, dt, (size_t)m * K + k)));
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, off));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = am;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float mx = 0.0f;
+        for (int w = 0; w < (int)(blockDim.x >> 5); ++w) mx = fmaxf(mx, red[w]);
+        const int e = row_scale_exp(mx);
+        rs[m] = make_float2(pow2_of(e), pow2_of(-e));
+    }
+}
+
+__global__ void chpe_prefill_xprep_kernel(const void *__restrict__ x, int dt, int M, int K, int n_tt, int n_kb,
+                                          const float2 *__restrict__ rs, uint16_t *__restrict__ xt) {
     pdl_begin();
     const size_t total = (size_t)n_tt * kPN * n_kb * (kPK / 8);
     const bool vec = (K % 8) == 0 && (reinterpret_cast<uintptr_t>(x) % 16) == 0;
@@ -445,32 +470,38 @@ __global__ void prefill_xprep_kernel(const void *__restrict__ x, int dt, int M, 
         uint4 out = make_uint4(0u, 0u, 0u, 0u);
         if (m < M && k0 < K) {
             const size_t base = (size_t)m * K + k0;
+            const float sc = rs[m].x;
+            float f[8];
             if (vec && dt == CHPE_X_F16) {
-                out = *reinterpret_cast<const uint4 *>(static_cast<const __half *>(x) + base);
+                const uint4 v = *reinterpret_cast<const uint4 *>(static_cast<const __half *>(x) + base);
+                const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float2 t = __half22float2(bits_h2(w[e]));
+                    f[2 * e] = t.x;
+                    f[2 * e + 1] = t.y;
+                }
             } else if (vec && dt == CHPE_X_BF16) {
                 const uint4 v = *reinterpret_cast<const uint4 *>(static_cast<const __nv_bfloat16 *>(x) + base);
                 const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-                uint32_t h[4];
 #pragma unroll
-                for (int e = 0; e < 4; ++e)
-                    h[e] = h2_bits(__float22half2_rn(__bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&w[e]))));
-                out = make_uint4(h[0], h[1], h[2], h[3]);
+                for (int e = 0; e < 4; ++e) {
+                    const float2 t = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&w[e]));
+                    f[2 * e] = t.x;
+                    f[2 * e + 1] = t.y;
+                }
             } else if (vec && dt == CHPE_X_F32) {
                 const float4 a = *reinterpret_cast<const float4 *>(static_cast<const float *>(x) + base);
                 const float4 b = *reinterpret_cast<const float4 *>(static_cast<const float *>(x) + base + 4);
-                out = make_uint4(h2_bits(__floats2half2_rn(a.x, a.y)), h2_bits(__floats2half2_rn(a.z, a.w)),
-                                 h2_bits(__floats2half2_rn(b.x, b.y)), h2_bits(__floats2half2_rn(b.z, b.w)));
+                f[0] = a.x, f[1] = a.y, f[2] = a.z, f[3] = a.w, f[4] = b.x, f[5] = b.y, f[6] = b.z, f[7] = b.w;
             } else {
-                uint32_t h[4];
 #pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const int ka = k0 + 2 * e;
-                    const float va = ka < K ? x_at(x, dt, base + 2 * e) : 0.0f;
-                    const float vb = ka + 1 < K ? x_at(x, dt, base + 2 * e + 1) : 0.0f;
-                    h[e] = h2_bits(__floats2half2_rn(va, vb));
-                }
-                out = make_uint4(h[0], h[1], h[2], h[3]);
+                for (int e = 0; e < 8; ++e) f[e] = k0 + e < K ? x_at(x, dt, base + e) : 0.0f;
             }
+            uint32_t h[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) h[e] = h2_bits(__floats2half2_rn(f[2 * e] * sc, f[2 * e + 1] * sc));
+            out = make_uint4(h[0], h[1], h[2], h[3]);
         }
         const int tt = m / kPN, r = m % kPN;
         uint8_t *tile = reinterpret_cast<uint8_t *>(xt) + ((size_t)tt * n_kb + kb) * kXTileBytes;
@@ -512,13 +543,10 @@ bool make_strip_map(CUtensorMap *map, const PrefillParams &p, uint32_t box_bytes
 
 template <int BITS, int META>
 cudaError_t launch_prefill_t(const PrefillParams &p, size_t smem, cudaStream_t st) {
-    auto kern = prefill_gemm_kernel<BITS, META>;
-    static bool attr_set = false;
-    if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess) return e;
-        attr_set = true;
-    }
+    auto kern = chpe_prefill_gemm_kernel<BITS, META>;
+    static KernelDeviceState kstate;  // the shared-memory limit is set once per device
+    cudaError_t pe = kernel_prepare(kstate, kern, kPThreads, smem, smem, nullptr);
+    if (pe != cudaSuccess) return pe;
     const KbSlice s0 = kb_slice(p, 0);
     CUtensorMap tm_codes, tm_meta;
     if (!make_strip_map(&tm_codes, p, s0.code_bytes) || !make_strip_map(&tm_meta, p, s0.meta_bytes))
@@ -529,10 +557,15 @@ cudaError_t launch_prefill_t(const PrefillParams &p, size_t smem, cudaStream_t s
 
 }  // namespace
 
-// Scratch bytes for the activation tiles of an M x K prefill.
-size_t prefill_xt_bytes(int M, int K) {
+// Scratch bytes for the activation tiles of an M x K prefill, then the
+// per-token row scales (float2 per token of the padded token tiles).
+size_t prefill_tiles_bytes(int M, int K) {
     const size_t n_tt = (size_t)(M + kPN - 1) / kPN, n_kb = (size_t)(K + kPK - 1) / kPK;
     return n_tt * n_kb * kXTileBytes;
+}
+size_t prefill_xt_bytes(int M, int K) {
+    const size_t n_tt = (size_t)(M + kPN - 1) / kPN;
+    return prefill_tiles_bytes(M, K) + n_tt * kPN * sizeof(float2);
 }
 
 // Whether the prefill kernel handles this weight format.
@@ -549,6 +582,8 @@ cudaError_t launch_prefill(const DevMatrix &w, const void *x, int x_dtype, int M
     PrefillParams p;
     p.codes = w.codes;
     p.xt = static_cast<const uint16_t *>(xt);
+    float2 *rs = reinterpret_cast<float2 *>(static_cast<uint8_t *>(xt) + prefill_tiles_bytes(M, w.K));
+    p.rs = rs;
     p.y = y;
     p.ldy = ldy;
     p.M = M;
@@ -567,8 +602,11 @@ cudaError_t launch_prefill(const DevMatrix &w, const void *x, int x_dtype, int M
     p.accumulate = accumulate;
     p.err = err;
     const size_t total = (size_t)p.n_tt * kPN * p.n_kb * (kPK / 8);
-    cudaError_t e = launch_pdl(prefill_xprep_kernel, dim3((unsigned)std::min<size_t>((total + 255) / 256, 148 * 16)),
-                               dim3(256), 0, st, x, x_dtype, M, w.K, p.n_tt, p.n_kb, static_cast<uint16_t *>(xt));
+    cudaError_t e = launch_pdl(chpe_prefill_rowscale_kernel, dim3((unsigned)M), dim3(256), 0, st, x, x_dtype, w.K, rs);
+    if (e != cudaSuccess) return e;
+    e = launch_pdl(chpe_prefill_xprep_kernel, dim3((unsigned)std::min<size_t>((total + 255) / 256, 148 * 16)),
+                   dim3(256), 0, st, x, x_dtype, M, w.K, p.n_tt, p.n_kb, static_cast<const float2 *>(rs),
+                   static_cast<uint16_t *>(xt));
     if (e != cudaSuccess) return e;
     const KbSlice s0 = kb_slice(p, 0);
     const size_t smem = psmem(s0.code_bytes, s0.meta_bytes).total + 1024;  // + alignment slack

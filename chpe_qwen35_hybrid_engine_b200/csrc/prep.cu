@@ -1,6 +1,8 @@
 // prep.cu -- activation-fragment preparation, dynamic int8 activation
 // quantization, weight repacking into the strip layout, and the GPU
 // quantizers used to build device tensors from fp32 weights.
+#include <cooperative_groups.h>
+
 #include <algorithm>
 
 #include "common.cuh"
@@ -13,105 +15,153 @@ namespace chpe {
 // activations
 // ---------------------------------------------------------------------------
 
-// 1 / sqrt(mean(x^2) + eps) of row tok (blocks of 256 threads): per-thread
-// partials in the fixed order of row_sumsq_part, a shuffle tree, the warp
-// partials in order -- the same bits as the GEMV kernel's fused fill.
-__device__ float row_inv_rms(const XSrc &s, int tok, int K, float *red) {
+// Statistics of row tok over the fill ranges (xsrc.cuh), computed by one CTA
+// of 256 threads: 1 / sqrt(mean(x^2) + eps) for RMSNorm (1 otherwise) in the
+// fill cluster's summation order.
+__device__ float row_inv_rms_ranges(const XSrc &s, int tok, int K, int nunits, float *red) {
+    if (s.op != kXRmsnorm) return 1.0f;
     const float *row = static_cast<const float *>(s.x) + (size_t)tok * s.ldx;
-    float acc = row_sumsq_part(row, K, threadIdx.x, blockDim.x);
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
-    __syncthreads();
+    const int C = fill_ctas(nunits);
     float tot = 0.0f;
-    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) tot += red[w];
-    __syncthreads();
+    for (int c = 0; c < C; ++c) {
+        int u0, u1;
+        fill_range(nunits, C, c, u0, u1);
+        tot += block_range_sumsq(row, min(4 * u0, K), min(4 * u1, K), threadIdx.x, kFillThreads, red, 0);
+    }
     return inv_rms_of(tot, K, s.eps);
 }
 
-// Activation fragments of the fp16 GEMV path.  Grid (units / 256, M): one
-// thread per fragment unit u = 4 * s + t of row tok (k-step s, lane column
-// t), i.e. columns 16s + 2t + {0, 1, 8, 9}.  Fragments are stored as 16-byte
-// units so a consumer fetches two k-steps (or, for fp32 input, the hi and lo
-// parts of one k-step) with one load:
+// Activation fragments of the fp16 GEMV path.  One cluster of C CTAs
+// (fill_ctas) per activation row tok = blockIdx.y; CTA c owns fragment units
+// [u0, u1) (fill_range) and loops over them 256 at a time.  Unit u = 4 * s + t
+// (k-step s, lane column t) holds columns 16s + 2t + {0, 1, 8, 9}; fragments
+// are stored as 16-byte units so a consumer fetches two k-steps (or, for fp32
+// input, the hi and lo parts of one k-step) with one load:
 //   split (fp32 x):  unit (s, m, t) = {hi(16s+2t..), hi(16s+2t+8..), lo(..), lo(..)}
 //   fp16/bf16 x:     unit (s/2, m, t) = {step 2u: ..., step 2u+1: ...}
+// Row statistics first: each CTA reduces its range (sum of squares for
+// RMSNorm, largest |value|), the CTAs exchange them through distributed shared
+// memory and every CTA combines them in range order, so the whole cluster
+// agrees on the RMSNorm scale and on the row's power-of-two scale 2^e
+// (row_scale_exp), which keeps every scaled value inside fp16's range;
+// xe[tok] = 2^-e undoes it in the GEMV epilogue.
 // `bits` selects the per-k-step power-of-two pre-scale that matches where the
 // GEMV kernel reads the codes (unpack_f16): 4-bit odd k-steps of a chunk /16,
 // 2-bit k-step j of a chunk / 4^(j%4), 8-bit none.  The sum of each E-column
 // block (what the zero-point term multiplies) is taken over the values the
-// MMA sees, unscaled, from the E/4 consecutive threads that hold the block.
-__global__ void __launch_bounds__(256) xfill_f16_kernel(const XSrc s, int M, int K, int Kp, int E, int split,
-                                                        int bits, uint2 *__restrict__ xf, float *__restrict__ xs) {
+// MMA sees, with the k-step pre-scale undone, from the E/4 consecutive threads
+// that hold the block.
+__global__ void __launch_bounds__(kFillThreads) chpe_xfill_f16_kernel(const XSrc s, int M, int K, int Kp, int E,
+                                                                     int split, int bits, uint2 *__restrict__ xf,
+                                                                     float *__restrict__ xs, float *__restrict__ xe) {
+    namespace cg = cooperative_groups;
+    cg::cluster_group cluster = cg::this_cluster();
     __shared__ float red[32];
+    __shared__ float2 stat;  // (sum of squares, largest |value|) of this CTA's range
     pdl_begin();
     const int tok = blockIdx.y;
-    const float inv = s.op == kXRmsnorm ? row_inv_rms(s, tok, K, red) : 1.0f;
-    const int u = blockIdx.x * blockDim.x + threadIdx.x;
     const int nunits = Kp / 4;
-    float part = 0.0f;
-    if (u < nunits) {
-        const int st = u >> 2, t = u & 3;
-        const int steps = (256 / bits) / 16;  // k-steps per chunk
-        const int j = st % steps;
-        const int sh = bits == 4 ? 4 * (j & 1) : bits == 2 ? 2 * (j & 3) : 0;
-        const float down = __int_as_float((127 - sh) << 23), up = __int_as_float((127 + sh) << 23);
-        const int kb = 16 * st + 2 * t;
-        const int kk[4] = {kb, kb + 1, kb + 8, kb + 9};
-        __half h[4], l[4];
+    const int C = (int)cluster.num_blocks();
+    const int c = (int)cluster.block_rank();
+    int u0, u1;
+    fill_range(nunits, C, c, u0, u1);
+    const int k0 = min(4 * u0, K), k1 = min(4 * u1, K);
+    const int tid = threadIdx.x;
+    float ss = 0.0f;
+    if (s.op == kXRmsnorm)
+        ss = block_range_sumsq(static_cast<const float *>(s.x) + (size_t)tok * s.ldx, k0, k1, tid, kFillThreads, red, 0);
+    float am = range_absmax(s, tok, k0, k1, tid, kFillThreads);
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            const float v = (kk[q] < K ? xsrc_value(s, tok, kk[q], inv) : 0.0f) * down;
-            h[q] = __float2half_rn(v);
-            l[q] = split ? __float2half_rn(v - __half2float(h[q])) : __float2half_rn(0.0f);
-            part += (__half2float(h[q]) + __half2float(l[q])) * up;
+    for (int off = 16; off > 0; off >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, off));
+    if ((tid & 31) == 0) red[tid >> 5] = am;
+    __syncthreads();
+    if (tid == 0) {
+        float m = 0.0f;
+        for (int w = 0; w < kFillThreads / 32; ++w) m = fmaxf(m, red[w]);
+        stat = make_float2(ss, m);
+    }
+    cluster.sync();
+    float tot = 0.0f, amax = 0.0f;
+    for (int r = 0; r < C; ++r) {
+        const float2 v = *cluster.map_shared_rank(&stat, r);
+        tot += v.x;
+        amax = fmaxf(amax, v.y);
+    }
+    cluster.sync();  // every peer has read this CTA's statistics
+    const float inv = s.op == kXRmsnorm ? inv_rms_of(tot, K, s.eps) : 1.0f;
+    const int e = row_scale_exp(s.op == kXRmsnorm ? amax * inv : amax);
+    if (c == 0 && tid == 0) xe[tok] = pow2_of(-e);
+    const int steps = (256 / bits) / 16;  // k-steps per chunk
+    for (int ub = u0; ub < u1; ub += kFillThreads) {
+        const int u = ub + tid;
+        float part = 0.0f;
+        if (u < u1) {
+            const int st = u >> 2, t = u & 3;
+            const int j = st % steps;
+            const int sh = bits == 4 ? 4 * (j & 1) : bits == 2 ? 2 * (j & 3) : 0;
+            const float down = pow2_of(e - sh), up = pow2_of(sh);
+            const int kb = 16 * st + 2 * t;
+            const int kk[4] = {kb, kb + 1, kb + 8, kb + 9};
+            __half h[4], l[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const float v = (kk[q] < K ? xsrc_value(s, tok, kk[q], inv) : 0.0f) * down;
+                h[q] = __float2half_rn(v);
+                l[q] = split ? __float2half_rn(v - __half2float(h[q])) : __float2half_rn(0.0f);
+                part += (__half2float(h[q]) + __half2float(l[q])) * up;
+            }
+            const uint2 hv = make_uint2(pack_h2(h[0], h[1]), pack_h2(h[2], h[3]));
+            if (split) {
+                const size_t v = ((size_t)st * M + tok) * 4 + t;
+                xf[2 * v] = hv;
+                xf[2 * v + 1] = make_uint2(pack_h2(l[0], l[1]), pack_h2(l[2], l[3]));
+            } else {
+                const size_t v = ((size_t)(st >> 1) * M + tok) * 4 + t;
+                xf[2 * v + (st & 1)] = hv;
+            }
         }
-        const uint2 hv = make_uint2(pack_h2(h[0], h[1]), pack_h2(h[2], h[3]));
-        if (split) {
-            const size_t v = ((size_t)st * M + tok) * 4 + t;
-            xf[2 * v] = hv;
-            xf[2 * v + 1] = make_uint2(pack_h2(l[0], l[1]), pack_h2(l[2], l[3]));
-        } else {
-            const size_t v = ((size_t)(st >> 1) * M + tok) * 4 + t;
-            xf[2 * v + (st & 1)] = hv;
+        // E/4 consecutive threads (8, 16 or 32, aligned) hold one E-column
+        // block; ranges are whole 32-unit groups, so a warp is all in or all out
+        if (ub + (tid & ~31) < u1) {
+            for (int off = E / 8; off > 0; off >>= 1) part += __shfl_xor_sync(0xffffffffu, part, off);
+            if (u < u1 && (u % (E / 4)) == 0) xs[(size_t)(u / (E / 4)) * 8 + tok] = part;
         }
     }
-    // E/4 consecutive threads (8, 16 or 32, aligned) hold one E-column block
-    for (int off = E / 8; off > 0; off >>= 1) part += __shfl_xor_sync(0xffffffffu, part, off);
-    if (u < nunits && (u % (E / 4)) == 0) xs[(size_t)(u / (E / 4)) * 8 + tok] = part;
 }
 
 cudaError_t launch_xfill_f16(const XSrc &s, int M, int K, int Kp, int e_cols, bool xsplit, int bits, void *xf,
-                             float *xs, cudaStream_t st) {
-    const int nunits = Kp / 4;
-    return launch_pdl(xfill_f16_kernel, dim3((nunits + 255) / 256, M), dim3(256), 0, st, s, M, K, Kp, e_cols,
-                      xsplit ? 1 : 0, bits, static_cast<uint2 *>(xf), xs);
+                             float *xs, float *xe, cudaStream_t st) {
+    const int C = fill_ctas(Kp / 4);
+    return launch_pdl_cluster(chpe_xfill_f16_kernel, dim3(C, M), dim3(kFillThreads), (unsigned)C, 0, st, s, M, K, Kp,
+                              e_cols, xsplit ? 1 : 0, bits, static_cast<uint2 *>(xf), xs, xe);
 }
 
 cudaError_t launch_xprep_f16(const void *x, int x_dtype, int M, int K, int Kp, int e_cols, bool xsplit, int bits,
-                             void *xf, float *xs, cudaStream_t st) {
+                             void *xf, float *xs, float *xe, cudaStream_t st) {
     XSrc s;
     s.op = kXPlain;
     s.x = x;
     s.dt = x_dtype;
     s.ldx = K;
-    return launch_xfill_f16(s, M, K, Kp, e_cols, xsplit, bits, xf, xs, st);
+    return launch_xfill_f16(s, M, K, Kp, e_cols, xsplit, bits, xf, xs, xe, st);
 }
 
 // The source op's values as fp32 rows [M][K] (for the int8 path, which
-// quantizes them per row, and for the outlier columns' fp32 activations).
-__global__ void __launch_bounds__(256) xmaterialize_kernel(const XSrc s, int K, float *__restrict__ out) {
+// quantizes them per row, and for the outlier columns' fp32 activations);
+// RMSNorm statistics in the fill's order.
+__global__ void __launch_bounds__(kFillThreads) chpe_xmaterialize_kernel(const XSrc s, int K, int Kp,
+                                                                        float *__restrict__ out) {
     __shared__ float red[32];
     pdl_begin();
     const int tok = blockIdx.y;
-    const float inv = s.op == kXRmsnorm ? row_inv_rms(s, tok, K, red) : 1.0f;
+    const float inv = row_inv_rms_ranges(s, tok, K, Kp / 4, red);
     for (int k = blockIdx.x * blockDim.x + threadIdx.x; k < K; k += gridDim.x * blockDim.x)
         out[(size_t)tok * K + k] = xsrc_value(s, tok, k, inv);
 }
 
-cudaError_t launch_xmaterialize(const XSrc &s, int M, int K, float *out, cudaStream_t st) {
+cudaError_t launch_xmaterialize(const XSrc &s, int M, int K, int Kp, float *out, cudaStream_t st) {
     const int gx = std::min(64, (K + 255) / 256);
-    return launch_pdl(xmaterialize_kernel, dim3(gx, M), dim3(256), 0, st, s, K, out);
+    return launch_pdl(chpe_xmaterialize_kernel, dim3(gx, M), dim3(kFillThreads), 0, st, s, K, Kp, out);
 }
 
 __device__ __forceinline__ uint32_t pack4_i8(const int8_t *p, int k, int K) {
@@ -125,7 +175,7 @@ __device__ __forceinline__ uint32_t pack4_i8(const int8_t *p, int k, int K) {
 }
 
 // int8 activations [M][K] -> fragments [kstep32][M][4] uint2.
-__global__ void xprep_s8_kernel(const int8_t *__restrict__ xq, int M, int K, int nsteps, uint2 *__restrict__ xf) {
+__global__ void chpe_xprep_s8_kernel(const int8_t *__restrict__ xq, int M, int K, int nsteps, uint2 *__restrict__ xf) {
     pdl_begin();
     const size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     const size_t total = (size_t)nsteps * M * 4;
@@ -141,14 +191,14 @@ __global__ void xprep_s8_kernel(const int8_t *__restrict__ xq, int M, int K, int
 cudaError_t launch_xprep_s8(const int8_t *xq, int M, int K, int Kp, void *xf, cudaStream_t st) {
     const int nsteps = Kp / 32;
     const size_t total = (size_t)nsteps * M * 4;
-    return launch_pdl(xprep_s8_kernel, dim3((unsigned)((total + 255) / 256)), dim3(256), 0, st, xq, M, K, nsteps,
+    return launch_pdl(chpe_xprep_s8_kernel, dim3((unsigned)((total + 255) / 256)), dim3(256), 0, st, xq, M, K, nsteps,
                       static_cast<uint2 *>(xf));
 }
 
 // Per-row dynamic int8 quantization, bit-exact with the reference
 // (src/kernels/neon.zig:644-670): s = max|x|/127 (1 when max <= 1e-9),
 // q = clamp(round_half_away(x * (1/s)), -128, 127).  One block per row.
-__global__ void act_quant_s8_kernel(const float *__restrict__ x, int M, int K, int nsteps, int8_t *__restrict__ q,
+__global__ void chpe_act_quant_s8_kernel(const float *__restrict__ x, int M, int K, int nsteps, int8_t *__restrict__ q,
                                     float *__restrict__ scales, uint2 *__restrict__ xf) {
     __shared__ float red[32];
     __shared__ float s_inv;
@@ -195,7 +245,7 @@ __global__ void act_quant_s8_kernel(const float *__restrict__ x, int M, int K, i
 
 cudaError_t launch_act_quant_s8(const float *x, int M, int K, int Kp, int8_t *q, float *scales, void *xf,
                                 cudaStream_t st) {
-    return launch_pdl(act_quant_s8_kernel, dim3(M), dim3(256), 0, st, x, M, K, Kp / 32, q, scales,
+    return launch_pdl(chpe_act_quant_s8_kernel, dim3(M), dim3(256), 0, st, x, M, K, Kp / 32, q, scales,
                       static_cast<uint2 *>(xf));
 }
 
@@ -215,7 +265,7 @@ __device__ __forceinline__ uint32_t src_code(const uint8_t *src, size_t stride, 
 }
 
 // One thread per 32-bit word of the code area of the strip layout.
-__global__ void repack_codes_kernel(const uint8_t *__restrict__ src, size_t stride, int N, int K, int sbits, int bits,
+__global__ void chpe_repack_codes_kernel(const uint8_t *__restrict__ src, size_t stride, int N, int K, int sbits, int bits,
                                     int layout, uint32_t xorv, uint8_t *__restrict__ dst, int n_strips,
                                     int n_blocks, int block_bytes) {
     const size_t wi = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -266,7 +316,7 @@ cudaError_t launch_repack_codes(const uint8_t *src, size_t row_stride, int src_b
                                 const DevMatrix &m, cudaStream_t st) {
     const size_t total = (size_t)m.n_strips * m.n_blocks * kChunksPerBlock * 128;
     note_launch();
-    repack_codes_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(src, row_stride, m.N, m.K, src_bits, m.bits,
+    chpe_repack_codes_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(src, row_stride, m.N, m.K, src_bits, m.bits,
                                                                         m.layout, xorv, m.codes, m.n_strips,
                                                                         m.n_blocks, m.block_bytes);
     return cudaGetLastError();
@@ -275,7 +325,7 @@ cudaError_t launch_repack_codes(const uint8_t *src, size_t row_stride, int src_b
 // One thread per metadata entry (strip, block, group-in-block, row).  The
 // group of entry gib of block b is b*span/group + gib; groups past the matrix
 // (K padding) and rows past N get zero entries.
-__global__ void meta_repack_kernel(int kind, const __half *__restrict__ s, const __half *__restrict__ z,
+__global__ void chpe_meta_repack_kernel(int kind, const __half *__restrict__ s, const __half *__restrict__ z,
                                    const float *__restrict__ fs, const float *__restrict__ fo, float zc, int N,
                                    int n_groups, int group, int span, int gpb, int n_strips, int n_blocks,
                                    int block_bytes, uint8_t *__restrict__ dst) {
@@ -314,7 +364,7 @@ cudaError_t launch_meta_repack(const __half *s, const __half *z, const float *fs
                                float zc_for_f32, const DevMatrix &m, cudaStream_t st) {
     const size_t total = (size_t)m.n_strips * m.n_blocks * m.gpb * 16;
     note_launch();
-    meta_repack_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(
+    chpe_meta_repack_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(
         m.meta_kind, s, z, fs, fo, zc_for_f32, m.N, m.n_groups, m.group, m.span, m.gpb, m.n_strips, m.n_blocks,
         m.block_bytes, m.codes);
     return cudaGetLastError();
@@ -322,7 +372,7 @@ cudaError_t launch_meta_repack(const __half *s, const __half *z, const float *fs
 
 // GPU grouped quantizers (the formulas of chpe_quantize_group_dev in the header):
 // one warp per (row, group); codes are written one byte per weight.
-__global__ void quant_group_kernel(const float *__restrict__ w, int N, int K, int group, int bits, int symmetric,
+__global__ void chpe_quant_group_kernel(const float *__restrict__ w, int N, int K, int group, int bits, int symmetric,
                                    uint8_t *__restrict__ codes, __half *__restrict__ scales,
                                    __half *__restrict__ zeros) {
     const size_t gw = ((size_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -381,8 +431,98 @@ cudaError_t launch_quant_group(const float *w, int N, int K, int group, int bits
     const size_t warps = (size_t)N * (K / group);
     const size_t threads = warps * 32;
     note_launch();
-    quant_group_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, st>>>(w, N, K, group, bits, symmetric, codes,
+    chpe_quant_group_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, st>>>(w, N, K, group, bits, symmetric, codes,
                                                                         scales, zeros);
+    return cudaGetLastError();
+}
+
+}  // namespace chpe
+
+namespace chpe {
+
+// ---------------------------------------------------------------------------
+// read-back (the inverse of the repack): the strip layout -> row-major codes
+// ---------------------------------------------------------------------------
+
+// Code of element (row, k) as stored in the strip layout (layout.h), with the
+// stored XOR undone: the code the matrix was uploaded with.
+__device__ __forceinline__ uint32_t strip_code(const DevMatrix &m, int row, int k, uint32_t xorv) {
+    const int strip = row / kStripRows, r16 = row % kStripRows;
+    const int g = r16 & 7, hi = r16 >> 3;
+    const int blk = k / m.span, kin = k % m.span;
+    const int kc = 256 / m.bits;  // columns per chunk
+    const int cib = kin / kc, cc = kin % kc;
+    const uint8_t *chunk =
+        m.codes + ((size_t)strip * m.n_blocks + blk) * m.block_bytes + (size_t)cib * kChunkBytes;
+    if (m.layout == kLayoutS8) {
+        const int rhi = cc / 16, t = (cc % 16) / 4, i = cc % 4;
+        const int lw = (4 * g + t) * 4 + hi + 2 * rhi;
+        return chunk[(size_t)lw * 4 + i];
+    }
+    const int j = cc / 16, c16 = cc % 16;
+    const int rhi = c16 / 8, t = (c16 % 8) / 2, odd = c16 & 1;
+    const int lw = (4 * g + t) * 4 + hi + 2 * rhi;
+    const uint32_t w = reinterpret_cast<const uint32_t *>(chunk)[lw];
+    uint32_t c;
+    if (m.bits == 4)
+        c = (w >> (4 * (j + 4 * odd))) & 0xFu;
+    else if (m.bits == 2)
+        c = (w >> (2 * (j + 8 * odd))) & 0x3u;
+    else
+        c = (w >> (8 * (2 * j + odd))) & 0xFFu;
+    return c ^ xorv;
+}
+
+// One thread per output byte of the row-major packed codes (LSB first).
+__global__ void chpe_unpack_codes_kernel(const DevMatrix m, uint32_t xorv, size_t row_bytes, uint8_t *__restrict__ out) {
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (size_t)m.N * row_bytes) return;
+    const int row = (int)(i / row_bytes);
+    const int byte = (int)(i % row_bytes);
+    const int per = 8 / m.bits;
+    uint32_t v = 0;
+    for (int q = 0; q < per; ++q) {
+        const int k = byte * per + q;
+        if (k < m.K) v |= strip_code(m, row, k, xorv) << (m.bits * q);
+    }
+    out[i] = (uint8_t)v;
+}
+
+// One thread per (row, group): the fp16 scale (and zero) of the group, or the
+// fp32 per-row scale of kMetaF32.
+__global__ void chpe_unpack_meta_kernel(const DevMatrix m, __half *__restrict__ s, __half *__restrict__ z,
+                                        float *__restrict__ fs) {
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int ng = m.meta_kind == kMetaF32 ? 1 : m.n_groups;
+    if (i >= (size_t)m.N * ng) return;
+    const int row = (int)(i / ng), grp = (int)(i % ng);
+    const int strip = row / kStripRows, r16 = row % kStripRows;
+    const long k0 = (long)grp * (m.meta_kind == kMetaF32 ? m.K : m.group);
+    const int blk = (int)(k0 / m.span);
+    const int gib = m.gpb > 1 ? (int)((k0 % m.span) / m.group) : 0;
+    const uint8_t *base = m.codes + ((size_t)strip * m.n_blocks + blk) * m.block_bytes + kBlockCodeBytes;
+    const int e = gib * 16 + (r16 & 7) * 2 + (r16 >> 3);
+    if (m.meta_kind == kMetaS16) {
+        s[i] = reinterpret_cast<const __half *>(base)[e];
+    } else if (m.meta_kind == kMetaSZ16) {
+        const __half2 v = reinterpret_cast<const __half2 *>(base)[e];
+        s[i] = __low2half(v);
+        if (z) z[i] = __high2half(v);
+    } else if (m.meta_kind == kMetaF32) {
+        fs[i] = reinterpret_cast<const float2 *>(base)[e].x;
+    }
+}
+
+cudaError_t launch_unpack(const DevMatrix &m, uint32_t xorv, size_t row_bytes, uint8_t *codes, __half *s, __half *z,
+                          float *fs, cudaStream_t st) {
+    const size_t n = (size_t)m.N * row_bytes;
+    note_launch();
+    chpe_unpack_codes_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(m, xorv, row_bytes, codes);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess || m.meta_kind == kMetaNone || (!s && !fs)) return e;
+    const size_t nm = (size_t)m.N * (m.meta_kind == kMetaF32 ? 1 : m.n_groups);
+    note_launch();
+    chpe_unpack_meta_kernel<<<(unsigned)((nm + 255) / 256), 256, 0, st>>>(m, s, z, fs);
     return cudaGetLastError();
 }
 

@@ -77,4 +77,85 @@ __device__ __forceinline__ float inv_rms_of(float total, int K, float eps) {
     return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(total, (float)K), eps)));
 }
 
+// ---------------------------------------------------------------------------
+// Row statistics of a fragment fill.  A row of Kp / 4 fragment units is cut
+// into C = fill_ctas(units) contiguous ranges of whole 32-unit groups, one per
+// CTA of a fill cluster; the sum of squares (RMSNorm) is the sum over the
+// ranges, in range order, of each range's 256-thread partial (row_sumsq_part
+// over the range, shuffle tree, warp partials in order).  The GEMV's fused
+// fill and the fp32 materialisation run the same ranges in one CTA, so all
+// three produce the same bits.
+// ---------------------------------------------------------------------------
+constexpr int kFillThreads = 256;
+constexpr int kFillMaxCtas = 8;  // a portable cluster
+
+__host__ __device__ inline int fill_ctas(int nunits) {
+    const int c = (nunits + kFillThreads - 1) / kFillThreads;
+    return c < 1 ? 1 : (c > kFillMaxCtas ? kFillMaxCtas : c);
+}
+// Units [u0, u1) of range c (multiples of 32 units = 128 columns).
+__host__ __device__ inline void fill_range(int nunits, int C, int c, int &u0, int &u1) {
+    const int n32 = (nunits + 31) / 32;
+    u0 = (int)((long)n32 * c / C) * 32;
+    const int e = (int)((long)n32 * (c + 1) / C) * 32;
+    u1 = e < nunits ? e : nunits;
+}
+
+// Sum of squares of columns [k0, k1) of an fp32 row by `nthreads` threads in
+// the fixed order of row_sumsq_part, reduced over the block (shuffle tree,
+// then the warp partials in order through red[]); every thread gets the total.
+__device__ __forceinline__ float block_range_sumsq(const float *row, int k0, int k1, int tid, int nthreads,
+                                                   float *red, int bar_id) {
+    float acc = k1 > k0 ? row_sumsq_part(row + k0, k1 - k0, tid, nthreads) : 0.0f;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+    if ((tid & 31) == 0) red[tid >> 5] = acc;
+    named_bar_sync(bar_id, nthreads);
+    float tot = 0.0f;
+    for (int w = 0; w < nthreads / 32; ++w) tot += red[w];
+    named_bar_sync(bar_id, nthreads);
+    return tot;
+}
+
+// Largest |value| a source produces over columns [k0, k1) (before the RMSNorm
+// scale, which is positive and common to the row: max |x[k] * gamma[k]|).
+__device__ __forceinline__ float range_absmax(const XSrc &s, int tok, int k0, int k1, int tid, int nthreads) {
+    float m = 0.0f;
+    if (s.op == kXRmsnorm) {
+        const float *row = static_cast<const float *>(s.x) + (size_t)tok * s.ldx;
+        for (int k = k0 + tid; k < k1; k += nthreads) m = fmaxf(m, fabsf(__fmul_rn(row[k], s.aux[k])));
+    } else {
+        for (int k = k0 + tid; k < k1; k += nthreads) m = fmaxf(m, fabsf(xsrc_value(s, tok, k, 1.0f)));
+    }
+    return m;
+}
+
+// Power-of-two scaling of an activation row before its fp16 split: e with
+// max|x| * 2^e in [2^14, 2^15), so fp16 (largest finite 65504) holds every
+// scaled value, including after the 4-bit / 2-bit k-step pre-scales, and the
+// hi + lo pair keeps ~22 bits of each value relative to the row's maximum.
+// A zero, NaN or infinite maximum leaves the row unscaled; e lies in
+// [-113, 126] (a finite maximum gives e >= -113), so 2^e, 2^-e and 2^(e - 6)
+// are normal fp32 numbers.  Powers of two are exact: the
+// GEMV multiplies its sums by 2^-e in the epilogue.
+__host__ __device__ inline int row_scale_exp(float m) {
+    if (!(m > 0.0f) || !(m <= 3.402823466e38f)) return 0;
+    union {
+        float f;
+        unsigned u;
+    } v;
+    v.f = m;
+    const int ex = (int)((v.u >> 23) & 0xffu) - 127;  // floor(log2 m); -127 for subnormals
+    const int e = 14 - ex;
+    return e < -113 ? -113 : (e > 126 ? 126 : e);
+}
+__host__ __device__ inline float pow2_of(int e) {
+    union {
+        float f;
+        unsigned u;
+    } v;
+    v.u = (unsigned)(127 + e) << 23;
+    return v.f;
+}
+
 }  // namespace chpe

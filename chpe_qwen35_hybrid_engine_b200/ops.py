@@ -70,6 +70,23 @@ class Tensor:
             self.ctx._check(self.ctx.lib.chpe_tensor_free(self.ctx.ptr, self.handle))
             self.handle = None
 
+    def unpack(self, n_groups: int | None = None, scales_f32: bool = False, zeros: bool = False):
+        """(codes [rows, ceil(cols*bits/8)] uint8, scales, zeros) read back from the
+        device layout (chpe_tensor_unpack); scales fp16 [rows, n_groups] (fp32
+        [rows] with scales_f32), zeros fp16 when requested, else None."""
+        codes = np.zeros((self.rows, (self.cols * self.bits + 7) // 8), np.uint8)
+        sc = zz = None
+        if scales_f32:
+            sc = np.zeros(self.rows, np.float32)
+        elif n_groups:
+            sc = np.zeros((self.rows, n_groups), np.float16)
+        if zeros:
+            zz = np.zeros((self.rows, n_groups), np.float16)
+        self.ctx._check(self.ctx.lib.chpe_tensor_unpack(self.ctx.ptr, self.handle, _np_ptr(codes),
+                                                        None if sc is None else _np_ptr(sc),
+                                                        None if zz is None else _np_ptr(zz)))
+        return codes, sc, zz
+
     def __repr__(self):
         return f"Tensor(rows={self.rows}, cols={self.cols}, bits={self.bits}, device_bytes={self.device_bytes})"
 
@@ -119,6 +136,18 @@ class Comm:
         """hidden[:n] += sum over ranks of part[:n] (device pointers)."""
         self.ctx._check(self.ctx.lib.chpe_allreduce_residual_dev(self.handle, _dev_ptr(part), _dev_ptr(hidden), n,
                                                                   _stream_ptr(stream)))
+
+    def failed(self) -> bool:
+        """True after a bounded wait of this object expired (chpe_comm_failed)."""
+        return bool(self.ctx.lib.chpe_comm_failed(self.handle))
+
+    def reset(self, group=None):
+        """Resynchronise after a failure: host barrier, chpe_comm_reset on every
+        rank, host barrier (no rank exchanges before all ranks have reset)."""
+        import torch.distributed as dist
+        dist.barrier(group=group)
+        self.ctx._check(self.ctx.lib.chpe_comm_reset(self.handle))
+        dist.barrier(group=group)
 
     def close(self):
         if self.handle:

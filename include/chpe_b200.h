@@ -142,6 +142,17 @@ int chpe_tensor_free(chpe_ctx *ctx, chpe_tensor *t);
 /* rows / cols / bits of a tensor and its device bytes (codes + metadata). */
 int chpe_tensor_info(const chpe_tensor *t, size_t *rows, size_t *cols, int *bits, size_t *device_bytes);
 
+/* Read a resident tensor back out of the device layout, bit for bit as it
+ * was uploaded: codes row-major [rows][ceil(cols*bits/8)] bytes packed least
+ * significant bits first (signed int8, offset-8 nibbles, 2-bit codebook codes
+ * or unsigned codes, as given to the upload), scales as fp16 [rows][groups]
+ * (fp32 [rows] for per-row affine cells; nothing for the per-tensor W8A8
+ * scale), zeros as fp16 [rows][groups] (scale + zero tensors only; else NULL).
+ * Host or device destination pointers; synchronous.  No counterpart in the
+ * reference (its weights never leave their host layout); it exists to show
+ * that the device repack is lossless. */
+int chpe_tensor_unpack(chpe_ctx *ctx, const chpe_tensor *t, void *codes, void *scales, void *zeros);
+
 /* Register a host weight region as the source of later `_parallel` calls.
  * Replaces the mmap'd archive handed to the engine (src/weight_archive.zig:173-211):
  * the shim registers each int8 weight tensor once at init. */
@@ -258,6 +269,16 @@ size_t chpe_comm_handle_bytes(void);
 int chpe_comm_handle(const chpe_comm *comm, void *out);
 int chpe_comm_open_peers(chpe_comm *comm, const void *handles);
 int chpe_allreduce_residual_dev(chpe_comm *comm, const float *part, float *hidden, size_t n, void *stream);
+/* A comm object whose bounded wait expired is failed: the ranks' epochs may
+ * be out of step, so every later chpe_allreduce_residual_dev on it returns
+ * CHPE_ETIMEOUT at once (and a launch already queued, e.g. inside a CUDA
+ * graph, skips the exchange and records the error for chpe_sync) until
+ * chpe_comm_reset.  chpe_comm_failed returns 1 when failed, 0 when not.
+ * chpe_comm_reset waits for the device, then clears this rank's epochs, flags
+ * and failed mark; call it on EVERY rank between two host barriers (no rank
+ * may issue an all-reduce before all ranks have reset). */
+int chpe_comm_failed(const chpe_comm *comm);
+int chpe_comm_reset(chpe_comm *comm);
 int chpe_comm_destroy(chpe_comm *comm);
 
 /* Dynamic per-row int8 activation quantization (device): for each of M rows of
@@ -293,18 +314,22 @@ int chpe_argmax_dev(chpe_ctx *ctx, const float *logits, int M, int n, int *idx, 
 
 /* Allocation-free variant of chpe_gemv_dev (plain GEMV, M = 1..8).  No
  * counterpart in the reference.  For callers that cannot allocate device
- * memory when they run a GEMV: code recording a CUDA graph, where cudaMalloc
- * may not be issued, and host engines that carve all device memory out of one
- * region reserved up front.  chpe_gemv_dev may grow the context's scratch with
- * cudaMalloc; this function never calls cudaMalloc, cudaFree or any allocating
- * routine.  Its scratch is one static device array of 16 MiB that every GPU
- * loading the library holds until exit; a shape whose scratch needs more
- * returns CHPE_EINVAL with the required size.  All calls share that array and
- * it keeps the last call's contents (its arrival and work counters are
- * cleared with a memset at the start of every call), so calls that overlap on
- * the GPU race.
- * The first call on each device looks up the array's device address; make
- * that first call before any stream capture. */
+ * memory when they run a GEMV: host engines that reserve all the device
+ * memory they will ever use once at start-up (one arena, sized next to the
+ * other jobs on a shared GPU) and treat any later cudaMalloc as a failure, and
+ * latency-critical decode loops that cannot afford cudaMalloc's implicit
+ * device synchronisation.  chpe_gemv_dev may grow the context's scratch with
+ * cudaMalloc; this function never calls cudaMalloc, cudaFree or any
+ * allocating routine.  Its scratch is one static device array of 16 MiB that
+ * every GPU loading the library holds until the process exits; a shape whose
+ * scratch needs more returns CHPE_EINVAL with the required size.  All calls
+ * share that array and it keeps the last call's contents (its arrival and
+ * work counters are cleared with a memset at the start of every call), so
+ * calls that overlap on the GPU race.
+ * The first call on each device (and the first after the device's context was
+ * destroyed and re-created, e.g. by cudaDeviceReset) looks up the array's
+ * device address with that device current; make that first call before any
+ * stream capture. */
 int chpe_gemv_noalloc_dev(chpe_ctx *ctx, const chpe_tensor *w, const void *x, int x_dtype, const float *x_scales,
                           int M, float *y, void *stream);
 

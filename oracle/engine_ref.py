@@ -13,6 +13,8 @@ specification (fp64 accumulation) on fp32 activations.
 """
 from __future__ import annotations
 
+import os
+
 import numpy as np
 
 from oracle import oracle as O
@@ -24,8 +26,10 @@ def _silu(x):
 
 
 class EngineRef:
-    def __init__(self, host: dict, geom, scheme: str):
+    def __init__(self, host: dict, geom, scheme: str, num_workers: int | None = None):
         self.h, self.g, self.scheme = host, geom, scheme
+        self.nw = num_workers or os.cpu_count() or 8
+        self._unpacked = {}  # q4g64: codes one per byte, made once per tensor
 
     # -- one projection: y[M, rows] = x[M, cols] . W^T ------------------------------
     def gemv(self, name, x):
@@ -35,22 +39,26 @@ class EngineRef:
             out = []
             for row in x:
                 q, s = O.quantize_act_i8(row)
-                out.append(O.gemv_parallel(codes, float(scales[0]), q, float(s)))
+                out.append(O.gemv_parallel(codes, float(scales[0]), q, float(s), num_workers=self.nw))
             return np.stack(out)
         if self.scheme == "q8g32":
-            return O.gemv_grouped(codes.view(np.int8), scales, None, 32, x, num_workers=8)
+            return O.gemv_grouped(codes.view(np.int8), scales, None, 32, x, num_workers=self.nw)
         # q4g64: two codes per byte, low nibble first
-        c = np.empty((codes.shape[0], codes.shape[1] * 2), np.uint8)
-        c[:, 0::2] = codes & 0x0F
-        c[:, 1::2] = codes >> 4
-        return O.gemv_grouped(c, scales, zeros, 64, x, num_workers=8)
+        c = self._unpacked.get(name)
+        if c is None:
+            c = np.empty((codes.shape[0], codes.shape[1] * 2), np.uint8)
+            c[:, 0::2] = codes & 0x0F
+            c[:, 1::2] = codes >> 4
+            self._unpacked[name] = c
+        return O.gemv_grouped(c, scales, zeros, 64, x, num_workers=self.nw)
 
     def gateup(self, l, x):
         """Batch 1: fused gate/up SwiGLU (src/engine.zig:682)."""
         if self.scheme == "w8a8":
             (wg, sg, _), (wu, su, _) = self.h[f"L{l}.gate"], self.h[f"L{l}.up"]
             q, s = O.quantize_act_i8(x[0])
-            return O.gemv_gateup_swiglu_parallel(wg, float(sg[0]), wu, float(su[0]), q, float(s))[None]
+            return O.gemv_gateup_swiglu_parallel(wg, float(sg[0]), wu, float(su[0]), q, float(s),
+                                                 num_workers=self.nw)[None]
         g = self.gemv(f"L{l}.gate", x)
         u = self.gemv(f"L{l}.up", x)
         return (_silu(g) * u).astype(np.float32)

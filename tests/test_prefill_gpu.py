@@ -1,8 +1,10 @@
 """Prefill dequant-GEMM (tcgen05, M >= 64) against the oracle and torch fp64.
 
-The weights are dequantized to fp16 (one rounding of q*s or (c-z)*s) and bf16
-activations are exact in fp16, so the result is within ~2^-12 relative per
-weight of the exact product: rel-L2 well under the path's 1e-3 (TOL).  Small
+The weights are dequantized to fp16 (one rounding of q*s or (c-z)*s); each
+activation row is scaled by a power of two into fp16's range, where bf16 and
+fp16 values are exact and fp32 values take one rounding, so the result is
+within ~2^-12 relative per term of the exact product: rel-L2 well under the
+path's 1e-3 (TOL).  fp32 inputs are compared with the fp32 oracle itself.  Small
 shapes are checked against the oracle's grouped GEMV (fp64 accumulation); the
 full config-3 shapes (M = 2048) against a torch fp64 dequant-matmul.
 """
@@ -63,11 +65,10 @@ def test_prefill_small_against_oracle(ctx, fmt, M, N, K, xdt):
     want = O.gemv_grouped(codes, s, z, group, xo, num_workers=8)
     got = y.cpu().numpy()
     assert np.isfinite(got).all()
-    # fp32 activations are rounded to fp16 first: compare against the same rounding
-    if xdt == "f32":
-        want = O.gemv_grouped(codes, s, z, group, xd.half().float().cpu().numpy(), num_workers=8)
+    # fp32 activations are compared with the fp32 oracle: the kernel scales each
+    # row by a power of two and rounds it to fp16 once (~2^-12 relative per value)
     assert rel_l2(got, want) < TOL, rel_l2(got, want)
-    assert rel_l2(got, want) < 3e-4
+    assert rel_l2(got, want) < (5e-4 if xdt == "f32" else 3e-4)
     # accumulate into an existing y, and determinism
     y0 = torch.from_numpy(rng.standard_normal((M, N)).astype(np.float32)).cuda()
     y1 = y0.clone()

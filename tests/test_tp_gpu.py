@@ -133,14 +133,33 @@ def _comm_rank(rank, world, port, q, skip_rank):
         want = h0 + s
         part = parts[rank].cuda()
         hidden = h0.cuda()
-        for it in range(3):  # three epochs in a row (both slot parities)
-            if it > 0:
+        refused = recovered = None
+        if skip_rank is None:
+            for it in range(3):  # three epochs in a row (both slot parities)
                 hidden.copy_(h0.cuda())
-            if rank != skip_rank:
                 comm.allreduce_residual(part, hidden, n)
+                torch.cuda.synchronize()
+            rc = ctx.lib.chpe_sync(ctx.ptr)
+        else:
+            if rank != skip_rank:
+                comm.allreduce_residual(part, hidden, n)  # the peer never joins: the wait expires
+                torch.cuda.synchronize()
+            rc = ctx.lib.chpe_sync(ctx.ptr)
+            if rank != skip_rank:
+                # the failed object refuses the next exchange instead of pairing slots of different epochs
+                from chpe_qwen35_hybrid_engine_b200._lib import ChpeError
+                try:
+                    comm.allreduce_residual(part, hidden, n)
+                    refused = False
+                except ChpeError as e:
+                    refused = comm.failed() and e.code == -5
+            # resynchronise every rank, then one exchange must be exact again
+            comm.reset()
+            hidden.copy_(h0.cuda())
+            comm.allreduce_residual(part, hidden, n)
             torch.cuda.synchronize()
-        rc = ctx.lib.chpe_sync(ctx.ptr)
-        out = (rank, rc, torch.equal(hidden.cpu(), want))
+            recovered = ctx.lib.chpe_sync(ctx.ptr) == 0 and not comm.failed()
+        out = (rank, rc, torch.equal(hidden.cpu(), want), refused, recovered)
         dist.barrier()  # peers keep their receive areas mapped until everyone is done
         comm.close()
         ctx.close()
@@ -153,9 +172,12 @@ def _comm_rank(rank, world, port, q, skip_rank):
 def test_p2p_allreduce_exact_and_timeout(ctx, skip_rank):
     """The one-shot NVLink all-reduce: every rank's hidden state equals
     h0 + (sum of the partials in rank order) bit for bit, over three epochs.
-    With skip_rank = 1 that rank never joins: rank 0's bounded wait runs out
-    (about 1 s per epoch), the kernel returns, and chpe_sync reports
-    CHPE_ETIMEOUT -- no GPU fault, the context stays usable."""
+    With skip_rank = 1 that rank never joins the first exchange: rank 0's
+    bounded wait runs out (about 1 s), the kernel returns, chpe_sync reports
+    CHPE_ETIMEOUT -- no GPU fault, the context stays usable -- and the comm
+    object is marked failed, so rank 0's next exchange is refused rather than
+    run with the ranks' epochs out of step.  After chpe_comm_reset on both
+    ranks (between host barriers) an exchange is exact again."""
     import torch
     import torch.multiprocessing as mp
     if torch.cuda.device_count() < 2:
@@ -169,14 +191,17 @@ def test_p2p_allreduce_exact_and_timeout(ctx, skip_rank):
     res = {}
     try:
         for _ in range(2):
-            rank, rc, equal = q.get(timeout=120)
-            res[rank] = (rc, equal)
+            rank, rc, equal, refused, recovered = q.get(timeout=120)
+            res[rank] = (rc, equal, refused, recovered)
     finally:
         for p in procs:
             p.join(timeout=60)
     assert all(p.exitcode == 0 for p in procs)
     if skip_rank is None:
-        assert res[0] == (0, True) and res[1] == (0, True)
+        assert res[0][:2] == (0, True) and res[1][:2] == (0, True)
     else:
         assert res[0][0] == -5  # CHPE_ETIMEOUT from rank 0's expired wait
+        assert res[0][2] is True  # the failed object refused the next exchange
+        assert res[0][3] and res[1][3]  # after the reset: exact on both ranks
+        assert res[0][1] and res[1][1]
 

@@ -1,13 +1,16 @@
 """The allocation-free GEMV entry point (chpe_gemv_noalloc_dev).
 
-Some callers cannot allocate device memory while they run a GEMV -- code
-recording a CUDA graph, or an engine that carved all its device memory out of
-one region up front.  This entry point keeps its scratch in a static device
-array instead of the context's cudaMalloc'd scratch.  These tests call it
-through the C ABI and compare it with chpe_gemv_dev on the same inputs, twice
-in a row (the static scratch keeps the previous call's contents, so the second
-call checks that nothing stale leaks into a result).  The file is named so
-pytest collects it last.
+Some callers cannot allocate device memory while they run a GEMV -- an engine
+that reserved all its device memory once at start-up and treats any later
+cudaMalloc as a failure, or a decode loop that cannot take cudaMalloc's
+implicit device synchronisation.  This entry point keeps its scratch in a
+static device array instead of the context's cudaMalloc'd scratch.  These
+tests call it through the C ABI on a fresh context (whose own scratch was
+never grown), check that the device's free memory does not move across two
+calls, and compare both calls bit for bit with chpe_gemv_dev on the same
+inputs: the two run the same kernel and launch plan, so every format gives
+identical bits, and the second call shows that nothing stale from the first
+leaks through the shared array.  The file is named so pytest collects it last.
 """
 import ctypes as C
 
@@ -30,11 +33,14 @@ def _noalloc(ctx, t, x, x_dtype, M, y, x_scales=None):
     return rc
 
 
-@pytest.mark.parametrize("fmt", ["q4_g64_bf16_m4", "q8_g32_f32_m1", "w8a8_m8"])
-def test_noalloc_matches_gemv_dev_twice(ctx, fmt):
+@pytest.mark.parametrize("fmt", ["q4_g64_bf16_m4", "q8_g32_f32_m1", "w8a8_m8", "q2_g64_f32_m8"])
+def test_noalloc_matches_gemv_dev_twice(fmt):
     import torch
     from chpe_qwen35_hybrid_engine_b200 import (SCHEME_I8_GROUP_F16, SCHEME_I8_TENSOR, SCHEME_U_GROUP_F16_ZERO,
-                                                X_BF16, X_F32, X_I8)
+                                                X_BF16, X_F32, X_I8, Context)
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    ctx = Context(0)  # fresh: its growable scratch has never been allocated
     rng = np.random.default_rng(42)
     if fmt == "q4_g64_bf16_m4":
         N, K, M = 3000, 4096, 4
@@ -42,6 +48,12 @@ def test_noalloc_matches_gemv_dev_twice(ctx, fmt):
         t = ctx.upload_matrix(4, SCHEME_U_GROUP_F16_ZERO, pack_codes(codes, 4), s, z, rows=N, cols=K, group=64)
         xs = [torch.randn(M, K, device="cuda").to(torch.bfloat16) for _ in range(2)]
         dt, scales = X_BF16, None
+    elif fmt == "q2_g64_f32_m8":
+        N, K, M = 2048, 4096, 8
+        codes, s, z = O.quantize_asym(rng.normal(0, 0.02, (N, K)).astype(np.float32), 2, 64)
+        t = ctx.upload_matrix(2, SCHEME_U_GROUP_F16_ZERO, pack_codes(codes, 2), s, z, rows=N, cols=K, group=64)
+        xs = [torch.randn(M, K, device="cuda") for _ in range(2)]
+        dt, scales = X_F32, None
     elif fmt == "q8_g32_f32_m1":
         N, K, M = 12288, 4096, 1
         codes = rng.integers(-127, 128, (N, K), dtype=np.int8)
@@ -55,15 +67,22 @@ def test_noalloc_matches_gemv_dev_twice(ctx, fmt):
         t = ctx.upload_matrix(8, SCHEME_I8_TENSOR, w, np.array([0.003], np.float32), rows=N, cols=K)
         xs = [torch.randint(-128, 128, (M, K), dtype=torch.int8, device="cuda") for _ in range(2)]
         dt, scales = X_I8, torch.rand(M, device="cuda") * 0.05 + 0.001
-    for x in xs:  # two calls in a row, different activations
-        ref = ctx.gemv(t, x, x_scales=scales)
-        y = torch.full((M, N), float("nan"), device="cuda")
+    ys = [torch.full((M, N), float("nan"), device="cuda") for _ in range(2)]
+    torch.cuda.synchronize()
+    free0 = torch.cuda.mem_get_info()[0]
+    for x, y in zip(xs, ys):  # two calls in a row, different activations
         assert _noalloc(ctx, t, x, dt, M, y, scales) == 0, ctx.lib.chpe_last_error_string(ctx.ptr)
+        torch.cuda.synchronize()
+    assert torch.cuda.mem_get_info()[0] == free0  # no device memory was allocated
+    for x, y in zip(xs, ys):
+        ref = ctx.gemv(t, x, x_scales=scales)
         torch.cuda.synchronize()
         assert torch.isfinite(y).all()
         assert rel_l2(y.cpu().numpy(), ref.cpu().numpy()) < TOL
+        assert torch.equal(y, ref)  # same kernel, same plan: identical bits
     ctx.sync()
     t.free()
+    ctx.close()
 
 
 def test_noalloc_rejects_shapes_beyond_its_scratch(ctx):
