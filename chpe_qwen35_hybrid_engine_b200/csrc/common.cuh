@@ -254,6 +254,13 @@ cudaError_t launch_pdl_cluster(void (*kern)(KArgs...), dim3 grid, dim3 block, un
     return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
 }
 
-__device__ __forceinline__ float silu_f(float g) { return g / (1.0f + expf(-g)); }
+// silu(g) = g / (1 + exp(-g)) (src/kernels/neon.zig:705-712), with exp taken
+// in double precision and rounded to float: that is the correctly rounded
+// float exp except in about one case in 10^9, so every implementation that
+// does the same (the oracle's, on the host) gets the same bits.  The W8A8
+// path re-quantizes every activation row to int8, where a last-bit
+// difference can flip a rounding and grow from there.
+__device__ __forceinline__ float exp_rn(float x) { return (float)exp((double)x); }
+__device__ __forceinline__ float silu_f(float g) { return __fdiv_rn(g, __fadd_rn(1.0f, exp_rn(-g))); }
 
 }  // namespace chpe

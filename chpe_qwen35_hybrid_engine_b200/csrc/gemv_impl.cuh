@@ -367,38 +367,19 @@ __device__ __forceinline__ void fused_fill_op(const GemvParams &p, uint8_t *xf_s
     const int tid = threadIdx.x;           // 0..255 (MMA warps)
     const int M = p.M, K = p.K;
     const XSrc &xs = p.xsrc;
-    // Row statistics over the whole row, in the fill kernel's order (the
-    // fill ranges one after the other): the RMSNorm scale and the row's
-    // power-of-two scale 2^e, so the fragments are the fill kernel's bits.
+    // Row statistics over the whole row in the fill kernel's order (the
+    // 256 MMA threads play the fill CTA's 512): the RMSNorm scale and the
+    // row's power-of-two scale 2^e, so the fragments are the fill kernel's bits.
     float inv[kMaxTokens], scl[kMaxTokens];
     const int nunits = (p.n_blocks * span) / 4;
-    const int C = fill_ctas(nunits);
 #pragma unroll
     for (int m = 0; m < kMaxTokens; ++m) {
         inv[m] = 1.0f;
         scl[m] = 1.0f;
         if (m >= M) continue;
-        float am = 0.0f;
-        if constexpr (OP == kXRmsnorm) {
-            const float *row = static_cast<const float *>(xs.x) + (size_t)m * xs.ldx;
-            float tot = 0.0f;
-            for (int c = 0; c < C; ++c) {
-                int u0, u1;
-                fill_range(nunits, C, c, u0, u1);
-                tot += block_range_sumsq(row, min(4 * u0, K), min(4 * u1, K), tid, kNW * 32, scratch, 1);
-            }
-            inv[m] = inv_rms_of(tot, K, xs.eps);
-        }
-        am = range_absmax(xs, m, 0, K, tid, kNW * 32);
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, off));
-        if ((tid & 31) == 0) scratch[tid >> 5] = am;
-        named_bar_sync(1, kNW * 32);
-        float mx = 0.0f;
-#pragma unroll
-        for (int w = 0; w < kNW; ++w) mx = fmaxf(mx, scratch[w]);
-        named_bar_sync(1, kNW * 32);
-        const int e = row_scale_exp(OP == kXRmsnorm ? mx * inv[m] : mx);
+        float amax;
+        block_row_stats(xs, m, K, nunits, tid, kNW * 32, scratch, 1, inv[m], amax);
+        const int e = row_scale_exp(amax);
         scl[m] = pow2_of(e);
         if (tid == 0) {
             xe_s[m] = pow2_of(-e);

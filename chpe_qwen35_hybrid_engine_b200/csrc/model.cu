@@ -9,6 +9,7 @@
 
 #include "../../include/chpe_b200.h"
 #include "common.cuh"
+#include "xsrc.cuh"
 
 namespace chpe {
 
@@ -27,29 +28,20 @@ __global__ void chpe_embed_i8_kernel(const int8_t *__restrict__ table, float sca
 }
 
 // src/kernels/neon.zig:673-702 rmsnorm: y = x * (1/sqrt(mean(x^2) + eps)) * gamma.
-// One block per row; the sum of squares is a fixed-order tree (deterministic,
-// not the reference's lane order, so the last bits may differ).
+// One block per row; the sum of squares in the reference's own lane order
+// (ref_order_inv_rms), so the result is the reference's bit for bit.
 __global__ void chpe_rmsnorm_kernel(const float *__restrict__ x, const float *__restrict__ gamma, int n, float eps,
-                               float *__restrict__ y) {
+                                    float *__restrict__ y) {
     pdl_begin();
-    __shared__ float red[32];
+    __shared__ float s_inv;
     const float *xr = x + (size_t)blockIdx.x * n;
     float *yr = y + (size_t)blockIdx.x * n;
-    float s = 0.0f;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) s = fmaf(xr[i], xr[i], s);
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
-    __syncthreads();
     if (threadIdx.x < 32) {
-        float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.0f;
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
-        if (threadIdx.x == 0) red[0] = v;
+        const float v = ref_order_inv_rms(xr, n, eps);
+        if (threadIdx.x == 0) s_inv = v;
     }
     __syncthreads();
-    const float mean = __fdiv_rn(red[0], (float)n);
-    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
+    const float inv = s_inv;
     for (int i = threadIdx.x; i < n; i += blockDim.x) yr[i] = __fmul_rn(__fmul_rn(xr[i], inv), gamma[i]);
 }
 

@@ -15,49 +15,38 @@ namespace chpe {
 // activations
 // ---------------------------------------------------------------------------
 
-// Statistics of row tok over the fill ranges (xsrc.cuh), computed by one CTA
-// of 256 threads: 1 / sqrt(mean(x^2) + eps) for RMSNorm (1 otherwise) in the
-// fill cluster's summation order.
-__device__ float row_inv_rms_ranges(const XSrc &s, int tok, int K, int nunits, float *red) {
-    if (s.op != kXRmsnorm) return 1.0f;
-    const float *row = static_cast<const float *>(s.x) + (size_t)tok * s.ldx;
-    const int C = fill_ctas(nunits);
-    float tot = 0.0f;
-    for (int c = 0; c < C; ++c) {
-        int u0, u1;
-        fill_range(nunits, C, c, u0, u1);
-        tot += block_range_sumsq(row, min(4 * u0, K), min(4 * u1, K), threadIdx.x, kFillThreads, red, 0);
-    }
-    return inv_rms_of(tot, K, s.eps);
-}
-
 // Activation fragments of the fp16 GEMV path.  One cluster of C CTAs
 // (fill_ctas) per activation row tok = blockIdx.y; CTA c owns fragment units
-// [u0, u1) (fill_range) and loops over them 256 at a time.  Unit u = 4 * s + t
+// [u0, u1) (fill_range), kFillThreads of them at a time.  Unit u = 4 * s + t
 // (k-step s, lane column t) holds columns 16s + 2t + {0, 1, 8, 9}; fragments
 // are stored as 16-byte units so a consumer fetches two k-steps (or, for fp32
 // input, the hi and lo parts of one k-step) with one load:
 //   split (fp32 x):  unit (s, m, t) = {hi(16s+2t..), hi(16s+2t+8..), lo(..), lo(..)}
 //   fp16/bf16 x:     unit (s/2, m, t) = {step 2u: ..., step 2u+1: ...}
-// Row statistics first: each CTA reduces its range (sum of squares for
-// RMSNorm, largest |value|), the CTAs exchange them through distributed shared
-// memory and every CTA combines them in range order, so the whole cluster
-// agrees on the RMSNorm scale and on the row's power-of-two scale 2^e
-// (row_scale_exp), which keeps every scaled value inside fp16's range;
-// xe[tok] = 2^-e undoes it in the GEMV epilogue.
+// Pass 1 reads each source value once (kept in registers, with its RMSNorm
+// gamma, for the first kFillCache units of a thread) and reduces the CTA's
+// range: the sum of squares (RMSNorm, in the canonical order of xsrc.cuh) and
+// the largest |value|.  Each CTA writes them into every peer's shared memory
+// (distributed shared memory, one cluster barrier) and all combine them in
+// range order, so the whole cluster agrees on the RMSNorm
+// scale and on the row's power-of-two scale 2^e (row_scale_exp), which keeps
+// every scaled value inside fp16's range; xe[tok] = 2^-e undoes it in the
+// GEMV epilogue.  Pass 2 scales, splits and stores.
 // `bits` selects the per-k-step power-of-two pre-scale that matches where the
 // GEMV kernel reads the codes (unpack_f16): 4-bit odd k-steps of a chunk /16,
 // 2-bit k-step j of a chunk / 4^(j%4), 8-bit none.  The sum of each E-column
 // block (what the zero-point term multiplies) is taken over the values the
 // MMA sees, with the k-step pre-scale undone, from the E/4 consecutive threads
 // that hold the block.
+constexpr int kFillCache = 4;  // units per thread held in registers between the passes
+
 __global__ void __launch_bounds__(kFillThreads) chpe_xfill_f16_kernel(const XSrc s, int M, int K, int Kp, int E,
                                                                      int split, int bits, uint2 *__restrict__ xf,
                                                                      float *__restrict__ xs, float *__restrict__ xe) {
     namespace cg = cooperative_groups;
     cg::cluster_group cluster = cg::this_cluster();
-    __shared__ float red[32];
-    __shared__ float2 stat;  // (sum of squares, largest |value|) of this CTA's range
+    __shared__ float red[2 * kFillWarps];
+    __shared__ float2 stats[kFillMaxCtas];  // (sum of squares, largest |value|) of every CTA of the row's cluster
     pdl_begin();
     const int tok = blockIdx.y;
     const int nunits = Kp / 4;
@@ -65,47 +54,117 @@ __global__ void __launch_bounds__(kFillThreads) chpe_xfill_f16_kernel(const XSrc
     const int c = (int)cluster.block_rank();
     int u0, u1;
     fill_range(nunits, C, c, u0, u1);
-    const int k0 = min(4 * u0, K), k1 = min(4 * u1, K);
-    const int tid = threadIdx.x;
-    float ss = 0.0f;
-    if (s.op == kXRmsnorm)
-        ss = block_range_sumsq(static_cast<const float *>(s.x) + (size_t)tok * s.ldx, k0, k1, tid, kFillThreads, red, 0);
-    float am = range_absmax(s, tok, k0, k1, tid, kFillThreads);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const bool rms = s.op == kXRmsnorm;
+    const float *xrow = static_cast<const float *>(s.x) + (size_t)tok * s.ldx;
+    // source value of column k: raw x for RMSNorm (normalised in pass 2), else the op's value
+    auto src = [&](int k) -> float {
+        if (k >= K) return 0.0f;
+        return rms ? xrow[k] : xsrc_value(s, tok, k, 1.0f);
+    };
+    float cv[kFillCache][4], cg4[kFillCache][4];  // cached values (and RMSNorm gammas)
+    float ss = 0.0f, am = 0.0f;
 #pragma unroll
-    for (int off = 16; off > 0; off >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, off));
-    if ((tid & 31) == 0) red[tid >> 5] = am;
+    for (int i = 0; i < kFillCache; ++i) {
+        const int u = u0 + tid + i * kFillThreads;
+        if (u < u1) {
+            int kk[4];
+            unit_cols(u, kk);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const float v = src(kk[q]);
+                cv[i][q] = v;
+                if (rms) {
+                    const float g = kk[q] < K ? s.aux[kk[q]] : 0.0f;
+                    cg4[i][q] = g;
+                    ss = fmaf(v, v, ss);
+                    am = fmaxf(am, fabsf(__fmul_rn(v, g)));
+                } else {
+                    am = fmaxf(am, fabsf(v));
+                }
+            }
+        }
+    }
+    for (int u = u0 + tid + kFillCache * kFillThreads; u < u1; u += kFillThreads) {  // units past the cache
+        int kk[4];
+        unit_cols(u, kk);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const float v = src(kk[q]);
+            if (rms) {
+                ss = fmaf(v, v, ss);
+                am = fmaxf(am, fabsf(__fmul_rn(v, kk[q] < K ? s.aux[kk[q]] : 0.0f)));
+            } else {
+                am = fmaxf(am, fabsf(v));
+            }
+        }
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+        ss += __shfl_xor_sync(0xffffffffu, ss, off);
+        am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, off));
+    }
+    if (lane == 0) {
+        red[warp] = ss;
+        red[kFillWarps + warp] = am;
+    }
     __syncthreads();
-    if (tid == 0) {
-        float m = 0.0f;
-        for (int w = 0; w < kFillThreads / 32; ++w) m = fmaxf(m, red[w]);
-        stat = make_float2(ss, m);
+    // thread r < C writes this CTA's statistics into slot c of CTA r (distributed
+    // shared memory); one cluster barrier later every CTA holds all of them
+    if (tid < C) {
+        float t = 0.0f, m = 0.0f;
+#pragma unroll
+        for (int w = 0; w < kFillWarps; ++w) {
+            t += red[w];
+            m = fmaxf(m, red[kFillWarps + w]);
+        }
+        *cluster.map_shared_rank(&stats[c], tid) = make_float2(t, m);
     }
     cluster.sync();
     float tot = 0.0f, amax = 0.0f;
     for (int r = 0; r < C; ++r) {
-        const float2 v = *cluster.map_shared_rank(&stat, r);
+        const float2 v = stats[r];
         tot += v.x;
         amax = fmaxf(amax, v.y);
     }
-    cluster.sync();  // every peer has read this CTA's statistics
-    const float inv = s.op == kXRmsnorm ? inv_rms_of(tot, K, s.eps) : 1.0f;
-    const int e = row_scale_exp(s.op == kXRmsnorm ? amax * inv : amax);
+    const float inv = rms ? inv_rms_of(tot, K, s.eps) : 1.0f;
+    const int e = row_scale_exp(rms ? amax * inv : amax);
     if (c == 0 && tid == 0) xe[tok] = pow2_of(-e);
     const int steps = (256 / bits) / 16;  // k-steps per chunk
-    for (int ub = u0; ub < u1; ub += kFillThreads) {
-        const int u = ub + tid;
+    for (int i = 0; u0 + i * kFillThreads < u1; ++i) {
+        const int u = u0 + tid + i * kFillThreads;
         float part = 0.0f;
         if (u < u1) {
             const int st = u >> 2, t = u & 3;
             const int j = st % steps;
             const int sh = bits == 4 ? 4 * (j & 1) : bits == 2 ? 2 * (j & 3) : 0;
             const float down = pow2_of(e - sh), up = pow2_of(sh);
-            const int kb = 16 * st + 2 * t;
-            const int kk[4] = {kb, kb + 1, kb + 8, kb + 9};
+            int kk[4];
+            unit_cols(u, kk);
+            float v4[4], g4[4];
+            if (i < kFillCache) {
+#pragma unroll
+                for (int ci = 0; ci < kFillCache; ++ci)
+                    if (ci == i) {
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) {
+                            v4[q] = cv[ci][q];
+                            g4[q] = cg4[ci][q];
+                        }
+                    }
+            } else {
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    v4[q] = src(kk[q]);
+                    g4[q] = rms && kk[q] < K ? s.aux[kk[q]] : 0.0f;
+                }
+            }
             __half h[4], l[4];
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
-                const float v = (kk[q] < K ? xsrc_value(s, tok, kk[q], inv) : 0.0f) * down;
+                float v = v4[q];
+                if (rms) v = __fmul_rn(__fmul_rn(v, inv), g4[q]);
+                v *= down;
                 h[q] = __float2half_rn(v);
                 l[q] = split ? __float2half_rn(v - __half2float(h[q])) : __float2half_rn(0.0f);
                 part += (__half2float(h[q]) + __half2float(l[q])) * up;
@@ -122,7 +181,7 @@ __global__ void __launch_bounds__(kFillThreads) chpe_xfill_f16_kernel(const XSrc
         }
         // E/4 consecutive threads (8, 16 or 32, aligned) hold one E-column
         // block; ranges are whole 32-unit groups, so a warp is all in or all out
-        if (ub + (tid & ~31) < u1) {
+        if (u0 + i * kFillThreads + 32 * warp < u1) {
             for (int off = E / 8; off > 0; off >>= 1) part += __shfl_xor_sync(0xffffffffu, part, off);
             if (u < u1 && (u % (E / 4)) == 0) xs[(size_t)(u / (E / 4)) * 8 + tok] = part;
         }
@@ -146,22 +205,30 @@ cudaError_t launch_xprep_f16(const void *x, int x_dtype, int M, int K, int Kp, i
     return launch_xfill_f16(s, M, K, Kp, e_cols, xsplit, bits, xf, xs, xe, st);
 }
 
-// The source op's values as fp32 rows [M][K] (for the int8 path, which
-// quantizes them per row, and for the outlier columns' fp32 activations);
-// RMSNorm statistics in the fill's order.
-__global__ void __launch_bounds__(kFillThreads) chpe_xmaterialize_kernel(const XSrc s, int K, int Kp,
-                                                                        float *__restrict__ out) {
-    __shared__ float red[32];
+// The source op's values as fp32 rows [M][K], for the int8 (W8A8) path, which
+// quantizes them per row exactly as the reference does, and for the outlier
+// columns' fp32 activations.  RMSNorm statistics in the reference's own order
+// (ref_order_inv_rms), so the int8 codes match the reference's bit for bit.
+__global__ void __launch_bounds__(256) chpe_xmaterialize_kernel(const XSrc s, int K, float *__restrict__ out) {
+    __shared__ float s_inv;
     pdl_begin();
     const int tok = blockIdx.y;
-    const float inv = row_inv_rms_ranges(s, tok, K, Kp / 4, red);
+    if (threadIdx.x < 32) {
+        const float v = s.op == kXRmsnorm ? ref_order_inv_rms(static_cast<const float *>(s.x) + (size_t)tok * s.ldx,
+                                                               K, s.eps)
+                                          : 1.0f;
+        if (threadIdx.x == 0) s_inv = v;
+    }
+    __syncthreads();
+    const float inv = s_inv;
     for (int k = blockIdx.x * blockDim.x + threadIdx.x; k < K; k += gridDim.x * blockDim.x)
         out[(size_t)tok * K + k] = xsrc_value(s, tok, k, inv);
 }
 
 cudaError_t launch_xmaterialize(const XSrc &s, int M, int K, int Kp, float *out, cudaStream_t st) {
-    const int gx = std::min(64, (K + 255) / 256);
-    return launch_pdl(chpe_xmaterialize_kernel, dim3(gx, M), dim3(kFillThreads), 0, st, s, K, Kp, out);
+    (void)Kp;
+    const int gx = std::min(32, (K + 255) / 256);
+    return launch_pdl(chpe_xmaterialize_kernel, dim3(gx, M), dim3(256), 0, st, s, K, out);
 }
 
 __device__ __forceinline__ uint32_t pack4_i8(const int8_t *p, int k, int K) {

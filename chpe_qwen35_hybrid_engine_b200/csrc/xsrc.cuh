@@ -78,16 +78,20 @@ __device__ __forceinline__ float inv_rms_of(float total, int K, float eps) {
 }
 
 // ---------------------------------------------------------------------------
-// Row statistics of a fragment fill.  A row of Kp / 4 fragment units is cut
-// into C = fill_ctas(units) contiguous ranges of whole 32-unit groups, one per
-// CTA of a fill cluster; the sum of squares (RMSNorm) is the sum over the
-// ranges, in range order, of each range's 256-thread partial (row_sumsq_part
-// over the range, shuffle tree, warp partials in order).  The GEMV's fused
-// fill and the fp32 materialisation run the same ranges in one CTA, so all
-// three produce the same bits.
+// Row statistics of a fragment fill.  A row of Kp / 4 fragment units (unit u
+// = columns 16(u/4) + 2(u%4) + {0, 1, 8, 9}) is cut into C = fill_ctas(units)
+// contiguous ranges of whole 32-unit groups, one per CTA of a fill cluster of
+// kFillThreads threads.  The RMSNorm sum of squares is defined in that
+// CTA's order: thread t sums (fmaf) the squares of its units u0 + t,
+// u0 + t + kFillThreads, ... element by element, a shuffle tree sums each
+// warp, the warp partials are added in warp order, and the ranges' partials
+// in range order.  block_row_stats computes the same bits in one block of 256
+// or 512 threads (a 256-thread block plays two threads of the 512), so the
+// fill kernel and the GEMV's fused fill agree.
 // ---------------------------------------------------------------------------
-constexpr int kFillThreads = 256;
+constexpr int kFillThreads = 512;
 constexpr int kFillMaxCtas = 8;  // a portable cluster
+constexpr int kFillWarps = kFillThreads / 32;
 
 __host__ __device__ inline int fill_ctas(int nunits) {
     const int c = (nunits + kFillThreads - 1) / kFillThreads;
@@ -100,21 +104,37 @@ __host__ __device__ inline void fill_range(int nunits, int C, int c, int &u0, in
     const int e = (int)((long)n32 * (c + 1) / C) * 32;
     u1 = e < nunits ? e : nunits;
 }
+// The four columns of fragment unit u.
+__host__ __device__ inline void unit_cols(int u, int kk[4]) {
+    const int kb = 16 * (u >> 2) + 2 * (u & 3);
+    kk[0] = kb;
+    kk[1] = kb + 1;
+    kk[2] = kb + 8;
+    kk[3] = kb + 9;
+}
 
-// Sum of squares of columns [k0, k1) of an fp32 row by `nthreads` threads in
-// the fixed order of row_sumsq_part, reduced over the block (shuffle tree,
-// then the warp partials in order through red[]); every thread gets the total.
-__device__ __forceinline__ float block_range_sumsq(const float *row, int k0, int k1, int tid, int nthreads,
-                                                   float *red, int bar_id) {
-    float acc = k1 > k0 ? row_sumsq_part(row + k0, k1 - k0, tid, nthreads) : 0.0f;
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
-    if ((tid & 31) == 0) red[tid >> 5] = acc;
-    named_bar_sync(bar_id, nthreads);
-    float tot = 0.0f;
-    for (int w = 0; w < nthreads / 32; ++w) tot += red[w];
-    named_bar_sync(bar_id, nthreads);
-    return tot;
+// 1 / sqrt(mean(x^2) + eps) of an fp32 row in the reference's own order
+// (src/kernels/neon.zig:673-702): four lanes, lane j summing x[4i + j]^2
+// (multiply, then add) over i in order, combined ((l0 + l1) + l2) + l3, then
+// the tail.  Lanes 0..3 of the calling warp each run one lane's chain (a
+// serial chain of K / 4 adds: bit-exact with the reference, at the price of
+// latency); every lane of the warp gets the result.
+__device__ __forceinline__ float ref_order_inv_rms(const float *row, int K, float eps) {
+    const int lane = threadIdx.x & 31;
+    float l = 0.0f;
+    const int n4 = K / 4;
+    if (lane < 4) {
+#pragma unroll 8
+        for (int i = 0; i < n4; ++i) {
+            const float v = row[4 * i + lane];
+            l = __fadd_rn(l, __fmul_rn(v, v));
+        }
+    }
+    const float l0 = __shfl_sync(0xffffffffu, l, 0), l1 = __shfl_sync(0xffffffffu, l, 1),
+                l2 = __shfl_sync(0xffffffffu, l, 2), l3 = __shfl_sync(0xffffffffu, l, 3);
+    float ss = __fadd_rn(__fadd_rn(__fadd_rn(l0, l1), l2), l3);
+    for (int k = 4 * n4; k < K; ++k) ss = __fadd_rn(ss, __fmul_rn(row[k], row[k]));
+    return inv_rms_of(ss, K, eps);
 }
 
 // Largest |value| a source produces over columns [k0, k1) (before the RMSNorm
@@ -128,6 +148,61 @@ __device__ __forceinline__ float range_absmax(const XSrc &s, int tok, int k0, in
         for (int k = k0 + tid; k < k1; k += nthreads) m = fmaxf(m, fabsf(xsrc_value(s, tok, k, 1.0f)));
     }
     return m;
+}
+
+// Full-row statistics in one block of nthreads (256 or 512): the RMSNorm
+// scale in the fill's summation order (1 for other sources) and the row's
+// largest |value| (after the RMSNorm scale).  Every range's partials are taken
+// in one pass (no barrier between ranges).  red holds
+// (kFillMaxCtas + 1) * kFillWarps floats.
+__device__ __forceinline__ void block_row_stats(const XSrc &s, int tok, int K, int nunits, int tid, int nthreads,
+                                                float *red, int bar_id, float &inv, float &amax) {
+    const bool rms = s.op == kXRmsnorm;
+    const int C = fill_ctas(nunits);
+    const int V = kFillThreads / nthreads;  // threads of the 512 this thread plays
+    if (rms) {
+        const float *row = static_cast<const float *>(s.x) + (size_t)tok * s.ldx;
+        for (int c = 0; c < C; ++c) {
+            int u0, u1;
+            fill_range(nunits, C, c, u0, u1);
+            for (int v = 0; v < V; ++v) {
+                const int vt = tid + v * nthreads;
+                float a = 0.0f;
+                for (int u = u0 + vt; u < u1; u += kFillThreads) {
+                    int kk[4];
+                    unit_cols(u, kk);
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        const float x = kk[q] < K ? row[kk[q]] : 0.0f;
+                        a = fmaf(x, x, a);
+                    }
+                }
+#pragma unroll
+                for (int off = 16; off > 0; off >>= 1) a += __shfl_xor_sync(0xffffffffu, a, off);
+                if ((vt & 31) == 0) red[c * kFillWarps + (vt >> 5)] = a;
+            }
+        }
+    }
+    float am = range_absmax(s, tok, 0, K, tid, nthreads);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, off));
+    if ((tid & 31) == 0) red[kFillMaxCtas * kFillWarps + (tid >> 5)] = am;
+    named_bar_sync(bar_id, nthreads);
+    inv = 1.0f;
+    if (rms) {
+        float tot = 0.0f;
+        for (int c = 0; c < C; ++c) {
+            float part = 0.0f;
+#pragma unroll
+            for (int w = 0; w < kFillWarps; ++w) part += red[c * kFillWarps + w];
+            tot += part;
+        }
+        inv = inv_rms_of(tot, K, s.eps);
+    }
+    float mx = 0.0f;
+    for (int w = 0; w < nthreads / 32; ++w) mx = fmaxf(mx, red[kFillMaxCtas * kFillWarps + w]);
+    named_bar_sync(bar_id, nthreads);
+    amax = rms ? mx * inv : mx;
 }
 
 // Power-of-two scaling of an activation row before its fp16 split: e with

@@ -25,6 +25,13 @@
 
 typedef _Float16 f16;
 
+/* exp of the reference's silu (`@exp` in src/kernels/neon.zig:705-712), taken
+ * in double and rounded to float: the correctly rounded float exp except in
+ * about one case in 10^9.  The CUDA path does the same, so the two agree bit
+ * for bit (any two float exps may differ in the last bit, which the int8
+ * activation re-quantization of the W8A8 path can turn into a flipped code). */
+static inline float exp_rn(float x) { return (float)exp((double)x); }
+
 /* ------------------------------------------------------------------------ */
 /* int8 dot kernels: src/kernels/neon.zig (x86 `else` branches)              */
 /* ------------------------------------------------------------------------ */
@@ -64,7 +71,7 @@ float oracle_dot_i8_gateup_swiglu(const int8_t *wg, const int8_t *wu, const int8
     }
     float g = (float)ag * (scale_gate * scale_x);
     float u = (float)au * (scale_up * scale_x);
-    float silu_g = g / (1.0f + expf(-g));
+    float silu_g = g / (1.0f + exp_rn(-g));
     return silu_g * u;
 }
 
@@ -113,7 +120,7 @@ void oracle_rmsnorm(const float *x, const float *gamma, float *y, size_t n, floa
 /* src/kernels/neon.zig:705-712  siluMul */
 void oracle_silu_mul(const float *g, const float *u, float *out, size_t n) {
     for (size_t i = 0; i < n; ++i) {
-        float s = g[i] / (1.0f + expf(-g[i]));
+        float s = g[i] / (1.0f + exp_rn(-g[i]));
         out[i] = s * u[i];
     }
 }

@@ -21,8 +21,11 @@ from oracle import oracle as O
 
 
 def _silu(x):
+    """g / (1 + exp(-g)) in float32, exp taken in float64 and rounded to float32
+    (as the oracle's C silu and the CUDA path do)."""
     x = np.asarray(x, np.float32)
-    return (x / (np.float32(1.0) + np.exp(-x))).astype(np.float32)
+    e = np.exp(-x.astype(np.float64)).astype(np.float32)
+    return (x / (np.float32(1.0) + e)).astype(np.float32)
 
 
 class EngineRef:
@@ -77,7 +80,12 @@ class EngineRef:
                 v = self.gemv(f"L{l}.v", x)
                 kv = v.shape[1]
                 o_in = h[f"L{l}.o"][0].shape[1] * (2 if self.scheme == "q4g64" else 1)
-                mix = v[:, np.arange(o_in) % kv]
+                i = np.arange(o_in)
+                if g.head_dim:  # head-aligned form: query head h of head_dim columns takes kv head h / group
+                    hd, grp = g.head_dim, g.q_heads // g.kv_heads
+                    mix = v[:, ((i // hd) // grp) * hd + i % hd]
+                else:  # the reference's form, out[i] = v[i % kv_dim] (src/engine.zig:619-623)
+                    mix = v[:, i % kv]
                 hidden = (hidden + self.gemv(f"L{l}.o", mix)).astype(np.float32)
             else:
                 qkv = self.gemv(f"L{l}.qkv", x)
