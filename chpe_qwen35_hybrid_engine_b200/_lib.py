@@ -69,6 +69,9 @@ SIGNATURES = {
     "chpe_mix_ssm_stub_dev": (I, [P, P, I, P, I, I, I, I, P, P]),
     "chpe_silu_mul_dev": (I, [P, P, P, SZ, P, P]),
     "chpe_argmax_dev": (I, [P, P, I, I, P, P, P]),
+    "chpe_attn_decode_dev": (I, [P, P, I, P, P, I, P, P, P, I, I, I, I, I, F, I, P, I, P]),
+    "chpe_deltanet_step_dev": (I, [P, P, I, P, P, P, P, P, I, I, I, I, P, I, P]),
+    "chpe_pos_advance_dev": (I, [P, P, I, P]),
     "chpe_xfrag_create": (I, [P, P, I, I, PP]),
     "chpe_xfrag_fill_dev": (I, [P, P, P, P, P]),
     "chpe_gemv_xfrag_dev": (I, [P, P, P, P, I, P]),

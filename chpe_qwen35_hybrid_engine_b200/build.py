@@ -24,7 +24,7 @@ LIB = os.path.join(HERE, "libchpe_b200.so")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVFLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall",
            "--expt-relaxed-constexpr", "-I", os.path.join(ROOT, "include")]
-SOURCES = ["gemv.cu", "gemv_b8.cu", "gemv_b4.cu", "gemv_b2.cu", "gemv_b2w.cu", "gemv_s8.cu", "prep.cu", "model.cu", "prefill.cu", "comm.cu", "abi.cu"]
+SOURCES = ["gemv.cu", "gemv_b8.cu", "gemv_b4.cu", "gemv_b2.cu", "gemv_b2w.cu", "gemv_s8.cu", "prep.cu", "model.cu", "mixers.cu", "prefill.cu", "comm.cu", "abi.cu"]
 
 
 def nvcc() -> str:

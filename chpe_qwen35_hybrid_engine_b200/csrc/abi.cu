@@ -37,6 +37,8 @@ struct chpe_ctx {
     size_t prefill_xt_bytes = 0;
     std::unordered_map<const void *, chpe_tensor *> registry;
     std::vector<chpe_tensor *> owned;
+    void *extra[4] = {nullptr, nullptr, nullptr, nullptr};  // scratch of the step helpers (mixers.cu)
+    size_t extra_bytes[4] = {0, 0, 0, 0};
 };
 
 namespace {
@@ -251,6 +253,10 @@ int ensure_scratch(chpe_ctx *ctx, const GemvPlan &P, cudaStream_t st) {
     }
     return CHPE_OK;
 }
+
+// Error words that are argument errors found on the device, not expired waits.
+constexpr int kErrTokenRange = 16;  // chpe_embed_i8_dev: token id outside the table
+constexpr int kErrCacheFull = 41;   // chpe_attn_decode_dev: step past max_seq
 
 // Bytes after the block sums that hold the fill's row unscale factors xe[8].
 constexpr size_t kXeBytes = 64;
@@ -503,6 +509,8 @@ int finish(chpe_ctx *ctx) {
     CK(cudaMemcpy(&h_err, ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost));
     if (h_err) {
         cudaMemset(ctx->d_err, 0, sizeof(int));
+        if (h_err == kErrTokenRange) return fail(ctx, CHPE_EINVAL, "a token id was outside the vocabulary");
+        if (h_err == kErrCacheFull) return fail(ctx, CHPE_EINVAL, "a step ran past the KV cache's max_seq positions");
         // a kernel that gave up may have left arrival / work counters set
         if (ctx->scr.counters) cudaMemset(ctx->scr.counters, 0, ctx->scr.counters_n * sizeof(unsigned));
         return fail(ctx, CHPE_ETIMEOUT, "kernel bounded wait expired (code %d)", h_err);
@@ -588,6 +596,7 @@ extern "C" int chpe_destroy(chpe_ctx *ctx) {
     cudaFree(ctx->d_xe);
     cudaFree(ctx->d_err);
     cudaFree(ctx->prefill_xt);
+    for (void *x : ctx->extra) cudaFree(x);
     cudaStreamDestroy(ctx->stream);
     delete ctx;
     return CHPE_OK;
@@ -1359,3 +1368,22 @@ extern "C" int chpe_gemv_noalloc_dev(chpe_ctx *ctx, const chpe_tensor *w, const 
 
 // Error word of a context (used by the step helpers in model.cu).
 int *chpe_ctx_error_word(chpe_ctx *ctx) { return ctx->d_err; }
+
+// Scratch slot `slot` (0..3) of a context, at least `bytes` long and zeroed
+// when (re)allocated -- the device is synchronised around a reallocation, so
+// a helper's first call at a size must come before any stream capture.
+int chpe_ctx_scratch(chpe_ctx *ctx, int slot, size_t bytes, void **out) {
+    if (slot < 0 || slot >= 4) return CHPE_EINVAL;
+    if (bytes > ctx->extra_bytes[slot]) {
+        cudaSetDevice(ctx->device);
+        if (ctx->extra[slot]) cudaFree(ctx->extra[slot]);
+        ctx->extra[slot] = nullptr;
+        ctx->extra_bytes[slot] = 0;
+        CK(cudaMalloc(&ctx->extra[slot], bytes));
+        CK(cudaMemset(ctx->extra[slot], 0, bytes));
+        CK(cudaDeviceSynchronize());
+        ctx->extra_bytes[slot] = bytes;
+    }
+    *out = ctx->extra[slot];
+    return CHPE_OK;
+}

@@ -5,8 +5,13 @@ Mirrors the reference's orchestration (src/engine.zig Qwen35Engine):
   stepBatch4  (:753-900)            unfused gate, up + siluMul, SSM stand-in silu(qkv)*z
   stepBatch8  (:902-1095)           same as batch 4 with 8 rows
 with the reference's stand-ins for the token mixers (full attention = V
-broadcast, :619-623; Gated DeltaNet = qkv gated by z, :651-654), RMSNorm before
-each block, residual adds, final RMSNorm, LM head and argmax (:1098-1110).
+broadcast, :619-623; Gated DeltaNet = qkv gated by z, :651-654) -- or, with
+Geometry.mixer = "real", GQA attention with RoPE over an fp32 KV cache
+(src/qwen72b_engine.zig:291-369) and the Gated-DeltaNet conv1d + recurrence
+(src/ssm.zig:11-99), the output gated by silu(z) -- RMSNorm before each
+block, residual adds, final RMSNorm, LM head and argmax (:1098-1110).  With
+real mixers the rows of an M-row step are consecutive positions of one
+sequence (speculative verification), and the position lives on the device.
 Every projection runs on the library's quantized GEMV; the residual add is the
 GEMV's accumulate into the hidden state.  A step of fixed row count is captured
 once into a CUDA graph and replayed; greedy decoding feeds the argmax of one
@@ -44,9 +49,34 @@ class Geometry:
     head_dim: int = 0       # 0: reference stand-in out[i] = v[i % kv_dim]; else head-aligned GQA stand-in
     q_heads: int = 16
     kv_heads: int = 4
+    # token mixers: "stub" -- the reference engine's stand-ins (src/engine.zig:619-623, :651-654);
+    # "real" -- GQA attention with RoPE over a KV cache and the Gated-DeltaNet recurrence
+    mixer: str = "stub"
+    rope_theta: float = 1e6   # src/chpe_engine.zig:103
+    ssm_heads: int = 16       # Gated-DeltaNet heads; key and value dims follow from ssm_qkv / ssm_z
+    max_seq: int = 2048       # KV-cache positions ("real" mixers)
 
     def is_attn(self, l: int) -> bool:
         return (l + 1) % self.attn_every == 0
+
+    @property
+    def attn_hd(self) -> int:
+        """Head dim of real attention: kv_dim / kv_heads."""
+        return self.kv_dim // self.kv_heads
+
+    @property
+    def attn_gated(self) -> bool:
+        """The q projection carries a per-head output gate after each head's
+        query (Qwen3.5: q_dim = 2 x q_heads x head_dim)."""
+        return self.q_dim == 2 * self.q_heads * self.attn_hd
+
+    @property
+    def ssm_dk(self) -> int:
+        return (self.ssm_qkv - self.ssm_z) // (2 * self.ssm_heads)
+
+    @property
+    def ssm_dv(self) -> int:
+        return self.ssm_z // self.ssm_heads
 
     def weight_count(self) -> int:
         H, F = self.hidden, self.ffn
@@ -73,6 +103,7 @@ class LayerWeights:
     in_gamma: object
     post_gamma: object
     proj: dict = field(default_factory=dict)  # name -> Tensor
+    mix: dict = field(default_factory=dict)   # real mixers: Gated-DeltaNet conv taps and decays
 
 
 SCHEMES = {"w8a8": (8, L.SCHEME_I8_TENSOR, 0), "q8g32": (8, L.SCHEME_I8_GROUP_F16, 32),
@@ -166,12 +197,18 @@ def build_random(ctx: Context, geom: Geometry, scheme: str, seed: int = 0, max_r
             lw.proj["qkv"] = mat(f"L{l}.qkv", geom.ssm_qkv, H, tp)
             lw.proj["z"] = mat(f"L{l}.z", geom.ssm_z, H, tp)
             lw.proj["out"] = mat(f"L{l}.out", H, geom.ssm_z, "row" if world > 1 else None)
+            if geom.mixer == "real":
+                lw.mix = _delta_weights(geom, gen, dev)
+                if host is not None:
+                    host[f"L{l}.conv_w"] = lw.mix["conv_w"].cpu().numpy()
+                    host[f"L{l}.decay"] = lw.mix["decay"].cpu().numpy()
         lw.proj["gate"] = mat(f"L{l}.gate", F, H, "ffn" if world > 1 else None)
         lw.proj["up"] = mat(f"L{l}.up", F, H, "ffn" if world > 1 else None)
         lw.proj["down"] = mat(f"L{l}.down", H, F, "row" if world > 1 else None)
         eng.layers.append(lw)
     eng.final_gamma = gamma("final_gamma")
     eng.head = mat("head", geom.vocab, H, tp)
+    eng.init_mixer_state()
     torch.cuda.synchronize(dev)
     return eng, host
 
@@ -232,6 +269,8 @@ def build_random_codes(ctx: Context, geom: Geometry, scheme: str, seed: int = 0,
             lw.proj["qkv"] = mat(split_rows(geom.ssm_qkv, "col"), H)
             lw.proj["z"] = mat(split_rows(geom.ssm_z, "col"), H)
             lw.proj["out"] = mat(H, split_cols(geom.ssm_z))
+            if geom.mixer == "real":
+                lw.mix = _delta_weights(geom, gen, dev)
         fr = split_rows(F, "ffn")
         lw.proj["gate"] = mat(fr, H)
         lw.proj["up"] = mat(fr, H)
@@ -239,8 +278,19 @@ def build_random_codes(ctx: Context, geom: Geometry, scheme: str, seed: int = 0,
         eng.layers.append(lw)
     eng.final_gamma = gam()
     eng.head = mat(split_rows(geom.vocab, "col"), H)
+    eng.init_mixer_state()
     torch.cuda.synchronize(dev)
     return eng
+
+
+def _delta_weights(geom: Geometry, gen, dev) -> dict:
+    """Gated-DeltaNet weights of one layer (random init): depthwise conv1d taps
+    [channels][4] ~ N(0, 0.3^2) and one decay per head, uniform in [0.5, 0.95]."""
+    import torch
+    C = geom.ssm_qkv
+    conv_w = (0.3 * torch.randn(C, 4, device=dev, generator=gen)).float().contiguous()
+    decay = (0.5 + 0.45 * torch.rand(geom.ssm_heads, device=dev, generator=gen)).float().contiguous()
+    return {"conv_w": conv_w, "decay": decay}
 
 
 def _row_split(cols: int, world: int, rank: int, scheme: str):
@@ -281,6 +331,45 @@ class HybridEngine:
             "argmax": torch.zeros(Mx, dtype=torch.int32, device=self.dev), "maxv": torch.zeros(Mx, **f32),
             "mix_out": torch.zeros(Mx, g.hidden, **f32),
         }
+        self.pos = torch.zeros(1, dtype=torch.int32, device=self.dev)  # positions cached (real mixers)
+        self.mstate = {}  # layer -> {"kc", "vc"} or {"ring", "state"}
+
+    # -- mixer state (real mixers) ----------------------------------------------------
+    def init_mixer_state(self):
+        """KV caches of the attention layers ([max_seq][local kv heads][head_dim]
+        fp32) and the conv rings / recurrent states of the Gated-DeltaNet layers."""
+        import torch
+        g = self.geom
+        if g.mixer != "real":
+            return
+        f32 = dict(dtype=torch.float32, device=self.dev)
+        for l, lw in enumerate(self.layers):
+            if "q" in lw.proj:
+                kvh = lw.proj["k"].rows // g.attn_hd
+                self.mstate[l] = {"kc": torch.zeros(g.max_seq, kvh, g.attn_hd, **f32),
+                                  "vc": torch.zeros(g.max_seq, kvh, g.attn_hd, **f32)}
+            else:
+                self.mstate[l] = {"ring": torch.zeros(16, g.ssm_qkv, **f32),
+                                  "state": torch.zeros(g.ssm_heads, g.ssm_dk, g.ssm_dv, **f32)}
+
+    def reset(self):
+        """Empty sequence: position 0, zero recurrent states and conv rings."""
+        self.pos.zero_()
+        for st in self.mstate.values():
+            if "state" in st:
+                st["state"].zero_()
+                st["ring"].zero_()
+
+    def _snapshot(self):
+        return self.pos.clone(), {l: {k: v.clone() for k, v in st.items() if k != "kc" and k != "vc"}
+                                  for l, st in self.mstate.items()}
+
+    def _restore(self, snap):
+        pos, st = snap
+        self.pos.copy_(pos)
+        for l, d in st.items():
+            for k, v in d.items():
+                self.mstate[l][k].copy_(v)
 
     # -- weights ---------------------------------------------------------------
     def n_weight_bytes(self) -> int:
@@ -354,14 +443,34 @@ class HybridEngine:
                                           _dev_ptr(b["tokens"]), M, _dev_ptr(b["hidden"]), sp))
         hid = b["hidden"]
         norm = dict(ldx=H, eps=g.eps)
+        real = g.mixer == "real"
         for l, lw in enumerate(self.layers):
             p = lw.proj
-            if "q" in p:  # full attention (GQA) block; stand-in mixer = V broadcast
+            if "q" in p and real:  # full attention: RoPE, KV cache, GQA softmax attention
+                q_out, k_out, v_out, att = b["a"], b["b"], b["c"], b["mix"]
+                run([p["q"], p["k"], p["v"]], [q_out, k_out, v_out], L.XOP_RMSNORM, hid, lw.in_gamma, **norm)
+                hd = g.attn_hd
+                kvh = p["k"].rows // hd
+                qh = p["q"].rows // (hd * (2 if g.attn_gated else 1))
+                ms = self.mstate[l]
+                ctx.attn_decode(q_out, k_out, v_out, ms["kc"], ms["vc"], self.pos, M, qh, kvh, hd, g.rope_theta,
+                                g.attn_gated, att, ldq=p["q"].rows, ldkv=p["k"].rows, ldo=qh * hd, stream=sp.value)
+                run_res(p["o"], L.XOP_PLAIN, att, ldx=qh * hd)
+            elif "q" in p:  # full attention (GQA) block; stand-in mixer = V broadcast
                 q_out, k_out, v_out = b["a"], b["b"], b["c"]
                 kv = p["v"].rows
                 run([p["q"], p["k"], p["v"]], [q_out, k_out, v_out], L.XOP_RMSNORM, hid, lw.in_gamma, **norm)
                 run_res(p["o"], L.XOP_ATTN_STUB, v_out, ldx=kv, kv_dim=kv, head_dim=g.head_dim,
                         group=g.q_heads // g.kv_heads)
+            elif real:  # Gated DeltaNet: conv1d + recurrence, output gated by silu(z)
+                qkv_out, z_out, y = b["a"], b["b"], b["mix"]
+                run([p["qkv"], p["z"]], [qkv_out, z_out], L.XOP_RMSNORM, hid, lw.in_gamma, **norm)
+                ms = self.mstate[l]
+                ctx.deltanet_step(qkv_out, lw.mix["conv_w"], ms["ring"], ms["state"], lw.mix["decay"], self.pos, M,
+                                  g.ssm_heads, g.ssm_dk, g.ssm_dv, y, ldqkv=p["qkv"].rows, ldo=g.ssm_z,
+                                  stream=sp.value)
+                run_res(p["out"], L.XOP_SSM_STUB, y, z_out, ldx=g.ssm_z, ld_aux=p["z"].rows, qkv_dim=g.ssm_z,
+                        silu_on_qkv=False)
             else:  # Gated DeltaNet block; stand-in mixer = qkv gated by z
                 qkv_out, z_out = b["a"], b["b"]
                 run([p["qkv"], p["z"]], [qkv_out, z_out], L.XOP_RMSNORM, hid, lw.in_gamma, **norm)
@@ -376,20 +485,46 @@ class HybridEngine:
         run([self.head], [b["logits"]], L.XOP_RMSNORM, hid, self.final_gamma, **norm)
         self._check(lib.chpe_argmax_dev(ctx.ptr, _dev_ptr(b["logits"]), M, self.head.rows, _dev_ptr(b["argmax"]),
                                         _dev_ptr(b["maxv"]), sp))
+        if real:
+            ctx.pos_advance(self.pos, M, stream=sp.value)
 
     def capture(self, M: int):
-        """Capture step(M) as a CUDA graph (after one eager warm-up run)."""
+        """Capture step(M) as a CUDA graph (after one eager warm-up run, whose
+        effect on the position, recurrent states and conv rings is undone)."""
         import torch
+        snap = self._snapshot()
         st = torch.cuda.Stream(self.dev)
         st.wait_stream(torch.cuda.current_stream(self.dev))
         with torch.cuda.stream(st):
             self.step(M, st)
+        torch.cuda.synchronize(self.dev)
+        self._restore(snap)
         torch.cuda.synchronize(self.dev)
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, stream=st):
             self.step(M, st)
         self.graphs[M] = g
         return g
+
+    def prefill(self, tokens, M: int = 8, use_graph: bool = True):
+        """Feed a context through the step, M positions at a time (the verify
+        step; with real mixers this fills the KV caches and recurrent states).
+        A last partial chunk runs eagerly with its own row count."""
+        import torch
+        b = self.buf
+        toks = np.asarray(tokens, np.int32)
+        if use_graph and M not in self.graphs:
+            self.capture(M)
+        i = 0
+        while i < len(toks):
+            n = min(M, len(toks) - i)
+            b["tokens"][:n].copy_(torch.from_numpy(toks[i:i + n]).to(self.dev))
+            if n == M and use_graph:
+                self.graphs[M].replay()
+            else:
+                self.step(n)
+            i += n
+        torch.cuda.synchronize(self.dev)
 
     def decode_greedy(self, first_tokens, steps: int, M: int = 1, use_graph: bool = True):
         """Greedy decode: each step's argmax rows become the next step's tokens.

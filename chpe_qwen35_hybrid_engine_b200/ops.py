@@ -333,6 +333,31 @@ class Context:
                                                                _dev_ptr(out), _stream_ptr(stream)))
         return out
 
+    # -- token mixers ----------------------------------------------------------------
+    def attn_decode(self, q, k, v, kcache, vcache, pos, M: int, q_heads: int, kv_heads: int, head_dim: int,
+                    rope_theta: float, gated: bool, out, ldq: int = 0, ldkv: int = 0, ldo: int = 0, stream=None):
+        """GQA decode attention with RoPE over a KV cache (chpe_attn_decode_dev):
+        rows 0..M-1 of q / k / v at positions pos .. pos+M-1 (pos a device int32
+        tensor); kcache / vcache [max_seq, kv_heads, head_dim] fp32."""
+        max_seq = kcache.shape[0]
+        self._check(self.lib.chpe_attn_decode_dev(
+            self.ptr, _dev_ptr(q), ldq or q.shape[-1], _dev_ptr(k), _dev_ptr(v), ldkv or k.shape[-1],
+            _dev_ptr(kcache), _dev_ptr(vcache), _dev_ptr(pos), M, q_heads, kv_heads, head_dim, max_seq,
+            C.c_float(rope_theta), int(gated), _dev_ptr(out), ldo or out.shape[-1], _stream_ptr(stream)))
+        return out
+
+    def deltanet_step(self, qkv, conv_w, ring, state, decay, pos, M: int, heads: int, key_dim: int, value_dim: int,
+                      out, ldqkv: int = 0, ldo: int = 0, stream=None):
+        """Gated-DeltaNet conv1d + recurrence over rows 0..M-1 (chpe_deltanet_step_dev)."""
+        self._check(self.lib.chpe_deltanet_step_dev(
+            self.ptr, _dev_ptr(qkv), ldqkv or qkv.shape[-1], _dev_ptr(conv_w), _dev_ptr(ring), _dev_ptr(state),
+            _dev_ptr(decay), _dev_ptr(pos), M, heads, key_dim, value_dim, _dev_ptr(out), ldo or out.shape[-1],
+            _stream_ptr(stream)))
+        return out
+
+    def pos_advance(self, pos, M: int, stream=None):
+        self._check(self.lib.chpe_pos_advance_dev(self.ptr, _dev_ptr(pos), M, _stream_ptr(stream)))
+
     # -- reference-shaped host operators ----------------------------------------
     def register_i8(self, weights: np.ndarray):
         self._check(self.lib.chpe_register_i8(self.ptr, _np_ptr(weights), weights.shape[0], weights.shape[1]))

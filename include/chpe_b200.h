@@ -312,6 +312,46 @@ int chpe_silu_mul_dev(chpe_ctx *ctx, const float *g, const float *u, size_t n, f
 /* src/engine.zig:1098-1110 computeArgmax (first index of the maximum), per row */
 int chpe_argmax_dev(chpe_ctx *ctx, const float *logits, int M, int n, int *idx, float *maxv, void *stream);
 
+/* ---- token mixers (device pointers, async) ---------------------------------
+ * Rows of a step are consecutive positions of one sequence: row m is at
+ * position *pos + m, where *pos (a device int) counts the positions already
+ * cached; chpe_pos_advance_dev(pos, M) moves it on after the step.
+ *
+ * Grouped-query decode attention with rotary position embeddings and a KV
+ * cache -- applyRope (src/qwen72b_engine.zig:90-111, src/chpe_engine.zig:191-212),
+ * the KV-cache update and the GQA softmax attention of forwardDecode
+ * (src/qwen72b_engine.zig:291-369, src/chpe_engine.zig:690-745):
+ *   q [M][ldq]: per q head head_dim values (followed by head_dim output-gate
+ *     values when gated: out = attn * sigmoid(gate), the Qwen3.5 layout)
+ *   k, v [M][ldkv]: kv_heads x head_dim values of the new positions
+ *   kcache, vcache: this layer's fp32 [max_seq][kv_heads][head_dim]; the
+ *     rotated keys and the values of the step's positions are written there
+ *   out [M][ldo]: q_heads x head_dim
+ * RoPE pairs element i with i + head_dim/2, angle = p / theta^(2i/head_dim);
+ * scores are scaled by 1/sqrt(head_dim); query head h reads kv head
+ * h / (q_heads / kv_heads).  M <= 8, head_dim <= 256, (q_heads / kv_heads) * M
+ * <= 64.  A step past max_seq records an error (chpe_sync) and writes nothing. */
+int chpe_attn_decode_dev(chpe_ctx *ctx, const float *q, int ldq, const float *k, const float *v, int ldkv,
+                         float *kcache, float *vcache, const int *pos, int M, int q_heads, int kv_heads,
+                         int head_dim, int max_seq, float rope_theta, int gated, float *out, int ldo, void *stream);
+/* Gated-DeltaNet linear attention with its causal conv1d -- Conv1DRingBuffer
+ * step / convolve and LinearAttentionState.update (src/ssm.zig:11-99):
+ *   qkv [M][ldqkv]: channels q (heads x key_dim), k (heads x key_dim),
+ *     v (heads x value_dim) of the step's rows (the in-projection's output)
+ *   conv_w [C][4]: per channel, tap j weighs the input j positions back
+ *     (C = heads * (2 key_dim + value_dim))
+ *   ring [16][C]: inputs of earlier positions (slot = position % 16), updated
+ *   state [heads][key_dim][value_dim] fp32, updated; decay [heads]
+ *   out [M][ldo]: y = q S per head (heads x value_dim)
+ * Per row, in order: conv over the last 4 inputs of each channel, then
+ * S = decay[h] * S + k^T v and y = q S.  key_dim 128, value_dim a multiple
+ * of 32, M <= 13. */
+int chpe_deltanet_step_dev(chpe_ctx *ctx, const float *qkv, int ldqkv, const float *conv_w, float *ring,
+                           float *state, const float *decay, const int *pos, int M, int heads, int key_dim,
+                           int value_dim, float *out, int ldo, void *stream);
+/* *pos += M on the device (after a step's mixers). */
+int chpe_pos_advance_dev(chpe_ctx *ctx, int *pos, int M, void *stream);
+
 /* Allocation-free variant of chpe_gemv_dev (plain GEMV, M = 1..8).  No
  * counterpart in the reference.  For callers that cannot allocate device
  * memory when they run a GEMV: host engines that reserve all the device

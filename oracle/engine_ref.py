@@ -6,7 +6,10 @@ Follows src/engine.zig Qwen35Engine: embedToken (:567-580), step (:583-734),
 stepBatch4 (:753-900), stepBatch8 (:902-1095) and computeArgmax (:1098-1110),
 with the reference's stand-in mixers (attention: V broadcast :619-623;
 Gated DeltaNet: qkv * silu(z) at batch 1 :651-654, silu(qkv) * z at batch 4/8
-:813/:988).  The per-tensor int8 scheme uses the oracle's restatement of the
+:813/:988), or -- geometry mixer "real" -- the reference's attention with RoPE
+and KV cache and its Gated-DeltaNet conv1d + recurrence (oracle/mixers_ref.py),
+the DeltaNet output gated by silu(z); rows of a step are then consecutive
+positions of one sequence.  The per-tensor int8 scheme uses the oracle's restatement of the
 reference's own operators (gemvParallel / gemvGateUpSwiGLUParallel /
 quantizeActivationInt8 / rmsnorm); the grouped schemes use the grouped GEMV
 specification (fp64 accumulation) on fp32 activations.
@@ -18,6 +21,7 @@ import os
 import numpy as np
 
 from oracle import oracle as O
+from oracle.mixers_ref import AttnLayerRef, DeltaLayerRef
 
 
 def _silu(x):
@@ -33,6 +37,16 @@ class EngineRef:
         self.h, self.g, self.scheme = host, geom, scheme
         self.nw = num_workers or os.cpu_count() or 8
         self._unpacked = {}  # q4g64: codes one per byte, made once per tensor
+        self.pos = 0
+        self.mix = {}
+        if getattr(geom, "mixer", "stub") == "real":
+            for l in range(geom.n_layers):
+                if geom.is_attn(l):
+                    self.mix[l] = AttnLayerRef(geom.max_seq, geom.q_heads, geom.kv_heads, geom.attn_hd,
+                                               geom.rope_theta, geom.attn_gated)
+                else:
+                    self.mix[l] = DeltaLayerRef(geom.ssm_heads, geom.ssm_dk, geom.ssm_dv, host[f"L{l}.conv_w"],
+                                                host[f"L{l}.decay"])
 
     # -- one projection: y[M, rows] = x[M, cols] . W^T ------------------------------
     def gemv(self, name, x):
@@ -74,7 +88,18 @@ class EngineRef:
         norm = lambda x, name: np.stack([O.rmsnorm(r, h[name], g.eps) for r in x])
         for l in range(g.n_layers):
             x = norm(hidden, f"L{l}.in_gamma")
-            if g.is_attn(l):
+            if g.is_attn(l) and l in self.mix:
+                q = self.gemv(f"L{l}.q", x)
+                k = self.gemv(f"L{l}.k", x)
+                v = self.gemv(f"L{l}.v", x)
+                mix = self.mix[l].step(q, k, v, self.pos)
+                hidden = (hidden + self.gemv(f"L{l}.o", mix)).astype(np.float32)
+            elif l in self.mix:
+                qkv = self.gemv(f"L{l}.qkv", x)
+                z = self.gemv(f"L{l}.z", x)
+                y = self.mix[l].step(qkv)
+                hidden = (hidden + self.gemv(f"L{l}.out", (y * _silu(z)).astype(np.float32))).astype(np.float32)
+            elif g.is_attn(l):
                 self.gemv(f"L{l}.q", x)
                 self.gemv(f"L{l}.k", x)
                 v = self.gemv(f"L{l}.v", x)
@@ -104,6 +129,7 @@ class EngineRef:
             hidden = (hidden + self.gemv(f"L{l}.down", mlp)).astype(np.float32)
         x = norm(hidden, "final_gamma")
         logits = self.gemv("head", x)
+        self.pos += M
         return [O.argmax(r)[0] for r in logits], logits
 
     def decode_greedy(self, first_tokens, steps):
