@@ -9,19 +9,27 @@ dataset and no checkpoint):
   decode_72b (default)  Qwen2.5-72B-shaped decode (80 GQA layers, hidden 8192,
                         FFN 29568, vocab 152064), 4-bit weights with an fp16
                         scale and zero per 64 columns, tensor parallel over the
-                        N GPUs (NCCL all-reduce after o and down), batch 1;
-                        the batch-8 step is reported beside it.  metric: tokens/s
-                        for the whole job.  At N = 1 the line also carries the
-                        Qwen3.5-9B-shaped decode (8-bit, fp16 scale per 32) at
-                        batch 1 and the batch-4 / batch-8 verify steps.
+                        N GPUs (the library's one-shot NVLink all-reduce kernel
+                        after o and down), batch 1, over a 1024-token seeded
+                        context prefilled through the engine (GQA attention
+                        with RoPE over an fp32 KV cache); the batch-8 verify
+                        step is reported beside it.  metric: tokens/s for the
+                        whole job.  At N = 1 the line also carries the
+                        Qwen3.5-9B-shaped decode (8-bit, fp16 scale per 32;
+                        Gated-DeltaNet recurrence and gated GQA attention, 512
+                        context tokens) at batch 1 and the batch-4 / batch-8
+                        verify steps, the single Q8 GEMV (q8_gemv), the 4-bit /
+                        2-bit GEMV sweep and the prefill GEMMs.
   decode_9b             the Qwen3.5-9B-shaped decode alone (N > 1: replicas).
   gemv                  one quantized GEMV y[M,N] = x[M,K] . dequant(W)^T
                         (--bits 8|4|2 --rows N --cols K --batch M --x f32|bf16);
                         metric: algorithmic HBM GB/s.  `q8_gemv` is the
                         12288x4096 int8 GEMV (fp16 scale per 32) at batch 1.
+  prefill               the prefill dequant-GEMM (tcgen05), metric TFLOP/s.
 
 A decode step is one token per row: embedding, every layer, final norm, LM
-head and argmax.  Timed steps replay one CUDA graph per step and feed each
+head and argmax; with M rows the rows are consecutive positions (speculative
+verification).  Timed steps replay one CUDA graph per step and feed each
 step's argmax into the next on the device; the weights (7 GB for the 9B shape,
 40 GB / N for the 72B shape) are far larger than the 126 MB L2, so every step
 streams them from HBM.  `e2e` runs the same steps with the token copied in from
@@ -29,7 +37,8 @@ pinned host memory and the argmax copied back to the host every step.  The
 roofline is that of the GEMV kernel: every GEMV of one step is captured on its
 own (activation fragments prepared beforehand) and its algorithmic bytes
 (packed codes + scales/zeros + activations read + outputs written) are divided
-by the replayed GEMV time.
+by the replayed GEMV time.  The CPU baseline is the reference engine's CPU
+step restated in C (oracle/cpu_baseline.c), whole steps on the host's cores.
 """
 from __future__ import annotations
 
@@ -229,19 +238,28 @@ def gemv_step_profile(ctx, eng, M, reps, dev):
     return ms, nbytes, len(groups)
 
 
-def decode_line(eng, stepper, M, args, world, dev, label, profile=True):
-    """Graph-replayed greedy decode at M rows; returns a dict of figures."""
+def decode_line(eng, stepper, M, args, world, dev, label, context_len, profile=True):
+    """Graph-replayed greedy decode at M rows after a seeded context of
+    context_len uniform token ids has been prefilled through the engine (8
+    positions per step); returns a dict of figures."""
     import torch
     from chpe_qwen35_hybrid_engine_b200 import kernel_launches
     b = eng.buf
     rng = np.random.default_rng(0)
-    context = rng.integers(0, eng.geom.vocab, 1024).astype(np.int32)  # seeded uniform token ids
+    context = rng.integers(0, eng.geom.vocab, context_len).astype(np.int32)  # seeded uniform token ids
     first = np.array([(int(context[-1]) + 7 * i) % eng.geom.vocab for i in range(M)], np.int32)
+    stepper.reset()
+    t0 = time.perf_counter()
+    stepper.prefill(context, M=8)
+    prefill_s = time.perf_counter() - t0
+    pos0 = int(eng.pos.item())
     b["tokens"][:M].copy_(torch.from_numpy(first).to(dev))
+    snap = eng._snapshot()
     n0 = kernel_launches()
     stepper.step(M)
     torch.cuda.synchronize(dev)
     launches_per_step = kernel_launches() - n0
+    eng._restore(snap)
     b["tokens"][:M].copy_(torch.from_numpy(first).to(dev))
     graph = stepper.capture(M)
     st = torch.cuda.Stream(dev)
@@ -275,10 +293,12 @@ def decode_line(eng, stepper, M, args, world, dev, label, profile=True):
     del feed
     stepper.graphs.clear()
     del graph
+    pos1 = int(eng.pos.item())
     out = {"label": label, "rows": M, "tok_s": round(M / (ms_step * 1e-3), 2),
            "ms_per_step": round(ms_step, 4), "e2e_tok_s": round(M / (e2e_ms * 1e-3), 2),
            "e2e_ms_per_step": round(e2e_ms, 4), "kernel_launches_per_step": int(launches_per_step),
-           "weight_bytes": int(eng.n_weight_bytes())}
+           "weight_bytes": int(eng.n_weight_bytes()), "context_tokens": int(context_len),
+           "positions": [pos0, pos1], "context_prefill_s": round(prefill_s, 3)}
     if profile:
         gms, gbytes, glaunch = gemv_step_profile(eng.ctx, eng, M, max(5, min(args.steps, 20)), dev)
         gms = dist_max(gms, world)
@@ -287,10 +307,39 @@ def decode_line(eng, stepper, M, args, world, dev, label, profile=True):
     return out
 
 
+def _decode_geometry(which, args):
+    """The benchmark model with the real token mixers and a KV cache sized for
+    the context plus every step the measurement runs (8 rows at most)."""
+    import dataclasses
+    from chpe_qwen35_hybrid_engine_b200.engine import QWEN25_72B, QWEN35_9B
+    base, ctx_len = (QWEN25_72B, 1024) if which == "decode_72b" else (QWEN35_9B, 512)
+    need = ctx_len + 8 * (2 * (args.warmup + args.steps) + 8)
+    return dataclasses.replace(base, mixer="real", max_seq=(need + 255) // 256 * 256), ctx_len
+
+
+def decode_config(which, world):
+    """The `config` of a decode line (both arms)."""
+    if which == "decode_72b":
+        return {"workload": "decode_72b",
+                "model": "Qwen2.5-72B-shaped: 80 GQA layers, hidden 8192, FFN 29568 SwiGLU, 64/8 heads of 128, "
+                         "vocab 152064",
+                "weights": "4-bit codes, fp16 scale + zero per 64 columns (seeded random codes and scales)",
+                "tensor_parallel": world, "global_batch": 1,
+                "context": "1024 seeded uniform token ids prefilled through the engine (RoPE, fp32 KV cache); "
+                           "decode continues from there",
+                "parallelism": f"tp{world}", "l2": "40 GB / N of weights per step >> 126 MB L2"}
+    return {"workload": "decode_9b",
+            "model": "Qwen3.5-9B-shaped hybrid: 24 Gated DeltaNet + 8 gated GQA layers, hidden 4096, FFN 12288, "
+                     "vocab 151936",
+            "weights": "8-bit codes, fp16 scale per 32 columns (random-init N(0,0.02))",
+            "context": "512 seeded uniform token ids prefilled through the engine",
+            "global_batch": world, "parallelism": f"replicas{world}", "l2": "7 GB of weights per step >> 126 MB L2"}
+
+
 def run_decode(args, rank, world, local_rank, which):
     import torch
     from chpe_qwen35_hybrid_engine_b200 import Context
-    from chpe_qwen35_hybrid_engine_b200.engine import QWEN25_72B, QWEN35_9B, build_random
+    from chpe_qwen35_hybrid_engine_b200.engine import build_random
     from chpe_qwen35_hybrid_engine_b200.tp import TensorParallelEngine
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
@@ -298,43 +347,41 @@ def run_decode(args, rank, world, local_rank, which):
     clk = ClockSampler(local_rank)
     extra = {}
     ctx = Context(local_rank)
+    geom, ctx_len = _decode_geometry(which, args)
     if which == "decode_72b":
-        tp = TensorParallelEngine(ctx, QWEN25_72B, "q4g64", rank, world, seed=0, max_rows=8, random_codes=True)
+        tp = TensorParallelEngine(ctx, geom, "q4g64", rank, world, seed=0, max_rows=8, random_codes=True)
         clk.start()
-        main = decode_line(tp.eng, tp, 1, args, world, dev, f"72b_tp{world}_b1")
+        main = decode_line(tp.eng, tp, 1, args, world, dev, f"72b_tp{world}_b1", ctx_len)
         clk.stop()
-        extra["decode_72b_b8"] = decode_line(tp.eng, tp, 8, args, world, dev, f"72b_tp{world}_b8")
+        extra["decode_72b_b8"] = decode_line(tp.eng, tp, 8, args, world, dev, f"72b_tp{world}_b8", ctx_len)
         tp.graphs.clear()
+        if tp.comm is not None:
+            tp.comm.close()
         del tp
-        config = {"workload": "decode_72b",
-                  "model": "Qwen2.5-72B-shaped: 80 GQA layers, hidden 8192, FFN 29568 SwiGLU, 64/8 heads of 128, "
-                           "vocab 152064",
-                  "weights": "4-bit codes, fp16 scale + zero per 64 columns (seeded random codes and scales)",
-                  "tensor_parallel": world, "global_batch": 1, "context": "1024 seeded uniform token ids",
-                  "parallelism": f"tp{world}", "l2": "40 GB / N of weights per step >> 126 MB L2"}
+        config = decode_config(which, world)
         scaling, units = "strong", 1
     else:
-        eng, _ = build_random(ctx, QWEN35_9B, "q8g32", seed=rank, max_rows=8)
+        eng, _ = build_random(ctx, geom, "q8g32", seed=rank, max_rows=8)
         clk.start()
-        main = decode_line(eng, eng, 1, args, world, dev, "9b_b1")
+        main = decode_line(eng, eng, 1, args, world, dev, "9b_b1", ctx_len)
         clk.stop()
         del eng
-        config = {"workload": "decode_9b",
-                  "model": "Qwen3.5-9B-shaped hybrid: 24 Gated DeltaNet + 8 GQA layers, hidden 4096, FFN 12288, "
-                           "vocab 151936",
-                  "weights": "8-bit codes, fp16 scale per 32 columns (random-init N(0,0.02), quantized on device)",
-                  "global_batch": world, "parallelism": f"replicas{world}",
-                  "l2": "7 GB of weights per step >> 126 MB L2"}
+        config = decode_config(which, world)
         scaling, units = "weak", world
     ctx.close()
     torch.cuda.empty_cache()
     if which == "decode_72b" and world == 1:
         ctx9 = Context(local_rank)
-        eng9, _ = build_random(ctx9, QWEN35_9B, "q8g32", seed=0, max_rows=8)
+        g9, c9 = _decode_geometry("decode_9b", args)
+        eng9, _ = build_random(ctx9, g9, "q8g32", seed=0, max_rows=8)
         for M in (1, 4, 8):
-            extra[f"decode_9b_b{M}"] = decode_line(eng9, eng9, M, args, 1, dev, f"9b_b{M}")
+            extra[f"decode_9b_b{M}"] = decode_line(eng9, eng9, M, args, 1, dev, f"9b_b{M}", c9)
+        eng9.graphs.clear()
         del eng9
         ctx9.close()
+        torch.cuda.empty_cache()
+        if not args.no_sweep:
+            extra.update(kernel_sweep(dev, local_rank, peaks))
     achieved = main["gemv_gbs"]
     n_launch = main["kernel_launches_per_step"] * args.steps
     if which == "decode_9b":
@@ -352,7 +399,7 @@ def run_decode(args, rank, world, local_rank, which):
                      "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": traffic,
                      "traffic_unit": "bytes per step (all GEMV launches of one step, per GPU)",
                      "peak_source": peaks["source"],
-                     "kernel": "gemv_kernel: all GEMVs of one step on one GPU, bytes / GEMV time",
+                     "kernel": "chpe_qgemv_kernel: all GEMVs of one step on one GPU, bytes / GEMV time",
                      "algorithmic_bytes_per_step": main["gemv_bytes_per_step"],
                      "gemv_ms_per_step": main["gemv_ms_per_step"]},
         "e2e": {"value": round(main["e2e_tok_s"] * units, 2), "unit": "tokens/s", "h2d_bytes_per_step": 4,
@@ -363,10 +410,112 @@ def run_decode(args, rank, world, local_rank, which):
     }
     line.update(extra)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        step_s, threads, sample = cpu_decode_sample(which, budget_s=10.0)
-        line["cpu_baseline"] = {"value": round(1.0 / step_s, 4), "unit": "tokens/s", "cores": threads,
-                                "kind": "port", "sample": sample}
+        line["cpu_baseline"] = cpu_decode_baseline(which)
     return line
+
+
+def kernel_sweep(dev, local_rank, peaks):
+    """The single-kernel benchmark configurations at N = 1, each kernel timed
+    alone in a CUDA graph over weight copies that rotate through > 3x L2:
+    the Q8 GEMV 12288x4096 (q8_gemv), the 4-bit / 2-bit GEMV sweep (K, N) in
+    {(4096,4096), (4096,12288), (12288,4096), (4096,151936)} at M = 1/4/8 with
+    bf16 activations, and the prefill GEMMs (M = 2048 bf16 tokens; Q8 g32 and
+    Q4 g64 weights of (4096,12288), (12288,4096), (4096,6144))."""
+    import torch
+    from chpe_qwen35_hybrid_engine_b200 import Context
+    ctx = Context(local_rank)
+    out = {}
+    hbm = peaks["hbm_gbs"]
+    g = torch.Generator(device=dev)
+    g.manual_seed(0)
+
+    def weights(bits, N, K, copies):
+        from chpe_qwen35_hybrid_engine_b200 import SCHEME_I8_GROUP_F16, SCHEME_U_GROUP_F16_ZERO
+        tens = []
+        for _ in range(copies):
+            if bits == 8:
+                codes = torch.randint(-127, 128, (N, K), dtype=torch.int8, device=dev, generator=g)
+                s = (0.02 / 127 * torch.exp(0.25 * torch.randn(N, K // 32, device=dev, generator=g))).half()
+                tens.append(ctx.upload_matrix(8, SCHEME_I8_GROUP_F16, codes, s, rows=N, cols=K, group=32))
+            else:
+                codes = torch.randint(0, 256, (N, K * bits // 8), dtype=torch.uint8, device=dev, generator=g)
+                s = (0.02 * 5 / ((1 << bits) - 1) * torch.exp(0.25 * torch.randn(N, K // 64, device=dev,
+                                                                                   generator=g))).half()
+                mid = (1 << bits) // 2
+                z = torch.randint(max(0, mid - 2), mid + 2, (N, K // 64), device=dev, generator=g).half()
+                tens.append(ctx.upload_matrix(bits, SCHEME_U_GROUP_F16_ZERO, codes, s, z, rows=N, cols=K, group=64))
+        return tens
+
+    def time_graph(issue, reps=3):
+        st = torch.cuda.Stream(dev)
+        st.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(st):
+            issue(st)
+        torch.cuda.synchronize(dev)
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=st):
+            issue(st)
+        for _ in range(2):
+            gr.replay()
+        ms = timed_replays(gr.replay, reps, 1, dev) / reps
+        del gr
+        return ms
+
+    def gemv_case(bits, N, K, M, xdt):
+        wb = N * K * bits // 8 + (N * K // 32) * 2 if bits == 8 else N * K * bits // 8 + (N * K // 64) * 4
+        copies = max(2, min(64, -(-3 * L2_BYTES // wb)))
+        tens = weights(bits, N, K, copies)
+        x = torch.randn(M, K, device=dev, generator=g)
+        from chpe_qwen35_hybrid_engine_b200 import X_BF16, X_F32
+        if xdt == "bf16":
+            x = x.to(torch.bfloat16)
+        xf = ctx.xfrag(tens[0], M, X_BF16 if xdt == "bf16" else X_F32)
+        ctx.xfrag_fill(xf, x)
+        y = torch.empty(M, N, device=dev)
+        per_graph = max(copies, 8)
+        ms = time_graph(lambda st: [ctx.gemv_xfrag(tens[i % copies], xf, y, stream=st) for i in range(per_graph)])
+        us = ms * 1e3 / per_graph
+        algo = wb + M * K * (2 if xdt == "bf16" else 4) + M * N * 4
+        gbs = algo / (us * 1e-6) / 1e9
+        xf.free()
+        for t in tens:
+            t.free()
+        torch.cuda.synchronize(dev)
+        return {"us": round(us, 3), "gbs": round(gbs, 1), "frac": round(gbs / hbm, 4), "algorithmic_bytes": int(algo),
+                "weight_copies": copies}
+
+    out["q8_gemv"] = dict(gemv_case(8, 12288, 4096, 1, "f32"),
+                          config="Q8 g32 (fp16 scale per 32), y[1,12288] = x[1,4096] fp32 . W^T")
+    sweep = {}
+    for bits in (4, 2):
+        for K, N in ((4096, 4096), (4096, 12288), (12288, 4096), (4096, 151936)):
+            for M in (1, 4, 8):
+                sweep[f"q{bits}_k{K}_n{N}_m{M}"] = gemv_case(bits, N, K, M, "bf16")
+    out["gemv_sweep"] = {"config": "unsigned 4/2-bit codes, fp16 scale + zero per 64, bf16 x; kernel alone",
+                         "peak_gbs": hbm, "cases": sweep}
+    pre = {}
+    peak_t = peaks["bf16_tflops"]
+    for bits in (8, 4):
+        for K, N in ((4096, 12288), (12288, 4096), (4096, 6144)):
+            wb = N * K * bits // 8
+            copies = max(2, min(16, -(-3 * L2_BYTES // wb)))
+            tens = weights(bits, N, K, copies)
+            M = 2048
+            x = torch.randn(M, K, device=dev, generator=g).to(torch.bfloat16)
+            y = torch.empty(M, N, device=dev)
+            ms = time_graph(lambda st: [ctx.gemm_prefill(tens[i % copies], x, out=y, stream=st)
+                                        for i in range(copies)]) / copies
+            tf = 2.0 * M * N * K / (ms * 1e-3) / 1e12
+            pre[f"q{bits}_k{K}_n{N}"] = {"ms": round(ms, 4), "tflops": round(tf, 1), "frac": round(tf / peak_t, 4)}
+            for t in tens:
+                t.free()
+            torch.cuda.synchronize(dev)
+    out["prefill"] = {"config": "M = 2048 bf16 tokens, Q8 g32 / Q4 g64 weights, tcgen05 (fp16 operands, fp32 TMEM "
+                                "accumulators); includes the activation tile prep", "peak_tflops": peak_t,
+                      "peak_source": peaks["source"] + " (bf16 burst)", "cases": pre}
+    ctx.close()
+    torch.cuda.empty_cache()
+    return out
 
 
 # ----------------------------------------------------------------------------
@@ -622,75 +771,30 @@ def cpu_baseline_gemv(c, budget_s=10.0):
                       f"{threads} threads"}
 
 
-class CpuDecodeSampler:
-    """Bounded sample of one decode step on the host cores: the GEMVs of one
-    decoder layer of each kind plus 4096 LM-head rows, run by the oracle's
-    grouped GEMV at full (unsharded) size, scaled to the layer count and
-    vocabulary.  The GEMVs are > 95 % of a CPU decode step's time."""
-
-    HEAD_ROWS = 4096
-
-    def __init__(self, which):
-        from chpe_qwen35_hybrid_engine_b200.engine import QWEN25_72B, QWEN35_9B
-        g = QWEN25_72B if which == "decode_72b" else QWEN35_9B
-        self.g, self.q4 = g, which == "decode_72b"
-        self.group = 64 if self.q4 else 32
-        self.threads = os.cpu_count() or 1
-        H, F = g.hidden, g.ffn
-        kinds = {"attn": [(g.q_dim, H), (g.kv_dim, H), (g.kv_dim, H), (H, H)]}
-        if g.attn_every > 1:
-            kinds["ssm"] = [(g.ssm_qkv, H), (g.ssm_z, H), (H, g.ssm_z)]
-        n_attn = sum(1 for l in range(g.n_layers) if g.is_attn(l))
-        self.count = {"attn": n_attn, "ssm": g.n_layers - n_attn, "mlp": g.n_layers, "head": g.vocab / self.HEAD_ROWS}
-        kinds["mlp"] = [(F, H), (F, H), (H, F)]
-        kinds["head"] = [(self.HEAD_ROWS, H)]
-        rng = np.random.default_rng(0)
-        self.mats = {}
-        for kind, shapes in kinds.items():
-            lst = []
-            for n, k in shapes:
-                if self.q4:
-                    c = rng.integers(0, 16, (n, k), dtype=np.uint8)
-                    s = (0.0067 * np.exp(rng.normal(0, 0.25, (n, k // 64)))).astype(np.float16)
-                    z = rng.integers(6, 10, (n, k // 64)).astype(np.float16)
-                else:
-                    c = rng.integers(-127, 128, (n, k), dtype=np.int8)
-                    s = (0.02 / 127 * np.exp(rng.normal(0, 0.25, (n, k // 32)))).astype(np.float16)
-                    z = None
-                lst.append((c, s, z, rng.standard_normal((1, k)).astype(np.float32)))
-            self.mats[kind] = lst
-
-    def step_seconds(self):
-        """One sample: estimated seconds of one full decode step."""
-        from oracle import oracle as O
-        total = 0.0
-        for kind, lst in self.mats.items():
-            t0 = time.perf_counter()
-            for c, s, z, x in lst:
-                O.gemv_grouped(c, s, z, self.group, x, num_workers=self.threads)
-            total += (time.perf_counter() - t0) * self.count[kind]
-        return total
-
-    def describe(self, n):
-        return (f"{n} samples of one decode step: GEMVs of one layer of each kind + {self.HEAD_ROWS} LM-head rows at "
-                f"full size, scaled to {self.g.n_layers} layers and vocab {self.g.vocab} (C oracle, fp64 "
-                f"accumulation, {self.threads} threads)")
-
-
-def cpu_decode_sample(which, budget_s=10.0):
-    s = CpuDecodeSampler(which)
-    s.step_seconds()  # warm-up
-    t0 = time.perf_counter()
-    est = []
-    while not est or time.perf_counter() - t0 < budget_s:
-        est.append(s.step_seconds())
-    return statistics.median(est), s.threads, s.describe(len(est))
+def cpu_decode_baseline(which, budget_s=12.0):
+    """The reference engine's CPU decode step (oracle/cpu_baseline.c: the
+    src/engine.zig worker pool and row split, the x86 int8 kernels for the 9B
+    shape, the dotTileRow4Bit fp32 loop for the 4-bit 72B shape), whole steps,
+    with every host thread and with the reference's NUM_WORKERS = 8
+    (src/engine.zig:92)."""
+    from oracle import cpu_baseline as CB
+    nproc = os.cpu_count() or 1
+    res = {}
+    for th in sorted({nproc, 8}, reverse=True):
+        tok_s, n, desc = CB.sample(which, th, budget_s=budget_s / 2, min_steps=2)
+        res[th] = (tok_s, n, desc)
+    tok_s, n, desc = res[nproc]
+    return {"value": round(tok_s, 4), "unit": "tokens/s", "cores": nproc, "kind": "port", "sample": desc,
+            "cpu_model": CB.cpu_model(),
+            "by_threads": {str(t): {"tokens_s": round(v[0], 4), "steps": v[1]} for t, v in res.items()}}
 
 
 def run_reference(args, rank, world, workload):
-    """Reference arm: the reference path's CPU arithmetic (the oracle's C
-    restatement, all host threads) on rank 0; other ranks do nothing.  The Zig
-    reference itself needs a Zig 0.17-dev toolchain absent from this image."""
+    """Reference arm on rank 0 (other ranks do nothing): the reference's CPU
+    path with every host thread -- for the decode workloads the engine step
+    restated in C (oracle/cpu_baseline.c), whole steps; for the single GEMV /
+    prefill the oracle's grouped specification.  The Zig reference itself
+    needs a Zig 0.17-dev toolchain absent from this image."""
     if rank != 0:
         return None
     threads = os.cpu_count() or 1
@@ -717,19 +821,23 @@ def run_reference(args, rank, world, workload):
         cfg = c.describe()
         scaling = "weak"
     else:
-        s = CpuDecodeSampler(workload)
-        for _ in range(args.warmup):
-            s.step_seconds()
-        est = [s.step_seconds() for _ in range(args.steps)]
+        from oracle import cpu_baseline as CB
+        d = CB.CpuDecoder(workload, threads)
+        try:
+            for _ in range(min(args.warmup, 2)):  # the host needs no more than a step to warm up
+                d.step()
+            est = [d.step() for _ in range(args.steps)]
+            sample = d.describe(args.steps) + f"; model built in {d.build_s:.1f} s"
+        finally:
+            d.close()
         step = statistics.mean(est)
         value, unit, metric, ms = round(1.0 / step, 4), "tokens/s", DECODE_METRIC, step * 1e3
-        sample = s.describe(args.steps)
-        cfg = {"workload": workload, "global_batch": 1,
-               "tensor_parallel": world if workload == "decode_72b" else 1}
+        cfg = decode_config(workload, world)
         scaling = "strong" if workload == "decode_72b" else "weak"
     return {"impl": "reference", "metric": metric, "value": value, "unit": unit, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
-            "scaling": scaling, "vs_baseline": None, "dtype": "int codes x fp32 activations (fp64 accumulate)",
+            "scaling": scaling, "vs_baseline": None,
+            "dtype": "int codes; W8A8 int32 dots (9B) / fp32 4-bit loop (72B) / fp64 grouped spec (gemv, prefill)",
             "data": "synthetic (seeded)", "config": cfg,
             "cpu_baseline": {"value": value, "unit": unit, "cores": threads, "kind": "port", "sample": sample},
             "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -743,6 +851,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="decode_72b", choices=["decode_72b", "decode_9b", "gemv", "q8_gemv", "prefill"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-sweep", action="store_true", help="decode: skip the single-kernel configurations at N = 1")
     ap.add_argument("--bits", type=int, default=8, choices=[8, 4, 2], help="gemv: code width")
     ap.add_argument("--rows", type=int, default=12288, help="gemv: N (output columns)")
     ap.add_argument("--cols", type=int, default=4096, help="gemv: K (reduction length)")

@@ -39,6 +39,8 @@ struct chpe_ctx {
     std::vector<chpe_tensor *> owned;
     void *extra[4] = {nullptr, nullptr, nullptr, nullptr};  // scratch of the step helpers (mixers.cu)
     size_t extra_bytes[4] = {0, 0, 0, 0};
+    unsigned extra_gen[4] = {0, 0, 0, 0};   // reallocations of each slot
+    unsigned extra_seen[4] = {0, 0, 0, 0};  // the generation whose contents a helper has filled
 };
 
 namespace {
@@ -1383,7 +1385,11 @@ int chpe_ctx_scratch(chpe_ctx *ctx, int slot, size_t bytes, void **out) {
         CK(cudaMemset(ctx->extra[slot], 0, bytes));
         CK(cudaDeviceSynchronize());
         ctx->extra_bytes[slot] = bytes;
+        ++ctx->extra_gen[slot];
     }
     *out = ctx->extra[slot];
     return CHPE_OK;
 }
+unsigned chpe_ctx_scratch_generation(chpe_ctx *ctx, int slot) { return ctx->extra_gen[slot]; }
+unsigned chpe_ctx_scratch_seen(chpe_ctx *ctx, int slot) { return ctx->extra_seen[slot]; }
+void chpe_ctx_scratch_mark_seen(chpe_ctx *ctx, int slot) { ctx->extra_seen[slot] = ctx->extra_gen[slot]; }

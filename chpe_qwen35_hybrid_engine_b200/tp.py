@@ -113,13 +113,38 @@ class TensorParallelEngine:
 
     def capture(self, M: int):
         import torch
+        snap = self.eng._snapshot()
         st = torch.cuda.Stream(self.eng.dev)
         st.wait_stream(torch.cuda.current_stream(self.eng.dev))
         with torch.cuda.stream(st):
             self.step(M, st)
+        torch.cuda.synchronize(self.eng.dev)
+        self.eng._restore(snap)
         torch.cuda.synchronize(self.eng.dev)
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, stream=st):
             self.step(M, st)
         self.graphs[M] = g
         return g
+
+    def reset(self):
+        self.eng.reset()
+
+    def prefill(self, tokens, M: int = 8):
+        """Feed a context M positions at a time through the tensor-parallel step
+        (every rank runs the same steps; a last partial chunk runs eagerly)."""
+        import torch
+        b = self.eng.buf
+        toks = np.asarray(tokens, np.int32)
+        if M not in self.graphs:
+            self.capture(M)
+        i = 0
+        while i < len(toks):
+            n = min(M, len(toks) - i)
+            b["tokens"][:n].copy_(torch.from_numpy(toks[i:i + n]).to(self.eng.dev))
+            if n == M:
+                self.graphs[M].replay()
+            else:
+                self.step(n)
+            i += n
+        torch.cuda.synchronize(self.eng.dev)

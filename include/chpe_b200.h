@@ -330,7 +330,11 @@ int chpe_argmax_dev(chpe_ctx *ctx, const float *logits, int M, int n, int *idx, 
  * RoPE pairs element i with i + head_dim/2, angle = p / theta^(2i/head_dim);
  * scores are scaled by 1/sqrt(head_dim); query head h reads kv head
  * h / (q_heads / kv_heads).  M <= 8, head_dim <= 256, (q_heads / kv_heads) * M
- * <= 64.  A step past max_seq records an error (chpe_sync) and writes nothing. */
+ * <= 64.  A step past max_seq records an error (chpe_sync) and writes nothing.
+ * The RoPE factors are tabulated per (theta, head_dim, max_seq) in the
+ * context on first use (that first call synchronises the stream, so it must
+ * come before any stream capture); two launches: per kv head and split of 64
+ * positions the partial softmax, then per query head the combination. */
 int chpe_attn_decode_dev(chpe_ctx *ctx, const float *q, int ldq, const float *k, const float *v, int ldkv,
                          float *kcache, float *vcache, const int *pos, int M, int q_heads, int kv_heads,
                          int head_dim, int max_seq, float rope_theta, int gated, float *out, int ldo, void *stream);
@@ -345,7 +349,7 @@ int chpe_attn_decode_dev(chpe_ctx *ctx, const float *q, int ldq, const float *k,
  *   out [M][ldo]: y = q S per head (heads x value_dim)
  * Per row, in order: conv over the last 4 inputs of each channel, then
  * S = decay[h] * S + k^T v and y = q S.  key_dim 128, value_dim a multiple
- * of 32, M <= 13. */
+ * of 32, M <= 8. */
 int chpe_deltanet_step_dev(chpe_ctx *ctx, const float *qkv, int ldqkv, const float *conv_w, float *ring,
                            float *state, const float *decay, const int *pos, int M, int heads, int key_dim,
                            int value_dim, float *out, int ldo, void *stream);
