@@ -238,6 +238,39 @@ def gemv_step_profile(ctx, eng, M, reps, dev):
     return ms, nbytes, len(groups)
 
 
+def exchange_step_profile(tp, M, reps, world, dev):
+    """The tensor-parallel exchanges of one step alone -- the all-reduce after
+    O and after down of every layer and the LM head's argmax merge -- on the
+    step's comm object, captured as one graph and replayed `reps` times
+    (every rank replays the same sequence).  Returns ms per step, max over
+    ranks."""
+    import torch
+    H = tp.geom.hidden
+    part = torch.randn(M, H, device=dev)
+    hidden = torch.zeros(M, H, device=dev)
+    idx = torch.zeros(M, dtype=torch.int32, device=dev)
+    val = torch.zeros(M, device=dev)
+    st = torch.cuda.Stream(dev)
+    st.wait_stream(torch.cuda.current_stream(dev))
+
+    def issue():
+        for _ in range(2 * tp.geom.n_layers):
+            tp.comm.allreduce_residual(part, hidden, M * H, stream=st)
+        tp.comm.argmax_merge(idx, val, M, tp.v0, stream=st)
+
+    with torch.cuda.stream(st):
+        issue()
+    torch.cuda.synchronize(dev)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=st):
+        issue()
+    for _ in range(3):
+        graph.replay()
+    ms = timed_replays(graph.replay, reps, world, dev) / reps
+    del graph
+    return ms
+
+
 def decode_line(eng, stepper, M, args, world, dev, label, context_len, profile=True):
     """Graph-replayed greedy decode at M rows after a seeded context of
     context_len uniform token ids has been prefilled through the engine (8
@@ -256,7 +289,9 @@ def decode_line(eng, stepper, M, args, world, dev, label, context_len, profile=T
     b["tokens"][:M].copy_(torch.from_numpy(first).to(dev))
     snap = eng._snapshot()
     n0 = kernel_launches()
+    torch.cuda.nvtx.range_push(f"{label}_step")  # one eager step: the range a launch-list capture selects
     stepper.step(M)
+    torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize(dev)
     launches_per_step = kernel_launches() - n0
     eng._restore(snap)
@@ -304,6 +339,13 @@ def decode_line(eng, stepper, M, args, world, dev, label, context_len, profile=T
         gms = dist_max(gms, world)
         out.update({"gemv_ms_per_step": round(gms, 4), "gemv_bytes_per_step": int(gbytes),
                     "gemv_launches_per_step": glaunch, "gemv_gbs": round(gbytes / (gms * 1e-3) / 1e9, 1)})
+        # where the step's time goes (each part timed alone; "other" is the rest:
+        # fills, mixers, norms, argmax and the launch gaps between kernels)
+        bd = {"gemv_ms": round(gms, 4)}
+        if getattr(stepper, "comm", None) is not None:
+            bd["exchange_ms"] = round(exchange_step_profile(stepper, M, max(5, min(args.steps, 20)), world, dev), 4)
+        bd["other_ms"] = round(ms_step - gms - bd.get("exchange_ms", 0.0), 4)
+        out["breakdown"] = bd
     return out
 
 
@@ -313,26 +355,30 @@ def _decode_geometry(which, args):
     import dataclasses
     from chpe_qwen35_hybrid_engine_b200.engine import QWEN25_72B, QWEN35_9B
     base, ctx_len = (QWEN25_72B, 1024) if which == "decode_72b" else (QWEN35_9B, 512)
+    if args.context is not None:
+        ctx_len = max(8, args.context)
     need = ctx_len + 8 * (2 * (args.warmup + args.steps) + 8)
     return dataclasses.replace(base, mixer="real", max_seq=(need + 255) // 256 * 256), ctx_len
 
 
-def decode_config(which, world):
+def decode_config(which, world, ctx_len=None):
     """The `config` of a decode line (both arms)."""
+    if ctx_len is None:
+        ctx_len = 1024 if which == "decode_72b" else 512
     if which == "decode_72b":
         return {"workload": "decode_72b",
                 "model": "Qwen2.5-72B-shaped: 80 GQA layers, hidden 8192, FFN 29568 SwiGLU, 64/8 heads of 128, "
                          "vocab 152064",
                 "weights": "4-bit codes, fp16 scale + zero per 64 columns (seeded random codes and scales)",
                 "tensor_parallel": world, "global_batch": 1,
-                "context": "1024 seeded uniform token ids prefilled through the engine (RoPE, fp32 KV cache); "
+                "context": f"{ctx_len} seeded uniform token ids prefilled through the engine (RoPE, fp32 KV cache); "
                            "decode continues from there",
                 "parallelism": f"tp{world}", "l2": "40 GB / N of weights per step >> 126 MB L2"}
     return {"workload": "decode_9b",
             "model": "Qwen3.5-9B-shaped hybrid: 24 Gated DeltaNet + 8 gated GQA layers, hidden 4096, FFN 12288, "
                      "vocab 151936",
             "weights": "8-bit codes, fp16 scale per 32 columns (random-init N(0,0.02))",
-            "context": "512 seeded uniform token ids prefilled through the engine",
+            "context": f"{ctx_len} seeded uniform token ids prefilled through the engine",
             "global_batch": world, "parallelism": f"replicas{world}", "l2": "7 GB of weights per step >> 126 MB L2"}
 
 
@@ -358,7 +404,7 @@ def run_decode(args, rank, world, local_rank, which):
         if tp.comm is not None:
             tp.comm.close()
         del tp
-        config = decode_config(which, world)
+        config = decode_config(which, world, ctx_len)
         scaling, units = "strong", 1
     else:
         eng, _ = build_random(ctx, geom, "q8g32", seed=rank, max_rows=8)
@@ -366,7 +412,7 @@ def run_decode(args, rank, world, local_rank, which):
         main = decode_line(eng, eng, 1, args, world, dev, "9b_b1", ctx_len)
         clk.stop()
         del eng
-        config = decode_config(which, world)
+        config = decode_config(which, world, ctx_len)
         scaling, units = "weak", world
     ctx.close()
     torch.cuda.empty_cache()
@@ -852,6 +898,8 @@ def main():
     ap.add_argument("--workload", default="decode_72b", choices=["decode_72b", "decode_9b", "gemv", "q8_gemv", "prefill"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-sweep", action="store_true", help="decode: skip the single-kernel configurations at N = 1")
+    ap.add_argument("--context", type=int, default=None,
+                    help="decode: context tokens prefilled before the timed steps (default 1024 for 72B, 512 for 9B)")
     ap.add_argument("--bits", type=int, default=8, choices=[8, 4, 2], help="gemv: code width")
     ap.add_argument("--rows", type=int, default=12288, help="gemv: N (output columns)")
     ap.add_argument("--cols", type=int, default=4096, help="gemv: K (reduction length)")

@@ -387,7 +387,7 @@ int gemv_core(chpe_ctx *ctx, const DevMatrix &w0, const DevMatrix *w1, int mode,
               int accumulate, const float *scale_override0, const float *scale_override1, cudaStream_t st,
               const XSrc *src = nullptr) {
     GemvPlan P;
-    plan_gemv(w0, f.M, mode, f.xsplit, &P);
+    plan_gemv(w0, f.M, mode, f.xsplit, &P, src == nullptr);
     int rc = check_frag(ctx, w0, P, f);
     if (rc) return rc;
     if ((rc = ensure_scratch(ctx, P, st))) return rc;
@@ -427,7 +427,7 @@ int gemv_multi_core(chpe_ctx *ctx, const DevMatrix *const *ms, int n, const Xfra
     cat.n_strips = total_sg * kSG;
     cat.N = cat.n_strips * kStripRows;
     GemvPlan P;
-    plan_gemv(cat, f.M, 0, f.xsplit, &P);
+    plan_gemv(cat, f.M, 0, f.xsplit, &P, src == nullptr);
     int rc = check_frag(ctx, w0, P, f);
     if (rc) return rc;
     if ((rc = ensure_scratch(ctx, P, st))) return rc;
@@ -1123,6 +1123,36 @@ extern "C" int chpe_xfrag_fill_op_dev(chpe_ctx *ctx, chpe_xfrag *xf, const chpe_
     if (f.layout != kLayoutF16) return fail(ctx, CHPE_EINVAL, "fused fill of int8 fragments needs fp32 rows");
     e = launch_xfill_f16(s, f.M, f.K, f.Kp, f.e_cols, f.xsplit, f.bits, f.xf, f.xs, f.xe, st);
     if (e != cudaSuccess) return fail(ctx, CHPE_ECUDA, "xfrag fill: %s", cudaGetErrorString(e));
+    return CHPE_OK;
+}
+
+int comm_fill_exchange(chpe_comm *c, const float *part, float *hidden, size_t n, FillExchange *out);
+chpe_ctx *comm_ctx(const chpe_comm *c);
+
+extern "C" int chpe_allreduce_fill_dev(chpe_comm *comm, const float *part, float *hidden, chpe_xfrag *xf,
+                                       const float *gamma, float eps, void *stream) {
+    chpe_ctx *ctx = comm_ctx(comm);
+    if (!ctx || !part || !hidden || !xf || !gamma) return fail(ctx, CHPE_EINVAL, "null argument");
+    const Xfrag &f = xf->f;
+    if (f.layout != kLayoutF16 || f.x_dtype != CHPE_X_F32 || xf->xrow)
+        return fail(ctx, CHPE_ENOTSUP, "fused exchange: fp32 fragments of an fp16-operand tensor without outliers");
+    FillExchange ex;
+    const int rc = comm_fill_exchange(comm, part, hidden, (size_t)f.M * f.K, &ex);
+    if (rc == CHPE_ETIMEOUT) return fail(ctx, rc, "comm object failed: reset it on every rank first");
+    if (rc != CHPE_OK) return fail(ctx, rc, "fused exchange refused");
+    if (!xfill_exchange_fits(f.M, f.Kp, ex.max_chunks))
+        return fail(ctx, CHPE_ENOTSUP, "fused exchange: %d rows of %d columns do not fit", f.M, f.K);
+    XSrc s;
+    s.op = kXRmsnorm;
+    s.x = hidden;
+    s.dt = CHPE_X_F32;
+    s.ldx = f.K;
+    s.aux = gamma;
+    s.ld_aux = f.K;
+    s.eps = eps;
+    const cudaError_t e = launch_xfill_f16(s, f.M, f.K, f.Kp, f.e_cols, f.xsplit, f.bits, f.xf, f.xs, f.xe,
+                                           static_cast<cudaStream_t>(stream), &ex);
+    if (e != cudaSuccess) return fail(ctx, CHPE_ECUDA, "fused exchange fill: %s", cudaGetErrorString(e));
     return CHPE_OK;
 }
 

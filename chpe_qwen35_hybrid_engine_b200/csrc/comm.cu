@@ -41,25 +41,9 @@
 namespace chpe {
 namespace {
 
-constexpr int kCommMaxRanks = 8;
 constexpr int kCommThreads = 256;
 constexpr int kCommChunk = 1024;  // floats per CTA
-constexpr int kErrCommWait = 31;
-constexpr int kErrCommFailed = 32;  // an all-reduce issued on a comm object that failed before
 
-__device__ __forceinline__ void st_release_sys(unsigned *p, unsigned v) {
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned *p) {
-    unsigned v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-
-struct CommPeers {
-    float *recv[kCommMaxRanks];      // each rank's receive area (peer mappings; own one locally)
-    unsigned *flags[kCommMaxRanks];  // each rank's flags [world][max_chunks]
-};
 
 __global__ void __launch_bounds__(kCommThreads) chpe_allreduce_residual_kernel(const CommPeers peers, int world, int rank,
                                                                           size_t slot_elems, int max_chunks,
@@ -96,18 +80,7 @@ __global__ void __launch_bounds__(kCommThreads) chpe_allreduce_residual_kernel(c
         st_release_sys(peers.flags[threadIdx.x] + (size_t)rank * max_chunks + c, epoch);
     // 3. wait for every peer's flag of this chunk (bounded)
     if (threadIdx.x < world && threadIdx.x != rank) {
-        const unsigned *f = peers.flags[rank] + (size_t)threadIdx.x * max_chunks + c;
-        const unsigned long long t0 = global_timer_ns();
-        bool ok = false;
-        while (true) {
-            if ((int)(ld_acquire_sys(f) - epoch) >= 0) {
-                ok = true;
-                break;
-            }
-            if (global_timer_ns() - t0 > kWaitTimeoutNs) break;
-            __nanosleep(32);
-        }
-        if (!ok) {
+        if (!wait_flag_bounded(peers.flags[rank] + (size_t)threadIdx.x * max_chunks + c, epoch)) {
             atomicExch(err, kErrCommWait);
             atomicExch(&ctr[2], 1u);  // failed: no later exchange on this object until a reset
             *host_failed = 1u;
@@ -133,6 +106,82 @@ __global__ void __launch_bounds__(kCommThreads) chpe_allreduce_residual_kernel(c
             if (!atomicAdd(&ctr[2], 0u)) ctr[0] = epoch;
         }
     }
+}
+
+// The vocabulary-split LM head's argmax: every rank holds, for each of M
+// rows, the (max value, index) of its shard; afterwards every rank holds the
+// global pair -- the largest value, ties to the smaller global index, as
+// src/engine.zig:1098-1110 computeArgmax breaks them within one shard.  One
+// CTA, the same exchange protocol as the all-reduce on chunk 0 of the receive
+// area (an exchange epoch of its own): thread m < M pushes row m's pair into
+// slot [epoch & 1][rank] of every peer, thread r raises flag [rank][0] at peer
+// r, waits (bounded) for peer r's flag, then thread m merges the pairs in rank
+// order.  A slot is rewritten two epochs later only: the exchange between
+// them needs every peer's flag, raised after that peer's previous kernel --
+// the one that read the slot -- has finished (stream order).
+__global__ void __launch_bounds__(32) chpe_argmax_merge_kernel(const CommPeers peers, int world, int rank,
+                                                               size_t slot_elems, int max_chunks,
+                                                               int *__restrict__ idx, float *__restrict__ maxv,
+                                                               int M, int index_base, unsigned *__restrict__ ctr,
+                                                               volatile unsigned *host_failed,
+                                                               int *__restrict__ err) {
+    __shared__ int s_ok;
+    pdl_begin();  // the local argmax is the previous kernel's output
+    if (*reinterpret_cast<volatile unsigned *>(&ctr[2])) {
+        if (threadIdx.x == 0) atomicExch(err, kErrCommFailed);
+        return;
+    }
+    const unsigned epoch = ctr[0] + 1u;
+    const int m = threadIdx.x;
+    if (m == 0) s_ok = 1;
+    float v = 0.0f;
+    int gi = 0;
+    if (m < M) {
+        v = maxv[m];
+        gi = idx[m] + index_base;
+    }
+    const size_t slot = ((size_t)(epoch & 1u) * world + rank) * slot_elems;
+    if (m < M)
+        for (int r = 0; r < world; ++r) {
+            if (r == rank) continue;
+            reinterpret_cast<float2 *>(peers.recv[r] + slot)[m] = make_float2(v, __int_as_float(gi));
+        }
+    __syncthreads();
+    if (m < world && m != rank) {
+        st_release_sys(peers.flags[m] + (size_t)rank * max_chunks, epoch);
+        if (!wait_flag_bounded(peers.flags[rank] + (size_t)m * max_chunks, epoch)) {
+            atomicExch(err, kErrCommWait);
+            atomicExch(&ctr[2], 1u);
+            *host_failed = 1u;
+            s_ok = 0;
+        }
+    }
+    __syncthreads();
+    if (s_ok && m < M) {
+        const float2 *own = reinterpret_cast<const float2 *>(peers.recv[rank] + (size_t)(epoch & 1u) * world * slot_elems);
+        float bv = 0.0f;
+        int bi = 0;
+        for (int r = 0; r < world; ++r) {
+            float rv;
+            int ri;
+            if (r == rank) {
+                rv = v;
+                ri = gi;
+            } else {
+                const float2 q = own[(size_t)r * (slot_elems / 2) + m];
+                rv = q.x;
+                ri = __float_as_int(q.y);
+            }
+            if (r == 0 || rv > bv || (rv == bv && ri < bi)) {
+                bv = rv;
+                bi = ri;
+            }
+        }
+        idx[m] = bi;
+        maxv[m] = bv;
+    }
+    __syncthreads();
+    if (m == 0 && !atomicAdd(&ctr[2], 0u)) ctr[0] = epoch;
 }
 
 }  // namespace
@@ -245,6 +294,44 @@ extern "C" int chpe_allreduce_residual_dev(chpe_comm *c, const float *part, floa
                                chpe_ctx_error_word(c->ctx));
     return e == cudaSuccess ? CHPE_OK : CHPE_ECUDA;
 }
+
+extern "C" int chpe_argmax_merge_dev(chpe_comm *c, int *idx, float *maxv, int M, int index_base, void *stream) {
+    if (!c || !idx || !maxv) return CHPE_EINVAL;
+    if (M < 1 || M > 32 || (size_t)2 * M > c->max_elems) return CHPE_EINVAL;
+    for (int r = 0; r < c->world; ++r)
+        if (!c->peers.recv[r] || !c->peers.flags[r]) return CHPE_ENOENT;
+    if (*reinterpret_cast<volatile unsigned *>(c->host_failed)) return CHPE_ETIMEOUT;
+    cudaError_t e = launch_pdl(chpe_argmax_merge_kernel, dim3(1), dim3(32), 0, static_cast<cudaStream_t>(stream),
+                               c->peers, c->world, c->rank, c->max_elems, c->max_chunks, idx, maxv, M, index_base,
+                               c->epoch, c->host_failed_dev, chpe_ctx_error_word(c->ctx));
+    return e == cudaSuccess ? CHPE_OK : CHPE_ECUDA;
+}
+
+// The exchange state a fused fill needs (launch_xfill_f16): refuses like
+// chpe_allreduce_residual_dev, and with CHPE_ENOTSUP when n partials do not
+// fit the receive area.
+int comm_fill_exchange(chpe_comm *c, const float *part, float *hidden, size_t n, FillExchange *out) {
+    if (!c || !part || !hidden || !out) return CHPE_EINVAL;
+    if (n > c->max_elems) return CHPE_ENOTSUP;
+    for (int r = 0; r < c->world; ++r)
+        if (!c->peers.recv[r] || !c->peers.flags[r]) return CHPE_ENOENT;
+    if (*reinterpret_cast<volatile unsigned *>(c->host_failed)) return CHPE_ETIMEOUT;
+    FillExchange ex;
+    ex.peers = c->peers;
+    ex.world = c->world;
+    ex.rank = c->rank;
+    ex.slot_elems = c->max_elems;
+    ex.max_chunks = c->max_chunks;
+    ex.part = part;
+    ex.hidden = hidden;
+    ex.ctr = c->epoch;
+    ex.host_failed = c->host_failed_dev;
+    ex.err = chpe_ctx_error_word(c->ctx);
+    *out = ex;
+    return CHPE_OK;
+}
+
+chpe_ctx *comm_ctx(const chpe_comm *c) { return c ? c->ctx : nullptr; }
 
 extern "C" int chpe_comm_failed(const chpe_comm *c) {
     if (!c) return CHPE_EINVAL;

@@ -260,6 +260,28 @@ cudaError_t launch_pdl_cluster(void (*kern)(KArgs...), dim3 grid, dim3 block, un
 // does the same (the oracle's, on the host) gets the same bits.  The W8A8
 // path re-quantizes every activation row to int8, where a last-bit
 // difference can flip a rounding and grow from there.
+// Flags between GPUs (tensor-parallel exchanges): a system-scope release
+// store after this thread's (and, through a preceding barrier, its block's)
+// writes to peer memory, and the matching acquire load.
+__device__ __forceinline__ void st_release_sys(unsigned *p, unsigned v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned *p) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+// Waits until *f - epoch >= 0 (wrapping), at most kWaitTimeoutNs; false when
+// the time ran out.
+__device__ __forceinline__ bool wait_flag_bounded(const unsigned *f, unsigned epoch) {
+    const unsigned long long t0 = global_timer_ns();
+    while (true) {
+        if ((int)(ld_acquire_sys(f) - epoch) >= 0) return true;
+        if (global_timer_ns() - t0 > kWaitTimeoutNs) return false;
+        __nanosleep(32);
+    }
+}
+
 __device__ __forceinline__ float exp_rn(float x) { return (float)exp((double)x); }
 __device__ __forceinline__ float silu_f(float g) { return __fdiv_rn(g, __fadd_rn(1.0f, exp_rn(-g))); }
 

@@ -35,7 +35,7 @@ static int epilogue_cols(const DevMatrix &w) {
     return std::min(grp, kc);
 }
 
-int plan_gemv(const DevMatrix &w, int M, int mode, bool xsplit, GemvPlan *plan) {
+int plan_gemv(const DevMatrix &w, int M, int mode, bool xsplit, GemvPlan *plan, bool allow_xstream) {
     GemvPlan P;
     P.mode = mode;
     P.xsplit = xsplit;
@@ -51,13 +51,38 @@ int plan_gemv(const DevMatrix &w, int M, int mode, bool xsplit, GemvPlan *plan) 
     // Fewest K-slices whose activation fragments fit the staging budget, with
     // equal slices; the work counters balance the work, not the slicing.
     int n_ks = std::min(ceil_div(w.n_blocks, std::min(bpk_max, w.n_blocks)), kMaxKs);
+    // More than two rows: the activations of all of K rarely fit beside a ring
+    // with room for two CTAs per SM, and K-slices cost partial sums.  Instead
+    // every ring stage can bring its block's activations along with its
+    // weights (re-read from L2 by each strip group): one K-slice, a ring of 3
+    // stages -- 2 when 3 would not let two CTAs share an SM.  Resident
+    // activations stay where they fit two CTAs per SM in one K-slice, and on
+    // matrices of fewer strip groups than half the SMs, which only K-slices
+    // spread over the GPU (measured on B200 at M = 4 and 8, Q4 and Q8,
+    // 1024..151936 rows, 4096..29568 columns).
+    P.sms = num_sms();
+    if (M > 2 && allow_xstream) {
+        const int bpk_res = ceil_div(w.n_blocks, n_ks);
+        const bool res_fits = ceil_div(w.n_blocks, bpk_res) == 1 &&
+                              smem_layout(w.layout, w.bits, bpk_res, M, xsplit, P.e_cols, w.block_bytes).total <=
+                                  kTwoCtaBytes;
+        if (!res_fits && 2 * P.n_sg >= P.sms) {
+            P.xstream = 1;
+            n_ks = 1;
+            P.nstages = 3;
+            if (smem_layout(w.layout, w.bits, w.n_blocks, M, xsplit, P.e_cols, w.block_bytes, 1, 3).total >
+                kTwoCtaBytes)
+                P.nstages = 2;
+        }
+    }
     const int bpk = ceil_div(w.n_blocks, n_ks);
     n_ks = ceil_div(w.n_blocks, bpk);
-    const size_t smem = smem_layout(w.layout, w.bits, bpk, M, xsplit, P.e_cols, w.block_bytes).total;
-    // at most two CTAs per SM (the kernel's registers: __launch_bounds__(kThreads, 2))
-    const int per_sm = std::max(1, (int)std::min<size_t>(2, kSmemBudget / (smem + 1024)));
+    const size_t smem =
+        smem_layout(w.layout, w.bits, bpk, M, xsplit, P.e_cols, w.block_bytes, P.xstream, P.nstages).total;
+    // at most two CTAs per SM (the kernel's registers: __launch_bounds__(kThreads, 2));
+    // each CTA also takes 1 KB of the SM's shared memory for itself
+    const int per_sm = std::max(1, (int)std::min<size_t>(2, kSmemPerSm / (smem + 1024)));
     const int nb_last = w.n_blocks - (n_ks - 1) * bpk;
-    P.sms = num_sms();
     // upper bound here; the launch recomputes the grid from the kernel's occupancy
     long gk = (long)P.sms * per_sm / n_ks;
     // at least ~4 blocks of work per CTA: small matrices get fewer CTAs
@@ -76,17 +101,22 @@ int plan_gemv(const DevMatrix &w, int M, int mode, bool xsplit, GemvPlan *plan) 
     long rounds = per_cta * 7 / (10 * bpk);
     if (rounds >= 2 && per_cta - rounds * bpk < bpk) --rounds;
     P.n_whole = (int)std::min<long>(P.n_sg, rounds * gk);
-    // More than two rows: one CTA per SM, each with many blocks of work, so
-    // whole strip groups alone balance well enough; partial sums only across
-    // K-slices, summed by chpe_qgemv_reduce_kernel.
+    // More than two rows, partial sums are summed by chpe_qgemv_reduce_kernel
+    // after the GEMV (an arrival count per unit measured slower).  Resident
+    // activations: whole strip groups alone (mostly one CTA per SM with many
+    // blocks of work), partial sums only across K-slices.  Streamed
+    // activations: whole strip groups alone where K is short (at most 8
+    // blocks) or where they give the CTAs of each SM about one unit in all,
+    // otherwise the rounds of whole strip groups plus chunks.
     if (M > 2) {
         P.rmode = 1;
-        P.n_whole = P.n_sg;
+        if (!P.xstream || w.n_blocks <= 8 || (2 * P.n_sg >= gk && P.n_sg <= gk)) P.n_whole = P.n_sg;
     }
     P.cfull = ceil_div(bpk, P.bc);
     P.ctot = std::max((n_ks - 1) * P.cfull + ceil_div(nb_last, P.bc), n_ks);
     // static units cover the ring's first fill (fetched before the upstream kernel ends)
-    P.pref = ceil_div(kStages, P.bc);
+    P.pref = ceil_div(P.nstages, P.bc);
+    if (n_ks == 1 && P.n_whole == P.n_sg) P.ctot = 1;  // every unit covers all of K: no partial sums
     P.items_min = slice_units(P.n_sg, P.n_whole, ceil_div(nb_last, P.bc));
     gk = std::min<long>(gk, P.items_min);
     P.n_ks = n_ks;

@@ -43,7 +43,7 @@
 namespace chpe {
 
 constexpr int kNW = 8;      // MMA warps per CTA (one chunk of each block)
-constexpr int kStages = 3;  // ring depth (blocks per strip)
+constexpr int kStages = 3;  // ring depth (blocks per strip); 2 when a stream's stages carry activations
 constexpr int kProducerWarp = kNW, kEpilogueWarp = kNW + 1;
 constexpr int kThreads = (kNW + 2) * 32;
 // activation fragments staged per CTA: small enough for two CTAs per SM at
@@ -52,7 +52,9 @@ constexpr int kThreads = (kNW + 2) * 32;
 // as much of K as fits (fewer K-slices, fewer partials)
 constexpr int kXMaxBytes = 40 * 1024;
 constexpr int kXMaxBytesWide = 100 * 1024;
+constexpr size_t kTwoCtaBytes = 112 * 1024;  // dynamic shared memory of a CTA that shares its SM with another
 constexpr int kSmemBudget = 220 * 1024;
+constexpr size_t kSmemPerSm = 228 * 1024;  // shared memory of one SM, the CTAs' reserved 1 KB included
 static_assert(kNW == kChunksPerBlock, "one block per stage, one chunk per warp");
 
 // 16 bytes of zeros: the activation operand of MMA columns past the last row
@@ -60,7 +62,9 @@ constexpr size_t kZeroSlot = 496;
 
 struct SmemLayout {
     size_t bar, tags, ring, xf, xs, red, info, xe, total;
-    int nbuf;  // accumulator hand-off buffers (2 or 4)
+    size_t stage;    // bytes of one ring stage
+    size_t sx, sxs;  // streamed activations: offsets of a stage's fragments and block sums
+    int nbuf;        // accumulator hand-off buffers (2 or 4)
 };
 
 // Hand-off of one finished unit from the MMA warps to the epilogue warp.
@@ -79,8 +83,13 @@ __host__ __device__ inline size_t xfrag_bytes_per_block(int layout, int bits, in
     return (size_t)kChunksPerBlock * steps * M * 32 * (xsplit ? 2 : 1);
 }
 
+// Shared memory of one CTA.  Resident activations (xstream 0): the ring holds
+// weights only and the CTA's K-slice of fragments and block sums sits in
+// xf / xs.  Streamed activations (xstream 1): each ring stage carries, behind
+// the block's weights, that block's fragments and block sums, and nothing is
+// resident -- a CTA then covers all of K with no partial sums.
 __host__ __device__ inline SmemLayout smem_layout(int layout, int bits, int bpk, int M, bool xsplit, int e_cols,
-                                                  int block_bytes) {
+                                                  int block_bytes, int xstream = 0, int nstages = kStages) {
     SmemLayout L;
     // hand-off buffers: four at M <= 2 (the epilogue warp may spend an L2
     // round trip per unit without holding up the MMA warps), two above
@@ -90,12 +99,17 @@ __host__ __device__ inline SmemLayout smem_layout(int layout, int bits, int bpk,
     size_t o = 512;
     static_assert((2 * kStages + 1 + 2 * kMaxRedBufs) * 8 <= 256 && 256 + 3 * kStages * 4 <= kZeroSlot,
                   "barrier / tag area");
+    const size_t xblk = xfrag_bytes_per_block(layout, bits, M, xsplit);
+    const size_t xsblk = layout == kLayoutF16 ? (size_t)kChunksPerBlock * ((256 / bits) / e_cols) * 32 : 0;
+    L.sx = align_up((size_t)kSG * block_bytes, 128);
+    L.sxs = align_up(L.sx + xblk, 128);
+    L.stage = xstream ? align_up(L.sxs + xsblk, 128) : (size_t)kSG * block_bytes;
     L.ring = o;
-    o += align_up((size_t)kStages * kSG * block_bytes, 128);
+    o += align_up((size_t)nstages * L.stage, 128);
     L.xf = o;
-    o = align_up(o + (size_t)bpk * xfrag_bytes_per_block(layout, bits, M, xsplit), 128);
+    if (!xstream) o = align_up(o + (size_t)bpk * xblk, 128);
     L.xs = o;
-    if (layout == kLayoutF16) o = align_up(o + (size_t)bpk * kChunksPerBlock * ((256 / bits) / e_cols) * 32, 128);
+    if (!xstream && layout == kLayoutF16) o = align_up(o + (size_t)bpk * xsblk, 128);
     L.red = o;  // nbuf buffers of per-warp accumulators [warp][strip][16 rows][M]
     o += (size_t)L.nbuf * kNW * kSG * 16 * M * 4;
     L.info = o;
@@ -135,8 +149,8 @@ __host__ __device__ inline Unit unit_of(int u, int nbk, int C, int ks, int n_ks,
 }
 __host__ __device__ inline int slice_units(int n_sg, int n_whole, int C) { return n_whole + (n_sg - n_whole) * C; }
 // Static units per CTA: enough blocks to fill the ring before the first draw.
-__host__ __device__ inline int static_units(int n_whole, int Gk, int nbk, int pref) {
-    return n_whole >= Gk ? (kStages + nbk - 1) / nbk : pref;
+__host__ __device__ inline int static_units(int n_whole, int Gk, int nbk, int pref, int nstages) {
+    return n_whole >= Gk ? (nstages + nbk - 1) / nbk : pref;
 }
 __host__ __device__ inline int grabs_total(int U, int pref, int Gk) { return (U > pref * Gk ? U - pref * Gk : 0) + Gk; }
 
@@ -462,10 +476,12 @@ __global__ void __launch_bounds__(kThreads, 2) chpe_qgemv_kernel(const GemvParam
     const int nb = b1 - b0;
     const int C = unit_chunks(nb, p.bc);                      // chunks per chunked strip group in this slice
     const int U = slice_units(p.n_sg, p.n_whole, C);          // units of this slice
-    const int PS = static_units(p.n_whole, Gk, nb, p.pref);  // static units per CTA
+    const int NS = p.nstages;                                 // ring stages (2 or 3)
+    const int PS = static_units(p.n_whole, Gk, nb, p.pref, NS);  // static units per CTA
     const int M = p.M;
     const int BB = p.block_bytes;
-    const SmemLayout L = smem_layout(LAYOUT, BITS, p.bpk, M, XSPLIT, E, BB);
+    const bool XS = p.xstream != 0;  // activations stream through the ring with the weights
+    const SmemLayout L = smem_layout(LAYOUT, BITS, p.bpk, M, XSPLIT, E, BB, p.xstream, NS);
 
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + L.bar);
     uint64_t *empty = full + kStages;
@@ -481,7 +497,7 @@ __global__ void __launch_bounds__(kThreads, 2) chpe_qgemv_kernel(const GemvParam
 
     if (threadIdx.x == 0) {
 #pragma unroll
-        for (int s = 0; s < kStages; ++s) {
+        for (int s = 0; s < NS; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], kNW);
         }
@@ -510,11 +526,30 @@ __global__ void __launch_bounds__(kThreads, 2) chpe_qgemv_kernel(const GemvParam
         const int n_grabs = grabs_total(U, PS, Gk);
         int it = 0, slot = 0, use = 0;  // ring position: items issued, slot, pass
         bool x_issued = false;
+        const uint32_t xblk = (uint32_t)xfrag_bytes_per_block(LAYOUT, BITS, M, XSPLIT);
+        const uint32_t xsblk = LAYOUT == kLayoutF16 ? (uint32_t)(kChunksPerBlock * NE * 32) : 0u;
+        int armed = 0;  // stages armed so far (their activations follow the upstream wait)
+        // Streamed activations of block bi of the slice into ring slot sl (lanes
+        // kSG and kSG + 1; only once the upstream grid has finished).
+        auto copy_xblock = [&](int sl, int bi) {
+            uint8_t *st = smem + L.ring + (size_t)sl * L.stage;
+            const size_t b = (size_t)(b0 + bi);
+            if (lane == kSG) bulk_g2s(st + L.sx, static_cast<const uint8_t *>(p.xf) + b * xblk, xblk, &full[sl]);
+            if (LAYOUT == kLayoutF16 && lane == kSG + 1)
+                bulk_g2s(st + L.sxs, reinterpret_cast<const uint8_t *>(p.xs) + b * xsblk, xsblk, &full[sl]);
+        };
         // After the upstream grid has finished: the activations (unless the
         // MMA warps build them) and, from then on, the work counter.
         auto issue_x = [&]() {
             grid_dependency_wait();
             x_issued = true;
+            if (XS) {
+                // the stages armed before the wait still miss their activations
+                // (at most NS of them, slots 0 .. it-1 of the first pass)
+                __syncwarp();
+                for (int q = 0; q < armed && q < NS; ++q) copy_xblock(q, tag_blk[q]);
+                return;
+            }
             if (p.fused || lane != 0) return;
             const uint32_t xb = (uint32_t)(nb * xfrag_bytes_per_block(LAYOUT, BITS, M, XSPLIT));
             uint32_t tx = xb;
@@ -561,7 +596,8 @@ __global__ void __launch_bounds__(kThreads, 2) chpe_qgemv_kernel(const GemvParam
                 valid = r.valid;
                 if (valid) src = p.src[r.r].codes + ((size_t)r.strip * p.n_blocks + b0 + un.bs) * BB;
             }
-            const uint32_t tx = (uint32_t)__popc(__ballot_sync(0xffffffffu, valid)) * (uint32_t)BB;
+            const uint32_t tx = (uint32_t)__popc(__ballot_sync(0xffffffffu, valid)) * (uint32_t)BB +
+                                (XS ? xblk + xsblk : 0u);
             uint8_t *dst = smem + L.ring + (size_t)lane * BB;
             for (int bi = un.bs; bi < un.be; ++bi, ++it) {
                 // the next unit's draw goes out with the first copy of this one,
@@ -580,14 +616,16 @@ __global__ void __launch_bounds__(kThreads, 2) chpe_qgemv_kernel(const GemvParam
                 }
                 __syncwarp();
                 if (valid)
-                    bulk_g2s_hint(dst + (size_t)slot * kSG * BB, src + (size_t)(bi - un.bs) * BB, (uint32_t)BB,
+                    bulk_g2s_hint(dst + (size_t)slot * L.stage, src + (size_t)(bi - un.bs) * BB, (uint32_t)BB,
                                   &full[slot], pol);
-                if (++slot == kStages) {
+                if (XS && x_issued) copy_xblock(slot, bi);
+                ++armed;
+                if (++slot == NS) {
                     slot = 0;
                     ++use;
                 }
                 // weights first, then (once) the upstream-dependent activations
-                if (!x_issued && it + 1 >= kStages) issue_x();
+                if (!x_issued && it + 1 >= NS) issue_x();
             }
         }
         if (!x_issued) issue_x();
@@ -598,11 +636,11 @@ __global__ void __launch_bounds__(kThreads, 2) chpe_qgemv_kernel(const GemvParam
             mbar_arrive(&full[slot]);
             ++it;
             // every issued copy has landed before the CTA may exit
-            for (int s = 0; s < kStages && s < it; ++s) {
-                const int last = s + ((it - 1 - s) / kStages) * kStages;
-                if (!mbar_wait_bounded(&full[s], (last / kStages) & 1)) atomicExch(p.err, kErrWaitFull);
+            for (int s = 0; s < NS && s < it; ++s) {
+                const int last = s + ((it - 1 - s) / NS) * NS;
+                if (!mbar_wait_bounded(&full[s], (last / NS) & 1)) atomicExch(p.err, kErrWaitFull);
             }
-            if (!p.fused && !mbar_wait_bounded(xbar, 0)) atomicExch(p.err, kErrWaitPrologue);
+            if (!p.fused && !XS && !mbar_wait_bounded(xbar, 0)) atomicExch(p.err, kErrWaitPrologue);
         }
     } else if (warp == kEpilogueWarp) {
         // ---------------- epilogue warp ----------------
@@ -685,23 +723,22 @@ __global__ void __launch_bounds__(kThreads, 2) chpe_qgemv_kernel(const GemvParam
         // past the last column read 16 zero bytes (stride 0) instead.
         constexpr bool PK = XM == 2;
         const bool has_x = g < (PK ? 2 * M : M);
-        const uint8_t *xb0;
-        uint32_t xstr;  // bytes per fragment unit (k-step, k-step pair, or S8 chunk)
+        uint32_t xlane;  // this lane's byte offset inside a fragment unit
+        uint32_t xstr;   // bytes per fragment unit (k-step, k-step pair, or S8 chunk)
         if (LAYOUT == kLayoutS8) {
-            xb0 = smem + L.xf + (g * 4 + t) * 8;
+            xlane = (g * 4 + t) * 8;
             xstr = (uint32_t)M * 32;
         } else if (PK) {
-            xb0 = smem + L.xf + ((g >> 1) * 4 + t) * 16 + (g & 1) * 8;
+            xlane = ((g >> 1) * 4 + t) * 16 + (g & 1) * 8;
             xstr = (uint32_t)M * 64;
         } else {
-            xb0 = smem + L.xf + (g * 4 + t) * 16;
+            xlane = (g * 4 + t) * 16;
             xstr = (uint32_t)M * 64;
         }
-        if (!has_x) {
-            xb0 = smem + kZeroSlot;
-            xstr = 0;
-        }
-        const float *xss = reinterpret_cast<const float *>(smem + L.xs);
+        if (!has_x) xstr = 0;
+        // resident activations: the slice's fragments; streamed: the stage's block
+        const uint8_t *xres = has_x ? smem + L.xf + xlane : smem + kZeroSlot;
+        const float *xss_res = reinterpret_cast<const float *>(smem + L.xs);
         float zc24[kSG];
 #pragma unroll
         for (int i = 0; i < kSG; ++i) zc24[i] = -p.src[source_of<MODE>(i)].zc * kTwoM24;
@@ -716,7 +753,7 @@ __global__ void __launch_bounds__(kThreads, 2) chpe_qgemv_kernel(const GemvParam
                                     b0, nb, KC * kChunksPerBlock);
             }
         }
-        if (!p.fused) {
+        if (!p.fused && !XS) {
             // A timed-out wait ends this warp's work; decisions are taken per warp
             // (__all_sync) and every wait is bounded, so no warp can be left stuck.
             if (!__all_sync(0xffffffffu, mbar_wait_bounded(xbar, 0))) {
@@ -759,8 +796,9 @@ __global__ void __launch_bounds__(kThreads, 2) chpe_qgemv_kernel(const GemvParam
             return true;
         };
 
-        for (int it = 0; !aborted; ++it) {
-            const int slot = it % kStages, use = it / kStages;
+        int slot = 0, use = 0;
+        for (;; ) {
+            if (aborted) break;
             if (!__all_sync(0xffffffffu, mbar_wait_bounded(&full[slot], use & 1))) {
                 if (lane == 0) atomicExch(p.err, kErrWaitFull);
                 aborted = true;
@@ -770,8 +808,11 @@ __global__ void __launch_bounds__(kThreads, 2) chpe_qgemv_kernel(const GemvParam
             if (sg < 0) break;
             const int bi = tag_blk[slot];
             const int flags = tag_flags[slot];
-            const uint8_t *stg = smem + L.ring + (size_t)slot * kSG * BB;
-            const int cs = bi * kChunksPerBlock + warp;  // chunk in slice
+            const uint8_t *stg = smem + L.ring + (size_t)slot * L.stage;
+            // chunk of the activations' array: in the slice (resident) or in the stage's block (streamed)
+            const int cs = XS ? warp : bi * kChunksPerBlock + warp;
+            const uint8_t *xb0 = XS ? (has_x ? stg + L.sx + xlane : smem + kZeroSlot) : xres;
+            const float *xss = XS ? reinterpret_cast<const float *>(stg + L.sxs) : xss_res;
             uint4 wv[kSG];
 #pragma unroll
             for (int i = 0; i < kSG; ++i)
@@ -852,6 +893,10 @@ __global__ void __launch_bounds__(kThreads, 2) chpe_qgemv_kernel(const GemvParam
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);
+            if (++slot == NS) {
+                slot = 0;
+                ++use;
+            }
             if (flags & kLast) {
                 if (!hand_off(sg, flags >> 1)) {
                     aborted = true;
@@ -897,6 +942,8 @@ cudaError_t launch_gemv_t(const GemvPlan &plan, const GemvParams &p_in, cudaStre
     GemvParams p = p_in;
     p.gk = (int)gk;
     p.rmode = plan.rmode;
+    p.xstream = plan.xstream;
+    p.nstages = plan.nstages;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)(gk * plan.n_ks));
     cfg.blockDim = dim3(kThreads);

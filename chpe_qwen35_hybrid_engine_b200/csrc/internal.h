@@ -48,6 +48,31 @@ struct XSrc {
     int kv_dim = 1, head_dim = 0, group = 1;  // attention stand-in
     int qkv_dim = 1, silu_on_qkv = 0;         // Gated-DeltaNet stand-in
 };
+// Tensor-parallel exchange (comm.cu): the peers' receive areas and flags as
+// this rank sees them.
+constexpr int kCommMaxRanks = 8;
+constexpr int kErrCommWait = 31;
+constexpr int kErrCommFailed = 32;  // an exchange issued on a comm object that failed before
+struct CommPeers {
+    float *recv[kCommMaxRanks];      // each rank's receive area [2][world][slot_elems] (peer mappings; own one locally)
+    unsigned *flags[kCommMaxRanks];  // each rank's flags [world][max_chunks]
+};
+// An all-reduce of partial sums fused in front of a fragment fill: before the
+// fill reads row tok of x (= hidden), each fill CTA sums its columns of the
+// ranks' partials [M][K] into hidden (same protocol and arithmetic as the
+// one-shot all-reduce; chunk = tok * ctas per row + cta).  world = 0: none.
+struct FillExchange {
+    CommPeers peers;
+    int world = 0, rank = 0;
+    size_t slot_elems = 0;
+    int max_chunks = 0;
+    const float *part = nullptr;  // this rank's partials [M][K]
+    float *hidden = nullptr;      // [M][K], += the sum of the ranks' partials (the fill's x)
+    unsigned *ctr = nullptr;      // epoch, arrival ticket, failed mark
+    unsigned *host_failed = nullptr;
+    int *err = nullptr;
+};
+
 struct GemvSrc {
     const uint8_t *codes;
     const float *bias;
@@ -96,6 +121,8 @@ struct GemvParams {
     unsigned *work_ctr;   // [n_ks] work counters (self-resetting)
     int rmode;            // chunk sums: 0 by the last chunk's CTA, 1 by chpe_qgemv_reduce_kernel (set at launch)
     int gk;               // CTAs per K-slice (set at launch)
+    int xstream;          // activations stream through the ring with the weights (set at launch)
+    int nstages;          // ring stages, 2 or 3 (set at launch)
     // fused fill: with `fused` set, every CTA builds the activation fragments
     // of its K-slice in shared memory from `xsrc` (fp32 rows [M][K]) instead
     // of copying prepared ones (xf / xs unused)
@@ -122,6 +149,8 @@ struct GemvPlan {
     int n_whole = 0, bc = 1, cfull = 1, ctot = 1, pref = 1;  // work units (GemvParams)
     long items_min = 0;  // units of the shortest K-slice (bound on CTAs per slice)
     int rmode = 0;       // chunk sums: 0 in the GEMV kernel, 1 by a second kernel (more than two rows)
+    int xstream = 0;     // 1: activations stream through the ring (more than two rows): no K-slices
+    int nstages = 3;     // ring stages
     int sms = 148;
     int e_cols = 0;  // epilogue block (columns)
     bool xsplit = false;
@@ -134,12 +163,17 @@ struct GemvPlan {
     int split_counters = 0;
 };
 
-int plan_gemv(const DevMatrix &w, int M, int mode, bool xsplit, GemvPlan *plan);
+// allow_xstream: 0 when the kernel builds the fragments itself (fused fill),
+// which needs them resident.
+int plan_gemv(const DevMatrix &w, int M, int mode, bool xsplit, GemvPlan *plan, bool allow_xstream = true);
 
 // Fragment fills write the row unscale factors xe[M] (2^-e of the row's
 // power-of-two scaling) beside the block sums.
 cudaError_t launch_xfill_f16(const XSrc &s, int M, int K, int Kp, int e_cols, bool xsplit, int bits, void *xf,
-                             float *xs, float *xe, cudaStream_t st);
+                             float *xs, float *xe, cudaStream_t st, const FillExchange *ex = nullptr);
+// Whether launch_xfill_f16 can fuse an exchange for rows of K (Kp padded)
+// columns: every CTA's columns fit its threads' register cache.
+bool xfill_exchange_fits(int M, int Kp, int max_chunks);
 cudaError_t launch_xmaterialize(const XSrc &s, int M, int K, int Kp, float *out, cudaStream_t st);
 
 // x-fragment preparation (fp activations -> fp16 fragments + block sums).

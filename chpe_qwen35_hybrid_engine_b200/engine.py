@@ -320,6 +320,7 @@ class HybridEngine:
         self.allreduce = None      # set by tensor parallelism: fn(tensor) summing across ranks (NCCL)
         self.comm = None           # or the NVLink one-shot all-reduce (ops.Comm)
         self.fuse_fills = False    # GEMVs build their own fragments (chpe_gemv_src_dev) instead of a shared fill
+        self.fuse_exchange = True  # tensor parallel: the all-reduce runs inside the next RMSNorm fill
         g, Mx = geom, max_rows
         f32 = dict(dtype=torch.float32, device=self.dev)
         widest = max(g.hidden, g.q_dim, g.ssm_qkv or 1, g.ffn)
@@ -407,13 +408,25 @@ class HybridEngine:
         # fragments, which on B200 costs more than the fill kernel it saves
         fused = self.fuse_fills and self.scheme != "w8a8"
 
+        pending = []  # a tensor-parallel partial whose all-reduce is due before hidden is next read
+
+        def flush():
+            if pending:
+                self.comm.allreduce_residual(pending.pop(), b["hidden"], M * H, stream=sp.value)
+
         def run(ts, ys, op, x, aux=None, mode=0, acc=False, **kw):
             """ys (+)= op(x, aux) . W^T for the tensors ts (one launch)."""
             if fused:
+                flush()
                 ctx.gemv_src(ts, ys, op, x, aux, M=M, mode=mode, accumulate=acc, stream=sp.value, **kw)
                 return
             xf = self._xf(("in", ts[0].cols), ts[0], M)
-            ctx.xfrag_fill_op(xf, op, x, aux, stream=sp.value, **kw)
+            if pending and op == L.XOP_RMSNORM and x is b["hidden"] and \
+                    self.comm.allreduce_fill(pending[-1], x, xf, aux, kw.get("eps", 0.0), stream=sp.value):
+                pending.pop()  # the all-reduce ran inside the RMSNorm fill
+            else:
+                flush()
+                ctx.xfrag_fill_op(xf, op, x, aux, stream=sp.value, **kw)
             if mode == 1:
                 self._check(lib.chpe_gemv_gateup_swiglu_xfrag_dev(ctx.ptr, ts[0].handle, ts[1].handle, xf.handle,
                                                                   _dev_ptr(ys[0]), sp))
@@ -434,7 +447,10 @@ class HybridEngine:
             part = b["mix_out"][:M]
             run([t], [part], op, x, aux, **kw)
             if self.comm is not None:
-                self.comm.allreduce_residual(part, hidden, M * H, stream=sp.value)
+                if self.fuse_exchange:
+                    pending.append(part)  # summed by the next RMSNorm fill of hidden
+                else:
+                    self.comm.allreduce_residual(part, hidden, M * H, stream=sp.value)
             else:
                 self.allreduce(part)
                 hidden[:M].add_(part)
@@ -483,6 +499,7 @@ class HybridEngine:
                 run([p["gate"], p["up"]], [b["b"], b["c"]], L.XOP_RMSNORM, hid, lw.post_gamma, **norm)
                 run_res(p["down"], L.XOP_SILU_MUL, b["b"], b["c"], ldx=p["gate"].rows, ld_aux=p["up"].rows)
         run([self.head], [b["logits"]], L.XOP_RMSNORM, hid, self.final_gamma, **norm)
+        flush()
         self._check(lib.chpe_argmax_dev(ctx.ptr, _dev_ptr(b["logits"]), M, self.head.rows, _dev_ptr(b["argmax"]),
                                         _dev_ptr(b["maxv"]), sp))
         if real:

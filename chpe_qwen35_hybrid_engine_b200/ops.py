@@ -137,6 +137,24 @@ class Comm:
         self.ctx._check(self.ctx.lib.chpe_allreduce_residual_dev(self.handle, _dev_ptr(part), _dev_ptr(hidden), n,
                                                                   _stream_ptr(stream)))
 
+    def allreduce_fill(self, part, hidden, xf, gamma, eps: float, stream=None) -> bool:
+        """hidden[:M] += sum over ranks of part[:M], then xf = fragments of
+        RMSNorm(hidden) * gamma, in one kernel (chpe_allreduce_fill_dev).
+        False (nothing launched) where the fused form does not apply."""
+        rc = self.ctx.lib.chpe_allreduce_fill_dev(self.handle, _dev_ptr(part), _dev_ptr(hidden), xf.handle,
+                                                  _dev_ptr(gamma), C.c_float(eps), _stream_ptr(stream))
+        if rc == L.ENOTSUP:
+            return False
+        self.ctx._check(rc)
+        return True
+
+    def argmax_merge(self, idx, maxv, M: int, index_base: int, stream=None):
+        """idx[:M] (int32, local to this rank's vocabulary shard) and maxv[:M]
+        become the global argmax over the ranks, ties to the smaller index
+        (chpe_argmax_merge_dev)."""
+        self.ctx._check(self.ctx.lib.chpe_argmax_merge_dev(self.handle, _dev_ptr(idx), _dev_ptr(maxv), M, index_base,
+                                                            _stream_ptr(stream)))
+
     def failed(self) -> bool:
         """True after a bounded wait of this object expired (chpe_comm_failed)."""
         return bool(self.ctx.lib.chpe_comm_failed(self.handle))

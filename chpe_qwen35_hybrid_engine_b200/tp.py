@@ -12,8 +12,9 @@ Partition (one exchange per block, as the model's structure allows):
     one-shot NVLink all-reduce kernel (every rank pushes its partial into every
     peer's memory, then sums in rank order), or by NCCL;
   * the LM head is column split over the vocabulary; each rank takes its local
-    argmax and the (value, index) pairs are all-gathered and reduced, ties to
-    the smaller index as in src/engine.zig:1098-1110.
+    argmax and the (value, index) pairs are exchanged and merged, ties to the
+    smaller index as in src/engine.zig:1098-1110: by the library's P2P merge
+    kernel with the one-shot all-reduce, or by NCCL all-gathers.
 """
 from __future__ import annotations
 
@@ -100,7 +101,10 @@ class TensorParallelEngine:
         e.step(M, stream)
         if self.world == 1:
             return
-        # local argmax -> global index; all-gather the (value, index) pairs of every rank
+        if self.comm is not None:  # the library's exchange: one kernel, every rank gets the global pair
+            self.comm.argmax_merge(e.buf["argmax"], e.buf["maxv"], M, self.v0, stream)
+            return
+        # NCCL: local argmax -> global index; all-gather the (value, index) pairs of every rank
         loc_i = (e.buf["argmax"][:M] + self.v0).to(torch.int32)
         loc_v = e.buf["maxv"][:M].clone()
         gv = [self.gather_v[r, :M] for r in range(self.world)]

@@ -269,6 +269,27 @@ size_t chpe_comm_handle_bytes(void);
 int chpe_comm_handle(const chpe_comm *comm, void *out);
 int chpe_comm_open_peers(chpe_comm *comm, const void *handles);
 int chpe_allreduce_residual_dev(chpe_comm *comm, const float *part, float *hidden, size_t n, void *stream);
+/* The vocabulary-split LM head's argmax over the ranks: on entry idx[m] and
+ * maxv[m] (m < M <= 32, device memory) hold row m's argmax within this rank's
+ * shard (index local to the shard) and its value; on return every rank holds
+ * the global pair -- index_base (the shard's first vocabulary row) is added
+ * to the local index, then the largest value wins and ties go to the smaller
+ * global index, the rule of src/engine.zig:1098-1110 computeArgmax.  Same
+ * exchange (pushes, flags, bounded waits, failure mark) as the all-reduce, in
+ * the same ordered sequence of exchanges on every rank.  Replaces an
+ * all-gather of the pairs; no counterpart in the single-process reference. */
+int chpe_argmax_merge_dev(chpe_comm *comm, int *idx, float *maxv, int M, int index_base, void *stream);
+/* The all-reduce fused with the fill that consumes it: hidden[m][:] += the
+ * sum over ranks of part_r[m][:] for the fragments' M rows of K columns (rows
+ * contiguous, stride K), then xf is filled with RMSNorm(hidden) * gamma --
+ * the same bits as chpe_allreduce_residual_dev followed by
+ * chpe_xfrag_fill_op_dev(CHPE_XOP_RMSNORM of hidden), in one kernel: each
+ * fill CTA exchanges its own columns.  CHPE_ENOTSUP (nothing launched) for
+ * fragments with outliers or int8 operands, or rows that do not fit; the
+ * caller then runs the two calls.  Same exchange sequence rule as the
+ * all-reduce; no counterpart in the single-process reference. */
+int chpe_allreduce_fill_dev(chpe_comm *comm, const float *part, float *hidden, chpe_xfrag *xf, const float *gamma,
+                            float eps, void *stream);
 /* A comm object whose bounded wait expired is failed: the ranks' epochs may
  * be out of step, so every later chpe_allreduce_residual_dev on it returns
  * CHPE_ETIMEOUT at once (and a launch already queued, e.g. inside a CUDA

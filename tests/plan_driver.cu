@@ -38,23 +38,24 @@ int main() {
         {2, kLayoutF16, kMetaSZ16, 64}, {2, kLayoutF16, kMetaS16, 128}, {4, kLayoutF16, kMetaF32, 0}};
     long plans = 0, bad = 0;
     for (int N : Ns) for (int K : Ks) for (auto f : fmts) for (int M = 1; M <= 8; ++M) for (int mode = 0; mode < 2; ++mode)
-        for (int xs = 0; xs < 2; ++xs) {
+        for (int xs = 0; xs < 2; ++xs) for (int ax = 0; ax < 2; ++ax) {
             int group = f.group ? f.group : K;
             if (f.layout == kLayoutF16 && K % group) continue;
             if (f.layout == kLayoutS8 && xs) continue;
             DevMatrix m = make(f.bits, f.layout, f.meta, N, K, group);
             GemvPlan P;
-            plan_gemv(m, M, mode, xs, &P);
+            plan_gemv(m, M, mode, xs, &P, ax != 0);
             ++plans;
             bool ok = P.n_ks >= 1 && P.n_ks <= kMaxKs && P.bpk >= 1 && (long)P.bpk * P.n_ks >= m.n_blocks &&
                       (long)P.bpk * (P.n_ks - 1) < m.n_blocks && P.grid >= P.n_ks && P.grid % P.n_ks == 0 &&
-                      P.smem <= (size_t)kSmemBudget;
+                      P.smem <= (size_t)kSmemBudget && (P.xstream == 0 || (M > 2 && P.n_ks == 1)) &&
+                      P.nstages >= 2 && P.nstages <= kStages;
             // the work units (static ones, then drawn ones, CTAs interleaved
             // in a fixed pseudo-random order) cover every block of every strip
             // group exactly once, every strip group's arrival count reaches its
             // chunk count exactly, and the last draw of each slice is the one
             // that resets its counter
-            ok = ok && P.bc >= 1 && P.pref * P.bc >= kStages && P.ctot >= P.n_ks && P.n_whole >= 0 &&
+            ok = ok && P.bc >= 1 && P.pref * P.bc >= P.nstages && P.ctot >= P.n_ks && P.n_whole >= 0 &&
                  P.n_whole <= P.n_sg && (P.ctot == 1 || P.ws_bytes >= (size_t)P.n_sg * P.ctot * kSG * 16 * M * 4) &&
                  P.split_counters == P.n_sg + P.n_ks;
             const int Gk = P.grid / P.n_ks;
@@ -65,7 +66,7 @@ int main() {
                 const int nbk = std::min(P.bpk, m.n_blocks - k * P.bpk);
                 const int C = unit_chunks(nbk, P.bc);
                 const int U = slice_units(P.n_sg, P.n_whole, C);
-                const int PS = static_units(P.n_whole, Gk, nbk, P.pref);
+                const int PS = static_units(P.n_whole, Gk, nbk, P.pref, P.nstages);
                 const long ntot = grabs_total(U, PS, Gk);
                 ok = Gk <= U;
                 auto take = [&](long u) {
@@ -111,8 +112,8 @@ int main() {
             for (int sg = 0; sg < P.n_sg && ok; ++sg) ok = arrivals[sg] == (sg < P.n_whole ? P.n_ks : P.ctot);
             if (!ok) {
                 ++bad;
-                if (bad < 20) printf("BAD N=%d K=%d bits=%d M=%d mode=%d n_ks=%d bpk=%d grid=%d smem=%zu\n", N, K, f.bits,
-                                     M, mode, P.n_ks, P.bpk, P.grid, P.smem);
+                if (bad < 20) printf("BAD N=%d K=%d bits=%d M=%d mode=%d xstream=%d n_ks=%d bpk=%d grid=%d smem=%zu\n", N, K, f.bits,
+                                     M, mode, P.xstream, P.n_ks, P.bpk, P.grid, P.smem);
             }
         }
     printf("plans=%ld bad=%ld\n", plans, bad);

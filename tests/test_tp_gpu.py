@@ -43,8 +43,10 @@ def _rank(rank, world, port, scheme, q, allreduce="nccl"):
                             device_id=torch.device("cuda", rank))
     try:
         ctx = Context(rank)
-        tp = TensorParallelEngine(ctx, _geom(), scheme, rank, world, seed=21, max_rows=8, allreduce=allreduce)
+        tp = TensorParallelEngine(ctx, _geom(), scheme, rank, world, seed=21, max_rows=8,
+                                  allreduce="p2p" if allreduce.startswith("p2p") else allreduce)
         e = tp.eng
+        e.fuse_exchange = allreduce != "p2p-separate"  # p2p: the all-reduce inside the next RMSNorm fill
         e.buf["tokens"][:1] = 33
         toks = []
         for _ in range(16):  # eager steps
@@ -80,7 +82,8 @@ def _rank(rank, world, port, scheme, q, allreduce="nccl"):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("scheme,allreduce", [("q4g64", "p2p"), ("q4g64", "nccl"), ("q8g32", "p2p")])
+@pytest.mark.parametrize("scheme,allreduce", [("q4g64", "p2p"), ("q4g64", "p2p-separate"), ("q4g64", "nccl"),
+                                              ("q8g32", "p2p")])
 def test_tp2_decode_matches_single_gpu(ctx, scheme, allreduce):
     import torch
     import torch.multiprocessing as mp
@@ -110,6 +113,39 @@ def test_tp2_decode_matches_single_gpu(ctx, scheme, allreduce):
     assert np.linalg.norm(logits_tp - ref) / np.linalg.norm(ref) < 1e-5
 
 
+def _fused_fill_check(ctx, comm, part, h0, rank):
+    """chpe_allreduce_fill_dev against chpe_allreduce_residual_dev followed by
+    the RMSNorm fill, on 8 rows of 8192 columns: hidden and the GEMV of the
+    fragments must agree bit for bit (two exchanges each, both slot parities)."""
+    import torch
+    from chpe_qwen35_hybrid_engine_b200 import SCHEME_U_GROUP_F16_ZERO, X_F32, _lib as L
+    from oracle import oracle as O
+    from tests._util import pack_codes
+    M, K, N = 8, 8192, 320
+    rng = np.random.default_rng(77)  # the same weights on every rank
+    codes, s, z = O.quantize_asym(rng.normal(0, 0.02, (N, K)).astype(np.float32), 4, 64)
+    t = ctx.upload_matrix(4, SCHEME_U_GROUP_F16_ZERO, pack_codes(codes, 4), s, z, rows=N, cols=K, group=64)
+    gamma = torch.from_numpy((1 + 0.1 * rng.standard_normal(K)).astype(np.float32)).cuda()
+    xa, xb = ctx.xfrag(t, M, X_F32), ctx.xfrag(t, M, X_F32)
+    p2 = part.view(M, K)
+    ok = True
+    for _ in range(2):
+        ha = h0.view(M, K).cuda()
+        hb = ha.clone()
+        comm.allreduce_residual(p2, ha, M * K)
+        ctx.xfrag_fill_op(xa, L.XOP_RMSNORM, ha, gamma, ldx=K, eps=1e-6)
+        assert comm.allreduce_fill(p2, hb, xb, gamma, 1e-6)
+        ya, yb = torch.empty(M, N, device="cuda"), torch.empty(M, N, device="cuda")
+        ctx.gemv_xfrag(t, xa, ya)
+        ctx.gemv_xfrag(t, xb, yb)
+        torch.cuda.synchronize()
+        ok = ok and torch.equal(ha, hb) and torch.equal(ya, yb)
+    xa.free()
+    xb.free()
+    t.free()
+    return ok
+
+
 def _comm_rank(rank, world, port, q, skip_rank):
     import torch
     import torch.distributed as dist
@@ -134,11 +170,25 @@ def _comm_rank(rank, world, port, q, skip_rank):
         part = parts[rank].cuda()
         hidden = h0.cuda()
         refused = recovered = None
+        merged = fused_same = None
         if skip_rank is None:
             for it in range(3):  # three epochs in a row (both slot parities)
                 hidden.copy_(h0.cuda())
                 comm.allreduce_residual(part, hidden, n)
                 torch.cuda.synchronize()
+            # the all-reduce fused into the RMSNorm fill: the same hidden bits and
+            # the same fragments (seen through a GEMV) as all-reduce, then fill
+            fused_same = _fused_fill_check(ctx, comm, part, h0, rank)
+            # argmax merges interleaved with all-reduces (one sequence of epochs)
+            merged = []
+            for it in range(3):
+                idx = torch.tensor(_MERGE_IDX[rank], dtype=torch.int32, device="cuda")
+                val = torch.tensor(_MERGE_VAL[rank], dtype=torch.float32, device="cuda")
+                comm.argmax_merge(idx, val, len(_MERGE_IDX[rank]), rank * 100)
+                hidden.copy_(h0.cuda())
+                comm.allreduce_residual(part, hidden, n)
+                torch.cuda.synchronize()
+                merged.append((idx.cpu().tolist(), val.cpu().tolist()))
             rc = ctx.lib.chpe_sync(ctx.ptr)
         else:
             if rank != skip_rank:
@@ -159,13 +209,30 @@ def _comm_rank(rank, world, port, q, skip_rank):
             comm.allreduce_residual(part, hidden, n)
             torch.cuda.synchronize()
             recovered = ctx.lib.chpe_sync(ctx.ptr) == 0 and not comm.failed()
-        out = (rank, rc, torch.equal(hidden.cpu(), want), refused, recovered)
+        out = (rank, rc, torch.equal(hidden.cpu(), want), refused, recovered, (merged, fused_same))
         dist.barrier()  # peers keep their receive areas mapped until everyone is done
         comm.close()
         ctx.close()
         q.put(out)
     finally:
         dist.destroy_process_group()
+
+
+# Per-rank local argmax pairs of five rows (vocabulary shards of 100 rows):
+# rank 1 wins; rank 0 wins; a tie won by rank 0's smaller global index (50 <
+# 103); a tie won by rank 1's (103 < 150); negative values.
+_MERGE_IDX = [[7, 9, 50, 150, 2], [3, 4, 3, 3, 8]]
+_MERGE_VAL = [[1.0, 5.0, 2.5, 2.5, -3.0], [2.0, 4.0, 2.5, 2.5, -1.0]]
+
+
+def _merge_want():
+    from chpe_qwen35_hybrid_engine_b200.tp import merge_argmax
+    out = []
+    for m in range(5):
+        vals = np.array([_MERGE_VAL[r][m] for r in (0, 1)], np.float32)
+        idxs = np.array([_MERGE_IDX[r][m] + 100 * r for r in (0, 1)])
+        out.append(merge_argmax(vals, idxs)[0])
+    return out
 
 
 @pytest.mark.parametrize("skip_rank", [None, 1])
@@ -191,14 +258,20 @@ def test_p2p_allreduce_exact_and_timeout(ctx, skip_rank):
     res = {}
     try:
         for _ in range(2):
-            rank, rc, equal, refused, recovered = q.get(timeout=120)
-            res[rank] = (rc, equal, refused, recovered)
+            rank, rc, equal, refused, recovered, merged = q.get(timeout=120)
+            res[rank] = (rc, equal, refused, recovered, merged)
     finally:
         for p in procs:
             p.join(timeout=60)
     assert all(p.exitcode == 0 for p in procs)
     if skip_rank is None:
         assert res[0][:2] == (0, True) and res[1][:2] == (0, True)
+        # the argmax merge: identical global pairs on both ranks, every time
+        want = (_merge_want(), [max(a, b) for a, b in zip(*_MERGE_VAL)])
+        for r in (0, 1):
+            for idx, val in res[r][4][0]:
+                assert (idx, val) == want
+            assert res[r][4][1] is True  # fused exchange + fill == all-reduce, then fill
     else:
         assert res[0][0] == -5  # CHPE_ETIMEOUT from rank 0's expired wait
         assert res[0][2] is True  # the failed object refused the next exchange

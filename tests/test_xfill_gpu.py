@@ -117,7 +117,11 @@ def test_fused_fill_gemv_equals_fill_then_gemv(ctx, bits, M):
     """chpe_gemv_src_dev (each GEMV CTA builds its fragments from the source op,
     RMSNorm statistics included) gives the same bits as chpe_xfrag_fill_op_dev
     followed by the fragment GEMVs: plain, accumulate, three tensors in one
-    launch, and gate/up SwiGLU."""
+    launch, and gate/up SwiGLU.  Above two activation rows the fragment GEMV
+    streams its activations through the weight ring in one K slice while the
+    fused GEMV keeps them resident (split K), so the two sum the same products
+    in different orders: there the bar is fp32 reordering, 2e-6 of the row
+    maximum."""
     import torch
     from chpe_qwen35_hybrid_engine_b200 import X_F32, _lib as L
     rng = np.random.default_rng(100 + bits * 10 + M)
@@ -158,9 +162,15 @@ def test_fused_fill_gemv_equals_fill_then_gemv(ctx, bits, M):
         got_acc = base.clone()
         ctx.gemv_src([t0], [got_acc], op, xx, aux, M=M, accumulate=True, **kw)
         torch.cuda.synchronize()
-        assert torch.equal(got[0], ref[0]) and torch.equal(got[1], ref[1]), op
-        assert torch.equal(got_gu, ref_gu), op
-        assert torch.equal(got_acc, ref_acc), op
+
+        def same(a, b):
+            if M <= 2:
+                return torch.equal(a, b)
+            tol = 2e-6 * b.abs().amax(dim=1, keepdim=True)
+            return bool(((a - b).abs() <= tol).all())
+        assert same(got[0], ref[0]) and same(got[1], ref[1]), op
+        assert same(got_gu, ref_gu), op
+        assert same(got_acc, ref_acc), op
     assert ctx.lib.chpe_sync(ctx.ptr) == 0
     xf.free()
     for t in (t0, t1, t2):
