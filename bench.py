@@ -59,17 +59,19 @@ sys.path.insert(0, ROOT)
 L2_BYTES = 126 * 1024 * 1024
 
 # DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of the dominant
-# kernel, from the ncu captures summarised under profiles/ (per launch; per
-# decode step for the decode workloads).  The 72B-shape step is too large to
-# capture whole: its traffic is the step's algorithmic bytes times the
-# traffic / algorithmic ratio of the captured 29568 x 8192 Q4 GEMV.
+# kernel, per launch, from single-launch ncu captures summarised under
+# profiles/.  A decode step is too large to capture whole: its traffic is the
+# step's algorithmic GEMV bytes times the traffic / algorithmic ratio of the
+# captured GEMV of the same format (Q4 g64 29568 x 8192, Q8 g32 12288 x 4096,
+# batch 1).
 NCU_TRAFFIC = {
-    ("gemv", 8, 12288, 4096, 1, "f32"): 53_589_504,
-    ("gemv", 4, 29568, 8192, 1, "f32"): 140_035_584,
+    ("gemv", 8, 12288, 4096, 1, "f32"): 53_648_128,
+    ("gemv", 4, 29568, 8192, 1, "f32"): 142_191_104,
+    ("gemv", 4, 29568, 8192, 8, "f32"): 142_469_120,
     ("prefill", 8, 12288, 4096, 2048): 138_023_168,
-    ("decode_9b", 1): 7_399_503_104,
 }
-Q4_TRAFFIC_RATIO = 140_035_584 / 136_400_384
+Q4_TRAFFIC_RATIO = 142_191_104 / 136_400_384
+Q8_TRAFFIC_RATIO = 53_648_128 / 53_542_912
 DECODE_METRIC = "decode tokens/s (quantized GEMV path; GEMV HBM GB/s vs peak in roofline)"
 
 
@@ -431,7 +433,7 @@ def run_decode(args, rank, world, local_rank, which):
     achieved = main["gemv_gbs"]
     n_launch = main["kernel_launches_per_step"] * args.steps
     if which == "decode_9b":
-        traffic = NCU_TRAFFIC[("decode_9b", 1)]
+        traffic = int(main["gemv_bytes_per_step"] * Q8_TRAFFIC_RATIO)
     else:
         traffic = int(main["gemv_bytes_per_step"] * Q4_TRAFFIC_RATIO)
     line = {
@@ -703,7 +705,7 @@ def run_gemv(args, rank, world, local_rank):
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": round(achieved / peaks["hbm_gbs"], 4),
                      "traffic": NCU_TRAFFIC.get(("gemv", c.bits, N, K, M, c.xdtype)),
-                     "peak_source": peaks["source"], "kernel": "gemv_kernel", "kernel_us": round(kern_ms * 1e3, 3),
+                     "peak_source": peaks["source"], "kernel": "chpe_qgemv_kernel", "kernel_us": round(kern_ms * 1e3, 3),
                      "algorithmic_bytes": algo},
         "e2e": {"value": round(world * algo / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
                 "h2d_bytes_per_step": int(xd.numel() * xd.element_size()), "d2h_bytes_per_step": int(M * N * 4)},

@@ -1140,7 +1140,7 @@ extern "C" int chpe_allreduce_fill_dev(chpe_comm *comm, const float *part, float
     const int rc = comm_fill_exchange(comm, part, hidden, (size_t)f.M * f.K, &ex);
     if (rc == CHPE_ETIMEOUT) return fail(ctx, rc, "comm object failed: reset it on every rank first");
     if (rc != CHPE_OK) return fail(ctx, rc, "fused exchange refused");
-    if (!xfill_exchange_fits(f.M, f.Kp, ex.max_chunks))
+    if (!xfill_exchange_fits(f.M, f.Kp))
         return fail(ctx, CHPE_ENOTSUP, "fused exchange: %d rows of %d columns do not fit", f.M, f.K);
     XSrc s;
     s.op = kXRmsnorm;

@@ -260,26 +260,34 @@ cudaError_t launch_pdl_cluster(void (*kern)(KArgs...), dim3 grid, dim3 block, un
 // does the same (the oracle's, on the host) gets the same bits.  The W8A8
 // path re-quantizes every activation row to int8, where a last-bit
 // difference can flip a rounding and grow from there.
-// Flags between GPUs (tensor-parallel exchanges): a system-scope release
-// store after this thread's (and, through a preceding barrier, its block's)
-// writes to peer memory, and the matching acquire load.
-__device__ __forceinline__ void st_release_sys(unsigned *p, unsigned v) {
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+// Tagged words of the tensor-parallel exchanges: one 64-bit store carries a
+// value and the epoch of its exchange (value bits | epoch << 32); naturally
+// aligned 64-bit accesses are single-copy atomic, so a reader sees both or
+// neither.  System scope: the writer and the reader sit on different GPUs.
+__device__ __forceinline__ void st_tagged(unsigned long long *p, float v, unsigned epoch) {
+    const unsigned long long w = ((unsigned long long)epoch << 32) | __float_as_uint(v);
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
 }
-__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned *p) {
-    unsigned v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
+__device__ __forceinline__ unsigned long long ld_tagged(const unsigned long long *p) {
+    unsigned long long w;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+    return w;
 }
-// Waits until *f - epoch >= 0 (wrapping), at most kWaitTimeoutNs; false when
-// the time ran out.
-__device__ __forceinline__ bool wait_flag_bounded(const unsigned *f, unsigned epoch) {
-    const unsigned long long t0 = global_timer_ns();
-    while (true) {
-        if ((int)(ld_acquire_sys(f) - epoch) >= 0) return true;
-        if (global_timer_ns() - t0 > kWaitTimeoutNs) return false;
-        __nanosleep(32);
+// The value of word p once it carries `epoch`; gives up (ok = false, returns
+// 0) when kWaitTimeoutNs have passed since t0, or at once if ok is false.
+__device__ __forceinline__ float wait_tagged(const unsigned long long *p, unsigned epoch, unsigned long long t0,
+                                             bool &ok) {
+    if (!ok) return 0.0f;
+    unsigned long long w = ld_tagged(p);
+    while ((unsigned)(w >> 32) != epoch) {
+        if (global_timer_ns() - t0 > kWaitTimeoutNs) {
+            ok = false;
+            return 0.0f;
+        }
+        __nanosleep(20);
+        w = ld_tagged(p);
     }
+    return __uint_as_float((unsigned)w);
 }
 
 __device__ __forceinline__ float exp_rn(float x) { return (float)exp((double)x); }

@@ -48,24 +48,24 @@ struct XSrc {
     int kv_dim = 1, head_dim = 0, group = 1;  // attention stand-in
     int qkv_dim = 1, silu_on_qkv = 0;         // Gated-DeltaNet stand-in
 };
-// Tensor-parallel exchange (comm.cu): the peers' receive areas and flags as
+// Tensor-parallel exchange (comm.cu): the peers' receive areas as
 // this rank sees them.
 constexpr int kCommMaxRanks = 8;
 constexpr int kErrCommWait = 31;
 constexpr int kErrCommFailed = 32;  // an exchange issued on a comm object that failed before
 struct CommPeers {
-    float *recv[kCommMaxRanks];      // each rank's receive area [2][world][slot_elems] (peer mappings; own one locally)
-    unsigned *flags[kCommMaxRanks];  // each rank's flags [world][max_chunks]
+    // each rank's receive area [2][world][slot_elems] of tagged words (value
+    // bits | epoch << 32): peer mappings, this rank's own one locally
+    unsigned long long *tagged[kCommMaxRanks];
 };
 // An all-reduce of partial sums fused in front of a fragment fill: before the
 // fill reads row tok of x (= hidden), each fill CTA sums its columns of the
-// ranks' partials [M][K] into hidden (same protocol and arithmetic as the
-// one-shot all-reduce; chunk = tok * ctas per row + cta).  world = 0: none.
+// ranks' partials [M][K] into hidden (the one-shot all-reduce's exchange and
+// arithmetic).  world = 0: none.
 struct FillExchange {
     CommPeers peers;
     int world = 0, rank = 0;
     size_t slot_elems = 0;
-    int max_chunks = 0;
     const float *part = nullptr;  // this rank's partials [M][K]
     float *hidden = nullptr;      // [M][K], += the sum of the ranks' partials (the fill's x)
     unsigned *ctr = nullptr;      // epoch, arrival ticket, failed mark
@@ -173,7 +173,7 @@ cudaError_t launch_xfill_f16(const XSrc &s, int M, int K, int Kp, int e_cols, bo
                              float *xs, float *xe, cudaStream_t st, const FillExchange *ex = nullptr);
 // Whether launch_xfill_f16 can fuse an exchange for rows of K (Kp padded)
 // columns: every CTA's columns fit its threads' register cache.
-bool xfill_exchange_fits(int M, int Kp, int max_chunks);
+bool xfill_exchange_fits(int M, int Kp);
 cudaError_t launch_xmaterialize(const XSrc &s, int M, int K, int Kp, float *out, cudaStream_t st);
 
 // x-fragment preparation (fp activations -> fp16 fragments + block sums).

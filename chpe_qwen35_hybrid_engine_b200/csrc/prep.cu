@@ -40,22 +40,20 @@ namespace chpe {
 // that hold the block.
 constexpr int kFillCache = 4;  // units per thread held in registers between the passes
 
-// The tensor-parallel all-reduce fused in front of a fill (FillExchange): the
-// one-shot exchange of comm.cu on this CTA's columns of row tok, leaving the
-// new hidden values in the thread's register cache.  1. this rank's partials
-// go into slot [epoch & 1][rank] of every peer (P2P stores), 2. one thread per
-// peer raises flag [rank][chunk] there and waits (bounded) for the peer's flag
-// here, 3. hidden += (sum of the ranks' partials in rank order), 4. the last
-// CTA of the launch advances the epoch.  A CTA whose wait expires marks the
-// comm object failed and leaves hidden as it was; it still takes part in the
-// cluster barrier of the fill, so no CTA is left waiting.
-__device__ __forceinline__ void fill_exchange(const FillExchange &ex, int tok, int K, int C, int c, int u0, int u1,
+// The tensor-parallel all-reduce fused in front of a fill (FillExchange), on
+// this CTA's columns of row tok, leaving the new hidden values in the
+// thread's register cache: the exchange of comm.cu (tagged words, one NVLink
+// trip), then hidden += (sum of the ranks' partials in rank order) -- the
+// one-shot all-reduce's arithmetic -- and the last CTA of the launch advances
+// the epoch.  A thread whose wait runs out (1 s for all its words) marks the
+// comm object failed; the CTA then leaves hidden as it was and still takes
+// part in the fill's cluster barrier, so no CTA is left waiting.
+__device__ __forceinline__ void fill_exchange(const FillExchange &ex, int tok, int K, int u0, int u1,
                                               float (&cv)[kFillCache][4]) {
     __shared__ int s_ok;
     const int tid = threadIdx.x;
     const bool failed = *reinterpret_cast<const volatile unsigned *>(&ex.ctr[2]) != 0u;
     const unsigned epoch = *reinterpret_cast<const volatile unsigned *>(&ex.ctr[0]) + 1u;
-    const int chunk = tok * C + c;
     const size_t base = (size_t)tok * K;
     const size_t slot = ((size_t)(epoch & 1u) * ex.world + ex.rank) * ex.slot_elems + base;
     if (tid == 0) s_ok = failed ? 0 : 1;
@@ -71,23 +69,36 @@ __device__ __forceinline__ void fill_exchange(const FillExchange &ex, int tok, i
             cv[i][q] = p;
             if (in && !failed)
                 for (int r = 0; r < ex.world; ++r)
-                    if (r != ex.rank) ex.peers.recv[r][slot + kk[q]] = p;
-        }
-    }
-    __syncthreads();
-    if (!failed && tid < ex.world && tid != ex.rank) {
-        st_release_sys(ex.peers.flags[tid] + (size_t)ex.rank * ex.max_chunks + chunk, epoch);
-        if (!wait_flag_bounded(ex.peers.flags[ex.rank] + (size_t)tid * ex.max_chunks + chunk, epoch)) {
-            atomicExch(ex.err, kErrCommWait);
-            atomicExch(&ex.ctr[2], 1u);  // failed: no later exchange on this object until a reset
-            *reinterpret_cast<volatile unsigned *>(ex.host_failed) = 1u;
-            s_ok = 0;
+                    if (r != ex.rank) st_tagged(ex.peers.tagged[r] + slot + kk[q], p, epoch);
         }
     }
     if (failed && tid == 0) atomicExch(ex.err, kErrCommFailed);
+    const unsigned long long *own = ex.peers.tagged[ex.rank] + (size_t)(epoch & 1u) * ex.world * ex.slot_elems + base;
+    bool ok = !failed;
+    const unsigned long long t0 = global_timer_ns();
+#pragma unroll
+    for (int i = 0; i < kFillCache; ++i) {
+        const int u = u0 + tid + i * kFillThreads;
+        int kk[4];
+        unit_cols(u, kk);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            if (u < u1 && kk[q] < K) {
+                float sum = 0.0f;
+                for (int r = 0; r < ex.world; ++r)
+                    sum += r == ex.rank ? cv[i][q] : wait_tagged(own + (size_t)r * ex.slot_elems + kk[q], epoch, t0, ok);
+                cv[i][q] = sum;  // the ranks' sum; hidden is added below
+            }
+        }
+    }
+    if (!ok && !failed) {
+        atomicExch(ex.err, kErrCommWait);
+        atomicExch(&ex.ctr[2], 1u);  // failed: no later exchange on this object until a reset
+        *reinterpret_cast<volatile unsigned *>(ex.host_failed) = 1u;
+        s_ok = 0;
+    }
     __syncthreads();
-    const bool ok = s_ok != 0;
-    const float *own = ex.peers.recv[ex.rank] + (size_t)(epoch & 1u) * ex.world * ex.slot_elems + base;
+    const bool all_ok = s_ok != 0;
 #pragma unroll
     for (int i = 0; i < kFillCache; ++i) {
         const int u = u0 + tid + i * kFillThreads;
@@ -97,11 +108,8 @@ __device__ __forceinline__ void fill_exchange(const FillExchange &ex, int tok, i
         for (int q = 0; q < 4; ++q) {
             if (u < u1 && kk[q] < K) {
                 float h = ex.hidden[base + kk[q]];
-                if (ok) {
-                    float sum = 0.0f;
-                    for (int r = 0; r < ex.world; ++r)
-                        sum += (r == ex.rank) ? cv[i][q] : own[(size_t)r * ex.slot_elems + kk[q]];
-                    h += sum;
+                if (all_ok) {
+                    h += cv[i][q];
                     ex.hidden[base + kk[q]] = h;
                 }
                 cv[i][q] = h;
@@ -144,7 +152,7 @@ __global__ void __launch_bounds__(kFillThreads) chpe_xfill_f16_kernel(const XSrc
     // with an exchange, the cache already holds the new hidden values (every
     // unit of the CTA fits the cache: xfill_exchange_fits)
     const bool exch = ex.world > 0;
-    if (exch) fill_exchange(ex, tok, K, C, c, u0, u1, cv);
+    if (exch) fill_exchange(ex, tok, K, u0, u1, cv);
     float ss = 0.0f, am = 0.0f;
 #pragma unroll
     for (int i = 0; i < kFillCache; ++i) {
@@ -270,7 +278,8 @@ __global__ void __launch_bounds__(kFillThreads) chpe_xfill_f16_kernel(const XSrc
     }
 }
 
-bool xfill_exchange_fits(int M, int Kp, int max_chunks) {
+bool xfill_exchange_fits(int M, int Kp) {
+    (void)M;
     const int nunits = Kp / 4, C = fill_ctas(nunits);
     int most = 0;
     for (int c = 0; c < C; ++c) {
@@ -278,7 +287,7 @@ bool xfill_exchange_fits(int M, int Kp, int max_chunks) {
         fill_range(nunits, C, c, u0, u1);
         most = std::max(most, u1 - u0);
     }
-    return most <= kFillCache * kFillThreads && M * C <= max_chunks;
+    return most <= kFillCache * kFillThreads;
 }
 
 cudaError_t launch_xfill_f16(const XSrc &s, int M, int K, int Kp, int e_cols, bool xsplit, int bits, void *xf,

@@ -254,15 +254,16 @@ int chpe_gemm_prefill_dev(chpe_ctx *ctx, const chpe_tensor *w, const void *x, in
 
 /* ---- tensor parallelism: one-shot all-reduce over NVLink peer memory ------
  * hidden[i] += sum over the `world` ranks of part_r[i], i < n, after the O and
- * down projections of a tensor-parallel block.  Each rank pushes its partial
- * into every peer's receive area (P2P stores through CUDA IPC mappings), raises
- * a flag there, waits (bounded: 1 s, then CHPE_ETIMEOUT at chpe_sync) for every
- * peer's flag and sums the partials in rank order -- identical bits on every
- * rank.  One kernel, no NCCL on this path.  Setup: chpe_comm_create on every
- * rank, exchange the chpe_comm_handle_bytes() handle of every rank (any host
- * transport), chpe_comm_open_peers with all ranks' handles in rank order.
- * Every rank must issue the same sequence of all-reduces.  No counterpart in
- * the single-process reference. */
+ * down projections of a tensor-parallel block.  Each rank stores its partial
+ * into every peer's receive area (P2P stores through CUDA IPC mappings), each
+ * value tagged with the exchange's epoch in the same 64-bit word, polls its
+ * own area until every peer's values carry the epoch (bounded: 1 s, then
+ * CHPE_ETIMEOUT at chpe_sync) and sums the partials in rank order -- identical
+ * bits on every rank.  One kernel, one NVLink trip, no NCCL on this path.
+ * Setup: chpe_comm_create on every rank, exchange the chpe_comm_handle_bytes()
+ * handle of every rank (any host transport), chpe_comm_open_peers with all
+ * ranks' handles in rank order.  Every rank must issue the same sequence of
+ * exchanges.  No counterpart in the single-process reference. */
 typedef struct chpe_comm chpe_comm;
 int chpe_comm_create(chpe_ctx *ctx, int world, int rank, size_t max_elems, chpe_comm **out);
 size_t chpe_comm_handle_bytes(void);
@@ -275,7 +276,7 @@ int chpe_allreduce_residual_dev(chpe_comm *comm, const float *part, float *hidde
  * the global pair -- index_base (the shard's first vocabulary row) is added
  * to the local index, then the largest value wins and ties go to the smaller
  * global index, the rule of src/engine.zig:1098-1110 computeArgmax.  Same
- * exchange (pushes, flags, bounded waits, failure mark) as the all-reduce, in
+ * exchange (tagged pushes, bounded waits, failure mark) as the all-reduce, in
  * the same ordered sequence of exchanges on every rank.  Replaces an
  * all-gather of the pairs; no counterpart in the single-process reference. */
 int chpe_argmax_merge_dev(chpe_comm *comm, int *idx, float *maxv, int M, int index_base, void *stream);
@@ -295,7 +296,7 @@ int chpe_allreduce_fill_dev(chpe_comm *comm, const float *part, float *hidden, c
  * CHPE_ETIMEOUT at once (and a launch already queued, e.g. inside a CUDA
  * graph, skips the exchange and records the error for chpe_sync) until
  * chpe_comm_reset.  chpe_comm_failed returns 1 when failed, 0 when not.
- * chpe_comm_reset waits for the device, then clears this rank's epochs, flags
+ * chpe_comm_reset waits for the device, then clears this rank's epochs, slots
  * and failed mark; call it on EVERY rank between two host barriers (no rank
  * may issue an all-reduce before all ranks have reset). */
 int chpe_comm_failed(const chpe_comm *comm);
