@@ -48,6 +48,7 @@ namespace {
 
 constexpr int kCommThreads = 256;
 constexpr int kCommChunk = 1024;  // values per CTA (4 per thread)
+static_assert(kCommMaxRanksDev == kCommMaxRanks, "one rank limit");
 
 __device__ __forceinline__ void mark_failed(unsigned *ctr, volatile unsigned *host_failed, int *err) {
     atomicExch(err, kErrCommWait);
@@ -93,15 +94,19 @@ __global__ void __launch_bounds__(kCommThreads) chpe_allreduce_residual_kernel(c
     const unsigned long long *own = peers.tagged[rank] + (size_t)(epoch & 1u) * world * slot_elems;
     const unsigned long long t0 = global_timer_ns();
     bool ok = true;
+    constexpr int NV = kCommChunk / kCommThreads;
+    size_t idx[NV];
+    bool valid[NV];
+    float sums[NV];
 #pragma unroll
-    for (int j = 0; j < kCommChunk / kCommThreads; ++j) {
-        const int i = i0 + threadIdx.x + j * kCommThreads;
-        if (i >= n) continue;
-        float s = 0.0f;
-        for (int r = 0; r < world && ok; ++r)
-            s += r == rank ? v[j] : wait_tagged(own + (size_t)r * slot_elems + i, epoch, t0, ok);
-        if (ok) hidden[i] += s;
+    for (int j = 0; j < NV; ++j) {
+        idx[j] = (size_t)(i0 + threadIdx.x + j * kCommThreads);
+        valid[j] = idx[j] < (size_t)n;
     }
+    sum_tagged<NV>(own, slot_elems, idx, valid, world, rank, v, epoch, t0, ok, sums);
+#pragma unroll
+    for (int j = 0; j < NV; ++j)
+        if (ok && valid[j]) hidden[idx[j]] += sums[j];
     if (!ok) mark_failed(ctr, host_failed, err);
     __syncthreads();
     if (threadIdx.x == 0) advance_epoch(ctr, epoch, gridDim.x);
@@ -140,12 +145,21 @@ __global__ void __launch_bounds__(32) chpe_argmax_merge_kernel(const CommPeers p
         const unsigned long long t0 = global_timer_ns();
         float bv = 0.0f;
         int bi = 0;
-        for (int r = 0; r < world && ok; ++r) {
+        unsigned long long wv[kCommMaxRanks], wi[kCommMaxRanks];  // every peer's pair, loaded up front
+#pragma unroll
+        for (int r = 0; r < kCommMaxRanks; ++r)
+            if (r < world && r != rank) {
+                wv[r] = ld_tagged(own + (size_t)r * slot_elems + 2 * m);
+                wi[r] = ld_tagged(own + (size_t)r * slot_elems + 2 * m + 1);
+            }
+#pragma unroll
+        for (int r = 0; r < kCommMaxRanks; ++r) {
+            if (r >= world || !ok) continue;
             float rv = v;
             int ri = gi;
             if (r != rank) {
-                rv = wait_tagged(own + (size_t)r * slot_elems + 2 * m, epoch, t0, ok);
-                ri = __float_as_int(wait_tagged(own + (size_t)r * slot_elems + 2 * m + 1, epoch, t0, ok));
+                rv = settle_tagged(own + (size_t)r * slot_elems + 2 * m, wv[r], epoch, t0, ok);
+                ri = __float_as_int(settle_tagged(own + (size_t)r * slot_elems + 2 * m + 1, wi[r], epoch, t0, ok));
             }
             if (r == 0 || rv > bv || (rv == bv && ri < bi)) {
                 bv = rv;

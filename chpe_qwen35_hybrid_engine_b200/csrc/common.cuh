@@ -260,6 +260,8 @@ cudaError_t launch_pdl_cluster(void (*kern)(KArgs...), dim3 grid, dim3 block, un
 // does the same (the oracle's, on the host) gets the same bits.  The W8A8
 // path re-quantizes every activation row to int8, where a last-bit
 // difference can flip a rounding and grow from there.
+constexpr int kCommMaxRanksDev = 8;  // ranks of a tensor-parallel group (= kCommMaxRanks of internal.h)
+
 // Tagged words of the tensor-parallel exchanges: one 64-bit store carries a
 // value and the epoch of its exchange (value bits | epoch << 32); naturally
 // aligned 64-bit accesses are single-copy atomic, so a reader sees both or
@@ -273,12 +275,12 @@ __device__ __forceinline__ unsigned long long ld_tagged(const unsigned long long
     asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
     return w;
 }
-// The value of word p once it carries `epoch`; gives up (ok = false, returns
-// 0) when kWaitTimeoutNs have passed since t0, or at once if ok is false.
-__device__ __forceinline__ float wait_tagged(const unsigned long long *p, unsigned epoch, unsigned long long t0,
-                                             bool &ok) {
+// Word w of p, loaded already, once it carries `epoch` (reloading p until
+// it does); gives up (ok = false, returns 0) when kWaitTimeoutNs have passed
+// since t0, or at once if ok is false.
+__device__ __forceinline__ float settle_tagged(const unsigned long long *p, unsigned long long w, unsigned epoch,
+                                               unsigned long long t0, bool &ok) {
     if (!ok) return 0.0f;
-    unsigned long long w = ld_tagged(p);
     while ((unsigned)(w >> 32) != epoch) {
         if (global_timer_ns() - t0 > kWaitTimeoutNs) {
             ok = false;
@@ -288,6 +290,31 @@ __device__ __forceinline__ float wait_tagged(const unsigned long long *p, unsign
         w = ld_tagged(p);
     }
     return __uint_as_float((unsigned)w);
+}
+
+// For each of NV values (index idx[j], valid[j]): the sum over ranks
+// r < world, in rank order, of value idx[j] of rank r's slot (own[j] for this
+// rank), into sums[j].  Every peer word of every value is loaded before any
+// is checked, so all their L2 round trips overlap.
+template <int NV>
+__device__ __forceinline__ void sum_tagged(const unsigned long long *slots, size_t rstride, const size_t (&idx)[NV],
+                                           const bool (&valid)[NV], int world, int rank, const float (&own)[NV],
+                                           unsigned epoch, unsigned long long t0, bool &ok, float (&sums)[NV]) {
+    unsigned long long w[NV][kCommMaxRanksDev];
+#pragma unroll
+    for (int j = 0; j < NV; ++j)
+#pragma unroll
+        for (int r = 0; r < kCommMaxRanksDev; ++r)
+            if (valid[j] && r < world && r != rank) w[j][r] = ld_tagged(slots + (size_t)r * rstride + idx[j]);
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+        float sum = 0.0f;
+#pragma unroll
+        for (int r = 0; r < kCommMaxRanksDev; ++r)
+            if (valid[j] && r < world)
+                sum += r == rank ? own[j] : settle_tagged(slots + (size_t)r * rstride + idx[j], w[j][r], epoch, t0, ok);
+        sums[j] = sum;
+    }
 }
 
 __device__ __forceinline__ float exp_rn(float x) { return (float)exp((double)x); }

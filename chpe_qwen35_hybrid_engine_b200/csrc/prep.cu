@@ -79,17 +79,18 @@ __device__ __forceinline__ void fill_exchange(const FillExchange &ex, int tok, i
 #pragma unroll
     for (int i = 0; i < kFillCache; ++i) {
         const int u = u0 + tid + i * kFillThreads;
+        if (u >= u1) continue;
         int kk[4];
         unit_cols(u, kk);
+        size_t idx[4];
+        bool valid[4];
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-            if (u < u1 && kk[q] < K) {
-                float sum = 0.0f;
-                for (int r = 0; r < ex.world; ++r)
-                    sum += r == ex.rank ? cv[i][q] : wait_tagged(own + (size_t)r * ex.slot_elems + kk[q], epoch, t0, ok);
-                cv[i][q] = sum;  // the ranks' sum; hidden is added below
-            }
+            idx[q] = (size_t)kk[q];
+            valid[q] = kk[q] < K;
         }
+        // the ranks' sums of the unit's four columns; hidden is added below
+        sum_tagged<4>(own, ex.slot_elems, idx, valid, ex.world, ex.rank, cv[i], epoch, t0, ok, cv[i]);
     }
     if (!ok && !failed) {
         atomicExch(ex.err, kErrCommWait);
@@ -125,6 +126,7 @@ __device__ __forceinline__ void fill_exchange(const FillExchange &ex, int tok, i
     }
 }
 
+template <bool EXCH>  // with the fused all-reduce (ex), or without (ex unused)
 __global__ void __launch_bounds__(kFillThreads) chpe_xfill_f16_kernel(const XSrc s, int M, int K, int Kp, int E,
                                                                      int split, int bits, uint2 *__restrict__ xf,
                                                                      float *__restrict__ xs, float *__restrict__ xe,
@@ -133,7 +135,7 @@ __global__ void __launch_bounds__(kFillThreads) chpe_xfill_f16_kernel(const XSrc
     cg::cluster_group cluster = cg::this_cluster();
     __shared__ float red[2 * kFillWarps];
     __shared__ float2 stats[kFillMaxCtas];  // (sum of squares, largest |value|) of every CTA of the row's cluster
-    pdl_begin();
+    grid_dependents_launch();
     const int tok = blockIdx.y;
     const int nunits = Kp / 4;
     const int C = (int)cluster.num_blocks();
@@ -149,10 +151,23 @@ __global__ void __launch_bounds__(kFillThreads) chpe_xfill_f16_kernel(const XSrc
         return rms ? xrow[k] : xsrc_value(s, tok, k, 1.0f);
     };
     float cv[kFillCache][4], cg4[kFillCache][4];  // cached values (and RMSNorm gammas)
+    // RMSNorm's gamma is a weight, not the upstream kernel's output: its loads
+    // go out before the wait for the upstream grid
+    if (rms) {
+#pragma unroll
+        for (int i = 0; i < kFillCache; ++i) {
+            const int u = u0 + tid + i * kFillThreads;
+            int kk[4];
+            unit_cols(u, kk);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) cg4[i][q] = (u < u1 && kk[q] < K) ? s.aux[kk[q]] : 0.0f;
+        }
+    }
+    grid_dependency_wait();
     // with an exchange, the cache already holds the new hidden values (every
     // unit of the CTA fits the cache: xfill_exchange_fits)
-    const bool exch = ex.world > 0;
-    if (exch) fill_exchange(ex, tok, K, u0, u1, cv);
+    constexpr bool exch = EXCH;
+    if constexpr (EXCH) fill_exchange(ex, tok, K, u0, u1, cv);
     float ss = 0.0f, am = 0.0f;
 #pragma unroll
     for (int i = 0; i < kFillCache; ++i) {
@@ -165,8 +180,7 @@ __global__ void __launch_bounds__(kFillThreads) chpe_xfill_f16_kernel(const XSrc
                 const float v = exch ? cv[i][q] : src(kk[q]);
                 cv[i][q] = v;
                 if (rms) {
-                    const float g = kk[q] < K ? s.aux[kk[q]] : 0.0f;
-                    cg4[i][q] = g;
+                    const float g = cg4[i][q];
                     ss = fmaf(v, v, ss);
                     am = fmaxf(am, fabsf(__fmul_rn(v, g)));
                 } else {
@@ -293,9 +307,12 @@ bool xfill_exchange_fits(int M, int Kp) {
 cudaError_t launch_xfill_f16(const XSrc &s, int M, int K, int Kp, int e_cols, bool xsplit, int bits, void *xf,
                              float *xs, float *xe, cudaStream_t st, const FillExchange *ex) {
     const int C = fill_ctas(Kp / 4);
+    if (ex && ex->world > 0)
+        return launch_pdl_cluster(chpe_xfill_f16_kernel<true>, dim3(C, M), dim3(kFillThreads), (unsigned)C, 0, st, s,
+                                  M, K, Kp, e_cols, xsplit ? 1 : 0, bits, static_cast<uint2 *>(xf), xs, xe, *ex);
     const FillExchange none{};
-    return launch_pdl_cluster(chpe_xfill_f16_kernel, dim3(C, M), dim3(kFillThreads), (unsigned)C, 0, st, s, M, K, Kp,
-                              e_cols, xsplit ? 1 : 0, bits, static_cast<uint2 *>(xf), xs, xe, ex ? *ex : none);
+    return launch_pdl_cluster(chpe_xfill_f16_kernel<false>, dim3(C, M), dim3(kFillThreads), (unsigned)C, 0, st, s, M,
+                              K, Kp, e_cols, xsplit ? 1 : 0, bits, static_cast<uint2 *>(xf), xs, xe, none);
 }
 
 cudaError_t launch_xprep_f16(const void *x, int x_dtype, int M, int K, int Kp, int e_cols, bool xsplit, int bits,

@@ -207,8 +207,11 @@ int chpe_xfrag_free(chpe_ctx *ctx, chpe_xfrag *xf);
  *                       silu(q) * z when silu_on_qkv (Gated-DeltaNet stand-in,
  *                       src/engine.zig:651-654 / :813 / :988)
  * Row strides ldx / ld_aux are in elements; every op other than PLAIN reads
- * fp32.  No counterpart in the reference, whose engine materialises each
- * producer's output before quantizing it for the next gemvParallel. */
+ * fp32.  RMSNorm's gamma is treated like a weight: the fill may read it
+ * before the kernel ahead of it on the stream has finished, so that kernel
+ * must not write it.  No counterpart in the reference, whose engine
+ * materialises each producer's output before quantizing it for the next
+ * gemvParallel. */
 #define CHPE_XOP_PLAIN 0
 #define CHPE_XOP_RMSNORM 1
 #define CHPE_XOP_SILU_MUL 2
