@@ -341,12 +341,15 @@ def decode_line(eng, stepper, M, args, world, dev, label, context_len, profile=T
         gms = dist_max(gms, world)
         out.update({"gemv_ms_per_step": round(gms, 4), "gemv_bytes_per_step": int(gbytes),
                     "gemv_launches_per_step": glaunch, "gemv_gbs": round(gbytes / (gms * 1e-3) / 1e9, 1)})
-        # where the step's time goes (each part timed alone; "other" is the rest:
-        # fills, mixers, norms, argmax and the launch gaps between kernels)
-        bd = {"gemv_ms": round(gms, 4)}
+        # where the step's time goes: the GEMVs timed alone, and the rest of
+        # the step (fills -- with tensor parallelism the ones that carry the
+        # exchanges --, mixers, norms, argmax, launch gaps); beside it the
+        # step's exchanges run alone as separate all-reduce kernels, the form
+        # the step itself does not use
+        bd = {"gemv_ms": round(gms, 4), "other_ms": round(ms_step - gms, 4)}
         if getattr(stepper, "comm", None) is not None:
-            bd["exchange_ms"] = round(exchange_step_profile(stepper, M, max(5, min(args.steps, 20)), world, dev), 4)
-        bd["other_ms"] = round(ms_step - gms - bd.get("exchange_ms", 0.0), 4)
+            bd["exchange_kernels_alone_ms"] = round(
+                exchange_step_profile(stepper, M, max(5, min(args.steps, 20)), world, dev), 4)
         out["breakdown"] = bd
     return out
 
@@ -398,6 +401,7 @@ def run_decode(args, rank, world, local_rank, which):
     geom, ctx_len = _decode_geometry(which, args)
     if which == "decode_72b":
         tp = TensorParallelEngine(ctx, geom, "q4g64", rank, world, seed=0, max_rows=8, random_codes=True)
+        tp.eng.push_exchange = args.exchange == "push"
         clk.start()
         main = decode_line(tp.eng, tp, 1, args, world, dev, f"72b_tp{world}_b1", ctx_len)
         clk.stop()
@@ -407,6 +411,8 @@ def run_decode(args, rank, world, local_rank, which):
             tp.comm.close()
         del tp
         config = decode_config(which, world, ctx_len)
+        if world > 1:
+            config["exchange"] = f"NVLink P2P, tagged words, sent by the {'GEMV' if args.exchange == 'push' else 'fill'}"
         scaling, units = "strong", 1
     else:
         eng, _ = build_random(ctx, geom, "q8g32", seed=rank, max_rows=8)
@@ -900,6 +906,9 @@ def main():
     ap.add_argument("--workload", default="decode_72b", choices=["decode_72b", "decode_9b", "gemv", "q8_gemv", "prefill"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-sweep", action="store_true", help="decode: skip the single-kernel configurations at N = 1")
+    ap.add_argument("--exchange", default="fill", choices=["fill", "push"],
+                    help="decode_72b, N > 1: the O / down partials are sent by the fill that sums them (fill) "
+                         "or by the GEMV that makes them (push)")
     ap.add_argument("--context", type=int, default=None,
                     help="decode: context tokens prefilled before the timed steps (default 1024 for 72B, 512 for 9B)")
     ap.add_argument("--bits", type=int, default=8, choices=[8, 4, 2], help="gemv: code width")

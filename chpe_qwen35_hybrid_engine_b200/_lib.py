@@ -84,7 +84,8 @@ SIGNATURES = {
     "chpe_comm_open_peers": (I, [P, P]),
     "chpe_allreduce_residual_dev": (I, [P, P, P, SZ, P]),
     "chpe_argmax_merge_dev": (I, [P, P, P, I, I, P]),
-    "chpe_allreduce_fill_dev": (I, [P, P, P, P, P, F, P]),
+    "chpe_allreduce_fill_dev": (I, [P, P, P, P, P, F, I, P]),
+    "chpe_gemv_xfrag_push_dev": (I, [P, P, P, P, P, P]),
     "chpe_comm_failed": (I, [P]),
     "chpe_comm_reset": (I, [P]),
     "chpe_comm_destroy": (I, [P]),

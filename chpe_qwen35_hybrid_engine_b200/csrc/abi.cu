@@ -385,7 +385,7 @@ void fill_params(GemvParams &p, int mode, const DevMatrix *const *ms, int n, con
 
 int gemv_core(chpe_ctx *ctx, const DevMatrix &w0, const DevMatrix *w1, int mode, const Xfrag &f, float *y, int ldy,
               int accumulate, const float *scale_override0, const float *scale_override1, cudaStream_t st,
-              const XSrc *src = nullptr) {
+              const XSrc *src = nullptr, const FillExchange *push = nullptr) {
     GemvPlan P;
     plan_gemv(w0, f.M, mode, f.xsplit, &P, src == nullptr);
     int rc = check_frag(ctx, w0, P, f);
@@ -402,6 +402,7 @@ int gemv_core(chpe_ctx *ctx, const DevMatrix &w0, const DevMatrix *w1, int mode,
         p.fused = 1;
         p.xe = ctx->d_xe;  // written by the kernel's fused fill (for the chunk-sum kernel)
     }
+    if (push) p.push = *push;
     cudaError_t e = launch_gemv(w0, w1, P, p, st);
     if (e != cudaSuccess) return fail(ctx, CHPE_ECUDA, "gemv launch: %s", cudaGetErrorString(e));
     return CHPE_OK;
@@ -1129,8 +1130,20 @@ extern "C" int chpe_xfrag_fill_op_dev(chpe_ctx *ctx, chpe_xfrag *xf, const chpe_
 int comm_fill_exchange(chpe_comm *c, const float *part, float *hidden, size_t n, FillExchange *out);
 chpe_ctx *comm_ctx(const chpe_comm *c);
 
+extern "C" int chpe_gemv_xfrag_push_dev(chpe_ctx *ctx, const chpe_tensor *w, const chpe_xfrag *xf, float *y,
+                                        chpe_comm *comm, void *stream) {
+    if (!ctx || !w || !xf || !y || !comm) return fail(ctx, CHPE_EINVAL, "null argument");
+    if (w->m.out_cols) return fail(ctx, CHPE_ENOTSUP, "pushing GEMV: tensors with outlier columns");
+    FillExchange ex;
+    const int rc = comm_fill_exchange(comm, y, y, (size_t)xf->f.M * w->m.N, &ex);
+    if (rc == CHPE_ETIMEOUT) return fail(ctx, rc, "comm object failed: reset it on every rank first");
+    if (rc != CHPE_OK) return fail(ctx, rc, "pushing GEMV refused");
+    return gemv_core(ctx, w->m, nullptr, 0, xf->f, y, w->m.N, 0, nullptr, nullptr, static_cast<cudaStream_t>(stream),
+                     nullptr, &ex);
+}
+
 extern "C" int chpe_allreduce_fill_dev(chpe_comm *comm, const float *part, float *hidden, chpe_xfrag *xf,
-                                       const float *gamma, float eps, void *stream) {
+                                       const float *gamma, float eps, int pushed, void *stream) {
     chpe_ctx *ctx = comm_ctx(comm);
     if (!ctx || !part || !hidden || !xf || !gamma) return fail(ctx, CHPE_EINVAL, "null argument");
     const Xfrag &f = xf->f;
@@ -1142,6 +1155,7 @@ extern "C" int chpe_allreduce_fill_dev(chpe_comm *comm, const float *part, float
     if (rc != CHPE_OK) return fail(ctx, rc, "fused exchange refused");
     if (!xfill_exchange_fits(f.M, f.Kp))
         return fail(ctx, CHPE_ENOTSUP, "fused exchange: %d rows of %d columns do not fit", f.M, f.K);
+    ex.pushed = pushed ? 1 : 0;
     XSrc s;
     s.op = kXRmsnorm;
     s.x = hidden;

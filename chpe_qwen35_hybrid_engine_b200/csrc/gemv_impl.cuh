@@ -266,7 +266,17 @@ __device__ __forceinline__ void finalize_entry(const GemvParams &p, int sg, int 
             out += os;
         }
         float *yp = p.ys[ref.r] + (size_t)tok * p.ldys[ref.r] + row;
-        *yp = p.accumulate ? *yp + out : out;
+        if (p.accumulate) out += *yp;
+        *yp = out;
+        if (p.push.world > 0) {
+            // the next exchange's epoch (set by the previous exchange, which has
+            // ended: read-only while this grid runs, so through the read-only cache)
+            const unsigned epoch = __ldg(p.push.ctr) + 1u;
+            const size_t off = ((size_t)(epoch & 1u) * p.push.world + p.push.rank) * p.push.slot_elems +
+                               (size_t)tok * p.ldys[ref.r] + row;
+            for (int r = 0; r < p.push.world; ++r)
+                if (r != p.push.rank) st_tagged(p.push.peers.tagged[r] + off, out, epoch);
+        }
     } else {
         float gv, uv;
         if (LAYOUT == kLayoutS8) {

@@ -65,6 +65,7 @@ struct CommPeers {
 struct FillExchange {
     CommPeers peers;
     int world = 0, rank = 0;
+    int pushed = 0;  // the partials are in the peers' slots already (a pushing GEMV sent them)
     size_t slot_elems = 0;
     const float *part = nullptr;  // this rank's partials [M][K]
     float *hidden = nullptr;      // [M][K], += the sum of the ranks' partials (the fill's x)
@@ -129,6 +130,12 @@ struct GemvParams {
     XSrc xsrc;
     int fused;
     int *err;
+    // tensor-parallel push (plain mode): every finished output y[tok][row]
+    // also goes, tagged with the comm object's next epoch, into slot
+    // [epoch & 1][push.rank] of every peer's receive area at tok * ldy + row;
+    // the RMSNorm fill that consumes the exchange then only collects.
+    // push.world = 0: none.
+    FillExchange push;
 };
 
 // Scratch a GEMV call needs, owned by the caller (context).

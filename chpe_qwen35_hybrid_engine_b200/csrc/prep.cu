@@ -67,7 +67,7 @@ __device__ __forceinline__ void fill_exchange(const FillExchange &ex, int tok, i
             const bool in = u < u1 && kk[q] < K;
             const float p = in ? ex.part[base + kk[q]] : 0.0f;
             cv[i][q] = p;
-            if (in && !failed)
+            if (in && !failed && !ex.pushed)
                 for (int r = 0; r < ex.world; ++r)
                     if (r != ex.rank) st_tagged(ex.peers.tagged[r] + slot + kk[q], p, epoch);
         }

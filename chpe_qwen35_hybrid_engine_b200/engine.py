@@ -321,6 +321,7 @@ class HybridEngine:
         self.comm = None           # or the NVLink one-shot all-reduce (ops.Comm)
         self.fuse_fills = False    # GEMVs build their own fragments (chpe_gemv_src_dev) instead of a shared fill
         self.fuse_exchange = True  # tensor parallel: the all-reduce runs inside the next RMSNorm fill
+        self.push_exchange = False  # ... and the O / down GEMV sends the partials (the fill only collects)
         g, Mx = geom, max_rows
         f32 = dict(dtype=torch.float32, device=self.dev)
         widest = max(g.hidden, g.q_dim, g.ssm_qkv or 1, g.ffn)
@@ -411,22 +412,27 @@ class HybridEngine:
         pending = []  # a tensor-parallel partial whose all-reduce is due before hidden is next read
 
         def flush():
-            if pending:
-                self.comm.allreduce_residual(pending.pop(), b["hidden"], M * H, stream=sp.value)
+            if pending:  # (a pushing GEMV's partial is sent again: the same words under the same epoch)
+                self.comm.allreduce_residual(pending.pop()[0], b["hidden"], M * H, stream=sp.value)
 
-        def run(ts, ys, op, x, aux=None, mode=0, acc=False, **kw):
-            """ys (+)= op(x, aux) . W^T for the tensors ts (one launch)."""
+        def run(ts, ys, op, x, aux=None, mode=0, acc=False, push=False, **kw):
+            """ys (+)= op(x, aux) . W^T for the tensors ts (one launch); push:
+            the GEMV also sends its outputs to the peers for the next exchange
+            (returns whether it did)."""
             if fused:
                 flush()
                 ctx.gemv_src(ts, ys, op, x, aux, M=M, mode=mode, accumulate=acc, stream=sp.value, **kw)
-                return
+                return False
             xf = self._xf(("in", ts[0].cols), ts[0], M)
             if pending and op == L.XOP_RMSNORM and x is b["hidden"] and \
-                    self.comm.allreduce_fill(pending[-1], x, xf, aux, kw.get("eps", 0.0), stream=sp.value):
+                    self.comm.allreduce_fill(pending[-1][0], x, xf, aux, kw.get("eps", 0.0), stream=sp.value,
+                                             pushed=pending[-1][1]):
                 pending.pop()  # the all-reduce ran inside the RMSNorm fill
             else:
                 flush()
                 ctx.xfrag_fill_op(xf, op, x, aux, stream=sp.value, **kw)
+            if push and self.comm.gemv_push(ts[0], xf, ys[0], stream=sp.value):
+                return True
             if mode == 1:
                 self._check(lib.chpe_gemv_gateup_swiglu_xfrag_dev(ctx.ptr, ts[0].handle, ts[1].handle, xf.handle,
                                                                   _dev_ptr(ys[0]), sp))
@@ -438,17 +444,19 @@ class HybridEngine:
         def run_res(t: Tensor, op, x, aux=None, **kw):
             """hidden += op(x) . W^T (the residual add of the block); with tensor
             parallelism the shard's partial sum is summed over the ranks first:
-            one NVLink all-reduce kernel that also adds into hidden (comm), or
-            an NCCL all-reduce and an add."""
+            inside the next RMSNorm fill of hidden (comm, fuse_exchange; with
+            push_exchange the GEMV itself sends the partial), by the one-shot
+            NVLink all-reduce kernel, or by an NCCL all-reduce and an add."""
             hidden = b["hidden"]
             if self.comm is None and self.allreduce is None:
                 run([t], [hidden], op, x, aux, acc=True, **kw)
                 return
             part = b["mix_out"][:M]
-            run([t], [part], op, x, aux, **kw)
+            pushed = bool(run([t], [part], op, x, aux, push=self.comm is not None and self.fuse_exchange and
+                              self.push_exchange, **kw))
             if self.comm is not None:
                 if self.fuse_exchange:
-                    pending.append(part)  # summed by the next RMSNorm fill of hidden
+                    pending.append((part, pushed))  # summed by the next RMSNorm fill of hidden
                 else:
                     self.comm.allreduce_residual(part, hidden, M * H, stream=sp.value)
             else:

@@ -137,12 +137,25 @@ class Comm:
         self.ctx._check(self.ctx.lib.chpe_allreduce_residual_dev(self.handle, _dev_ptr(part), _dev_ptr(hidden), n,
                                                                   _stream_ptr(stream)))
 
-    def allreduce_fill(self, part, hidden, xf, gamma, eps: float, stream=None) -> bool:
+    def allreduce_fill(self, part, hidden, xf, gamma, eps: float, stream=None, pushed: bool = False) -> bool:
         """hidden[:M] += sum over ranks of part[:M], then xf = fragments of
-        RMSNorm(hidden) * gamma, in one kernel (chpe_allreduce_fill_dev).
-        False (nothing launched) where the fused form does not apply."""
+        RMSNorm(hidden) * gamma, in one kernel (chpe_allreduce_fill_dev);
+        pushed: part came from gemv_push, which sent it already.  False
+        (nothing launched) where the fused form does not apply."""
         rc = self.ctx.lib.chpe_allreduce_fill_dev(self.handle, _dev_ptr(part), _dev_ptr(hidden), xf.handle,
-                                                  _dev_ptr(gamma), C.c_float(eps), _stream_ptr(stream))
+                                                  _dev_ptr(gamma), C.c_float(eps), int(pushed), _stream_ptr(stream))
+        if rc == L.ENOTSUP:
+            return False
+        self.ctx._check(rc)
+        return True
+
+    def gemv_push(self, w, xf, y, stream=None) -> bool:
+        """y = xf . W^T, every output also sent to the peers for the next
+        exchange, which must be allreduce_fill(y, ..., pushed=True)
+        (chpe_gemv_xfrag_push_dev).  False (nothing launched) for tensors the
+        pushing GEMV does not take (outlier columns)."""
+        rc = self.ctx.lib.chpe_gemv_xfrag_push_dev(self.ctx.ptr, w.handle, xf.handle, _dev_ptr(y), self.handle,
+                                                   _stream_ptr(stream))
         if rc == L.ENOTSUP:
             return False
         self.ctx._check(rc)

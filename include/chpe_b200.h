@@ -293,7 +293,17 @@ int chpe_argmax_merge_dev(chpe_comm *comm, int *idx, float *maxv, int M, int ind
  * caller then runs the two calls.  Same exchange sequence rule as the
  * all-reduce; no counterpart in the single-process reference. */
 int chpe_allreduce_fill_dev(chpe_comm *comm, const float *part, float *hidden, chpe_xfrag *xf, const float *gamma,
-                            float eps, void *stream);
+                            float eps, int pushed, void *stream);
+/* The O / down projection of a tensor-parallel block with its half of the
+ * exchange built in: y[m][:] = xf . W^T (M rows of W's row count, stride
+ * that count) as chpe_gemv_xfrag_dev, and every finished output is also
+ * stored, tagged with the exchange's epoch, into every peer's receive area
+ * by the GEMV's own CTAs, overlapped with the weight streaming.  The very
+ * next exchange on `comm` must then be chpe_allreduce_fill_dev(part = y,
+ * pushed = 1), which only collects and sums.  (pushed = 0: the fill sends
+ * the partials itself.)  No counterpart in the single-process reference. */
+int chpe_gemv_xfrag_push_dev(chpe_ctx *ctx, const chpe_tensor *w, const chpe_xfrag *xf, float *y, chpe_comm *comm,
+                             void *stream);
 /* A comm object whose bounded wait expired is failed: the ranks' epochs may
  * be out of step, so every later chpe_allreduce_residual_dev on it returns
  * CHPE_ETIMEOUT at once (and a launch already queued, e.g. inside a CUDA

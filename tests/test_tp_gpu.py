@@ -47,6 +47,7 @@ def _rank(rank, world, port, scheme, q, allreduce="nccl"):
                                   allreduce="p2p" if allreduce.startswith("p2p") else allreduce)
         e = tp.eng
         e.fuse_exchange = allreduce != "p2p-separate"  # p2p: the all-reduce inside the next RMSNorm fill
+        e.push_exchange = allreduce == "p2p-push"  # ... with the partials sent by the O / down GEMVs
         e.buf["tokens"][:1] = 33
         toks = []
         for _ in range(16):  # eager steps
@@ -82,8 +83,8 @@ def _rank(rank, world, port, scheme, q, allreduce="nccl"):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("scheme,allreduce", [("q4g64", "p2p"), ("q4g64", "p2p-separate"), ("q4g64", "nccl"),
-                                              ("q8g32", "p2p")])
+@pytest.mark.parametrize("scheme,allreduce", [("q4g64", "p2p"), ("q4g64", "p2p-push"), ("q4g64", "p2p-separate"),
+                                              ("q4g64", "nccl"), ("q8g32", "p2p")])
 def test_tp2_decode_matches_single_gpu(ctx, scheme, allreduce):
     import torch
     import torch.multiprocessing as mp
@@ -116,7 +117,8 @@ def test_tp2_decode_matches_single_gpu(ctx, scheme, allreduce):
 def _fused_fill_check(ctx, comm, part, h0, rank):
     """chpe_allreduce_fill_dev against chpe_allreduce_residual_dev followed by
     the RMSNorm fill, on 8 rows of 8192 columns: hidden and the GEMV of the
-    fragments must agree bit for bit (two exchanges each, both slot parities)."""
+    fragments must agree bit for bit (two exchanges each, both slot parities);
+    then with the partial sent by a pushing GEMV (three exchanges each)."""
     import torch
     from chpe_qwen35_hybrid_engine_b200 import SCHEME_U_GROUP_F16_ZERO, X_F32, _lib as L
     from oracle import oracle as O
@@ -140,6 +142,30 @@ def _fused_fill_check(ctx, comm, part, h0, rank):
         ctx.gemv_xfrag(t, xb, yb)
         torch.cuda.synchronize()
         ok = ok and torch.equal(ha, hb) and torch.equal(ya, yb)
+    # the partial made by a pushing GEMV (chpe_gemv_xfrag_push_dev), collected
+    # by the fill: the same bits as GEMV, all-reduce, fill
+    Kin = 1024
+    rr = np.random.default_rng(100 + rank)  # each rank its own projection
+    c2, s2, z2 = O.quantize_asym(rr.normal(0, 0.02, (K, Kin)).astype(np.float32), 4, 64)
+    t2 = ctx.upload_matrix(4, SCHEME_U_GROUP_F16_ZERO, pack_codes(c2, 4), s2, z2, rows=K, cols=Kin, group=64)
+    xin = ctx.xfrag(t2, M, X_F32)
+    for _ in range(3):
+        ctx.xfrag_fill(xin, torch.from_numpy(rr.standard_normal((M, Kin)).astype(np.float32)).cuda())
+        ha = h0.view(M, K).cuda()
+        hc = ha.clone()
+        pa, pc = torch.empty(M, K, device="cuda"), torch.empty(M, K, device="cuda")
+        ctx.gemv_xfrag(t2, xin, pa)
+        comm.allreduce_residual(pa, ha, M * K)
+        ctx.xfrag_fill_op(xa, L.XOP_RMSNORM, ha, gamma, ldx=K, eps=1e-6)
+        assert comm.gemv_push(t2, xin, pc)
+        assert comm.allreduce_fill(pc, hc, xb, gamma, 1e-6, pushed=True)
+        ya, yc = torch.empty(M, N, device="cuda"), torch.empty(M, N, device="cuda")
+        ctx.gemv_xfrag(t, xa, ya)
+        ctx.gemv_xfrag(t, xb, yc)
+        torch.cuda.synchronize()
+        ok = ok and torch.equal(pa, pc) and torch.equal(ha, hc) and torch.equal(ya, yc)
+    xin.free()
+    t2.free()
     xa.free()
     xb.free()
     t.free()
