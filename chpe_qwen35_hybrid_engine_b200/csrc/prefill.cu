@@ -432,25 +432,56 @@ __device__ __forceinline__ float x_at(const void *x, int dt, size_t i) {
                                : __half2float(static_cast<const __half *>(x)[i]);
 }
 
-// Row scaling of the prefill activations: one block per token row computes
-// max |x| and stores (2^e, 2^-e) with max |x| * 2^e in [2^14, 2^15)
-// (row_scale_exp), so the fp16 tiles hold every row whatever its magnitude;
+// Row scaling of the prefill activations: each token row's max |x| gives
+// (2^e, 2^-e) with max |x| * 2^e in [2^14, 2^15) (row_scale_exp), so the
+// fp16 tiles hold every row whatever its magnitude;
 // the epilogue multiplies the row's sums by 2^-e (powers of two are exact).
-__global__ void __launch_bounds__(256) chpe_prefill_rowscale_kernel(const void *__restrict__ x, int dt, int K,
+// One warp per row (8 rows per CTA); rows whose start is 16-byte aligned and
+// whose length is a whole number of 16-byte vectors are read 16 bytes per
+// lane and load (all of a lane's loads in flight), the rest element-wise.
+// max |x| does not depend on the order, so both give the same scale.
+__device__ __forceinline__ float absmax16(uint32_t w, int dt) {
+    float a, b;
+    if (dt == CHPE_X_BF16) {
+        a = __uint_as_float(w << 16);
+        b = __uint_as_float(w & 0xffff0000u);
+    } else {
+        a = __half2float(__ushort_as_half((unsigned short)(w & 0xffffu)));
+        b = __half2float(__ushort_as_half((unsigned short)(w >> 16)));
+    }
+    return fmaxf(fabsf(a), fabsf(b));
+}
+
+__global__ void __launch_bounds__(256) chpe_prefill_rowscale_kernel(const void *__restrict__ x, int dt, int M, int K,
                                                                    float2 *__restrict__ rs) {
-    __shared__ float red[8];
     pdl_begin();
-    const int m = blockIdx.x;
+    const int lane = threadIdx.x & 31;
+    const int m = blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (m >= M) return;
+    const size_t esz = dt == CHPE_X_F32 ? 4 : 2;
+    const char *row = static_cast<const char *>(x) + (size_t)m * K * esz;
+    const size_t bytes = (size_t)K * esz;
     float am = 0.0f;
-    for (int k = threadIdx.x; k < K; k += blockDim.x) am = fmaxf(am, fabsf(x_at(x, dt, (size_t)m * K + k)));
+    if ((reinterpret_cast<uintptr_t>(row) & 15) == 0 && (bytes & 15) == 0) {
+        const uint4 *v = reinterpret_cast<const uint4 *>(row);
+        const int nv = (int)(bytes / 16);
+        for (int i = lane; i < nv; i += 32) {
+            const uint4 q = __ldg(v + i);
+            if (dt == CHPE_X_F32) {
+                am = fmaxf(am, fmaxf(fmaxf(fabsf(__uint_as_float(q.x)), fabsf(__uint_as_float(q.y))),
+                                     fmaxf(fabsf(__uint_as_float(q.z)), fabsf(__uint_as_float(q.w)))));
+            } else {
+                am = fmaxf(am, fmaxf(fmaxf(absmax16(q.x, dt), absmax16(q.y, dt)),
+                                     fmaxf(absmax16(q.z, dt), absmax16(q.w, dt))));
+            }
+        }
+    } else {
+        for (int k = lane; k < K; k += 32) am = fmaxf(am, fabsf(x_at(x, dt, (size_t)m * K + k)));
+    }
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, off));
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = am;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        float mx = 0.0f;
-        for (int w = 0; w < (int)(blockDim.x >> 5); ++w) mx = fmaxf(mx, red[w]);
-        const int e = row_scale_exp(mx);
+    if (lane == 0) {
+        const int e = row_scale_exp(am);
         rs[m] = make_float2(pow2_of(e), pow2_of(-e));
     }
 }
@@ -602,7 +633,8 @@ cudaError_t launch_prefill(const DevMatrix &w, const void *x, int x_dtype, int M
     p.accumulate = accumulate;
     p.err = err;
     const size_t total = (size_t)p.n_tt * kPN * p.n_kb * (kPK / 8);
-    cudaError_t e = launch_pdl(chpe_prefill_rowscale_kernel, dim3((unsigned)M), dim3(256), 0, st, x, x_dtype, w.K, rs);
+    cudaError_t e =
+        launch_pdl(chpe_prefill_rowscale_kernel, dim3((unsigned)((M + 7) / 8)), dim3(256), 0, st, x, x_dtype, M, w.K, rs);
     if (e != cudaSuccess) return e;
     e = launch_pdl(chpe_prefill_xprep_kernel, dim3((unsigned)std::min<size_t>((total + 255) / 256, 148 * 16)),
                    dim3(256), 0, st, x, x_dtype, M, w.K, p.n_tt, p.n_kb, static_cast<const float2 *>(rs),
